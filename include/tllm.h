@@ -1,0 +1,150 @@
+/*
+ * tllm.h -- C ABI of libtllm.so, the sm_100a decode hot path of triton-llm.
+ *
+ * Every entry point takes plain device pointers, element counts, a dtype enum
+ * and an optional stream (NULL = the library's stream for the current device).
+ * No entry point allocates device memory except the tllm_malloc* family: the
+ * caller (Python's triton_llm.gpu, or the model's workspace) owns all buffers,
+ * including the scratch buffers some kernels need.
+ *
+ * Every function returns a tllm_status (0 = success). On failure the
+ * thread-local message is available from tllm_last_error_string().
+ *
+ * Reference interfaces replaced (paths are inside ziliangpeng/triton-llm):
+ *   runtime  -> triton_llm/gpu.py:114-131 (cudaMalloc/cudaFree/cudaMemcpy
+ *               through ctypes), gpu.py:230-263 (allocate/to_device/
+ *               to_host/synchronize), gpu.py:179-181 (check_error)
+ *   kernels  -> triton_llm/kernels/*.py wrappers, cited per function below.
+ */
+#ifndef TLLM_H_
+#define TLLM_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void *tllm_stream_t; /* a cudaStream_t; NULL = library stream */
+
+typedef enum {
+  TLLM_OK = 0,
+  TLLM_ERR_INVALID_ARG = 1, /* bad shape / size / pointer: Python ValueError */
+  TLLM_ERR_CUDA = 2,        /* CUDA runtime error: Python RuntimeError */
+  TLLM_ERR_UNSUPPORTED = 3, /* valid but not built (e.g. head_dim 24) */
+  TLLM_ERR_NO_DEVICE = 4,   /* no CUDA device visible */
+  TLLM_ERR_NCCL = 5,        /* NCCL failure or NCCL library missing */
+  TLLM_ERR_TIMEOUT = 6,     /* a bounded wait ran out */
+  TLLM_ERR_INJECTED = 7     /* failure injected through TLLM_FAULT_INJECT */
+} tllm_status;
+
+typedef enum {
+  TLLM_F32 = 0,
+  TLLM_BF16 = 1,
+  TLLM_I32 = 2
+} tllm_dtype;
+
+/* ------------------------------------------------------------------------ */
+/* Runtime: devices, streams, memory (replaces triton_llm/gpu.py)            */
+/* ------------------------------------------------------------------------ */
+
+/* Message of the last failing call on this thread ("" if none). */
+const char *tllm_last_error_string(void);
+/* Library version, e.g. 100 for 0.1.0. */
+int tllm_version(void);
+
+int tllm_device_count(int *count);
+int tllm_set_device(int device);
+int tllm_get_device(int *device);
+/* The library stream of the current device (created on first use). */
+int tllm_get_stream(tllm_stream_t *stream);
+
+/* gpu.py:230-236 allocate(): stream-ordered pool allocation on the library
+ * stream (cudaMallocAsync); the pool keeps freed memory for reuse. */
+int tllm_malloc(void **ptr, size_t nbytes);
+/* gpu.py:194-200 DeviceTensor.__del__: stream-ordered free. */
+int tllm_free(void *ptr);
+/* Plain cudaMalloc/cudaFree for buffers that other devices map. */
+int tllm_malloc_static(void **ptr, size_t nbytes);
+int tllm_free_static(void *ptr);
+/* Page-locked host memory for the end-to-end copies. */
+int tllm_host_alloc(void **ptr, size_t nbytes);
+int tllm_host_free(void *ptr);
+
+/* gpu.py:215-224 from_numpy / gpu.py:202-213 to_numpy: the copy is queued
+ * on the library stream and the call returns once it is complete. */
+int tllm_memcpy_h2d(void *dst, const void *src, size_t nbytes);
+int tllm_memcpy_d2h(void *dst, const void *src, size_t nbytes);
+int tllm_memcpy_d2d(void *dst, const void *src, size_t nbytes);
+/* Asynchronous variants on `stream` (host side must be pinned to overlap). */
+int tllm_memcpy_h2d_async(void *dst, const void *src, size_t nbytes,
+                          tllm_stream_t stream);
+int tllm_memcpy_d2h_async(void *dst, const void *src, size_t nbytes,
+                          tllm_stream_t stream);
+int tllm_memset(void *ptr, int value, size_t nbytes, tllm_stream_t stream);
+/* gpu.py:252-263 synchronize(): waits for the library stream. */
+int tllm_synchronize(void);
+int tllm_stream_synchronize(tllm_stream_t stream);
+int tllm_device_synchronize(void);
+
+/* Stream and event helpers for timing and overlap. */
+int tllm_stream_create(tllm_stream_t *stream);
+int tllm_stream_destroy(tllm_stream_t stream);
+int tllm_event_create(void **event);
+int tllm_event_destroy(void *event);
+int tllm_event_record(void *event, tllm_stream_t stream);
+int tllm_event_elapsed_ms(void *start, void *end, float *ms);
+int tllm_stream_wait_event(tllm_stream_t stream, void *event);
+
+/* Device-side error word of the current device (bit set: 1 = a bounded
+ * wait ran out, 2 = a device-side length exceeded its bound, 4 = a token id
+ * was out of range). Waits for the library stream first; reset != 0 clears
+ * the word. Kernels report through it instead of trapping. */
+int tllm_device_error(int *code, int reset);
+
+/* Memory info of the current device (bytes). */
+int tllm_mem_info(size_t *free_bytes, size_t *total_bytes);
+
+/* ------------------------------------------------------------------------ */
+/* Attention                                                                 */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * Split-KV GQA decode attention over a preallocated KV cache.
+ *
+ * Replaces triton_llm/kernels/attention_gqa.py:149-269 (attention_gqa) on
+ * its decode path (seq_q == 1, causal=False, as called from
+ * smollm2_triton/model.py:310-314), batched over B independent sequences.
+ *
+ *   q        (B, n_head, head_dim) f32
+ *   k_cache  (B, n_kv_head, max_seq, head_dim) kv_dtype
+ *   v_cache  (B, n_kv_head, max_seq, head_dim) kv_dtype
+ *   seq_lens (B,) int32 on the device: keys to attend for each sequence
+ *            (0 <= seq_lens[b] <= max_seq; 0 yields a zero output row)
+ *   out      (B, n_head, head_dim) f32
+ *   head h reads kv head h / (n_head / n_kv_head) (attention_gqa.py:76).
+ *   sm_scale <= 0 selects 1/sqrt(head_dim) (attention_gqa.py:235-236).
+ *   max_len  host-side upper bound on max(seq_lens); it sizes the split
+ *            grid (values above max_seq are clamped).
+ *
+ * Scratch (caller owned, see tllm_gqa_decode_workspace):
+ *   partial   f32 buffer of `partial_bytes`
+ *   counters  int32 (B * n_kv_head) zero-filled once; every call leaves
+ *             them at zero again.
+ */
+int tllm_gqa_decode_workspace(int batch, int n_head, int n_kv_head,
+                              int head_dim, int max_seq, int kv_dtype,
+                              size_t *partial_bytes, size_t *counter_bytes);
+int tllm_gqa_decode(const float *q, const void *k_cache, const void *v_cache,
+                    int kv_dtype, const int32_t *seq_lens, float *out,
+                    int batch, int n_head, int n_kv_head, int head_dim,
+                    int max_seq, int max_len, float sm_scale, void *partial,
+                    size_t partial_bytes, int32_t *counters,
+                    tllm_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TLLM_H_ */

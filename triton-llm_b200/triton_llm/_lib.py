@@ -1,0 +1,146 @@
+"""ctypes binding of libtllm.so (the sm_100a kernels and device runtime).
+
+The shared library is built in-tree by ``triton-llm_b200/csrc/build.py`` (or
+``__graft_entry__.build()``). There is no fallback: if the library or a CUDA
+device is missing, every entry point raises. Status codes returned by the C
+ABI (include/tllm.h) are mapped onto the exception types the reference uses:
+
+* ``TLLM_ERR_INVALID_ARG`` -> ``ValueError`` (reference kernels raise
+  ``ValueError`` for bad shapes, e.g. triton_llm/kernels/attention_gqa.py:189)
+* ``TLLM_ERR_NO_DEVICE``   -> ``RuntimeError("No supported GPU runtime found...")``
+  (same text as triton_llm/gpu.py:83-86, which callers match on)
+* anything else            -> ``RuntimeError("GPU runtime error (cuda): ...")``
+  (triton_llm/gpu.py:179-181)
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().with_name("libtllm.so")
+
+OK = 0
+ERR_INVALID_ARG = 1
+ERR_CUDA = 2
+ERR_UNSUPPORTED = 3
+ERR_NO_DEVICE = 4
+ERR_NCCL = 5
+ERR_TIMEOUT = 6
+ERR_INJECTED = 7
+
+F32 = 0
+BF16 = 1
+I32 = 2
+
+_vp = ctypes.c_void_p
+_i = ctypes.c_int
+_sz = ctypes.c_size_t
+_f = ctypes.c_float
+_pvp = ctypes.POINTER(ctypes.c_void_p)
+_pi = ctypes.POINTER(ctypes.c_int)
+_psz = ctypes.POINTER(ctypes.c_size_t)
+_pf = ctypes.POINTER(ctypes.c_float)
+
+# name -> argtypes (restype is always int except tllm_last_error_string)
+SIGNATURES: dict[str, list] = {
+    "tllm_version": [],
+    "tllm_device_count": [_pi],
+    "tllm_set_device": [_i],
+    "tllm_get_device": [_pi],
+    "tllm_get_stream": [_pvp],
+    "tllm_malloc": [_pvp, _sz],
+    "tllm_free": [_vp],
+    "tllm_malloc_static": [_pvp, _sz],
+    "tllm_free_static": [_vp],
+    "tllm_host_alloc": [_pvp, _sz],
+    "tllm_host_free": [_vp],
+    "tllm_memcpy_h2d": [_vp, _vp, _sz],
+    "tllm_memcpy_d2h": [_vp, _vp, _sz],
+    "tllm_memcpy_d2d": [_vp, _vp, _sz],
+    "tllm_memcpy_h2d_async": [_vp, _vp, _sz, _vp],
+    "tllm_memcpy_d2h_async": [_vp, _vp, _sz, _vp],
+    "tllm_memset": [_vp, _i, _sz, _vp],
+    "tllm_synchronize": [],
+    "tllm_stream_synchronize": [_vp],
+    "tllm_device_synchronize": [],
+    "tllm_stream_create": [_pvp],
+    "tllm_stream_destroy": [_vp],
+    "tllm_event_create": [_pvp],
+    "tllm_event_destroy": [_vp],
+    "tllm_event_record": [_vp, _vp],
+    "tllm_event_elapsed_ms": [_vp, _vp, _pf],
+    "tllm_stream_wait_event": [_vp, _vp],
+    "tllm_device_error": [_pi, _i],
+    "tllm_mem_info": [_psz, _psz],
+    # attention
+    "tllm_gqa_decode_workspace": [_i, _i, _i, _i, _i, _i, _psz, _psz],
+    "tllm_gqa_decode": [_vp, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _i, _i, _i,
+                        _f, _vp, _sz, _vp, _vp],
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load():
+    """Load libtllm.so once; raises RuntimeError('Failed to load ...')."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = os.environ.get("TLLM_LIB", str(LIB_PATH))
+        try:
+            lib = ctypes.CDLL(path)
+        except OSError as e:
+            raise RuntimeError(
+                f"Failed to load libtllm.so from {path}: {e}. Build it with "
+                "`python triton-llm_b200/csrc/build.py`.") from e
+        for name, argtypes in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = argtypes
+            fn.restype = ctypes.c_int
+        lib.tllm_last_error_string.argtypes = []
+        lib.tllm_last_error_string.restype = ctypes.c_char_p
+        _lib = lib
+    return _lib
+
+
+def last_error() -> str:
+    msg = load().tllm_last_error_string()
+    return msg.decode(errors="replace") if msg else ""
+
+
+def check(status: int, what: str = "") -> None:
+    """Raise the Python exception matching a tllm_status."""
+    if status == OK:
+        return
+    msg = last_error()
+    where = f"{what}: " if what else ""
+    if status == ERR_INVALID_ARG:
+        raise ValueError(f"{where}{msg}")
+    if status == ERR_NO_DEVICE:
+        raise RuntimeError(
+            "No supported GPU runtime found. libtllm.so loaded but no CUDA "
+            f"device is visible ({msg}).")
+    if status == ERR_UNSUPPORTED:
+        raise NotImplementedError(f"{where}{msg}")
+    raise RuntimeError(f"GPU runtime error (cuda): {status} ({where}{msg})")
+
+
+def call(name: str, *args) -> None:
+    """Call a tllm_* entry point and raise on a non-zero status."""
+    check(getattr(load(), name)(*args), name)
+
+
+def ptr(x) -> int | None:
+    """Raw device address of a DeviceTensor / int / None."""
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    return x.data_ptr()
