@@ -151,7 +151,8 @@ def profiled_traffic(key: str):
     p = REPO / "profiles" / "traffic.json"
     if p.exists():
         try:
-            return json.loads(p.read_text()).get(key)
+            d = json.loads(p.read_text()).get(key)
+            return d.get("bytes_per_launch") if d else None
         except Exception:
             return None
     return None
@@ -166,7 +167,9 @@ class GQAWorkload:
     dtype = "bf16"
     kernel = "gqa_decode"
 
-    def __init__(self, copies=6):
+    BENCH_COPIES = 6
+
+    def __init__(self, copies=BENCH_COPIES):
         import inputs
         self.B, self.H, self.Hkv, self.D, self.S = 64, 9, 3, 64, 2048
         self.lens, self.q, ks, vs = inputs.cfg2_inputs()
@@ -184,8 +187,8 @@ class GQAWorkload:
                 "head_dim": self.D, "kv_lens": "U[128,2048] seed 1",
                 "sum_kv_len": int(self.lens.sum()),
                 "kv_dtype": "bf16", "kv_layout": "(B, n_kv, 2048, d) prealloc",
-                "l2": f"{self.copies} rotating cache copies "
-                      f"({self.copies * self.kv_bytes / 1e6:.0f} MB touched > 126 MB L2)"}
+                "l2": f"{self.BENCH_COPIES} rotating cache copies "
+                      f"({self.BENCH_COPIES * self.kv_bytes / 1e6:.0f} MB touched > 126 MB L2)"}
 
     def setup(self):
         from triton_llm import gpu
