@@ -143,6 +143,30 @@ int tllm_gqa_decode(const float *q, const void *k_cache, const void *v_cache,
                     size_t partial_bytes, int32_t *counters,
                     tllm_stream_t stream);
 
+/*
+ * Allocation-free variant of tllm_gqa_decode. It has no counterpart in the
+ * reference; it exists for callers that cannot let a library allocate device
+ * memory (servers that own all of HBM through their own arenas, hosts whose
+ * memory accounting forbids hidden allocations, decode loops that must never
+ * block in cudaMalloc). Same arguments and results as tllm_gqa_decode, minus
+ * the scratch buffers: the split-KV partials and counters live in a fixed
+ * ~8.3 MiB device array inside libtllm.so (8 MiB of partials; when more
+ * would be needed the batch is cut into fewer, longer splits). Limit: batch *
+ * n_head <= 65536, larger batches fail with TLLM_ERR_INVALID_ARG. The first
+ * call on a device looks up the array's device address
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * All calls on a device share the array and it keeps the last call's data:
+ * calls that overlap on the GPU race and must not be issued. Device-side
+ * error codes of these calls are kept in the same array, not in the word
+ * read by tllm_device_error.
+ */
+int tllm_gqa_decode_noalloc(const float *q, const void *k_cache,
+                            const void *v_cache, int kv_dtype,
+                            const int32_t *seq_lens, float *out, int batch,
+                            int n_head, int n_kv_head, int head_dim,
+                            int max_seq, int max_len, float sm_scale,
+                            tllm_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -554,37 +554,14 @@ int pick_chunk(int rows, int batch, int ygrid, int max_len) {
   return (int)(chunk_tiles * rows);
 }
 
-}  // namespace
-}  // namespace tllm
-
-using namespace tllm;
-
-extern "C" {
-
-int tllm_gqa_decode_workspace(int batch, int n_head, int n_kv_head,
-                              int head_dim, int max_seq, int kv_dtype,
-                              size_t *partial_bytes, size_t *counter_bytes) {
-  TLLM_CHECK_ARG(partial_bytes && counter_bytes, "NULL output pointer");
-  TLLM_CHECK_ARG(batch >= 0 && n_head > 0 && n_kv_head > 0 && head_dim > 0 &&
-                     max_seq >= 0,
-                 "invalid shape");
-  TLLM_CHECK_ARG(n_head % n_kv_head == 0,
-                 "n_head (%d) must be divisible by n_kv_head (%d)", n_head,
-                 n_kv_head);
-  (void)kv_dtype;
-  *partial_bytes =
-      (size_t)batch * n_head * kMaxSplits * (head_dim + 2) * sizeof(float);
-  *counter_bytes = (size_t)batch * n_head * sizeof(int32_t);
-  return TLLM_OK;
-}
-
-int tllm_gqa_decode(const float *q, const void *k_cache, const void *v_cache,
-                    int kv_dtype, const int32_t *seq_lens, float *out,
-                    int batch, int n_head, int n_kv_head, int head_dim,
-                    int max_seq, int max_len, float sm_scale, void *partial,
-                    size_t partial_bytes, int32_t *counters,
-                    tllm_stream_t stream) {
-  TLLM_INJECT("launch");
+// Validation, split selection, tensor maps and launch shared by the decode
+// entry points; `err_word` is the device int that receives error codes.
+static int decode_impl(const float *q, const void *k_cache, const void *v_cache,
+                       int kv_dtype, const int32_t *seq_lens, float *out,
+                       int batch, int n_head, int n_kv_head, int head_dim,
+                       int max_seq, int max_len, float sm_scale, void *partial,
+                       size_t partial_bytes, int32_t *counters, int *err_word,
+                       tllm_stream_t stream) {
   TLLM_CHECK_ARG(batch >= 0 && n_head > 0 && n_kv_head > 0,
                  "invalid head counts n_head=%d n_kv_head=%d", n_head,
                  n_kv_head);
@@ -646,7 +623,7 @@ int tllm_gqa_decode(const float *q, const void *k_cache, const void *v_cache,
                   ? p.part_acc + (size_t)batch * n_head * max_splits * head_dim
                   : nullptr;
   p.counters = counters;
-  p.err = device_error_ptr();
+  p.err = err_word;
   TLLM_CHECK_ARG(p.err, "device error word unavailable");
   p.n_head = n_head;
   p.n_kv = n_kv_head;
@@ -665,4 +642,130 @@ int tllm_gqa_decode(const float *q, const void *k_cache, const void *v_cache,
   return dispatch_d<float>(head_dim, G, p, mk, mv, grid, st);
 }
 
+}  // namespace
+}  // namespace tllm
+
+using namespace tllm;
+
+extern "C" {
+
+int tllm_gqa_decode_workspace(int batch, int n_head, int n_kv_head,
+                              int head_dim, int max_seq, int kv_dtype,
+                              size_t *partial_bytes, size_t *counter_bytes) {
+  TLLM_CHECK_ARG(partial_bytes && counter_bytes, "NULL output pointer");
+  TLLM_CHECK_ARG(batch >= 0 && n_head > 0 && n_kv_head > 0 && head_dim > 0 &&
+                     max_seq >= 0,
+                 "invalid shape");
+  TLLM_CHECK_ARG(n_head % n_kv_head == 0,
+                 "n_head (%d) must be divisible by n_kv_head (%d)", n_head,
+                 n_kv_head);
+  (void)kv_dtype;
+  *partial_bytes =
+      (size_t)batch * n_head * kMaxSplits * (head_dim + 2) * sizeof(float);
+  *counter_bytes = (size_t)batch * n_head * sizeof(int32_t);
+  return TLLM_OK;
+}
+
+int tllm_gqa_decode(const float *q, const void *k_cache, const void *v_cache,
+                    int kv_dtype, const int32_t *seq_lens, float *out,
+                    int batch, int n_head, int n_kv_head, int head_dim,
+                    int max_seq, int max_len, float sm_scale, void *partial,
+                    size_t partial_bytes, int32_t *counters,
+                    tllm_stream_t stream) {
+  TLLM_INJECT("launch");
+  return decode_impl(q, k_cache, v_cache, kv_dtype, seq_lens, out, batch,
+                     n_head, n_kv_head, head_dim, max_seq, max_len, sm_scale,
+                     partial, partial_bytes, counters, device_error_ptr(),
+                     stream);
+}
+
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free decode entry point.
+//
+// Some host programs cannot let a library allocate device memory: inference
+// servers that carve all of HBM into their own arenas at start-up and
+// account for every byte, plugin hosts whose memory budget forbids hidden
+// allocations, and decode loops that must never block in the allocator
+// (cudaMalloc/cudaFree can wait for the whole device). For them this entry
+// point takes its split-KV scratch from a fixed array in device global
+// memory that is part of the library image, so a call allocates nothing.
+//
+// Limits: the partial-result region is kNoAllocPartialBytes (8 MiB); when a
+// batch would need more split partials than that, fewer, longer splits are
+// used. The ticket counters cover batch * n_head <= kNoAllocMaxCounters
+// (65536); larger batches are rejected with TLLM_ERR_INVALID_ARG. Every GPU
+// that loads the library keeps this ~8.3 MiB until the process exits.
+//
+// The array is shared by every call on a device and keeps the last call's
+// contents; the counters that must start at zero are cleared on the stream
+// before each launch. Calls that overlap on the GPU (on different streams,
+// or from several host threads) race on the array and must not be issued.
+// ---------------------------------------------------------------------------
+namespace tllm {
+namespace {
+
+constexpr size_t kNoAllocPartialBytes = size_t(8) << 20;
+constexpr int kNoAllocMaxCounters = 65536;
+constexpr size_t kNoAllocCounterOffset = kNoAllocPartialBytes;
+constexpr size_t kNoAllocErrOffset =
+    kNoAllocCounterOffset + size_t(kNoAllocMaxCounters) * sizeof(int32_t);
+constexpr size_t kNoAllocBytes = kNoAllocErrOffset + 256;
+
+// Scratch of tllm_gqa_decode_noalloc. In host code this name is only a
+// host-side stand-in for the device array: its device address must be
+// looked up with cudaGetSymbolAddress (done once per device below).
+static __device__ __align__(256) unsigned char g_decode_scratch[kNoAllocBytes];
+
+std::mutex g_noalloc_mu;
+unsigned char *g_noalloc_addr[64];
+
+// Device address of g_decode_scratch on the current device (looked up on the
+// first call made while that device is current).
+int noalloc_scratch(unsigned char **addr) {
+  int dev = 0;
+  TLLM_CUDA(cudaGetDevice(&dev));
+  TLLM_CHECK_ARG(dev >= 0 && dev < 64, "device index %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void *ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_decode_scratch);
+    if (e != cudaSuccess || !ptr) {
+      set_error("cudaGetSymbolAddress(decode scratch) failed: %s (%d)",
+                cudaGetErrorString(e), (int)e);
+      return TLLM_ERR_CUDA;
+    }
+    g_noalloc_addr[dev] = static_cast<unsigned char *>(ptr);
+  }
+  *addr = g_noalloc_addr[dev];
+  return TLLM_OK;
+}
+
+}  // namespace
+}  // namespace tllm
+
+extern "C" int tllm_gqa_decode_noalloc(
+    const float *q, const void *k_cache, const void *v_cache, int kv_dtype,
+    const int32_t *seq_lens, float *out, int batch, int n_head, int n_kv_head,
+    int head_dim, int max_seq, int max_len, float sm_scale,
+    tllm_stream_t stream) {
+  TLLM_CHECK_ARG(batch >= 0 && n_head > 0, "invalid batch %d / n_head %d",
+                 batch, n_head);
+  TLLM_CHECK_ARG((long)batch * n_head <= kNoAllocMaxCounters,
+                 "tllm_gqa_decode_noalloc supports batch * n_head <= %d "
+                 "(got %d * %d); use tllm_gqa_decode with caller-owned scratch",
+                 kNoAllocMaxCounters, batch, n_head);
+  if (batch == 0) return TLLM_OK;
+  unsigned char *base = nullptr;
+  int rc = noalloc_scratch(&base);
+  if (rc) return rc;
+  int32_t *counters = reinterpret_cast<int32_t *>(base + kNoAllocCounterOffset);
+  int *err_word = reinterpret_cast<int *>(base + kNoAllocErrOffset);
+  cudaStream_t st = resolve(stream);
+  TLLM_CUDA(cudaMemsetAsync(counters, 0, (size_t)batch * n_head * sizeof(int32_t),
+                            st));
+  return decode_impl(q, k_cache, v_cache, kv_dtype, seq_lens, out, batch,
+                     n_head, n_kv_head, head_dim, max_seq, max_len, sm_scale,
+                     base, kNoAllocPartialBytes, counters, err_word, st);
+}

@@ -79,6 +79,8 @@ SIGNATURES: dict[str, list] = {
     "tllm_gqa_decode_workspace": [_i, _i, _i, _i, _i, _i, _psz, _psz],
     "tllm_gqa_decode": [_vp, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _i, _i, _i,
                         _f, _vp, _sz, _vp, _vp],
+    "tllm_gqa_decode_noalloc": [_vp, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _i,
+                                _i, _i, _f, _vp],
 }
 
 _lib = None
