@@ -103,6 +103,15 @@ int tllm_stream_wait_event(tllm_stream_t stream, void *event);
  * the word. Kernels report through it instead of trapping. */
 int tllm_device_error(int *code, int reset);
 
+/* CUDA graphs of the library's work (decode steps are replayed as graphs so
+ * that host launch cost leaves the critical path). Capture is thread-local:
+ * every tllm_* call made by this thread on `stream` between begin and end is
+ * recorded, not executed. */
+int tllm_graph_capture_begin(tllm_stream_t stream);
+int tllm_graph_capture_end(tllm_stream_t stream, void **graph_exec);
+int tllm_graph_launch(void *graph_exec, tllm_stream_t stream);
+int tllm_graph_destroy(void *graph_exec);
+
 /* Memory info of the current device (bytes). */
 int tllm_mem_info(size_t *free_bytes, size_t *total_bytes);
 

@@ -139,3 +139,16 @@ def test_uniform_length_without_lens_array(gpu):
                max_len=S)
     ref = ops.gqa_decode(q, kc, vc, np.full(B, S))
     np.testing.assert_allclose(od.to_numpy(), ref, atol=ATOL)
+
+
+@pytest.mark.parametrize("env", [{"TLLM_GQA_NO_MMA": "1"}, {}])
+def test_every_kernel_path(env):
+    """Tensor-core and CUDA-core kernels each match the oracle on bf16."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+    script = Path(__file__).with_name("_gqa_paths_check.py")
+    r = subprocess.run([sys.executable, str(script)], env={**os.environ, **env},
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr

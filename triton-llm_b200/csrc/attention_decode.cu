@@ -62,6 +62,13 @@ struct Vec<__nv_bfloat16> {
   }
 };
 
+// 2^x with the MUFU instruction (relative error ~2^-22; -inf -> +0).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 struct DecodeParams {
   const float *q;        // (B, n_head, D)
   float *out;            // (B, n_head, D)
@@ -249,14 +256,14 @@ __global__ void __launch_bounds__(kThreads)
           tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
         const float mnew = fmaxf(m_run[g], tmax);
         if (mnew != -INFINITY) {
-          const float alpha = exp2f(m_run[g] - mnew);
+          const float alpha = fast_exp2(m_run[g] - mnew);
           m_run[g] = mnew;
           l_run[g] *= alpha;
 #pragma unroll
           for (int e = 0; e < S::NV * S::VEC; ++e) acc[g][e] *= alpha;
 #pragma unroll
           for (int it = 0; it < S::ITERS; ++it) {
-            const float pv = exp2f(sc[it][g] - mnew);  // exp2(-inf) = 0
+            const float pv = fast_exp2(sc[it][g] - mnew);  // exp2(-inf) = 0
             sc[it][g] = pv;
             l_run[g] += pv;
           }
@@ -351,7 +358,7 @@ __global__ void __launch_bounds__(kThreads)
       for (int w = 0; w < kConsumerWarps; ++w) {
         const float wm = w_m[w * G + g];
         if (wm != -INFINITY) {
-          const float sc = exp2f(wm - mx);
+          const float sc = fast_exp2(wm - mx);
           num = fmaf(w_acc[(w * G + g) * D + d], sc, num);
           den = fmaf(w_l[w * G + g], sc, den);
         }
@@ -396,7 +403,7 @@ __global__ void __launch_bounds__(kThreads)
     float den = 0.f;
     for (int s = lane; s < n_splits; s += 32) {
       const float ms = __ldcg(&p.part_ml[(base + s) * 2]);
-      const float w = (ms == -INFINITY) ? 0.f : exp2f(ms - mx);
+      const float w = (ms == -INFINITY) ? 0.f : fast_exp2(ms - mx);
       sw[g * kMaxSplits + s] = w;
       den = fmaf(__ldcg(&p.part_ml[(base + s) * 2 + 1]), w, den);
     }
@@ -420,6 +427,411 @@ __global__ void __launch_bounds__(kThreads)
 }
 
 // --------------------------------------------------------------------------
+// Tensor-core variant for bf16 caches (head_dim 64 / 128).
+//
+// Same decomposition, ring and split merge as above, but the products run on
+// the tensor cores with mma.sync m16n8k16 (bf16 in, fp32 accumulate):
+//   S (16 heads x 16 keys) = Q (16 x D) . K_w^T      per consumer warp
+//   O (16 heads x D)      += P (16 x 16 keys) . V_w
+// where warp w owns keys [16w, 16w + 16) of every 64-key tile. The query
+// heads of the CTA are the 16 M rows (rows >= G are zero). q and p are each
+// split into a bf16 head and a bf16 residual (x = hi + lo) and both halves
+// are multiplied, so scores and weights keep ~16 mantissa bits: the result
+// matches fp32 arithmetic on the bf16 cache to ~1e-6 relative. K/V tiles
+// arrive through TMA with 128-byte swizzle (64-dim sub-tiles of 128 B rows),
+// which makes the ldmatrix reads bank-conflict free.
+// --------------------------------------------------------------------------
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0,
+                                        uint32_t &r1, uint32_t &r2,
+                                        uint32_t &r3) {
+  asm volatile(
+      "ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+      : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+      : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0,
+                                          uint32_t &r1, uint32_t &r2,
+                                          uint32_t &r3) {
+  asm volatile(
+      "ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+      : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+      : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4],
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// (x0, x1) -> bf16x2 with x0 in the low half (round to nearest even)
+__device__ __forceinline__ uint32_t pack_bf16x2(float x0, float x1) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(x1), "f"(x0));
+  return r;
+}
+// x = hi + lo with hi, lo bf16 pairs
+__device__ __forceinline__ void split_bf16x2(float x0, float x1, uint32_t &hi,
+                                             uint32_t &lo) {
+  hi = pack_bf16x2(x0, x1);
+  lo = pack_bf16x2(x0 - bf16lo(hi), x1 - bf16hi(hi));
+}
+
+
+template <int D>
+struct MmaShape {
+  static constexpr int KT = 64;                    // keys per tile
+  static constexpr int SUB = D / 64;               // 128-byte sub-tiles per row
+  static constexpr int SUB_BYTES = KT * 128;       // 8 KB
+  static constexpr int TILE_BYTES = SUB * SUB_BYTES;
+  static constexpr int STAGES = D <= 64 ? 4 : 3;
+  static constexpr int KSTEPS = D / 16;
+  static constexpr int NT = D / 8;
+  static constexpr size_t RING =
+      2 * (size_t)STAGES * TILE_BYTES + 2 * STAGES * sizeof(uint64_t);
+};
+
+template <int D>
+__global__ void __launch_bounds__(kThreads)
+    gqa_decode_mma_kernel(const DecodeParams p, const int G,
+                          const __grid_constant__ CUtensorMap tmk,
+                          const __grid_constant__ CUtensorMap tmv) {
+  using S = MmaShape<D>;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t *k_st = smem;
+  uint8_t *v_st = smem + S::STAGES * S::TILE_BYTES;
+  uint64_t *full =
+      reinterpret_cast<uint64_t *>(smem + 2 * S::STAGES * S::TILE_BYTES);
+  uint64_t *empty = full + S::STAGES;
+  __shared__ int s_flag;
+
+  const int b = blockIdx.z;
+  const int y = blockIdx.y;
+  const int kvh = y / p.n_gsub;
+  const int gsub = y - kvh * p.n_gsub;
+  const int j = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+
+  int len = p.seq_lens ? p.seq_lens[b] : p.max_len;
+  len = len < 0 ? 0 : (len > p.max_seq ? p.max_seq : len);
+  int n_splits = (len + p.chunk - 1) / p.chunk;
+  if (n_splits < 1) n_splits = 1;
+  if (n_splits > p.max_splits) {
+    if (tid == 0 && j == 0) atomicOr(p.err, DEV_ERR_LEN_CLAMPED);
+    n_splits = p.max_splits;
+    len = n_splits * p.chunk;
+  }
+  if (j >= n_splits) return;
+  const int start = j * p.chunk;
+  const int end = min(start + p.chunk, len);
+  const int nrows = end > start ? end - start : 0;
+  const int ntiles = (nrows + S::KT - 1) / S::KT;
+  const int head0 = kvh * p.group + gsub * G;
+
+  if (tid == 0) {
+    for (int s = 0; s < S::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumerWarps);
+    }
+    fence_mbar_init();
+    s_flag = 0;
+  }
+  __syncthreads();
+
+  bool failed = false;
+  if (warp == kConsumerWarps) {
+    if (lane == 0) {
+      const int plane = b * p.n_kv + kvh;
+      for (int t = 0; t < ntiles; ++t) {
+        const int s = t % S::STAGES;
+        if (t >= S::STAGES &&
+            !mbar_wait_bounded(&empty[s], ((t / S::STAGES) - 1) & 1)) {
+          failed = true;
+          break;
+        }
+        mbar_expect_tx(&full[s], 2 * S::TILE_BYTES);
+        const int row = start + t * S::KT;
+#pragma unroll
+        for (int sub = 0; sub < S::SUB; ++sub) {
+          tma_load_3d(k_st + s * S::TILE_BYTES + sub * S::SUB_BYTES, &tmk,
+                      &full[s], sub * 64, row, plane);
+          tma_load_3d(v_st + s * S::TILE_BYTES + sub * S::SUB_BYTES, &tmv,
+                      &full[s], sub * 64, row, plane);
+        }
+      }
+    }
+  }
+
+  const int r0 = lane >> 2;          // fragment rows r0 and r0 + 8
+  const int cq = (lane & 3) * 2;     // fragment column pair
+  float o[S::NT][4];
+  float m_r[2] = {-INFINITY, -INFINITY};
+  float l_r[2] = {0.f, 0.f};
+  if (warp < kConsumerWarps) {
+    // ---- q fragments (A operand), scaled and split into hi / lo
+    uint32_t qh[S::KSTEPS][4], ql[S::KSTEPS][4];
+#pragma unroll
+    for (int kk = 0; kk < S::KSTEPS; ++kk) {
+#pragma unroll
+      for (int f = 0; f < 4; ++f) {
+        const int row = r0 + ((f & 1) ? 8 : 0);
+        const int col = kk * 16 + cq + ((f & 2) ? 8 : 0);
+        float x0 = 0.f, x1 = 0.f;
+        if (row < G) {
+          const float2 v = *reinterpret_cast<const float2 *>(
+              p.q + ((size_t)b * p.n_head + head0 + row) * D + col);
+          x0 = v.x * p.qscale;
+          x1 = v.y * p.qscale;
+        }
+        split_bf16x2(x0, x1, qh[kk][f], ql[kk][f]);
+      }
+    }
+#pragma unroll
+    for (int n = 0; n < S::NT; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[n][e] = 0.f;
+
+    // ldmatrix lane addressing (row = key within the warp's 16, 16-B chunk)
+    const int k_key = warp * 16 + ((lane >> 4) & 1) * 8 + (lane & 7);
+    const int k_dof = ((lane >> 3) & 1) * 8;
+    const int v_key = warp * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
+    const int v_dof = ((lane >> 4) & 1) * 8;
+
+    for (int t = 0; t < ntiles; ++t) {
+      const int s = t % S::STAGES;
+      const bool ok = __all_sync(
+          0xffffffffu, mbar_wait_bounded(&full[s], (t / S::STAGES) & 1));
+      if (!ok) {
+        failed = true;
+        break;
+      }
+      uint8_t *kt = k_st + s * S::TILE_BYTES;
+      uint8_t *vt = v_st + s * S::TILE_BYTES;
+      const int valid = min(S::KT, nrows - t * S::KT);
+
+      // ---- S = Q K^T over this warp's 16 keys
+      float sc[2][4];
+#pragma unroll
+      for (int n = 0; n < 2; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sc[n][e] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < S::KSTEPS; ++kk) {
+        const int dim = kk * 16 + k_dof;
+        const int sub = dim >> 6;
+        const int chunk = (dim & 63) >> 3;
+        const uint32_t addr = smem_u32(kt + sub * S::SUB_BYTES + k_key * 128 +
+                                       ((chunk ^ (k_key & 7)) << 4));
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(addr, b0, b1, b2, b3);
+        mma_bf16(sc[0], qh[kk], b0, b1);
+        mma_bf16(sc[0], ql[kk], b0, b1);
+        mma_bf16(sc[1], qh[kk], b2, b3);
+        mma_bf16(sc[1], ql[kk], b2, b3);
+      }
+      const bool partial = valid < S::KT;
+      if (partial) {
+#pragma unroll
+        for (int n = 0; n < 2; ++n)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int key = warp * 16 + n * 8 + cq + (e & 1);
+            if (key >= valid) sc[n][e] = -INFINITY;
+          }
+      }
+
+      // ---- online softmax on rows r0 (e = 0,1) and r0 + 8 (e = 2,3)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float mx = fmaxf(fmaxf(sc[0][2 * h], sc[0][2 * h + 1]),
+                         fmaxf(sc[1][2 * h], sc[1][2 * h + 1]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float mn = fmaxf(m_r[h], mx);
+        const float msafe = (mn == -INFINITY) ? 0.f : mn;
+        if (mn != m_r[h]) {
+          const float alpha = fast_exp2(m_r[h] - msafe);  // 0 when m was -inf
+          l_r[h] *= alpha;
+#pragma unroll
+          for (int n = 0; n < S::NT; ++n) {
+            o[n][2 * h] *= alpha;
+            o[n][2 * h + 1] *= alpha;
+          }
+          m_r[h] = mn;
+        }
+#pragma unroll
+        for (int n = 0; n < 2; ++n) {
+          sc[n][2 * h] = fast_exp2(sc[n][2 * h] - msafe);
+          sc[n][2 * h + 1] = fast_exp2(sc[n][2 * h + 1] - msafe);
+          l_r[h] += sc[n][2 * h] + sc[n][2 * h + 1];
+        }
+      }
+      uint32_t ph[4], pl[4];
+      split_bf16x2(sc[0][0], sc[0][1], ph[0], pl[0]);
+      split_bf16x2(sc[0][2], sc[0][3], ph[1], pl[1]);
+      split_bf16x2(sc[1][0], sc[1][1], ph[2], pl[2]);
+      split_bf16x2(sc[1][2], sc[1][3], ph[3], pl[3]);
+
+      if (partial && warp * 16 + 16 > valid) {
+        // rows past the end may hold anything (even NaN): zero this warp's
+        // share of them so that 0 * row stays 0 in P . V
+        for (int idx = lane; idx < 16 * S::SUB * 8; idx += 32) {
+          const int key = warp * 16 + idx / (S::SUB * 8);
+          const int rem = idx % (S::SUB * 8);
+          if (key >= valid)
+            *reinterpret_cast<uint4 *>(vt + (rem >> 3) * S::SUB_BYTES +
+                                       key * 128 + ((rem & 7) << 4)) =
+                make_uint4(0, 0, 0, 0);
+        }
+        __syncwarp();
+      }
+
+      // ---- O += P V
+#pragma unroll
+      for (int jj = 0; jj < D / 16; ++jj) {
+        const int dim = jj * 16 + v_dof;
+        const int sub = dim >> 6;
+        const int chunk = (dim & 63) >> 3;
+        const uint32_t addr = smem_u32(vt + sub * S::SUB_BYTES + v_key * 128 +
+                                       ((chunk ^ (v_key & 7)) << 4));
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(addr, b0, b1, b2, b3);
+        mma_bf16(o[2 * jj], ph, b0, b1);
+        mma_bf16(o[2 * jj], pl, b0, b1);
+        mma_bf16(o[2 * jj + 1], ph, b2, b3);
+        mma_bf16(o[2 * jj + 1], pl, b2, b3);
+      }
+      if (partial) fence_proxy_async();  // generic writes before the next TMA
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    // quad-reduce the row sums (each lane holds 4 of the warp's 16 keys)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      l_r[h] += __shfl_xor_sync(0xffffffffu, l_r[h], 1);
+      l_r[h] += __shfl_xor_sync(0xffffffffu, l_r[h], 2);
+    }
+  }
+  if (failed) {
+    atomicOr(p.err, DEV_ERR_WAIT_TIMEOUT);
+    s_flag = 1;
+  }
+  __syncthreads();
+  if (s_flag) {
+    if (tid == 0)
+      for (int s = 0; s < S::STAGES; ++s)
+        mbar_wait_bounded(&full[s], 0, 1u << 12);
+    return;
+  }
+
+  // ---- merge the 4 consumer warps (rows < G)
+  float *w_acc = reinterpret_cast<float *>(smem);   // [4][G][D]
+  float *w_m = w_acc + kConsumerWarps * G * D;      // [4][G]
+  float *w_l = w_m + kConsumerWarps * G;            // [4][G]
+  if (warp < kConsumerWarps) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int row = r0 + 8 * h;
+      if (row < G) {
+#pragma unroll
+        for (int n = 0; n < S::NT; ++n) {
+          *reinterpret_cast<float2 *>(&w_acc[(warp * G + row) * D + n * 8 + cq]) =
+              make_float2(o[n][2 * h], o[n][2 * h + 1]);
+        }
+        if ((lane & 3) == 0) {
+          w_m[warp * G + row] = m_r[h];
+          w_l[warp * G + row] = l_r[h];
+        }
+      }
+    }
+  }
+  __syncthreads();
+
+  const bool single = (n_splits == 1);
+  for (int idx = tid; idx < G * D; idx += kThreads) {
+    const int g = idx / D;
+    const int d = idx - g * D;
+    float mx = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) mx = fmaxf(mx, w_m[w * G + g]);
+    float num = 0.f, den = 0.f;
+    if (mx != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        const float wm = w_m[w * G + g];
+        if (wm != -INFINITY) {
+          const float sc = fast_exp2(wm - mx);
+          num = fmaf(w_acc[(w * G + g) * D + d], sc, num);
+          den = fmaf(w_l[w * G + g], sc, den);
+        }
+      }
+    }
+    const size_t row = (size_t)b * p.n_head + head0 + g;
+    if (single) {
+      p.out[row * D + d] = den > 0.f ? num / den : 0.f;
+    } else {
+      const size_t slot = row * p.max_splits + j;
+      p.part_acc[slot * D + d] = num;
+      if (d == 0) {
+        p.part_ml[slot * 2 + 0] = mx;
+        p.part_ml[slot * 2 + 1] = den;
+      }
+    }
+  }
+  if (single) return;
+
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    int *ctr = p.counters + (size_t)b * gridDim.y + y;
+    const int ticket = atomicAdd(ctr, 1);
+    s_flag = (ticket == n_splits - 1) ? 2 : 0;
+    if (s_flag) *ctr = 0;
+  }
+  __syncthreads();
+  if (s_flag != 2) return;
+  __threadfence();
+
+  float *sw = reinterpret_cast<float *>(smem);  // [G][kMaxSplits]
+  for (int g = warp; g < G; g += kConsumerWarps + 1) {
+    const size_t base = ((size_t)b * p.n_head + head0 + g) * p.max_splits;
+    float mx = -INFINITY;
+    for (int s = lane; s < n_splits; s += 32)
+      mx = fmaxf(mx, __ldcg(&p.part_ml[(base + s) * 2]));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    float den = 0.f;
+    for (int s = lane; s < n_splits; s += 32) {
+      const float ms = __ldcg(&p.part_ml[(base + s) * 2]);
+      const float w = (ms == -INFINITY) ? 0.f : fast_exp2(ms - mx);
+      sw[g * kMaxSplits + s] = w;
+      den = fmaf(__ldcg(&p.part_ml[(base + s) * 2 + 1]), w, den);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1)
+      den += __shfl_xor_sync(0xffffffffu, den, off);
+    const float inv = den > 0.f ? 1.f / den : 0.f;
+    for (int s = lane; s < n_splits; s += 32) sw[g * kMaxSplits + s] *= inv;
+  }
+  __syncthreads();
+  for (int idx = tid; idx < G * D; idx += kThreads) {
+    const int g = idx / D;
+    const int d = idx - g * D;
+    const size_t row = (size_t)b * p.n_head + head0 + g;
+    const size_t base = row * p.max_splits;
+    float o2 = 0.f;
+    for (int s = 0; s < n_splits; ++s)
+      o2 = fmaf(sw[g * kMaxSplits + s], __ldcg(&p.part_acc[(base + s) * D + d]),
+                o2);
+    p.out[row * D + d] = o2;
+  }
+}
+
+// --------------------------------------------------------------------------
 // Host side
 // --------------------------------------------------------------------------
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -437,9 +849,10 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // Tensor map over a KV cache viewed as (planes, max_seq, D) with a box of
-// (rows x D) elements.
+// (rows x box_inner) elements; swizzle128 selects the 128-byte swizzle.
 int make_kv_map(CUtensorMap *m, const void *base, int dtype, int D,
-                int max_seq, long planes, int rows) {
+                int max_seq, long planes, int rows, int box_inner = 0,
+                bool swizzle128 = false) {
   auto fn = encode_fn();
   if (!fn) {
     set_error("cuTensorMapEncodeTiled is not available from the driver");
@@ -448,13 +861,16 @@ int make_kv_map(CUtensorMap *m, const void *base, int dtype, int D,
   const int esz = dtype_size(dtype);
   cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)max_seq, (cuuint64_t)planes};
   cuuint64_t strides[2] = {(cuuint64_t)D * esz, (cuuint64_t)D * esz * max_seq};
-  cuuint32_t box[3] = {(cuuint32_t)D, (cuuint32_t)rows, 1};
+  cuuint32_t box[3] = {(cuuint32_t)(box_inner > 0 ? box_inner : D),
+                       (cuuint32_t)rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = fn(m,
                   dtype == TLLM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
                   3, const_cast<void *>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                             : CU_TENSOR_MAP_SWIZZLE_NONE,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
@@ -526,9 +942,53 @@ int dispatch_d(int D, int G, const DecodeParams &p, const CUtensorMap &mk,
   return TLLM_ERR_UNSUPPORTED;
 }
 
-// Keys per CTA: a multiple of the tile height chosen so that the launch has
-// roughly `target` CTAs doing work, never more than kMaxSplits splits.
+template <int D>
+int launch_mma(const DecodeParams &p, int G, const CUtensorMap &mk,
+               const CUtensorMap &mv, dim3 grid, cudaStream_t st) {
+  using S = MmaShape<D>;
+  const size_t merge = (size_t)kConsumerWarps * G * (D + 2) * sizeof(float);
+  const size_t sweights = (size_t)G * kMaxSplits * sizeof(float);
+  size_t smem = S::RING;
+  if (merge > smem) smem = merge;
+  if (sweights > smem) smem = sweights;
+  auto kern = gqa_decode_mma_kernel<D>;
+  static bool configured[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    TLLM_CUDA(cudaFuncSetAttribute(
+        kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  kern<<<grid, kThreads, smem, st>>>(p, G, mk, mv);
+  TLLM_LAUNCH_CHECK();
+  return TLLM_OK;
+}
+
+bool use_mma(int kv_dtype, int D) {
+  static int env = -1;
+  if (env < 0) {
+    const char *e = getenv("TLLM_GQA_NO_MMA");
+    env = (e && atoi(e) > 0) ? 1 : 0;
+  }
+  return !env && kv_dtype == TLLM_BF16 && (D == 64 || D == 128);
+}
+
+int pick_group_tile_mma(int group) {
+  for (int g = 16; g >= 1; --g)
+    if (group % g == 0) return g;
+  return 1;
+}
+
+// Keys per CTA: a multiple of the tile height. Every CTA pays a fixed cost
+// (first TMA round trip, the four-warp merge, the split merge) that only
+// long chunks amortise, while too few CTAs leave SMs idle; on B200 the best
+// chunk measured was ~3/8 of the longest sequence's tiles, between 3 and 32
+// tiles (config 2: 12 of 32, config 3: 3-4 of 12, config 4: 16-32 of 128).
+// Never more than kMaxSplits splits.
 int pick_chunk(int rows, int batch, int ygrid, int max_len) {
+  (void)batch;
+  (void)ygrid;
   const long tiles = (max_len + rows - 1) / rows;
   if (tiles <= 1) return rows;
   static int env_tiles = -1;
@@ -540,14 +1000,9 @@ int pick_chunk(int rows, int batch, int ygrid, int max_len) {
   if (env_tiles > 0) {
     chunk_tiles = env_tiles;
   } else {
-    // The average sequence is taken as half of max_len (ragged batches).
-    const long target = 4L * sm_count();
-    const long pairs = (long)batch * ygrid;
-    long want_splits = (target + pairs - 1) / pairs;  // per (b, y) at max_len
-    if (want_splits < 1) want_splits = 1;
-    want_splits *= 2;
-    chunk_tiles = (tiles + want_splits - 1) / want_splits;
-    if (chunk_tiles < 2) chunk_tiles = 2;
+    chunk_tiles = (3 * tiles + 7) / 8;
+    if (chunk_tiles < 3) chunk_tiles = 3;
+    if (chunk_tiles > 32) chunk_tiles = 32;
   }
   long min_tiles = (tiles + kMaxSplits - 1) / kMaxSplits;
   if (chunk_tiles < min_tiles) chunk_tiles = min_tiles;
@@ -580,9 +1035,10 @@ static int decode_impl(const float *q, const void *k_cache, const void *v_cache,
   if (sm_scale <= 0.f) sm_scale = 1.0f / sqrtf((float)head_dim);
 
   const int group = n_head / n_kv_head;
-  const int G = pick_group_tile(group);
+  const bool mma = use_mma(kv_dtype, head_dim);
+  const int G = mma ? pick_group_tile_mma(group) : pick_group_tile(group);
   const int n_gsub = group / G;
-  const int rows = tile_rows(kv_dtype, head_dim);
+  const int rows = mma ? MmaShape<64>::KT : tile_rows(kv_dtype, head_dim);
   TLLM_CHECK_ARG(rows >= 1, "head_dim %d too large", head_dim);
   const int ygrid = n_kv_head * n_gsub;
   TLLM_CHECK_ARG(ygrid <= 65535 && batch <= 65535, "grid too large");
@@ -608,10 +1064,10 @@ static int decode_impl(const float *q, const void *k_cache, const void *v_cache,
 
   CUtensorMap mk, mv;
   int rc = make_kv_map(&mk, k_cache, kv_dtype, head_dim, max_seq,
-                       (long)batch * n_kv_head, rows);
+                       (long)batch * n_kv_head, rows, mma ? 64 : 0, mma);
   if (rc) return rc;
   rc = make_kv_map(&mv, v_cache, kv_dtype, head_dim, max_seq,
-                   (long)batch * n_kv_head, rows);
+                   (long)batch * n_kv_head, rows, mma ? 64 : 0, mma);
   if (rc) return rc;
 
   DecodeParams p;
@@ -637,6 +1093,9 @@ static int decode_impl(const float *q, const void *k_cache, const void *v_cache,
 
   dim3 grid(max_splits, ygrid, batch);
   cudaStream_t st = resolve(stream);
+  if (mma)
+    return head_dim == 64 ? launch_mma<64>(p, G, mk, mv, grid, st)
+                          : launch_mma<128>(p, G, mk, mv, grid, st);
   if (kv_dtype == TLLM_BF16)
     return dispatch_d<__nv_bfloat16>(head_dim, G, p, mk, mv, grid, st);
   return dispatch_d<float>(head_dim, G, p, mk, mv, grid, st);

@@ -328,6 +328,41 @@ int tllm_device_error(int *code, int reset) {
   return TLLM_OK;
 }
 
+int tllm_graph_capture_begin(tllm_stream_t stream) {
+  TLLM_CUDA(cudaStreamBeginCapture(resolve(stream),
+                                   cudaStreamCaptureModeThreadLocal));
+  return TLLM_OK;
+}
+
+int tllm_graph_capture_end(tllm_stream_t stream, void **graph_exec) {
+  TLLM_CHECK_ARG(graph_exec, "graph_exec is NULL");
+  cudaGraph_t g = nullptr;
+  TLLM_CUDA(cudaStreamEndCapture(resolve(stream), &g));
+  cudaGraphExec_t ge = nullptr;
+  cudaError_t e = cudaGraphInstantiate(&ge, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) {
+    set_error("cudaGraphInstantiate failed: %s (%d)", cudaGetErrorString(e),
+              (int)e);
+    return TLLM_ERR_CUDA;
+  }
+  *graph_exec = ge;
+  return TLLM_OK;
+}
+
+int tllm_graph_launch(void *graph_exec, tllm_stream_t stream) {
+  TLLM_CHECK_ARG(graph_exec, "graph_exec is NULL");
+  TLLM_CUDA(cudaGraphLaunch(static_cast<cudaGraphExec_t>(graph_exec),
+                            resolve(stream)));
+  return TLLM_OK;
+}
+
+int tllm_graph_destroy(void *graph_exec) {
+  if (!graph_exec) return TLLM_OK;
+  TLLM_CUDA(cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(graph_exec)));
+  return TLLM_OK;
+}
+
 int tllm_mem_info(size_t *free_bytes, size_t *total_bytes) {
   TLLM_CHECK_ARG(free_bytes && total_bytes, "NULL argument");
   TLLM_CUDA(cudaMemGetInfo(free_bytes, total_bytes));

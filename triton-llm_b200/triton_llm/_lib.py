@@ -75,6 +75,10 @@ SIGNATURES: dict[str, list] = {
     "tllm_stream_wait_event": [_vp, _vp],
     "tllm_device_error": [_pi, _i],
     "tllm_mem_info": [_psz, _psz],
+    "tllm_graph_capture_begin": [_vp],
+    "tllm_graph_capture_end": [_vp, _pvp],
+    "tllm_graph_launch": [_vp, _vp],
+    "tllm_graph_destroy": [_vp],
     # attention
     "tllm_gqa_decode_workspace": [_i, _i, _i, _i, _i, _i, _psz, _psz],
     "tllm_gqa_decode": [_vp, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _i, _i, _i,

@@ -362,3 +362,38 @@ def mem_info():
     f, t = ctypes.c_size_t(), ctypes.c_size_t()
     _lib.call("tllm_mem_info", ctypes.byref(f), ctypes.byref(t))
     return f.value, t.value
+
+
+class Graph:
+    """A CUDA graph of library work captured on the library stream.
+
+        with gpu.Graph() as g:      # calls inside are recorded, not run
+            step()
+        g.launch()                  # replays them with one launch
+    """
+
+    def __init__(self):
+        _initialize()
+        self._exec = None
+
+    def __enter__(self):
+        _lib.call("tllm_graph_capture_begin", None)
+        return self
+
+    def __exit__(self, exc_type, exc, tb):
+        e = ctypes.c_void_p()
+        status = _lib.load().tllm_graph_capture_end(None, ctypes.byref(e))
+        if exc_type is None:
+            _lib.check(status, "tllm_graph_capture_end")
+            self._exec = e
+        return False
+
+    def launch(self):
+        _lib.call("tllm_graph_launch", self._exec, None)
+
+    def __del__(self):
+        try:
+            if _lib._lib is not None and self._exec:
+                _lib._lib.tllm_graph_destroy(self._exec)
+        except Exception:
+            pass
