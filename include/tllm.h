@@ -153,6 +153,106 @@ int tllm_gqa_decode(const float *q, const void *k_cache, const void *v_cache,
                     tllm_stream_t stream);
 
 /*
+ * GQA attention for query rows that each read a prefix of one cached
+ * sequence: row r attends to the first row_len[r] cache rows of sequence
+ * row_seq[r] (row_seq NULL: sequence r). q and out of (row r, head h) are at
+ * r * *_row_stride + h * *_head_stride elements. Used for the prefill
+ * (causal: row_len = position + 1) and for the reference's flat layout
+ * (Q as (n_head * seq_q, d_k) is row stride d_k, head stride seq_q * d_k).
+ * Replaces triton_llm/kernels/attention_gqa.py:149-269 (causal branch) and
+ * the prefill attention of smollm2_triton/model.py:341-343. Scratch as for
+ * tllm_gqa_decode with batch = rows.
+ */
+int tllm_gqa_rows(const float *q, long q_row_stride, long q_head_stride,
+                  const void *k_cache, const void *v_cache, int kv_dtype,
+                  const int32_t *row_seq, const int32_t *row_len, float *out,
+                  long out_row_stride, long out_head_stride, int rows,
+                  int n_head, int n_kv_head, int head_dim, int cache_batch,
+                  int max_seq, int max_len, float sm_scale, void *partial,
+                  size_t partial_bytes, int32_t *counters,
+                  tllm_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Projections (GEMM with fused epilogues)                                   */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * y = epilogue(x @ W^T) for x (M, K) f32 and W (N, K) in w_dtype (F32 or
+ * BF16; BF16 needs K % 64 == 0). Replaces triton_llm/kernels/gemm.py:53-109
+ * plus the add / swiglu / gelu / apply_rope calls that follow it in
+ * smollm2_triton/model.py:281-365 and gpt2_triton/model.py:319-361.
+ *
+ * op 0 STORE : out[m, n] = acc (+ bias[n])
+ * op 1 RESID : out[m, n] = resid[m, n] + acc (+ bias[n]); resid may be out
+ * op 2 GELU  : out[m, n] = gelu_tanh(acc + bias[n])   (gelu.py:17-28, :50-51)
+ * op 3 SWIGLU: W rows are gate/up interleaved in blocks of 8;
+ *              out[m, j] = silu(gate_j) * up_j        (swiglu.py:51-56)
+ * op 4 QKV   : W rows are the q, k, v heads (n_head + 2 n_kv_head heads of
+ *              head_dim rows), each head stored as blocks of 8 dims
+ *              (8b..8b+7, D/2+8b..D/2+8b+7). Row m is token row_pos[m] of
+ *              cache sequence row_seq[m]: q heads (rotated if cos_t != NULL)
+ *              go to q_out (M, n_head, D); k heads (rotated) and v heads are
+ *              written into the caches (B, n_kv_head, max_seq, D) at
+ *              row_pos[m] (rope.py:49-66 + smollm2_triton/model.py:296-302);
+ *              if lens_out != NULL, lens_out[row_seq[m]] = row_pos[m] + 1.
+ * Scratch for split-K: tllm_linear_workspace; counters zero-filled once.
+ */
+int tllm_linear_workspace(int M, int N, int K, size_t *partial_bytes,
+                          size_t *counter_bytes);
+int tllm_linear(const float *x, const void *w, int w_dtype, int M, int N,
+                int K, int op, const float *bias, float *out, int ld_out,
+                const float *resid, const float *cos_t, const float *sin_t,
+                const int32_t *row_seq, const int32_t *row_pos, float *q_out,
+                void *k_cache, void *v_cache, int kv_dtype, int max_seq,
+                int n_head, int n_kv_head, int head_dim, int32_t *lens_out,
+                void *partial, size_t partial_bytes, int32_t *counters,
+                tllm_stream_t stream);
+
+/* C = A @ B, fp32, A (M, K), B (K, N) row-major: the reference's weight
+ * layout (triton_llm/kernels/gemm.py:53-109). */
+int tllm_gemm_f32(const float *a, const float *b, float *c, int M, int N,
+                  int K, tllm_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Norms, embedding, sampling, elementwise                                   */
+/* ------------------------------------------------------------------------ */
+
+/* triton_llm/kernels/rms_norm.py:68-115: y = (x / sqrt(mean(x^2) + eps)) * w */
+int tllm_rmsnorm(const float *x, const float *w, float *y, int M, int N,
+                 float eps, tllm_stream_t stream);
+/* triton_llm/kernels/layernorm.py:79-152 (two-pass mean / variance) */
+int tllm_layernorm(const float *x, const float *gamma, const float *beta,
+                   float *y, int M, int N, float eps, tllm_stream_t stream);
+/* out[m] = wte[ids[m]] (+ wpe[pos[m]] if wpe): triton_llm/kernels/
+ * embedding.py:98-187 and smollm2_triton/model.py:547-560. Out-of-range ids
+ * give a zero row and set bit 4 of the device error word. */
+int tllm_embedding(const int32_t *ids, const void *wte, int wte_dtype,
+                   const float *wpe, const int32_t *pos, float *out, int M,
+                   int n_embd, int vocab, int max_pos, tllm_stream_t stream);
+/* ids[m] = first argmax of logits[m, :V] (smollm2_triton/model.py:583);
+ * pos_inc[m] += 1 when pos_inc != NULL. ld = row stride (0: V). */
+int tllm_argmax(const float *logits, int M, int V, int ld, int32_t *ids,
+                int32_t *pos_inc, tllm_stream_t stream);
+/* triton_llm/kernels/rope.py:153-222: in-place rotate-half RoPE of x
+ * (n_rows, d), row r at position (r % seq_len) + position_offset, tables
+ * (max_seq, d/2) f32. */
+int tllm_rope(float *x, const float *cos_t, const float *sin_t, int n_rows,
+              int d, int seq_len, int position_offset, tllm_stream_t stream);
+/* op 0: out = silu(a) * b (swiglu.py:70-119); op 1: out = a + b
+ * (add.py:54-95); op 2: out = gelu_tanh(a) (gelu.py:56-83). */
+int tllm_elementwise(int op, const float *a, const float *b, float *out,
+                     long n, tllm_stream_t stream);
+/* Row softmax (triton_llm/kernels/softmax.py:105-180). */
+int tllm_softmax(const float *x, float *y, int M, int N, tllm_stream_t stream);
+
+/* Synthetic data on the device: element i = (sum of four 16-bit hashes of
+ * (seed, i) - 131070) * std / (65536 / sqrt(3)), mean 0, standard deviation
+ * std (bf16: rounded to nearest even). Used for random-init weights and
+ * prefilled KV contexts in benchmarks. */
+int tllm_fill_random(void *ptr, int dtype, long n, uint64_t seed, float std,
+                     tllm_stream_t stream);
+
+/*
  * Allocation-free variant of tllm_gqa_decode. It has no counterpart in the
  * reference; it exists for callers that cannot let a library allocate device
  * memory (servers that own all of HBM through their own arenas, hosts whose

@@ -1,0 +1,385 @@
+"""Row, elementwise and projection kernels vs the reference's goldens and the
+oracle (GPU).
+
+Tolerances follow the reference's own kernel tests: 1e-5 for RMSNorm and
+LayerNorm (tests/test_rms_norm.py, tests/test_layernorm.py), 1e-6 relative
+for SwiGLU / add (exact up to expf), 1e-4 for RoPE and GEMM. The fused
+projection (tllm_linear) is checked against an fp64 product of the weights
+the device holds; bf16 weights are exact, the activations are split into a
+bf16 head and residual, so the bound is 3e-5 of the row's sum |x| |w|.
+KV append through the QKV epilogue is checked bit-exact against the oracle's
+rotation of the same projection output.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import ops
+
+pytestmark = pytest.mark.gpu
+
+F32 = np.float32
+
+
+@pytest.fixture(scope="module")
+def gpu():
+    from triton_llm import gpu as g
+    g._initialize()
+    g.device_error(reset=True)
+    yield g
+    assert g.device_error(reset=True) == 0, "kernel reported a device error"
+
+
+# ---------------------------------------------------------------- goldens --
+def test_rmsnorm_golden(gpu, golden):
+    from triton_llm.kernels import rms_norm
+    g = golden("kernels")
+    for key in sorted(k for k in g if k.startswith("rms/") and k.endswith("/x")):
+        name = key.split("/")[1]
+        x, w = g[f"rms/{name}/x"], g[f"rms/{name}/w"]
+        o = gpu.allocate(x.shape, np.float32)
+        rms_norm(gpu.to_device(x), gpu.to_device(w), o, 1e-5)
+        np.testing.assert_allclose(o.to_numpy(), g[f"rms/{name}/out"], rtol=1e-5,
+                                   atol=1e-5, err_msg=name)
+    o = gpu.allocate((1, 1), np.float32)
+    rms_norm(gpu.to_device(np.array([[3.0]], F32)), gpu.to_device(np.array([2.0], F32)),
+             o, 1e-5)
+    np.testing.assert_allclose(o.to_numpy(), g["rms/known/out"], rtol=1e-6)
+
+
+def test_layernorm_golden(gpu, golden):
+    from triton_llm.kernels import layer_norm
+    g = golden("kernels")
+    for name in ("3_768", "2_100"):
+        out = layer_norm(g[f"ln/{name}/x"], g[f"ln/{name}/g"], g[f"ln/{name}/b"], 1e-5)
+        np.testing.assert_allclose(out, g[f"ln/{name}/out"], rtol=1e-5, atol=1e-5)
+
+
+def test_elementwise_golden(gpu, golden):
+    from triton_llm.kernels import add, gelu, swiglu
+    g = golden("kernels")
+    x, y = g["swiglu/x"], g["swiglu/y"]
+    s = swiglu(gpu.to_device(x), gpu.to_device(y)).to_numpy()
+    np.testing.assert_allclose(s, g["swiglu/out"], rtol=1e-6, atol=1e-6)
+    np.testing.assert_allclose(gelu(x), g["gelu/out"], rtol=1e-6, atol=1e-6)
+    a = add(gpu.to_device(x), gpu.to_device(y)).to_numpy()
+    np.testing.assert_array_equal(a, g["add/out"])
+
+
+def test_embedding_golden(gpu, golden):
+    from triton_llm.kernels import embedding
+    g = golden("kernels")
+    out = embedding(g["emb/ids"], g["emb/wte"], g["emb/wpe"], position_offset=9)
+    np.testing.assert_array_equal(out, g["emb/out"])
+
+
+def test_gemm_golden(gpu, golden):
+    from triton_llm.kernels import gemm
+    g = golden("kernels")
+    for name in ("1_576_192", "3_64_100", "5_130_70"):
+        a, b = g[f"gemm/{name}/a"], g[f"gemm/{name}/b"]
+        o = gemm(gpu.to_device(a), gpu.to_device(b)).to_numpy()
+        np.testing.assert_allclose(o, g[f"gemm/{name}/out"], rtol=1e-4, atol=1e-4,
+                                   err_msg=name)
+
+
+def test_rope_golden(gpu, golden):
+    from triton_llm.kernels import apply_rope, precompute_cos_sin
+    g = golden("kernels")
+    c, s = precompute_cos_sin(256, 64, 100000.0)
+    for key in [k for k in g if k.startswith("rope/apply/") and k.endswith("/x")]:
+        name = key.split("/")[2]
+        x = g[key]
+        if name.endswith("_d128"):
+            cc, ss = precompute_cos_sin(8192, 128, 500000.0)
+            seq, off = 1, 8000
+        else:
+            cc, ss = c, s
+            _, seq, off = (int(t) for t in name.split("_"))
+        xd = gpu.to_device(x)
+        apply_rope(xd, gpu.to_device(cc), gpu.to_device(ss), seq_len=seq,
+                   position_offset=off)
+        np.testing.assert_allclose(xd.to_numpy(), g[f"rope/apply/{name}/out"],
+                                   rtol=1e-5, atol=1e-5, err_msg=name)
+
+
+def test_softmax_and_argmax(gpu):
+    from triton_llm import _lib
+    from triton_llm.kernels import softmax
+    rng = np.random.default_rng(3)
+    x = (rng.standard_normal((5, 49152)) * 4).astype(F32)
+    np.testing.assert_allclose(softmax(x), ops.softmax(x), rtol=1e-5, atol=1e-9)
+    # argmax: first maximal index wins, like np.argmax
+    x[1, 100] = x[1, 7] = 1e3
+    x[3, :] = 0.0
+    xd = gpu.to_device(x)
+    ids = gpu.zeros((5,), np.int32)
+    pos = gpu.to_device(np.arange(5, dtype=np.int32))
+    _lib.call("tllm_argmax", xd.ptr, 5, 49152, 49152, ids.ptr, pos.ptr, None)
+    np.testing.assert_array_equal(ids.to_numpy(), np.argmax(x, axis=-1))
+    np.testing.assert_array_equal(pos.to_numpy(), np.arange(5) + 1)
+
+
+def test_fill_random_matches_host_formula(gpu):
+    """The device N(0, std) fill is reproducible on the host (splitmix64
+    hash, Irwin-Hall sum of four 16-bit fields)."""
+    from triton_llm import _lib
+    n, seed, std = 4099, 77, 0.02
+    t = gpu.allocate((n,), np.float32)
+    _lib.call("tllm_fill_random", t.ptr, _lib.F32, n, seed, float(std), None)
+    got = t.to_numpy()
+
+    def mix64(z):
+        z = z + np.uint64(0x9E3779B97F4A7C15)
+        z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+        return z ^ (z >> np.uint64(31))
+
+    with np.errstate(over="ignore"):
+        h = mix64(np.uint64(seed) ^ mix64(np.arange(n, dtype=np.uint64)))
+    s = sum(((h >> np.uint64(16 * i)) & np.uint64(0xFFFF)).astype(np.int64)
+            for i in range(4))
+    scale = F32(std) / (F32(65536.0) * F32(0.57735026918962576))
+    ref = (s - 131070).astype(F32) * scale
+    np.testing.assert_allclose(got, ref, rtol=1e-6, atol=1e-9)
+    assert abs(got.std() - std) < 0.05 * std
+
+
+# ------------------------------------------------------- fused projection --
+def _linear_case(gpu, M, N, K, bf16, seed=0):
+    from triton_llm.kernels.linear import Linear
+    rng = np.random.default_rng(seed)
+    w = (rng.standard_normal((N, K), dtype=F32) * 0.05).astype(F32)
+    x = rng.standard_normal((M, K), dtype=F32)
+    lin = Linear(w, "bfloat16" if bf16 else "float32")
+    wd = ops.bf16_round(w) if bf16 else w
+    ref = x.astype(np.float64) @ wd.astype(np.float64).T
+    bound = np.abs(x).astype(np.float64) @ np.abs(wd).astype(np.float64).T
+    return lin, x, wd, ref, bound
+
+
+def _close(out, ref, bound, rel=3e-5, msg=""):
+    err = np.abs(out.astype(np.float64) - ref)
+    lim = rel * bound + 1e-6
+    bad = err > lim
+    assert not bad.any(), f"{msg}: {bad.sum()} outside bound, worst {(err / lim).max():.2f}x"
+
+
+@pytest.mark.parametrize("bf16", [True, False])
+@pytest.mark.parametrize("M", [1, 3, 8, 9, 17, 33, 64, 100, 130])
+def test_linear_store_bias(gpu, M, bf16):
+    from triton_llm.kernels.linear import LinearWorkspace, linear
+    N, K = 576, 576
+    lin, x, wd, ref, bound = _linear_case(gpu, M, N, K, bf16, seed=M)
+    b = np.linspace(-1, 1, N).astype(F32)
+    from triton_llm import gpu as g
+    lin.b = g.to_device(b)
+    out = gpu.allocate((M, N), np.float32)
+    linear(gpu.to_device(x), lin, out_dev=out, ws=LinearWorkspace([(M, N, K)]), M=M)
+    _close(out.to_numpy(), ref + b, bound, msg=f"M={M}")
+
+
+@pytest.mark.parametrize("bf16", [True, False])
+def test_linear_split_k_deterministic(gpu, bf16):
+    """Few weight tiles and long K: the kernel splits K across CTAs and the
+    last CTA sums the splits in a fixed order -> bitwise repeatable."""
+    from triton_llm.kernels.linear import LinearWorkspace, linear
+    M, N, K = 4, 256, 8192
+    lin, x, wd, ref, bound = _linear_case(gpu, M, N, K, bf16, seed=11)
+    ws = LinearWorkspace([(M, N, K)])
+    xd = gpu.to_device(x)
+    outs = []
+    for _ in range(3):
+        out = gpu.allocate((M, N), np.float32)
+        linear(xd, lin, out_dev=out, ws=ws, M=M)
+        outs.append(out.to_numpy())
+    _close(outs[0], ref, bound, msg="split-K")
+    np.testing.assert_array_equal(outs[0], outs[1])
+    np.testing.assert_array_equal(outs[0], outs[2])
+    # the counters are left at zero for the next call / graph replay
+    assert not ws.counters.to_numpy().any()
+
+
+@pytest.mark.parametrize("bf16", [True, False])
+def test_linear_residual_in_place(gpu, bf16):
+    from triton_llm import _lib
+    from triton_llm.kernels.linear import LinearWorkspace, linear
+    M, N, K = 5, 576, 1536
+    lin, x, wd, ref, bound = _linear_case(gpu, M, N, K, bf16, seed=5)
+    h = np.random.default_rng(6).standard_normal((M, N), dtype=F32)
+    hd = gpu.to_device(h)
+    linear(gpu.to_device(x), lin, out_dev=hd, op=_lib.EPI_RESID, resid_dev=hd,
+           ws=LinearWorkspace([(M, N, K)]), M=M)
+    _close(hd.to_numpy(), ref + h, bound, msg="resid")
+
+
+@pytest.mark.parametrize("bf16", [True, False])
+def test_linear_gelu(gpu, bf16):
+    from triton_llm import _lib
+    from triton_llm.kernels.linear import LinearWorkspace, linear
+    M, N, K = 7, 3072, 768
+    lin, x, wd, ref, bound = _linear_case(gpu, M, N, K, bf16, seed=7)
+    out = gpu.allocate((M, N), np.float32)
+    linear(gpu.to_device(x), lin, out_dev=out, op=_lib.EPI_GELU,
+           ws=LinearWorkspace([(M, N, K)]), M=M)
+    # gelu' <= 1.13: the product bound carries over
+    np.testing.assert_allclose(out.to_numpy(), ops.gelu(ref.astype(F32)),
+                               atol=1.2 * 3e-5 * bound.max() + 1e-6)
+
+
+@pytest.mark.parametrize("bf16", [True, False])
+@pytest.mark.parametrize("M", [1, 64])
+def test_linear_swiglu(gpu, M, bf16):
+    from triton_llm import _lib
+    from triton_llm.kernels.linear import Linear, LinearWorkspace, linear, swiglu_rows
+    F, K = 1536, 576
+    rng = np.random.default_rng(M)
+    wg = (rng.standard_normal((F, K), dtype=F32) * 0.05).astype(F32)
+    wu = (rng.standard_normal((F, K), dtype=F32) * 0.05).astype(F32)
+    x = rng.standard_normal((M, K), dtype=F32)
+    dt = "bfloat16" if bf16 else "float32"
+    lin = Linear(swiglu_rows(wg, wu), dt)
+    rd = ops.bf16_round if bf16 else (lambda a: a)
+    gref = x.astype(np.float64) @ rd(wg).astype(np.float64).T
+    uref = x.astype(np.float64) @ rd(wu).astype(np.float64).T
+    out = gpu.allocate((M, F), np.float32)
+    linear(gpu.to_device(x), lin, out_dev=out, op=_lib.EPI_SWIGLU,
+           ws=LinearWorkspace([(M, 2 * F, K)]), M=M)
+    ref = ops.swiglu(gref.astype(F32), uref.astype(F32))
+    np.testing.assert_allclose(out.to_numpy(), ref, rtol=2e-4, atol=2e-4)
+
+
+def test_linear_rejects_bad_shapes(gpu):
+    from triton_llm.kernels.linear import Linear, linear
+    lin = Linear(np.zeros((16, 96), F32), "bfloat16")
+    with pytest.raises(ValueError):
+        linear(gpu.allocate((1, 96), np.float32), lin, out_dev=gpu.allocate((1, 16), np.float32))
+    lin = Linear(np.zeros((16, 64), F32), "bfloat16")
+    with pytest.raises(ValueError):
+        linear(gpu.allocate((1, 32), np.float32), lin, out_dev=gpu.allocate((1, 16), np.float32))
+
+
+@pytest.mark.parametrize("kv_bf16", [True, False])
+@pytest.mark.parametrize("w_bf16", [True, False])
+@pytest.mark.parametrize("H,Hkv,D", [(9, 3, 64), (24, 8, 128), (4, 2, 16)])
+def test_qkv_rope_append_bit_exact(gpu, H, Hkv, D, w_bf16, kv_bf16):
+    """QKV epilogue: q rotated into q_out, k rotated and v appended at
+    (seq, kv_head, pos) of the cache, lens_out[seq] = pos + 1 -- bit-exact
+    against the oracle's RoPE applied to the same projection (EPI_STORE of
+    the same weights runs the same reduction order)."""
+    from triton_llm import _lib
+    from triton_llm.kernels.linear import (Linear, LinearWorkspace, head_row_order,
+                                           linear, qkv_rows)
+    n = H * D
+    K = 576 if D != 16 else 64
+    rows = (H + 2 * Hkv) * D
+    rng = np.random.default_rng(H * 1000 + D)
+    wq = (rng.standard_normal((H * D, K), dtype=F32) * 0.05).astype(F32)
+    wk = (rng.standard_normal((Hkv * D, K), dtype=F32) * 0.05).astype(F32)
+    wv = (rng.standard_normal((Hkv * D, K), dtype=F32) * 0.05).astype(F32)
+    B, S, M = 3, 40, 5
+    x = rng.standard_normal((M, K), dtype=F32)
+    row_seq = np.array([0, 2, 2, 1, 0], np.int32)
+    row_pos = np.array([0, 17, 18, 39, 1], np.int32)
+    cos, sin = ops.precompute_cos_sin(64, D, 100000.0)
+    dt = "bfloat16" if w_bf16 else "float32"
+    wperm, _ = qkv_rows(wq, wk, wv, D)
+    lin = Linear(wperm, dt)
+    ws = LinearWorkspace([(M, rows, K)])
+    xd = gpu.to_device(x)
+    # plain projection with the same weights and shape -> same sums
+    plain = gpu.allocate((M, rows), np.float32)
+    linear(xd, lin, out_dev=plain, ws=ws, M=M)
+    y = plain.to_numpy()
+    inv = np.argsort(np.concatenate([h * D + head_row_order(D)
+                                     for h in range(H + 2 * Hkv)]))
+    y = y[:, inv]                                  # back to natural head order
+    q, k, v = y[:, :n], y[:, n:n + Hkv * D], y[:, n + Hkv * D:]
+    kvdt = "bfloat16" if kv_bf16 else np.float32
+    kc = gpu.zeros((B, Hkv, S, D), kvdt)
+    vc = gpu.zeros((B, Hkv, S, D), kvdt)
+    q_out = gpu.allocate((M, H, D), np.float32)
+    lens = gpu.zeros((B,), np.int32)
+    linear(xd, lin, op=_lib.EPI_QKV, ws=ws, M=M, qkv=dict(
+        cos=gpu.to_device(cos), sin=gpu.to_device(sin), row_seq=gpu.to_device(row_seq),
+        row_pos=gpu.to_device(row_pos), q_out=q_out, k_cache=kc, v_cache=vc,
+        n_head=H, n_kv_head=Hkv, head_dim=D, lens_out=lens))
+    qr = ops.rope_positions(q.reshape(M * H, D), cos, sin,
+                            np.repeat(row_pos, H)).reshape(M, H, D)
+    kr = ops.rope_positions(k.reshape(M * Hkv, D), cos, sin,
+                            np.repeat(row_pos, Hkv)).reshape(M, Hkv, D)
+    np.testing.assert_array_equal(q_out.to_numpy(), qr)
+    kexp = np.zeros((B, Hkv, S, D), F32)
+    vexp = np.zeros((B, Hkv, S, D), F32)
+    for m in range(M):
+        kexp[row_seq[m], :, row_pos[m]] = kr[m]
+        vexp[row_seq[m], :, row_pos[m]] = v[m].reshape(Hkv, D)
+    st = ops.bf16_round if kv_bf16 else (lambda a: a)
+    np.testing.assert_array_equal(gpu.to_host(kc), st(kexp))
+    np.testing.assert_array_equal(gpu.to_host(vc), st(vexp))
+    # every row writes lens_out[seq] = pos + 1; rows of one sequence race, so
+    # only sequences written by one row (or ordered by position) are pinned
+    got = lens.to_numpy()
+    assert got[1] == 40
+    assert got[0] in (1, 2) and got[2] in (18, 19)
+
+
+def test_qkv_rejects_out_of_range_position(gpu):
+    """A position outside the cache is not written; the kernel flags it."""
+    from triton_llm import _lib
+    from triton_llm.kernels.linear import Linear, LinearWorkspace, linear, qkv_rows
+    H, Hkv, D, K = 2, 1, 64, 64
+    w = np.ones(((H + 2 * Hkv) * D, K), F32) * 0.01
+    lin = Linear(w, "bfloat16")
+    kc = gpu.zeros((1, Hkv, 8, D), "bfloat16")
+    vc = gpu.zeros((1, Hkv, 8, D), "bfloat16")
+    gpu.device_error(reset=True)
+    linear(gpu.to_device(np.ones((1, K), F32)), lin, op=_lib.EPI_QKV,
+           ws=LinearWorkspace([(1, w.shape[0], K)]), M=1, qkv=dict(
+               row_seq=gpu.zeros((1,), np.int32),
+               row_pos=gpu.to_device(np.array([8], np.int32)),
+               q_out=gpu.allocate((1, H, D), np.float32), k_cache=kc, v_cache=vc,
+               n_head=H, n_kv_head=Hkv, head_dim=D))
+    gpu.synchronize()
+    assert gpu.device_error(reset=True) & 2
+    assert not gpu.to_host(kc).any() and not gpu.to_host(vc).any()
+
+
+# ----------------------------------------------------- prefill attention --
+def test_prefill_flat_matches_reference_goldens(gpu, golden):
+    """attention_gqa(seq_q > 1, causal) on the reference's prefill cases."""
+    from triton_llm.kernels import attention_gqa
+    g = golden("kernels")
+    names = sorted({k.split("/")[1] for k in g
+                    if k.startswith("gqa/prefill_") or k.startswith("gqa/causal_")})
+    assert len(names) >= 6
+    for n in names:
+        nh, nkv, causal = (int(x) for x in g[f"gqa/{n}/meta"])
+        o = attention_gqa(gpu.to_device(g[f"gqa/{n}/q"]), gpu.to_device(g[f"gqa/{n}/k"]),
+                          gpu.to_device(g[f"gqa/{n}/v"]), nh, nkv, causal=bool(causal))
+        gpu.synchronize()
+        np.testing.assert_allclose(o.to_numpy(), g[f"gqa/{n}/out"], atol=1e-4,
+                                   err_msg=n)
+
+
+@pytest.mark.parametrize("bf16", [True, False])
+def test_gqa_rows_ragged_prefill(gpu, bf16):
+    """Row API: rows of three sequences, each attending its own prefix."""
+    from triton_llm.kernels import gqa_rows
+    H, Hkv, D, S = 9, 3, 64, 300
+    rng = np.random.default_rng(9)
+    kc = ops.bf16_round(rng.standard_normal((3, Hkv, S, D), dtype=F32))
+    vc = ops.bf16_round(rng.standard_normal((3, Hkv, S, D), dtype=F32))
+    row_seq = np.array([0, 0, 1, 2, 2, 2, 1], np.int32)
+    row_len = np.array([1, 2, 300, 64, 65, 129, 0], np.int32)
+    R = len(row_seq)
+    q = rng.standard_normal((R, H, D), dtype=F32)
+    up = gpu.to_device_bf16 if bf16 else gpu.to_device
+    out = gpu.allocate((R, H * D), np.float32)
+    gqa_rows(gpu.to_device(q), up(kc), up(vc), gpu.to_device(row_seq),
+             gpu.to_device(row_len), out, R, H, H * D, D, H * D, D, S)
+    got = out.to_numpy().reshape(R, H, D)
+    ref = ops.gqa_decode(q, kc[row_seq], vc[row_seq], row_len)
+    np.testing.assert_allclose(got, ref, atol=1e-4)

@@ -1,0 +1,265 @@
+"""SmolLM2 / Llama and GPT-2 models on the GPU vs the reference's goldens and
+the oracle.
+
+Bars (the decode path's parity targets):
+
+* fp32 storage (the reference's numerics): logits within 1e-4 of the
+  reference's own outputs (scaled by the logits' magnitude for GPT-2's
+  unscaled test weights), greedy tokens identical;
+* bf16 weights with an fp32 KV cache: the weights of the parity slices are
+  bf16 values already, so this runs the tensor-core projections against the
+  reference's fp32 outputs directly (activations keep ~16 mantissa bits);
+* bf16 weights and KV cache: logits within 2e-2 of the oracle run with the
+  same storage points, greedy tokens identical for 32 steps.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import inputs
+from oracle import models as omodels
+
+pytestmark = pytest.mark.gpu
+
+F32 = np.float32
+
+
+@pytest.fixture(scope="module")
+def gpu():
+    from triton_llm import gpu as g
+    g._initialize()
+    g.device_error(reset=True)
+    yield g
+    assert g.device_error(reset=True) == 0, "kernel reported a device error"
+
+
+def _smol(shape, weights, dtype=None, kv_dtype=None):
+    from smollm2_triton import SmolLM2Config, SmolLM2ForCausalLM
+    return SmolLM2ForCausalLM(SmolLM2Config(**shape.config_kwargs()), weights,
+                              dtype=dtype, kv_dtype=kv_dtype)
+
+
+def _smol_run(model, prompt, n_new):
+    """The reference's greedy loop through _forward_cached (as the goldens)."""
+    model._init_cache_gpu(max_seq=len(prompt) + n_new)
+    logits = model._forward_cached(np.array([prompt], np.int32))
+    toks, steps = list(prompt), []
+    for step in range(n_new):
+        last = logits[0, -1]
+        steps.append(last.copy())
+        t = int(np.argmax(last))
+        toks.append(t)
+        if step < n_new - 1:
+            logits = model._forward_cached(np.array([[t]], np.int32))
+    return np.array(toks, np.int32), np.stack(steps)
+
+
+def _same_tokens(got, want, ref_logits, tol):
+    """Tokens must agree; a divergence is only allowed at a near-tie of the
+    reference's logits (gap below ``tol``), after which nothing is compared."""
+    n0 = len(want) - len(ref_logits)
+    for i in range(len(want)):
+        if got[i] == want[i]:
+            continue
+        step = i - n0
+        assert step >= 0, f"prompt token {i} differs"
+        lg = ref_logits[step]
+        gap = abs(float(lg[want[i]]) - float(lg[got[i]]))
+        assert gap < tol, f"token {i}: {got[i]} vs {want[i]}, reference gap {gap}"
+        return i
+    return len(want)
+
+
+# ------------------------------------------------------------ SmolLM2 -----
+def test_smol_tiny_fp32_matches_reference(gpu, golden):
+    g = golden("smol_tiny")
+    m = _smol(inputs.SMOL_TINY, inputs.llama_weights_legacy(inputs.SMOL_TINY, 42))
+    toks, logits = _smol_run(m, [5, 12, 7], 5)
+    np.testing.assert_array_equal(toks, g["tokens"])
+    np.testing.assert_allclose(logits, g["logits"], atol=1e-4, rtol=1e-4)
+
+
+def test_smol_tiny_generate_matches_reference(gpu, golden):
+    """generate_gpu(temperature=0) = the reference's greedy generate."""
+    g = golden("smol_tiny")
+    m = _smol(inputs.SMOL_TINY, inputs.llama_weights_legacy(inputs.SMOL_TINY, 42))
+    out = m.generate_gpu(np.array([[5, 12, 7]], np.int32), max_new_tokens=5,
+                         temperature=0.0)
+    np.testing.assert_array_equal(out[0], g["tokens"])
+    streamed = [t for t, _ in m.generate_stream_gpu(np.array([[5, 12, 7]], np.int32),
+                                                    max_new_tokens=5, temperature=0.0)]
+    np.testing.assert_array_equal(streamed, g["tokens"][3:])
+
+
+@pytest.mark.parametrize("kv", ["float32", "bfloat16"])
+def test_smol_tiny_bf16_vs_oracle(gpu, kv):
+    w = inputs.llama_weights_legacy(inputs.SMOL_TINY, 42)
+    m = _smol(inputs.SMOL_TINY, w, dtype="bfloat16", kv_dtype=kv)
+    from smollm2_triton import SmolLM2Config
+    o = omodels.SmolLM2Oracle(SmolLM2Config(**inputs.SMOL_TINY.config_kwargs()), w,
+                              weight_dtype="bfloat16", kv_dtype=kv)
+    want, wl = o.generate(np.array([[5, 12, 7]], np.int32), 32)
+    toks, logits = _smol_run(m, [5, 12, 7], 32)
+    upto = _same_tokens(toks, want[0], wl, 2e-2)
+    steps = max(upto - 3, 1)
+    np.testing.assert_allclose(logits[:steps], wl[:steps], atol=2e-2)
+
+
+@pytest.mark.parametrize("mode", ["float32", "bf16w"])
+def test_smol135m_slice_matches_reference(gpu, golden, mode):
+    """SmolLM2-135M geometry (config 3): fp32, and bf16 weights with an fp32
+    cache (exact weights), both against the reference's own logits."""
+    g = golden("smol135m_slice")
+    w = inputs.round_linear_weights_bf16(inputs.llama_weights(inputs.SMOL_135M, 0))
+    if mode == "float32":
+        m = _smol(inputs.SMOL_135M, w)
+        tol = 1e-4
+    else:
+        m = _smol(inputs.SMOL_135M, w, dtype="bfloat16", kv_dtype="float32")
+        tol = 1e-3
+    prompt = g["tokens"][:8].tolist()
+    toks, logits = _smol_run(m, prompt, 3)
+    np.testing.assert_array_equal(toks, g["tokens"])
+    np.testing.assert_allclose(logits, g["logits"], atol=tol)
+
+
+def test_smol135m_bf16_32_steps_vs_oracle(gpu):
+    """bf16 weights + bf16 cache (the config-3 serving precision): 32 greedy
+    steps identical to the oracle with the same storage points."""
+    from smollm2_triton import SmolLM2Config
+    w = inputs.round_linear_weights_bf16(inputs.llama_weights(inputs.SMOL_135M, 0))
+    prompt = np.random.default_rng(5).integers(0, 49152, 12).tolist()
+    m = _smol(inputs.SMOL_135M, w, dtype="bfloat16")
+    o = omodels.SmolLM2Oracle(SmolLM2Config(**inputs.SMOL_135M.config_kwargs()), w,
+                              weight_dtype="bfloat16")
+    want, wl = o.generate(np.array([prompt], np.int32), 32)
+    toks, logits = _smol_run(m, prompt, 32)
+    upto = _same_tokens(toks, want[0], wl, 2e-2)
+    steps = max(upto - len(prompt), 1)
+    np.testing.assert_allclose(logits[:steps], wl[:steps], atol=2e-2)
+
+
+@pytest.mark.parametrize("mode", ["float32", "bf16w"])
+def test_llama3b_slice_matches_reference(gpu, golden, mode):
+    """Llama-3.2-3B geometry (24/8/128, 2 layers, 128256 vocab)."""
+    g = golden("llama3b_2l_slice")
+    w = inputs.round_linear_weights_bf16(inputs.llama_weights(inputs.LLAMA3B_2L, 0))
+    if mode == "float32":
+        m = _smol(inputs.LLAMA3B_2L, w)
+        tol = 1e-4
+    else:
+        m = _smol(inputs.LLAMA3B_2L, w, dtype="bfloat16", kv_dtype="float32")
+        tol = 1e-3
+    prompt = g["tokens"][:4].tolist()
+    toks, logits = _smol_run(m, prompt, 2)
+    np.testing.assert_array_equal(toks, g["tokens"])
+    np.testing.assert_allclose(logits, g["logits"], atol=tol)
+
+
+def test_generate_batch_equals_single(gpu):
+    """Ragged batched greedy generation (one CUDA graph per step) gives each
+    prompt the tokens it gets alone (up to a near-tie of the logits: the
+    batch changes the GEMM tiling and so the fp32 summation order)."""
+    w = inputs.round_linear_weights_bf16(inputs.llama_weights(inputs.SMOL_135M, 0))
+    m = _smol(inputs.SMOL_135M, w, dtype="bfloat16")
+    rng = np.random.default_rng(2)
+    prompts = [rng.integers(0, 49152, n).tolist() for n in (1, 7, 30, 12)]
+    batch = m.generate_batch(prompts, max_new_tokens=10)
+    for p, got in zip(prompts, batch):
+        assert len(got) == len(p) + 10
+        want, logits = _smol_run(m, p, 10)
+        assert _same_tokens(got, want, logits, 1e-3) > len(p)
+
+
+def test_decode_graph_replay_equals_eager(gpu):
+    """A captured decode step replays the eager step bit for bit."""
+    from smollm2_triton.engine import LlamaSession, LlamaWeights
+    from smollm2_triton import SmolLM2Config
+    cfg = SmolLM2Config(**inputs.SMOL_135M.config_kwargs())
+    wts = LlamaWeights(cfg, None, "bfloat16", seed=3, max_pos=256)
+    prompts = [[1, 2, 3], [4, 5, 6, 7, 8], [9]]
+    eager = LlamaSession(wts, 3, 64)
+    eager.prefill(prompts)
+    graph = LlamaSession(wts, 3, 64)
+    graph.prefill(prompts)
+    graph.capture()
+    for _ in range(6):
+        eager.step()
+        graph.step()
+        np.testing.assert_array_equal(graph.ids.to_numpy(), eager.ids.to_numpy())
+        np.testing.assert_array_equal(graph.logits.to_numpy(), eager.logits.to_numpy())
+    np.testing.assert_array_equal(graph.pos.to_numpy(), [9, 11, 7])
+
+
+def test_forward_gpu_validation(gpu):
+    m = _smol(inputs.SMOL_TINY, inputs.llama_weights_legacy(inputs.SMOL_TINY, 42))
+    with pytest.raises(ValueError):
+        m.forward_gpu(np.zeros((2, 3), np.int32))
+    with pytest.raises(RuntimeError):
+        m._forward_cached(np.array([[1]], np.int32))
+    with pytest.raises(ValueError):
+        m._init_cache_gpu(max_seq=513)
+    m._init_cache_gpu(max_seq=4)
+    m._forward_cached(np.array([[1, 2, 3]], np.int32))
+    with pytest.raises(ValueError):
+        m._forward_cached(np.array([[1, 2]], np.int32))     # decode needs seq=1
+    m._forward_cached(np.array([[4]], np.int32))
+    with pytest.raises(ValueError):
+        m._forward_cached(np.array([[5]], np.int32))        # cache full
+    # forward without cache = prefill logits of the cached path
+    full = m.forward_gpu(np.array([[5, 12, 7]], np.int32))
+    m._init_cache_gpu(max_seq=8)
+    cached = m._forward_cached(np.array([[5, 12, 7]], np.int32))
+    np.testing.assert_array_equal(full, cached)
+
+
+# --------------------------------------------------------------- GPT-2 -----
+def _gpt2(shape, weights, dtype="float32"):
+    from gpt2_triton import GPT2Config, GPT2Model
+    return GPT2Model(GPT2Config(**shape.config_kwargs()), weights, dtype=dtype)
+
+
+def _gpt2_run(model, prompt, n_new):
+    model._init_cache()
+    logits = model.forward(np.array([prompt], np.int32), use_cache=True)
+    toks, steps = list(prompt), []
+    for step in range(n_new):
+        last = logits[0, -1]
+        steps.append(last.copy())
+        t = int(np.argmax(last))
+        toks.append(t)
+        if step < n_new - 1:
+            logits = model.forward(np.array([[t]], np.int32), use_cache=True)
+    return np.array(toks, np.int32), np.stack(steps)
+
+
+def test_gpt2_tiny_matches_reference(gpu, golden):
+    g = golden("gpt2_tiny")
+    m = _gpt2(inputs.GPT2_TINY, inputs.gpt2_weights_legacy(inputs.GPT2_TINY, 42))
+    toks, logits = _gpt2_run(m, [5, 12, 7, 0, 3], 10)
+    np.testing.assert_array_equal(toks, g["tokens"])
+    scale = np.abs(g["logits"]).max()
+    np.testing.assert_allclose(logits, g["logits"], atol=1e-4 * scale, rtol=1e-4)
+
+
+def test_gpt2_tiny_generate_and_full_forward(gpu, golden):
+    g = golden("gpt2_tiny")
+    m = _gpt2(inputs.GPT2_TINY, inputs.gpt2_weights_legacy(inputs.GPT2_TINY, 42))
+    out = m.generate(np.array([[5, 12, 7, 0, 3]], np.int32), max_new_tokens=10,
+                     temperature=0.0)
+    np.testing.assert_array_equal(out[0], g["tokens"])
+    # the no-cache forward over the whole sequence predicts the same tokens
+    full = m.forward(out[:, :-1], use_cache=False)
+    np.testing.assert_array_equal(np.argmax(full[0, 4:], axis=-1), g["tokens"][5:])
+
+
+def test_gpt2_small_slice_matches_reference(gpu, golden):
+    """BASELINE config 1 geometry (GPT-2 small, fp32)."""
+    g = golden("gpt2_small_slice")
+    m = _gpt2(inputs.GPT2_SMALL, inputs.gpt2_weights(inputs.GPT2_SMALL, 0))
+    prompt = g["tokens"][:8].tolist()
+    toks, logits = _gpt2_run(m, prompt, 2)
+    np.testing.assert_array_equal(toks, g["tokens"])
+    np.testing.assert_allclose(logits, g["logits"], atol=1e-4)

@@ -26,6 +26,9 @@
 #include "common.cuh"
 
 namespace tllm {
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();  // tma.cu
+
 namespace {
 
 constexpr int kConsumerWarps = 4;
@@ -70,9 +73,11 @@ __device__ __forceinline__ float fast_exp2(float x) {
 }
 
 struct DecodeParams {
-  const float *q;        // (B, n_head, D)
-  float *out;            // (B, n_head, D)
+  const float *q;        // row b, head h at q + b * q_sb + h * q_sh
+  float *out;            // row b, head h at out + b * o_sb + h * o_sh
   const int *seq_lens;   // (B,) or null (every sequence has max_len keys)
+  const int *row_seq;    // (B,) cache sequence of each row, or null (= row)
+  long q_sb, q_sh, o_sb, o_sh;
   float *part_acc;       // (B, n_head, max_splits, D)
   float *part_ml;        // (B, n_head, max_splits, 2)
   int *counters;         // (B, gridDim.y)
@@ -154,7 +159,7 @@ __global__ void __launch_bounds__(kThreads)
   // ---------------------------------------------------------------- producer
   if (warp == kConsumerWarps) {
     if (lane == 0) {
-      const int plane = b * p.n_kv + kvh;
+      const int plane = (p.row_seq ? p.row_seq[b] : b) * p.n_kv + kvh;
       for (int t = 0; t < ntiles; ++t) {
         const int s = t % kStages;
         if (t >= kStages) {
@@ -183,7 +188,7 @@ __global__ void __launch_bounds__(kThreads)
     float qr[G][S::NV * S::VEC];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      const float *qp = p.q + ((size_t)b * p.n_head + head0 + g) * D;
+      const float *qp = p.q + b * p.q_sb + (long)(head0 + g) * p.q_sh;
 #pragma unroll
       for (int v = 0; v < S::NV; ++v) {
         const float4 *q4 =
@@ -366,7 +371,8 @@ __global__ void __launch_bounds__(kThreads)
     }
     const size_t row = (size_t)b * p.n_head + head0 + g;
     if (single) {
-      p.out[row * D + d] = den > 0.f ? num / den : 0.f;
+      p.out[b * p.o_sb + (long)(head0 + g) * p.o_sh + d] =
+          den > 0.f ? num / den : 0.f;
     } else {
       const size_t slot = row * p.max_splits + j;
       p.part_acc[slot * D + d] = num;
@@ -422,7 +428,7 @@ __global__ void __launch_bounds__(kThreads)
     float o = 0.f;
     for (int s = 0; s < n_splits; ++s)
       o = fmaf(sw[g * kMaxSplits + s], __ldcg(&p.part_acc[(base + s) * D + d]), o);
-    p.out[row * D + d] = o;
+    p.out[b * p.o_sb + (long)(head0 + g) * p.o_sh + d] = o;
   }
 }
 
@@ -505,6 +511,11 @@ __global__ void __launch_bounds__(kThreads)
       reinterpret_cast<uint64_t *>(smem + 2 * S::STAGES * S::TILE_BYTES);
   uint64_t *empty = full + S::STAGES;
   __shared__ int s_flag;
+  // 128-byte-swizzled TMA tiles need 1024-byte aligned stage buffers
+  if (smem_u32(smem) & 1023) {
+    if (threadIdx.x == 0) atomicOr(p.err, DEV_ERR_SMEM_ALIGN);
+    return;
+  }
 
   const int b = blockIdx.z;
   const int y = blockIdx.y;
@@ -544,7 +555,7 @@ __global__ void __launch_bounds__(kThreads)
   bool failed = false;
   if (warp == kConsumerWarps) {
     if (lane == 0) {
-      const int plane = b * p.n_kv + kvh;
+      const int plane = (p.row_seq ? p.row_seq[b] : b) * p.n_kv + kvh;
       for (int t = 0; t < ntiles; ++t) {
         const int s = t % S::STAGES;
         if (t >= S::STAGES &&
@@ -582,7 +593,7 @@ __global__ void __launch_bounds__(kThreads)
         float x0 = 0.f, x1 = 0.f;
         if (row < G) {
           const float2 v = *reinterpret_cast<const float2 *>(
-              p.q + ((size_t)b * p.n_head + head0 + row) * D + col);
+              p.q + b * p.q_sb + (long)(head0 + row) * p.q_sh + col);
           x0 = v.x * p.qscale;
           x1 = v.y * p.qscale;
         }
@@ -771,7 +782,8 @@ __global__ void __launch_bounds__(kThreads)
     }
     const size_t row = (size_t)b * p.n_head + head0 + g;
     if (single) {
-      p.out[row * D + d] = den > 0.f ? num / den : 0.f;
+      p.out[b * p.o_sb + (long)(head0 + g) * p.o_sh + d] =
+          den > 0.f ? num / den : 0.f;
     } else {
       const size_t slot = row * p.max_splits + j;
       p.part_acc[slot * D + d] = num;
@@ -827,26 +839,14 @@ __global__ void __launch_bounds__(kThreads)
     for (int s = 0; s < n_splits; ++s)
       o2 = fmaf(sw[g * kMaxSplits + s], __ldcg(&p.part_acc[(base + s) * D + d]),
                 o2);
-    p.out[row * D + d] = o2;
+    p.out[b * p.o_sb + (long)(head0 + g) * p.o_sh + d] = o2;
   }
 }
 
 // --------------------------------------------------------------------------
 // Host side
 // --------------------------------------------------------------------------
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void *ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr,
-                                cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  });
-  return fn;
-}
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() { return tensor_map_encoder(); }
 
 // Tensor map over a KV cache viewed as (planes, max_seq, D) with a box of
 // (rows x box_inner) elements; swizzle128 selects the 128-byte swizzle.
@@ -933,12 +933,13 @@ template <typename T>
 int dispatch_d(int D, int G, const DecodeParams &p, const CUtensorMap &mk,
                const CUtensorMap &mv, dim3 grid, cudaStream_t st) {
   switch (D) {
+    case 16: return dispatch_g<T, 16>(G, p, mk, mv, grid, st);
     case 32: return dispatch_g<T, 32>(G, p, mk, mv, grid, st);
     case 64: return dispatch_g<T, 64>(G, p, mk, mv, grid, st);
     case 128: return dispatch_g<T, 128>(G, p, mk, mv, grid, st);
     case 256: return dispatch_g<T, 256>(G, p, mk, mv, grid, st);
   }
-  set_error("head_dim %d not built (32, 64, 128, 256 are)", D);
+  set_error("head_dim %d not built (16, 32, 64, 128, 256 are)", D);
   return TLLM_ERR_UNSUPPORTED;
 }
 
@@ -1011,12 +1012,17 @@ int pick_chunk(int rows, int batch, int ygrid, int max_len) {
 
 // Validation, split selection, tensor maps and launch shared by the decode
 // entry points; `err_word` is the device int that receives error codes.
-static int decode_impl(const float *q, const void *k_cache, const void *v_cache,
-                       int kv_dtype, const int32_t *seq_lens, float *out,
-                       int batch, int n_head, int n_kv_head, int head_dim,
-                       int max_seq, int max_len, float sm_scale, void *partial,
-                       size_t partial_bytes, int32_t *counters, int *err_word,
-                       tllm_stream_t stream) {
+//   rows = query rows (B for decode); row r reads cache sequence
+//   row_seq[r] (r if null) for seq_lens[r] keys (max_len if null); q / out
+//   of row r, head h live at r * q_sb + h * q_sh (resp. o_sb, o_sh);
+//   cache_batch = sequences in the cache.
+static int rows_impl(const float *q, long q_sb, long q_sh, const void *k_cache,
+                     const void *v_cache, int kv_dtype, const int32_t *seq_lens,
+                     const int32_t *row_seq, float *out, long o_sb, long o_sh,
+                     int batch, int n_head, int n_kv_head, int head_dim,
+                     int cache_batch, int max_seq, int max_len, float sm_scale,
+                     void *partial, size_t partial_bytes, int32_t *counters,
+                     int *err_word, tllm_stream_t stream) {
   TLLM_CHECK_ARG(batch >= 0 && n_head > 0 && n_kv_head > 0,
                  "invalid head counts n_head=%d n_kv_head=%d", n_head,
                  n_kv_head);
@@ -1031,6 +1037,9 @@ static int decode_impl(const float *q, const void *k_cache, const void *v_cache,
   TLLM_CHECK_ARG(((uintptr_t)k_cache & 15) == 0 && ((uintptr_t)v_cache & 15) == 0,
                  "KV cache must be 16-byte aligned");
   TLLM_CHECK_ARG(((uintptr_t)q & 15) == 0, "q must be 16-byte aligned");
+  TLLM_CHECK_ARG(q_sb % 4 == 0 && q_sh % 4 == 0 && o_sb >= 0 && o_sh >= 0,
+                 "q strides must be multiples of 4 elements");
+  TLLM_CHECK_ARG(cache_batch > 0, "cache_batch must be > 0");
   if (max_len <= 0 || max_len > max_seq) max_len = max_seq;
   if (sm_scale <= 0.f) sm_scale = 1.0f / sqrtf((float)head_dim);
 
@@ -1064,16 +1073,21 @@ static int decode_impl(const float *q, const void *k_cache, const void *v_cache,
 
   CUtensorMap mk, mv;
   int rc = make_kv_map(&mk, k_cache, kv_dtype, head_dim, max_seq,
-                       (long)batch * n_kv_head, rows, mma ? 64 : 0, mma);
+                       (long)cache_batch * n_kv_head, rows, mma ? 64 : 0, mma);
   if (rc) return rc;
   rc = make_kv_map(&mv, v_cache, kv_dtype, head_dim, max_seq,
-                   (long)batch * n_kv_head, rows, mma ? 64 : 0, mma);
+                   (long)cache_batch * n_kv_head, rows, mma ? 64 : 0, mma);
   if (rc) return rc;
 
   DecodeParams p;
   p.q = q;
   p.out = out;
   p.seq_lens = seq_lens;
+  p.row_seq = row_seq;
+  p.q_sb = q_sb;
+  p.q_sh = q_sh;
+  p.o_sb = o_sb;
+  p.o_sh = o_sh;
   p.part_acc = static_cast<float *>(partial);
   p.part_ml = p.part_acc
                   ? p.part_acc + (size_t)batch * n_head * max_splits * head_dim
@@ -1132,10 +1146,27 @@ int tllm_gqa_decode(const float *q, const void *k_cache, const void *v_cache,
                     size_t partial_bytes, int32_t *counters,
                     tllm_stream_t stream) {
   TLLM_INJECT("launch");
-  return decode_impl(q, k_cache, v_cache, kv_dtype, seq_lens, out, batch,
-                     n_head, n_kv_head, head_dim, max_seq, max_len, sm_scale,
-                     partial, partial_bytes, counters, device_error_ptr(),
-                     stream);
+  const long hd = (long)n_head * head_dim;
+  return rows_impl(q, hd, head_dim, k_cache, v_cache, kv_dtype, seq_lens,
+                   nullptr, out, hd, head_dim, batch, n_head, n_kv_head,
+                   head_dim, batch, max_seq, max_len, sm_scale, partial,
+                   partial_bytes, counters, device_error_ptr(), stream);
+}
+
+int tllm_gqa_rows(const float *q, long q_row_stride, long q_head_stride,
+                  const void *k_cache, const void *v_cache, int kv_dtype,
+                  const int32_t *row_seq, const int32_t *row_len, float *out,
+                  long out_row_stride, long out_head_stride, int rows,
+                  int n_head, int n_kv_head, int head_dim, int cache_batch,
+                  int max_seq, int max_len, float sm_scale, void *partial,
+                  size_t partial_bytes, int32_t *counters,
+                  tllm_stream_t stream) {
+  TLLM_INJECT("launch");
+  return rows_impl(q, q_row_stride, q_head_stride, k_cache, v_cache, kv_dtype,
+                   row_len, row_seq, out, out_row_stride, out_head_stride,
+                   rows, n_head, n_kv_head, head_dim, cache_batch, max_seq,
+                   max_len, sm_scale, partial, partial_bytes, counters,
+                   device_error_ptr(), stream);
 }
 
 }  // extern "C"
@@ -1224,7 +1255,9 @@ extern "C" int tllm_gqa_decode_noalloc(
   cudaStream_t st = resolve(stream);
   TLLM_CUDA(cudaMemsetAsync(counters, 0, (size_t)batch * n_head * sizeof(int32_t),
                             st));
-  return decode_impl(q, k_cache, v_cache, kv_dtype, seq_lens, out, batch,
-                     n_head, n_kv_head, head_dim, max_seq, max_len, sm_scale,
-                     base, kNoAllocPartialBytes, counters, err_word, st);
+  const long hd = (long)n_head * head_dim;
+  return rows_impl(q, hd, head_dim, k_cache, v_cache, kv_dtype, seq_lens,
+                   nullptr, out, hd, head_dim, batch, n_head, n_kv_head,
+                   head_dim, batch, max_seq, max_len, sm_scale, base,
+                   kNoAllocPartialBytes, counters, err_word, st);
 }

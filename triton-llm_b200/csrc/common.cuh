@@ -48,6 +48,7 @@ enum DeviceError : int {
   DEV_ERR_WAIT_TIMEOUT = 1,   // an mbarrier wait ran out of polls
   DEV_ERR_LEN_CLAMPED = 2,    // a device-side length exceeded its bound
   DEV_ERR_TOKEN_RANGE = 4,    // a token id outside [0, vocab)
+  DEV_ERR_SMEM_ALIGN = 8,     // dynamic shared memory not 1024-byte aligned
 };
 int *device_error_ptr();
 

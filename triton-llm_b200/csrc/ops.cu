@@ -1,0 +1,436 @@
+// Row-wise and elementwise kernels of the decode step and the drop-in kernel
+// API: RMSNorm, LayerNorm, embedding gather, greedy argmax, RoPE, SwiGLU,
+// add, GELU, row softmax, a plain fp32 GEMM for the (K, N) weight layout of
+// triton_llm/kernels/gemm.py, and a counter-based random fill used to build
+// synthetic weights and KV contexts on the device.
+#include <cmath>
+
+#include "common.cuh"
+
+namespace tllm {
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  return v;
+}
+
+// Block-wide sum over blockDim.x threads (<= 1024); every thread gets it.
+__device__ float block_sum(float v, float *red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  const int nw = (blockDim.x + 31) >> 5;
+  float t = lane < nw ? red[lane] : 0.f;
+  t = warp_sum(t);
+  return t;
+}
+
+// y = (x / sqrt(sum(x^2) / N + eps)) * w   (triton_llm/kernels/rms_norm.py:50-55)
+__global__ void rmsnorm_kernel(const float *x, const float *w, float *y, int N,
+                               float eps) {
+  __shared__ float red[32];
+  const float *xr = x + (size_t)blockIdx.x * N;
+  float *yr = y + (size_t)blockIdx.x * N;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < N; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+  ss = block_sum(ss, red);
+  const float rms = sqrtf(ss / (float)N + eps);
+  for (int i = threadIdx.x; i < N; i += blockDim.x) yr[i] = (xr[i] / rms) * w[i];
+}
+
+// two-pass LayerNorm (triton_llm/kernels/layernorm.py:56-66)
+__global__ void layernorm_kernel(const float *x, const float *g, const float *b,
+                                 float *y, int N, float eps) {
+  __shared__ float red[32];
+  const float *xr = x + (size_t)blockIdx.x * N;
+  float *yr = y + (size_t)blockIdx.x * N;
+  float s = 0.f;
+  for (int i = threadIdx.x; i < N; i += blockDim.x) s += xr[i];
+  const float mean = block_sum(s, red) / (float)N;
+  float v = 0.f;
+  for (int i = threadIdx.x; i < N; i += blockDim.x) {
+    const float c = xr[i] - mean;
+    v = fmaf(c, c, v);
+  }
+  const float var = block_sum(v, red) / (float)N;
+  const float rstd = 1.f / sqrtf(var + eps);
+  for (int i = threadIdx.x; i < N; i += blockDim.x)
+    yr[i] = (xr[i] - mean) * rstd * g[i] + b[i];
+}
+
+// out[m] = wte[ids[m]] (+ wpe[pos[m]])   (triton_llm/kernels/embedding.py:75-94,
+// smollm2_triton/model.py:547-560)
+template <bool BF16>
+__global__ void embedding_kernel(const int *ids, const void *wte,
+                                 const float *wpe, const int *pos, float *out,
+                                 int n, int vocab, int max_pos, int *err) {
+  const int m = blockIdx.x;
+  const int id = ids[m];
+  const bool ok = id >= 0 && id < vocab;
+  if (!ok && threadIdx.x == 0) atomicOr(err, DEV_ERR_TOKEN_RANGE);
+  const int p = pos ? pos[m] : 0;
+  const bool pok = !wpe || (p >= 0 && p < max_pos);
+  if (!pok && threadIdx.x == 0) atomicOr(err, DEV_ERR_LEN_CLAMPED);
+  float *o = out + (size_t)m * n;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    float v = 0.f;
+    if (ok) {
+      if (BF16)
+        v = __uint_as_float(
+            (uint32_t)static_cast<const uint16_t *>(wte)[(size_t)id * n + i] << 16);
+      else
+        v = static_cast<const float *>(wte)[(size_t)id * n + i];
+    }
+    if (wpe && pok) v += wpe[(size_t)p * n + i];
+    o[i] = v;
+  }
+}
+
+// ids[m] = first index of the maximum of logits[m, :V] (np.argmax semantics,
+// smollm2_triton/model.py:583); optionally pos[m] += 1 (decode bookkeeping).
+__global__ void argmax_kernel(const float *logits, int ld, int V, int *ids,
+                              int *pos) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const float *row = logits + (size_t)blockIdx.x * ld;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float v = row[i];
+    if (v > best || (v == best && i < bi)) {
+      best = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, off);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+    if (ov > best || (ov == best && oi < bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) {
+    sv[warp] = best;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    best = lane < nw ? sv[lane] : -INFINITY;
+    bi = lane < nw ? si[lane] : 0x7fffffff;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      if (ov > best || (ov == best && oi < bi)) {
+        best = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      ids[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+      if (pos) pos[blockIdx.x] += 1;
+    }
+  }
+}
+
+// In-place rotate-half RoPE of rows (n_rows, d): row r at position
+// (r % seq_len) + offset (triton_llm/kernels/rope.py:49-66). Products are
+// rounded separately (no FMA), like the numpy restatement.
+__global__ void rope_kernel(float *x, const float *cos_t, const float *sin_t,
+                            int n_rows, int d, int seq_len, int offset) {
+  const int half = d / 2;
+  const long total = (long)n_rows * half;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total;
+       i += (long)gridDim.x * blockDim.x) {
+    const int r = (int)(i / half);
+    const int j = (int)(i - (long)r * half);
+    const int p = r % seq_len + offset;
+    float *row = x + (size_t)r * d;
+    const float xe = row[j], xo = row[j + half];
+    const float c = cos_t[(size_t)p * half + j], s = sin_t[(size_t)p * half + j];
+    row[j] = __fsub_rn(__fmul_rn(xe, c), __fmul_rn(xo, s));
+    row[j + half] = __fadd_rn(__fmul_rn(xe, s), __fmul_rn(xo, c));
+  }
+}
+
+enum ElemOp : int { EL_SWIGLU = 0, EL_ADD = 1, EL_GELU = 2 };
+
+__global__ void elementwise_kernel(int op, const float *a, const float *b,
+                                   float *out, long n) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n;
+       i += (long)gridDim.x * blockDim.x) {
+    const float x = a[i];
+    float r;
+    if (op == EL_SWIGLU) {
+      // triton_llm/kernels/swiglu.py:51-56
+      const float e = expf(-fabsf(x));
+      const float sig = x >= 0.f ? 1.f / (1.f + e) : e / (1.f + e);
+      r = x * sig * b[i];
+    } else if (op == EL_ADD) {
+      r = x + b[i];  // triton_llm/kernels/add.py:49-51
+    } else {
+      // triton_llm/kernels/gelu.py:17-28, :50-51
+      const float u = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+      const float e = expf(-2.f * fabsf(u));
+      const float t = (u < 0.f ? -1.f : 1.f) * (1.f - e) / (1.f + e);
+      r = 0.5f * x * (1.f + t);
+    }
+    out[i] = r;
+  }
+}
+
+// Row softmax (triton_llm/kernels/softmax.py): max-subtracted exp, then /sum.
+__global__ void softmax_kernel(const float *x, float *y, int N) {
+  __shared__ float red[32];
+  const float *xr = x + (size_t)blockIdx.x * N;
+  float *yr = y + (size_t)blockIdx.x * N;
+  float mx = -INFINITY;
+  for (int i = threadIdx.x; i < N; i += blockDim.x) mx = fmaxf(mx, xr[i]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1)
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[warp] = mx;
+  __syncthreads();
+  const int nw = (blockDim.x + 31) >> 5;
+  float t = lane < nw ? red[lane] : -INFINITY;
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1)
+    t = fmaxf(t, __shfl_xor_sync(0xffffffffu, t, off));
+  mx = t;
+  __syncthreads();
+  float s = 0.f;
+  for (int i = threadIdx.x; i < N; i += blockDim.x) s += expf(xr[i] - mx);
+  s = block_sum(s, red);
+  for (int i = threadIdx.x; i < N; i += blockDim.x) yr[i] = expf(xr[i] - mx) / s;
+}
+
+// C[M, N] = A[M, K] @ B[K, N], fp32, both row-major (the reference's
+// (in, out) weight layout, triton_llm/kernels/gemm.py:40-50). 64x64 tiles,
+// 16x16 threads with 4x4 outputs each.
+__global__ void __launch_bounds__(256)
+    gemm_f32_kn_kernel(const float *A, const float *B, float *C, int M, int N,
+                       int K) {
+  __shared__ float As[16][64 + 4];
+  __shared__ float Bs[16][64 + 4];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int m0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    for (int i = threadIdx.x; i < 16 * 64; i += 256) {
+      const int kk = i / 64, mm = i % 64;
+      const int gm = m0 + mm, gk = k0 + kk;
+      As[kk][mm] = (gm < M && gk < K) ? A[(size_t)gm * K + gk] : 0.f;
+      const int gn = n0 + mm;
+      Bs[kk][mm] = (gk < K && gn < N) ? B[(size_t)gk * N + gn] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        a[i] = As[kk][ty * 4 + i];
+        b[i] = Bs[kk][tx * 4 + i];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int gm = m0 + ty * 4 + i, gn = n0 + tx * 4 + j;
+      if (gm < M && gn < N) C[(size_t)gm * N + gn] = acc[i][j];
+    }
+}
+
+// Counter-based values for synthetic inputs: element i gets
+// sum of four 16-bit hashes of (seed, i), centred and scaled so the result
+// has mean 0 and standard deviation `std` (Irwin-Hall approximation of a
+// normal). Only integer arithmetic and one float multiply: the numpy
+// restatement in tests regenerates the identical values.
+__host__ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+__global__ void fill_random_kernel(void *ptr, int bf16, long n, uint64_t seed,
+                                   float scale) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n;
+       i += (long)gridDim.x * blockDim.x) {
+    const uint64_t h = mix64(seed ^ mix64((uint64_t)i));
+    const int s = (int)(h & 0xffff) + (int)((h >> 16) & 0xffff) +
+                  (int)((h >> 32) & 0xffff) + (int)(h >> 48) - 131070;
+    const float v = (float)s * scale;
+    if (bf16)
+      static_cast<uint16_t *>(ptr)[i] = f32_to_bf16_bits(v);
+    else
+      static_cast<float *>(ptr)[i] = v;
+  }
+}
+
+int grid_for(long n, int threads) {
+  long g = (n + threads - 1) / threads;
+  const long cap = 32L * sm_count();
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return (int)g;
+}
+
+int row_threads(int n) {
+  int t = 32;
+  while (t < n && t < 1024) t <<= 1;
+  return t < 128 ? (n > 32 ? 128 : 32) : t;
+}
+
+}  // namespace
+}  // namespace tllm
+
+using namespace tllm;
+
+extern "C" {
+
+int tllm_rmsnorm(const float *x, const float *w, float *y, int M, int N,
+                 float eps, tllm_stream_t stream) {
+  TLLM_INJECT("launch");
+  TLLM_CHECK_ARG(M >= 0 && N >= 0, "negative shape");
+  if (M == 0) return TLLM_OK;
+  TLLM_CHECK_ARG(N > 0, "RMSNorm requires the last dimension N > 0");
+  TLLM_CHECK_ARG(x && w && y, "NULL pointer");
+  rmsnorm_kernel<<<M, row_threads(N) > 256 ? 256 : row_threads(N), 0,
+                   resolve(stream)>>>(x, w, y, N, eps);
+  TLLM_LAUNCH_CHECK();
+  return TLLM_OK;
+}
+
+int tllm_layernorm(const float *x, const float *g, const float *b, float *y,
+                   int M, int N, float eps, tllm_stream_t stream) {
+  TLLM_INJECT("launch");
+  TLLM_CHECK_ARG(M >= 0 && N >= 0, "negative shape");
+  if (M == 0) return TLLM_OK;
+  TLLM_CHECK_ARG(N > 0, "LayerNorm requires the last dimension N > 0");
+  TLLM_CHECK_ARG(x && g && b && y, "NULL pointer");
+  layernorm_kernel<<<M, 256, 0, resolve(stream)>>>(x, g, b, y, N, eps);
+  TLLM_LAUNCH_CHECK();
+  return TLLM_OK;
+}
+
+int tllm_embedding(const int32_t *ids, const void *wte, int wte_dtype,
+                   const float *wpe, const int32_t *pos, float *out, int M,
+                   int n_embd, int vocab, int max_pos, tllm_stream_t stream) {
+  TLLM_INJECT("launch");
+  TLLM_CHECK_ARG(M >= 0 && n_embd > 0 && vocab > 0, "invalid shape");
+  if (M == 0) return TLLM_OK;
+  TLLM_CHECK_ARG(ids && wte && out, "NULL pointer");
+  TLLM_CHECK_ARG(!wpe || pos, "positions are required with wpe");
+  int *err = device_error_ptr();
+  TLLM_CHECK_ARG(err, "device error word unavailable");
+  if (wte_dtype == TLLM_BF16)
+    embedding_kernel<true><<<M, 256, 0, resolve(stream)>>>(
+        ids, wte, wpe, pos, out, n_embd, vocab, max_pos, err);
+  else
+    embedding_kernel<false><<<M, 256, 0, resolve(stream)>>>(
+        ids, wte, wpe, pos, out, n_embd, vocab, max_pos, err);
+  TLLM_LAUNCH_CHECK();
+  return TLLM_OK;
+}
+
+int tllm_argmax(const float *logits, int M, int V, int ld, int32_t *ids,
+                int32_t *pos_inc, tllm_stream_t stream) {
+  TLLM_INJECT("launch");
+  TLLM_CHECK_ARG(M >= 0 && V > 0, "invalid shape");
+  if (M == 0) return TLLM_OK;
+  TLLM_CHECK_ARG(logits && ids, "NULL pointer");
+  argmax_kernel<<<M, 1024, 0, resolve(stream)>>>(logits, ld > 0 ? ld : V, V,
+                                                 ids, pos_inc);
+  TLLM_LAUNCH_CHECK();
+  return TLLM_OK;
+}
+
+int tllm_rope(float *x, const float *cos_t, const float *sin_t, int n_rows,
+              int d, int seq_len, int position_offset, tllm_stream_t stream) {
+  TLLM_INJECT("launch");
+  TLLM_CHECK_ARG(d >= 2 && d % 2 == 0, "d_k must be even and >= 2, got %d", d);
+  if (n_rows == 0) return TLLM_OK;
+  TLLM_CHECK_ARG(seq_len >= 1, "seq_len must be >= 1, got %d", seq_len);
+  TLLM_CHECK_ARG(position_offset >= 0, "position_offset must be >= 0");
+  TLLM_CHECK_ARG(x && cos_t && sin_t, "NULL pointer");
+  const long n = (long)n_rows * (d / 2);
+  rope_kernel<<<grid_for(n, 256), 256, 0, resolve(stream)>>>(
+      x, cos_t, sin_t, n_rows, d, seq_len, position_offset);
+  TLLM_LAUNCH_CHECK();
+  return TLLM_OK;
+}
+
+int tllm_elementwise(int op, const float *a, const float *b, float *out,
+                     long n, tllm_stream_t stream) {
+  TLLM_INJECT("launch");
+  TLLM_CHECK_ARG(op >= 0 && op <= 2, "unknown elementwise op %d", op);
+  TLLM_CHECK_ARG(n >= 0, "negative size");
+  if (n == 0) return TLLM_OK;
+  TLLM_CHECK_ARG(a && out && (op == EL_GELU || b), "NULL pointer");
+  elementwise_kernel<<<grid_for(n, 256), 256, 0, resolve(stream)>>>(op, a, b,
+                                                                   out, n);
+  TLLM_LAUNCH_CHECK();
+  return TLLM_OK;
+}
+
+int tllm_softmax(const float *x, float *y, int M, int N, tllm_stream_t stream) {
+  TLLM_INJECT("launch");
+  TLLM_CHECK_ARG(M >= 0 && N >= 0, "negative shape");
+  if (M == 0 || N == 0) return TLLM_OK;
+  TLLM_CHECK_ARG(x && y, "NULL pointer");
+  softmax_kernel<<<M, 256, 0, resolve(stream)>>>(x, y, N);
+  TLLM_LAUNCH_CHECK();
+  return TLLM_OK;
+}
+
+int tllm_gemm_f32(const float *a, const float *b, float *c, int M, int N,
+                  int K, tllm_stream_t stream) {
+  TLLM_INJECT("launch");
+  TLLM_CHECK_ARG(M >= 0 && N >= 0 && K >= 0, "negative shape");
+  if (M == 0 || N == 0) return TLLM_OK;
+  TLLM_CHECK_ARG(c, "NULL output");
+  cudaStream_t st = resolve(stream);
+  if (K == 0) {
+    TLLM_CUDA(cudaMemsetAsync(c, 0, (size_t)M * N * sizeof(float), st));
+    return TLLM_OK;
+  }
+  TLLM_CHECK_ARG(a && b, "NULL input");
+  dim3 grid((N + 63) / 64, (M + 63) / 64);
+  gemm_f32_kn_kernel<<<grid, 256, 0, st>>>(a, b, c, M, N, K);
+  TLLM_LAUNCH_CHECK();
+  return TLLM_OK;
+}
+
+int tllm_fill_random(void *ptr, int dtype, long n, uint64_t seed, float std,
+                     tllm_stream_t stream) {
+  TLLM_CHECK_ARG(dtype == TLLM_F32 || dtype == TLLM_BF16, "dtype F32 or BF16");
+  TLLM_CHECK_ARG(n >= 0, "negative size");
+  if (n == 0) return TLLM_OK;
+  TLLM_CHECK_ARG(ptr, "NULL pointer");
+  // Irwin-Hall of four U[0, 65536): variance 4 * 65536^2 / 12
+  const float scale = std / (65536.0f * 0.57735026918962576f);
+  fill_random_kernel<<<grid_for(n, 256), 256, 0, resolve(stream)>>>(
+      ptr, dtype == TLLM_BF16, n, seed, scale);
+  TLLM_LAUNCH_CHECK();
+  return TLLM_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,343 @@
+"""Batched decode engine for SmolLM2 / Llama models on sm_100a.
+
+The math is the reference's cached forward pass
+(smollm2_triton/model.py:231-379) for B independent sequences at once:
+
+  h = embed(ids)                                        model.py:271, 547-560
+  per layer:
+    x = rmsnorm(h) ; q, k, v = x Wq, x Wk, x Wv         model.py:281-287
+    rope(q), rope(k) ; cache[pos] = k, v                model.py:296-302
+    o = gqa_attention(q, cache[:len])                   model.py:305-314
+    h = h + o Wo                                        model.py:351-353
+    x = rmsnorm(h) ; h = h + swiglu(x Wg, x Wu) Wd      model.py:357-365
+  logits = rmsnorm(h) W_lm                              model.py:371-375
+
+mapped onto seven kernels per layer: RMSNorm, the QKV projection with RoPE
+and the KV-cache append in its epilogue, split-KV attention, the o
+projection with the residual add in its epilogue, RMSNorm, the gate/up
+projection with SwiGLU in its epilogue, and the down projection with the
+residual add. Token ids, positions and lengths live on the device and greedy
+sampling is an on-device argmax, so a decode step has no host round trip and
+can be captured as one CUDA graph.
+
+KV cache layout: per layer k and v (B, n_kv_head, max_seq, head_dim), the
+reference's (n_kv_head, max_seq, d_k) (model.py:219-225) with a batch axis.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from triton_llm import gpu, _lib
+from triton_llm.kernels import gqa_decode, gqa_rows, DecodeWorkspace
+from triton_llm.kernels.linear import (Linear, LinearWorkspace, linear, qkv_rows,
+                                       swiglu_rows)
+from triton_llm.kernels.rope import precompute_cos_sin
+from triton_llm.kernels.embedding import embedding_dev
+
+
+def _dtype_of(config, dtype):
+    d = dtype or getattr(config, "torch_dtype", "float32") or "float32"
+    return "bfloat16" if d in ("bfloat16", "bf16") else "float32"
+
+
+class LlamaWeights:
+    """All weights of a Llama-family model on the device, in kernel layout."""
+
+    def __init__(self, config, weights=None, dtype=None, seed=None, std=0.02,
+                 max_pos=None):
+        c = self.config = config
+        self.dtype = _dtype_of(config, dtype)
+        self.bf16 = self.dtype == "bfloat16"
+        self.H = c.num_attention_heads
+        self.Hkv = c.num_key_value_heads
+        self.n = c.hidden_size
+        self.D = self.n // self.H
+        self.F = c.intermediate_size
+        self.V = c.vocab_size
+        self.L = c.num_hidden_layers
+        self.eps = float(c.rms_norm_eps)
+        if self.H % self.Hkv:
+            raise ValueError(f"n_head ({self.H}) must be divisible by n_kv_head ({self.Hkv})")
+        self.max_pos = int(max_pos or c.max_position_embeddings)
+        cos, sin = precompute_cos_sin(self.max_pos, self.D, c.rope_theta)
+        self.cos, self.sin = gpu.to_device(cos), gpu.to_device(sin)
+        if weights is not None:
+            self._from_state_dict(weights)
+        else:
+            self._random(seed if seed is not None else 0, std)
+
+    # -- from a HF-style state dict (numpy arrays, (out, in) Linear layout)
+    def _from_state_dict(self, w):
+        dt = self.dtype
+        f32 = lambda a: gpu.to_device(np.ascontiguousarray(a, np.float32))  # noqa: E731
+        self.layers = []
+        for i in range(self.L):
+            p = f"model.layers.{i}."
+            wqkv, _ = qkv_rows(w[p + "self_attn.q_proj.weight"], w[p + "self_attn.k_proj.weight"],
+                               w[p + "self_attn.v_proj.weight"], self.D)
+            self.layers.append(dict(
+                qkv=Linear(wqkv, dt),
+                o=Linear(w[p + "self_attn.o_proj.weight"], dt),
+                gu=Linear(swiglu_rows(np.asarray(w[p + "mlp.gate_proj.weight"], np.float32),
+                                      np.asarray(w[p + "mlp.up_proj.weight"], np.float32)), dt),
+                down=Linear(w[p + "mlp.down_proj.weight"], dt),
+                ln1=f32(w[p + "input_layernorm.weight"]),
+                ln2=f32(w[p + "post_attention_layernorm.weight"]),
+            ))
+        self.norm = f32(w["model.norm.weight"])
+        emb = w["model.embed_tokens.weight"]
+        self.lm_head = Linear(w["lm_head.weight"] if "lm_head.weight" in w else emb, dt)
+        if "lm_head.weight" in w:
+            self.embed = Linear(emb, dt).w
+        else:
+            if not getattr(self.config, "tie_word_embeddings", True):
+                raise KeyError("lm_head.weight is missing from weights and "
+                               "tie_word_embeddings is False")
+            self.embed = self.lm_head.w        # tied: one device copy
+
+    # -- random-init N(0, std) on the device (benchmarks)
+    def _random(self, seed, std):
+        dt = _lib.BF16 if self.bf16 else _lib.F32
+        counter = [seed * 1000003]
+
+        def rnd(shape, s=std):
+            t = gpu.allocate(shape, "bfloat16" if self.bf16 else np.float32)
+            counter[0] += 1
+            _lib.call("tllm_fill_random", t.ptr, dt, int(np.prod(shape)),
+                      counter[0], float(s), None)
+            return t
+
+        def lin(N, K):
+            obj = Linear.__new__(Linear)
+            obj.N, obj.K, obj.bf16, obj.b = N, K, self.bf16, None
+            obj.w = rnd((N, K))
+            return obj
+
+        def norm_w():
+            t = gpu.allocate((self.n,), np.float32)
+            counter[0] += 1
+            _lib.call("tllm_fill_random", t.ptr, _lib.F32, self.n, counter[0],
+                      float(std), None)
+            return t
+
+        n, D = self.n, self.D
+        self.layers = []
+        for _ in range(self.L):
+            self.layers.append(dict(qkv=lin((self.H + 2 * self.Hkv) * D, n),
+                                    o=lin(n, self.H * D), gu=lin(2 * self.F, n),
+                                    down=lin(n, self.F), ln1=norm_w(), ln2=norm_w()))
+        self.norm = norm_w()
+        self.lm_head = lin(self.V, n)
+        self.embed = self.lm_head.w
+
+    def linear_shapes(self, M):
+        n, D = self.n, self.D
+        return [(M, (self.H + 2 * self.Hkv) * D, n), (M, n, self.H * D),
+                (M, 2 * self.F, n), (M, n, self.F), (M, self.V, n)]
+
+    def nbytes(self):
+        per = 2 if self.bf16 else 4
+        n, D = self.n, self.D
+        layer = ((self.H + 2 * self.Hkv) * D * n + n * self.H * D + 2 * self.F * n
+                 + n * self.F) * per + 2 * n * 4
+        return self.L * layer + self.V * n * per + n * 4
+
+
+class LlamaSession:
+    """KV caches and step buffers for ``batch`` sequences of a model."""
+
+    def __init__(self, wts: LlamaWeights, batch: int, max_seq: int,
+                 max_prefill_rows: int = 0, attn_budget_bytes: int = 256 << 20,
+                 kv_dtype: str | None = None):
+        self.w = wts
+        self.B = int(batch)
+        self.S = int(max_seq)
+        if self.S > wts.max_pos:
+            raise ValueError(f"max_seq ({self.S}) exceeds the RoPE table "
+                             f"({wts.max_pos} positions)")
+        B, S, Hkv, D = self.B, self.S, wts.Hkv, wts.D
+        # KV cache precision follows the weights unless given ("float32" keeps
+        # the reference's fp32 cache under bf16 weights)
+        self.kv_bf16 = wts.bf16 if kv_dtype is None else kv_dtype in ("bfloat16", "bf16")
+        kvdt = "bfloat16" if self.kv_bf16 else np.float32
+        per_layer = 2 * B * Hkv * S * D
+        self.kv_arena = gpu.zeros((wts.L * per_layer,), kvdt)
+        esz = 2 if self.kv_bf16 else 4
+        self.kv = []
+        for i in range(wts.L):
+            k = gpu.sub_view(self.kv_arena, (2 * i) * (per_layer // 2) * esz,
+                             (B, Hkv, S, D))
+            v = gpu.sub_view(self.kv_arena, (2 * i + 1) * (per_layer // 2) * esz,
+                             (B, Hkv, S, D))
+            self.kv.append((k, v))
+        self.pos = gpu.zeros((B,), np.int32)     # next position of each sequence
+        self.lens = gpu.zeros((B,), np.int32)    # keys attended in the current step
+        self.ids = gpu.zeros((B,), np.int32)     # tokens fed to the next step
+        self.row_seq = gpu.to_device(np.arange(B, dtype=np.int32))
+        self._buffers(B)
+        self.attn_ws = DecodeWorkspace(B, wts.H, Hkv, D, S,
+                                       _lib.BF16 if self.kv_bf16 else _lib.F32)
+        self.lin_ws = LinearWorkspace(wts.linear_shapes(B))
+        self._prefill_rows = 0
+        if max_prefill_rows:
+            self._prefill_buffers(max_prefill_rows, attn_budget_bytes)
+        self.graph = None
+
+    def _buffers(self, M):
+        w = self.w
+        f = lambda *s: gpu.allocate(s, np.float32)  # noqa: E731
+        self.h, self.x = f(M, w.n), f(M, w.n)
+        self.q, self.attn = f(M, w.H, w.D), f(M, w.H * w.D)
+        self.act, self.logits = f(M, w.F), f(M, w.V)
+
+    def _prefill_buffers(self, M, attn_budget):
+        w = self.w
+        f = lambda *s: gpu.allocate(s, np.float32)  # noqa: E731
+        self.p_h, self.p_x = f(M, w.n), f(M, w.n)
+        self.p_q, self.p_attn = f(M, w.H, w.D), f(M, w.H * w.D)
+        self.p_act = f(M, w.F)
+        self.p_ids = gpu.allocate((M,), np.int32)
+        self.p_seq = gpu.allocate((M,), np.int32)
+        self.p_pos = gpu.allocate((M,), np.int32)
+        self.p_len = gpu.allocate((M,), np.int32)
+        self.p_last = gpu.allocate((self.B,), np.int32)
+        self.p_lin_ws = LinearWorkspace(w.linear_shapes(M)[:4])
+        ws = DecodeWorkspace.__new__(DecodeWorkspace)
+        ws.partial_bytes = int(attn_budget)
+        ws.partial = gpu.allocate((max(attn_budget // 4, 1),), np.float32)
+        ws.counters = gpu.zeros((M * w.H,), np.int32)
+        self.p_attn_ws = ws
+        self._prefill_rows = M
+
+    # ------------------------------------------------------------------
+    def _layer(self, i, M, h, x, q, attn, act, row_seq, row_pos, lens, ws,
+               decode, attn_ws, row_len=None, max_len=None):
+        w = self.w
+        L = w.layers[i]
+        k, v = self.kv[i]
+        _lib.call("tllm_rmsnorm", h.ptr, L["ln1"].ptr, x.ptr, M, w.n, w.eps, None)
+        linear(x, L["qkv"], op=_lib.EPI_QKV, ws=ws, M=M, qkv=dict(
+            cos=w.cos, sin=w.sin, row_seq=row_seq, row_pos=row_pos, q_out=q,
+            k_cache=k, v_cache=v, n_head=w.H, n_kv_head=w.Hkv, head_dim=w.D,
+            lens_out=lens if decode else None))
+        if decode:
+            gqa_decode(q, k, v, lens, gpu.view(attn, (M, w.H, w.D)), max_len=self.S,
+                       workspace=attn_ws)
+        else:
+            gqa_rows(q, k, v, row_seq, row_len, attn, M, w.H, w.H * w.D, w.D,
+                     w.H * w.D, w.D, max_len or self.S, workspace=attn_ws)
+        linear(attn, L["o"], out_dev=h, op=_lib.EPI_RESID, resid_dev=h, ws=ws, M=M)
+        _lib.call("tllm_rmsnorm", h.ptr, L["ln2"].ptr, x.ptr, M, w.n, w.eps, None)
+        linear(x, L["gu"], out_dev=act, op=_lib.EPI_SWIGLU, ws=ws, M=M)
+        linear(act, L["down"], out_dev=h, op=_lib.EPI_RESID, resid_dev=h, ws=ws, M=M)
+
+    def prefill(self, prompts, all_logits=False):
+        """Run the prompts of sequences 0..len(prompts)-1 through the model.
+
+        Every sequence restarts at position 0. Returns the logits of the last
+        prompt token of each sequence (host, (n, V)), or of every prompt
+        token when ``all_logits`` (host, (sum(len), V)). Afterwards
+        ``ids`` holds the greedy next token of each sequence and ``pos``
+        the prompt lengths, ready for ``decode_step``.
+        """
+        w = self.w
+        prompts = [np.asarray(p, np.int32).reshape(-1) for p in prompts]
+        nseq = len(prompts)
+        if nseq > self.B:
+            raise ValueError(f"{nseq} prompts for a batch of {self.B}")
+        lens = np.array([len(p) for p in prompts], np.int64)
+        if (lens <= 0).any():
+            raise ValueError("every prompt needs at least one token")
+        if lens.max() > self.S:
+            raise ValueError(f"prompt of {lens.max()} tokens exceeds max_seq {self.S}")
+        M = int(lens.sum())
+        if M > self._prefill_rows:
+            self._prefill_buffers(M, 256 << 20)
+        ids = np.concatenate(prompts)
+        seq = np.repeat(np.arange(nseq, dtype=np.int32), lens)
+        pos = np.concatenate([np.arange(n, dtype=np.int32) for n in lens])
+        self.p_ids.from_numpy(np.pad(ids, (0, self._prefill_rows - M)))
+        self.p_seq.from_numpy(np.pad(seq, (0, self._prefill_rows - M)))
+        self.p_pos.from_numpy(np.pad(pos, (0, self._prefill_rows - M)))
+        self.p_len.from_numpy(np.pad(pos + 1, (0, self._prefill_rows - M)))
+        h, x = self.p_h, self.p_x
+        embedding_dev(gpu.sub_view(self.p_ids, 0, (M,)), w.embed, h)
+        for i in range(w.L):
+            self._layer(i, M, h, x, self.p_q, self.p_attn, self.p_act, self.p_seq,
+                        self.p_pos, None, self.p_lin_ws, False, self.p_attn_ws,
+                        row_len=self.p_len, max_len=int(lens.max()))
+        if all_logits:
+            logits = gpu.allocate((M, w.V), np.float32)
+            _lib.call("tllm_rmsnorm", h.ptr, w.norm.ptr, x.ptr, M, w.n, w.eps, None)
+            linear(x, w.lm_head, out_dev=logits, ws=self.p_lin_ws, M=M)
+            host = logits.to_numpy()
+            last_rows = np.cumsum(lens) - 1
+            next_ids = np.argmax(host[last_rows], axis=-1).astype(np.int32)
+        else:
+            # last prompt row of every sequence -> the decode buffers
+            last_rows = (np.cumsum(lens) - 1).astype(np.int32)
+            for b, r in enumerate(last_rows):
+                gpu.copy_d2d(gpu.sub_view(self.h, b * w.n * 4, (w.n,)),
+                             gpu.sub_view(h, int(r) * w.n * 4, (w.n,)))
+            _lib.call("tllm_rmsnorm", self.h.ptr, w.norm.ptr, self.x.ptr, nseq, w.n,
+                      w.eps, None)
+            linear(self.x, w.lm_head, out_dev=self.logits, ws=self.lin_ws, M=nseq)
+            host = self.logits.to_numpy()[:nseq]
+            next_ids = np.argmax(host, axis=-1).astype(np.int32)
+        ids_full = np.zeros(self.B, np.int32)
+        ids_full[:nseq] = next_ids
+        pos_full = np.zeros(self.B, np.int32)
+        pos_full[:nseq] = lens
+        self.ids.from_numpy(ids_full)
+        self.pos.from_numpy(pos_full)
+        self.lens.from_numpy(pos_full)
+        return host
+
+    def set_state(self, pos: np.ndarray, ids: np.ndarray):
+        """Set positions (= cached lengths) and next tokens directly."""
+        self.pos.from_numpy(np.asarray(pos, np.int32))
+        self.lens.from_numpy(np.asarray(pos, np.int32))
+        self.ids.from_numpy(np.asarray(ids, np.int32))
+
+    def decode_step(self, sample=True):
+        """One greedy decode step for all B sequences, device only.
+
+        Reads ``ids`` / ``pos``; leaves the step's logits in ``self.logits``
+        and (sample=True) the argmax in ``ids`` with ``pos`` advanced.
+        Returns the number of kernel launches.
+        """
+        w = self.w
+        B = self.B
+        embedding_dev(self.ids, w.embed, self.h)
+        for i in range(w.L):
+            self._layer(i, B, self.h, self.x, self.q, self.attn, self.act,
+                        self.row_seq, self.pos, self.lens, self.lin_ws, True,
+                        self.attn_ws)
+        _lib.call("tllm_rmsnorm", self.h.ptr, w.norm.ptr, self.x.ptr, B, w.n, w.eps, None)
+        linear(self.x, w.lm_head, out_dev=self.logits, ws=self.lin_ws, M=B)
+        n = 1 + 7 * w.L + 2
+        if sample:
+            _lib.call("tllm_argmax", self.logits.ptr, B, w.V, w.V, self.ids.ptr,
+                      self.pos.ptr, None)
+            n += 1
+        return n
+
+    def capture(self):
+        """Capture one greedy decode step as a CUDA graph (self.graph)."""
+        g = gpu.Graph()
+        with g:
+            self.decode_step(True)
+        self.graph = g
+        return g
+
+    def step(self):
+        """Run one decode step (the captured graph when there is one)."""
+        if self.graph is not None:
+            self.graph.launch()
+        else:
+            self.decode_step(True)
+
+    def kv_bytes_per_step(self, lens: np.ndarray) -> int:
+        w = self.w
+        return int(2 * w.L * w.Hkv * w.D * (2 if self.kv_bf16 else 4) * int(np.sum(lens)))

@@ -38,6 +38,7 @@ I32 = 2
 _vp = ctypes.c_void_p
 _i = ctypes.c_int
 _sz = ctypes.c_size_t
+_l = ctypes.c_long
 _f = ctypes.c_float
 _pvp = ctypes.POINTER(ctypes.c_void_p)
 _pi = ctypes.POINTER(ctypes.c_int)
@@ -85,7 +86,27 @@ SIGNATURES: dict[str, list] = {
                         _f, _vp, _sz, _vp, _vp],
     "tllm_gqa_decode_noalloc": [_vp, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _i,
                                 _i, _i, _f, _vp],
+    "tllm_gqa_rows": [_vp, _l, _l, _vp, _vp, _i, _vp, _vp, _vp, _l, _l, _i, _i,
+                      _i, _i, _i, _i, _i, _f, _vp, _sz, _vp, _vp],
+    # projections
+    "tllm_linear_workspace": [_i, _i, _i, _psz, _psz],
+    "tllm_linear": [_vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _i, _vp, _vp, _vp,
+                    _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _sz,
+                    _vp, _vp],
+    "tllm_gemm_f32": [_vp, _vp, _vp, _i, _i, _i, _vp],
+    # rows / elementwise
+    "tllm_rmsnorm": [_vp, _vp, _vp, _i, _i, _f, _vp],
+    "tllm_layernorm": [_vp, _vp, _vp, _vp, _i, _i, _f, _vp],
+    "tllm_embedding": [_vp, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _vp],
+    "tllm_argmax": [_vp, _i, _i, _i, _vp, _vp, _vp],
+    "tllm_rope": [_vp, _vp, _vp, _i, _i, _i, _i, _vp],
+    "tllm_elementwise": [_i, _vp, _vp, _vp, _l, _vp],
+    "tllm_softmax": [_vp, _vp, _i, _i, _vp],
+    "tllm_fill_random": [_vp, _i, _l, ctypes.c_uint64, _f, _vp],
 }
+
+EPI_STORE, EPI_RESID, EPI_GELU, EPI_SWIGLU, EPI_QKV = 0, 1, 2, 3, 4
+EL_SWIGLU, EL_ADD, EL_GELU = 0, 1, 2
 
 _lib = None
 _lock = threading.Lock()

@@ -1,0 +1,108 @@
+"""Projection weights and the fused GEMM (tllm_linear).
+
+``Linear`` holds one projection on the device in the layout the kernels
+read: HF (out, in) rows, bf16 or fp32, with the row order the epilogue
+expects -- gate/up rows interleaved in blocks of 8 for SwiGLU, and each
+q/k/v head stored as (8b..8b+7, D/2+8b..D/2+8b+7) blocks so the RoPE pair
+(d, d + D/2) of the reference's rotate-half (triton_llm/kernels/rope.py:
+49-66) lands in one thread. ``LinearWorkspace`` holds the split-K scratch
+shared by every projection of a model.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from triton_llm import gpu, _lib
+
+
+def swiglu_rows(gate: np.ndarray, up: np.ndarray) -> np.ndarray:
+    """(F, K) gate and up -> (2F, K) interleaved in blocks of 8 rows."""
+    F, K = gate.shape
+    if F % 8:
+        raise ValueError(f"intermediate size {F} must be a multiple of 8")
+    g = gate.reshape(F // 8, 8, K)
+    u = up.reshape(F // 8, 8, K)
+    return np.ascontiguousarray(np.stack([g, u], axis=1).reshape(2 * F, K))
+
+
+def head_row_order(D: int) -> np.ndarray:
+    """Permutation of one head's D rows: (8b..8b+7, D/2+8b..D/2+8b+7)."""
+    if D % 16:
+        raise ValueError(f"head_dim {D} must be a multiple of 16")
+    order = []
+    for b in range(D // 16):
+        order += list(range(8 * b, 8 * b + 8))
+        order += list(range(D // 2 + 8 * b, D // 2 + 8 * b + 8))
+    return np.array(order, np.int64)
+
+
+def qkv_rows(wq, wk, wv, D, bq=None, bk=None, bv=None):
+    """Stack q, k, v heads (HF (out, in)) with the per-head RoPE row order."""
+    w = np.concatenate([wq, wk, wv], axis=0)
+    n_heads = w.shape[0] // D
+    perm = (np.arange(n_heads)[:, None] * D + head_row_order(D)[None, :]).reshape(-1)
+    w = np.ascontiguousarray(w[perm])
+    b = None
+    if bq is not None:
+        b = np.ascontiguousarray(np.concatenate([bq, bk, bv])[perm], np.float32)
+    return w, b
+
+
+class Linear:
+    """A projection y = x W^T (+ b) with W (N, K) on the device."""
+
+    def __init__(self, w: np.ndarray, dtype: str = "bfloat16", bias=None):
+        w = np.ascontiguousarray(w, np.float32)
+        self.N, self.K = w.shape
+        self.bf16 = dtype in ("bfloat16", "bf16")
+        self.w = gpu.to_device_bf16(w) if self.bf16 else gpu.to_device(w)
+        self.b = gpu.to_device(np.ascontiguousarray(bias, np.float32)) if bias is not None else None
+
+    @property
+    def dtype(self):
+        return _lib.BF16 if self.bf16 else _lib.F32
+
+
+class LinearWorkspace:
+    """Split-K scratch of tllm_linear, sized for the largest (M, N, K)."""
+
+    def __init__(self, shapes):
+        pb_max, cb_max = 0, 0
+        for (M, N, K) in shapes:
+            pb, cb = ctypes.c_size_t(), ctypes.c_size_t()
+            _lib.call("tllm_linear_workspace", int(M), int(N), int(K),
+                      ctypes.byref(pb), ctypes.byref(cb))
+            pb_max = max(pb_max, pb.value)
+            cb_max = max(cb_max, cb.value)
+        self.partial_bytes = pb_max
+        self.partial = gpu.allocate((max(pb_max // 4, 1),), np.float32)
+        self.counters = gpu.zeros((max(cb_max // 4, 1),), np.int32)
+
+
+def linear(x_dev, lin: Linear, out_dev=None, op=_lib.EPI_STORE, resid_dev=None,
+           ws: LinearWorkspace | None = None, M=None, ld_out=0, qkv=None,
+           stream=None):
+    """Run one projection. ``qkv`` = dict(cos, sin, row_seq, row_pos, q_out,
+    k_cache, v_cache, n_head, n_kv_head, head_dim, lens_out) for op QKV."""
+    M = int(x_dev.shape[0]) if M is None else int(M)
+    K = int(x_dev.shape[-1])
+    if K != lin.K:
+        raise ValueError(f"linear: x has K={K}, weight has K={lin.K}")
+    q = qkv or {}
+    kc = q.get("k_cache")
+    _lib.call(
+        "tllm_linear", x_dev.ptr, lin.w.ptr, lin.dtype, M, lin.N, lin.K, int(op),
+        _lib.ptr(lin.b), _lib.ptr(out_dev), int(ld_out), _lib.ptr(resid_dev),
+        _lib.ptr(q.get("cos")), _lib.ptr(q.get("sin")), _lib.ptr(q.get("row_seq")),
+        _lib.ptr(q.get("row_pos")), _lib.ptr(q.get("q_out")), _lib.ptr(kc),
+        _lib.ptr(q.get("v_cache")),
+        _lib.BF16 if (kc is not None and kc.is_bf16) else _lib.F32,
+        int(kc.shape[2]) if kc is not None else 0, int(q.get("n_head", 0)),
+        int(q.get("n_kv_head", 0)), int(q.get("head_dim", 0)),
+        _lib.ptr(q.get("lens_out")),
+        ws.partial.ptr if ws else None, ws.partial_bytes if ws else 0,
+        ws.counters.ptr if ws else None, stream)
+    return out_dev

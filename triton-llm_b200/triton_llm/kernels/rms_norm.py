@@ -1,0 +1,20 @@
+"""RMSNorm (drop-in for triton_llm/kernels/rms_norm.py:68-115)."""
+
+from __future__ import annotations
+
+from triton_llm import gpu, _lib
+
+
+def rms_norm(x_dev: "gpu.DeviceTensor", w_dev: "gpu.DeviceTensor",
+             out_dev: "gpu.DeviceTensor", eps: float = 1e-5) -> "gpu.DeviceTensor":
+    """y = (x / sqrt(mean(x^2) + eps)) * w over the last dimension."""
+    M, N = x_dev.shape
+    assert tuple(w_dev.shape) == (N,), f"w_dev shape mismatch: expected ({N},), got {w_dev.shape}"
+    assert tuple(out_dev.shape) == (M, N), \
+        f"out_dev shape mismatch: expected ({M},{N}), got {out_dev.shape}"
+    if M == 0:
+        return out_dev
+    if N == 0:
+        raise ValueError("RMSNorm requires the last dimension N > 0")
+    _lib.call("tllm_rmsnorm", x_dev.ptr, w_dev.ptr, out_dev.ptr, M, N, float(eps), None)
+    return out_dev
