@@ -1,30 +1,43 @@
 """Benchmark of the B200 decode hot path.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
-                    [--impl b200|reference]
+                    [--impl b200|reference] [--no-cpu-baseline]
 
 Prints ONE JSON line on rank 0. Under torchrun (N > 1) every rank drives
-its own GPU; ranks meet only at host barriers (gloo) around the timed
-region, and the time reported is the maximum over ranks.
+its own GPU as an independent data-parallel replica; ranks meet only at host
+barriers (gloo) around the timed regions, and every time reported is the
+maximum over ranks.
 
 Workloads:
-  gqa   config 2: split-KV GQA decode attention, 64 ragged sequences
-        (lengths U[128, 2048], seed 1), 9 q / 3 kv heads, head_dim 64, bf16
-        KV cache resident in HBM. One step = one attention launch over the
-        whole batch; "tokens" = sequences decoded. Each rank runs its own
-        batch (weak scaling). Rotating cache copies keep the working set
-        above L2.
+  llama3b  (default) config 4: Llama-3.2-3B architecture, bf16 weights and
+           KV cache, random-init weights N(0, 0.02); per rank a ragged batch
+           of 64 sequences whose cached contexts are uniform in
+           [1024, 8192] (K/V filled N(0, 1)); K greedy decode steps. The
+           64*N lengths come from one seeded stream and are partitioned
+           across ranks balancing total context (triton_llm.shard), so the
+           per-GPU work is fixed as N grows (weak scaling).
+  gqa      config 2: the isolated split-KV GQA decode-attention kernel, 64
+           ragged sequences (U[128, 2048], seed 1), 9 q / 3 kv heads,
+           head_dim 64, bf16 cache; one step = one launch over the batch.
 
-The reference arm (--impl reference) times the reference's math on the
-host cores: the CPU oracle (a numpy restatement of the reference kernels,
-oracle/), on the same workload with every host core, rank 0 only.
+value = decode tokens/s of the whole job (device time of K steps, each step
+one CUDA-graph replay of the whole decode step, inputs resident in HBM).
+e2e   = the same through the serving loop with host token buffers: every step
+copies the batch's token ids from pinned host memory, replays the step and
+reads the sampled ids back.
+roofline = the dominant kernel (split-KV attention), timed in an
+attention-only graph replay of the step's L layer launches on the same cache
+right after the timed region, with its algorithmic bytes per launch.
+
+The reference arm (--impl reference) times the reference's math on the host
+cores: the CPU oracle (oracle/, a numpy restatement of the reference's
+model and kernels) on a bounded sample of the same workload, rank 0 only.
 """
 
 from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import statistics
 import subprocess
@@ -61,21 +74,19 @@ class Ranks:
         if self.pg:
             self.pg.barrier()
 
-    def max(self, x: float) -> float:
+    def _reduce(self, x: float, op) -> float:
         if not self.pg:
             return x
         import torch
         t = torch.tensor([x], dtype=torch.float64)
-        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        self.pg.all_reduce(t, op=op)
         return float(t.item())
 
+    def max(self, x: float) -> float:
+        return self._reduce(x, self.pg.ReduceOp.MAX) if self.pg else x
+
     def sum(self, x: float) -> float:
-        if not self.pg:
-            return x
-        import torch
-        t = torch.tensor([x], dtype=torch.float64)
-        self.pg.all_reduce(t, op=self.pg.ReduceOp.SUM)
-        return float(t.item())
+        return self._reduce(x, self.pg.ReduceOp.SUM) if self.pg else x
 
     def close(self):
         if self.pg:
@@ -85,7 +96,7 @@ class Ranks:
 
 # ----------------------------------------------------------------- clocks ----
 class ClockSampler:
-    """nvidia-smi sampled every 200 ms during the timed region."""
+    """nvidia-smi sampled every 200 ms during a timed region."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -104,6 +115,7 @@ class ClockSampler:
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
                  "--format=csv,noheader,nounits", "-lms", "200"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
         except Exception:
             self.proc = None
 
@@ -124,13 +136,21 @@ class ClockSampler:
         os.unlink(self.path)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+        sm = [x for x in (num(r[1]) for r in rows) if x is not None]
+        mx = [x for x in (num(r[2]) for r in rows) if x is not None]
+        pw = [x for x in (num(r[3]) for r in rows) if x is not None]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4)
                           if r[5 + i].lower().startswith("active")})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None,
+                "power_w_max": max(pw) if pw else None,
                 "reasons": reasons, "samples": len(rows)}
 
 
@@ -146,8 +166,8 @@ def measured_peaks():
 
 
 def profiled_traffic(key: str):
-    """Per-launch DRAM bytes of the dominant kernel from a committed ncu
-    summary (profiles/traffic.json), or None."""
+    """Per-launch DRAM bytes of a kernel from a committed ncu summary
+    (profiles/traffic.json), or None."""
     p = REPO / "profiles" / "traffic.json"
     if p.exists():
         try:
@@ -158,19 +178,241 @@ def profiled_traffic(key: str):
     return None
 
 
-# ------------------------------------------------------------- workloads ----
+def _time_graph(gpu, graph, reps):
+    """Mean ms of one replay of ``graph`` over ``reps`` replays (events on
+    the library stream, one untimed replay first)."""
+    graph.launch()
+    gpu.device_synchronize()
+    e0, e1 = gpu.Event(), gpu.Event()
+    e0.record()
+    for _ in range(reps):
+        graph.launch()
+    e1.record()
+    gpu.device_synchronize()
+    return e0.elapsed_ms(e1) / reps
+
+
+# -------------------------------------------------------- config 4: Llama ----
+class LlamaDecodeWorkload:
+    """Llama-3.2-3B ragged-batch decode (bf16)."""
+
+    name = "llama3b"
+    scaling = "weak"
+    dtype = "bf16"
+    model = "Llama-3.2-3B-Instruct"
+    per_rank = 64
+    lo, hi = 1024, 8192
+    len_seed = 4
+
+    def __init__(self, ranks, steps, warmup):
+        from triton_llm import shard
+        self.ranks = ranks
+        self.steps, self.warmup = steps, warmup
+        n = ranks.world
+        self.all_lens = shard.ragged_lengths(self.per_rank * n, self.lo, self.hi,
+                                             self.len_seed)
+        self.parts = shard.partition(self.all_lens, n, self.per_rank)
+        self.idx = self.parts[ranks.rank]
+        self.lens = self.all_lens[self.idx].astype(np.int32)
+        self.B = len(self.lens)
+        # room for the warm-up and timed steps after the longest context
+        self.S = ((self.hi + steps + warmup + 2 + 63) // 64) * 64
+
+    def config(self):
+        return {"workload": "cfg4 Llama-3.2-3B ragged-batch greedy decode",
+                "model": self.model, "layers": 28, "hidden": 3072,
+                "heads": "24 q / 8 kv, head_dim 128", "ffn": 8192, "vocab": 128256,
+                "batch_per_gpu": self.B, "global_batch": self.B * self.ranks.world,
+                "ctx": f"U[{self.lo},{self.hi}] seed {self.len_seed}, "
+                       "partitioned by total context",
+                "sum_ctx_this_rank": int(self.lens.sum()),
+                "weights": "random N(0,0.02) bf16 (seed 0), tied embeddings",
+                "kv_cache": f"bf16 (B, 8, {self.S}, 128) per layer, filled N(0,1)",
+                "parallelism": f"dp{self.ranks.world} (independent replicas, no collective)",
+                "timed": "K steps, each one CUDA-graph replay of the full decode step "
+                         "(embedding, 28 x [rmsnorm, qkv+rope+append, attention, o+resid, "
+                         "rmsnorm, gate/up+swiglu, down+resid], norm, lm_head, argmax)",
+                "l2": "inputs larger than L2: every step reads all weights (6.4 GB) and "
+                      "the whole cached context (~34 GB) once"}
+
+    def setup(self):
+        from triton_llm import gpu, _lib
+        from smollm2_triton import SmolLM2Config
+        from smollm2_triton.engine import LlamaSession, LlamaWeights
+        self.gpu = gpu
+        cfg = SmolLM2Config.from_pretrained(self.model)
+        self.cfg = cfg
+        self.wts = LlamaWeights(cfg, None, "bfloat16", seed=0, std=0.02, max_pos=self.S)
+        self.sess = LlamaSession(self.wts, self.B, self.S)
+        s = self.sess
+        _lib.call("tllm_fill_random", s.kv_arena.ptr, _lib.BF16,
+                  int(np.prod(s.kv_arena.shape)), 1000 + self.ranks.rank, 1.0, None)
+        rng = np.random.default_rng(100 + self.ranks.rank)
+        self.ids0 = rng.integers(0, cfg.vocab_size, self.B).astype(np.int32)
+        self.reset()
+        self.launches_per_step = s.decode_step(True)
+        gpu.device_synchronize()
+        self.reset()
+        # pinned token buffers of the serving loop
+        self.ids_host = gpu.pinned_empty((self.B,), np.int32)
+        self.out_host = gpu.pinned_empty((self.B,), np.int32)
+        self.h2d = self.B * 4
+        self.d2h = self.B * 4
+
+    def reset(self):
+        self.sess.set_state(self.lens, self.ids0)
+
+    def capture(self):
+        self.sess.capture()
+
+    def step(self):
+        self.sess.step()
+
+    def units_per_step(self):
+        return self.B
+
+    def e2e_begin(self):
+        self.reset()
+        self.ids_host[...] = self.ids0
+
+    def step_e2e(self):
+        self.sess.step_host(self.ids_host, self.out_host)
+        self.ids_host[...] = self.out_host
+
+    # ---- dominant kernel: attention, timed alone on the same cache ----
+    def kernel_roofline(self, gpu, peak):
+        from triton_llm.kernels import gqa_rows
+        s, w = self.sess, self.wts
+        g = gpu.Graph()
+        with g:
+            for i in range(w.L):
+                k, v = s.kv[i]
+                gqa_rows(s.q, k, v, s.row_seq, s.lens, s.attn, s.B, w.H, w.H * w.D,
+                         w.D, w.H * w.D, w.D, s.S, workspace=s.attn_ws)
+        ms = _time_graph(gpu, g, 5) / w.L
+        lens = s.lens.to_numpy().astype(np.int64)
+        alg = (2 * w.Hkv * w.D * 2 * int(lens.sum())            # K and V, bf16
+               + 2 * s.B * w.H * w.D * 4 + s.B * 4)             # q, out, lens
+        achieved = alg / (ms / 1e3) / 1e9
+        return {"kernel": "gqa_decode_mma_kernel<128> (+ split merge)",
+                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "bound": "hbm",
+                "algorithmic_bytes_per_launch": alg,
+                "launch_ms": round(ms, 5),
+                "timing": f"attention-only CUDA graph of the {w.L} layer launches of "
+                          "one step on the same cache, 5 replays, CUDA events",
+                "traffic": profiled_traffic("llama3b_attention")}
+
+    def projection_roofline(self, gpu, peak):
+        """All projection GEMMs of one step replayed alone (weights stream)."""
+        from triton_llm import _lib
+        from triton_llm.kernels.linear import linear
+        s, w = self.sess, self.wts
+        B = s.B
+        g = gpu.Graph()
+        alg = 0
+        with g:
+            for i in range(w.L):
+                L = w.layers[i]
+                k, v = s.kv[i]
+                linear(s.x, L["qkv"], op=_lib.EPI_QKV, ws=s.lin_ws, M=B, qkv=dict(
+                    cos=w.cos, sin=w.sin, row_seq=s.row_seq, row_pos=s.pos, q_out=s.q,
+                    k_cache=k, v_cache=v, n_head=w.H, n_kv_head=w.Hkv, head_dim=w.D))
+                linear(s.attn, L["o"], out_dev=s.x, op=_lib.EPI_STORE, ws=s.lin_ws, M=B)
+                linear(s.x, L["gu"], out_dev=s.act, op=_lib.EPI_SWIGLU, ws=s.lin_ws, M=B)
+                linear(s.act, L["down"], out_dev=s.x, op=_lib.EPI_STORE, ws=s.lin_ws, M=B)
+            linear(s.x, w.lm_head, out_dev=s.logits, ws=s.lin_ws, M=B)
+        for (M, N, K) in w.linear_shapes(B)[:4]:
+            alg += w.L * (N * K * 2 + M * K * 4 + M * N * 4)
+        M, N, K = w.linear_shapes(B)[4]
+        alg += N * K * 2 + M * K * 4 + M * N * 4
+        n_launch = 4 * w.L + 1
+        ms = _time_graph(gpu, g, 5)
+        achieved = alg / (ms / 1e3) / 1e9
+        return {"kernels": "linear_tc_kernel (qkv+rope+append, o, gate/up+swiglu, "
+                           "down, lm_head)",
+                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "bound": "hbm",
+                "algorithmic_bytes_per_step": alg, "ms_per_step": round(ms, 4),
+                "launches_per_step": n_launch,
+                "timing": "projection-only CUDA graph of one step, 5 replays"}
+
+    def check(self):
+        """Last layer's attention of the last step for two sequences vs the
+        oracle, on the device's own q and cache."""
+        from oracle import ops
+        gpu, s, w = self.gpu, self.sess, self.wts
+        k, v = s.kv[w.L - 1]
+        n = 2
+        shp = (n, w.Hkv, s.S, w.D)
+        kc = gpu.to_host(gpu.sub_view(k, 0, shp))
+        vc = gpu.to_host(gpu.sub_view(v, 0, shp))
+        q = s.q.to_numpy()[:n]
+        lens = s.lens.to_numpy()[:n]
+        out = gpu.split_to_host(s.attn, n).reshape(n, w.H, w.D)
+        ref = ops.gqa_decode(q, kc, vc, lens)
+        return float(np.abs(out - ref).max())
+
+
+def llama_cpu_sample(ctx: int, steps: int, model="Llama-3.2-3B-Instruct", log=None):
+    """The oracle's decode step for ONE sequence at context ``ctx`` through
+    2 of the model's layers and the lm_head, timed with numpy using every
+    host core, extrapolated to the full depth. Returns (tokens/s, text)."""
+    import inputs
+    from oracle.models import SmolLM2Oracle
+    from smollm2_triton import SmolLM2Config
+    full = SmolLM2Config.from_pretrained(model)
+    shape = inputs.LLAMA3B_2L
+    w = inputs.llama_weights(shape, 0)
+    cfg = SmolLM2Config(**shape.config_kwargs())
+    cfg.max_position_embeddings = ctx + steps + 8
+    o = SmolLM2Oracle(cfg, w, weight_dtype="bfloat16")
+    del w
+    rng = np.random.default_rng(7)
+    o.init_cache(ctx + steps + 8)
+    for c in o.cache:
+        c["k"][:, :ctx] = inputs.bf16_round(rng.standard_normal(c["k"][:, :ctx].shape, dtype=np.float32))
+        c["v"][:, :ctx] = inputs.bf16_round(rng.standard_normal(c["v"][:, :ctx].shape, dtype=np.float32))
+
+    def timed(n):
+        o.cache_len = ctx
+        o.forward_cached(np.array([[1]], np.int32))       # warm
+        ts = []
+        for i in range(n):
+            o.cache_len = ctx
+            t = time.perf_counter()
+            o.forward_cached(np.array([[i % 1000]], np.int32))
+            ts.append(time.perf_counter() - t)
+        return statistics.median(ts)
+
+    t2 = timed(steps)
+    layers = o.layers
+    o.layers = layers[:1]
+    t1 = timed(max(2, min(steps, 6)))
+    o.layers = layers
+    t_layer = max(t2 - t1, 1e-6)
+    t_head = max(t1 - t_layer, 0.0)
+    per_token = t_head + full.num_hidden_layers * t_layer
+    text = (f"oracle decode step, 1 sequence at ctx {ctx}, 2 of {full.num_hidden_layers} "
+            f"layers + lm_head timed ({steps} steps; layer {t_layer * 1e3:.1f} ms, "
+            f"head {t_head * 1e3:.1f} ms), extrapolated to {full.num_hidden_layers} layers; "
+            "batch 1 like the reference, numpy restatement (oracle/)")
+    return 1.0 / per_token, text
+
+
+# ------------------------------------------------- config 2: attention only ----
 class GQAWorkload:
     """BASELINE config 2 (isolated GQA decode attention)."""
 
     name = "gqa"
     scaling = "weak"
     dtype = "bf16"
-    kernel = "gqa_decode"
 
-    BENCH_COPIES = 6
+    COPIES = 6
 
-    def __init__(self, copies=BENCH_COPIES):
+    def __init__(self, ranks=None, steps=0, warmup=0, copies=COPIES):
         import inputs
+        self.ranks = ranks
         self.B, self.H, self.Hkv, self.D, self.S = 64, 9, 3, 64, 2048
         self.lens, self.q, ks, vs = inputs.cfg2_inputs()
         self.kc = inputs.pack_cache(ks, self.S)
@@ -179,7 +421,8 @@ class GQAWorkload:
         L = int(self.lens.sum())
         self.kv_bytes = 2 * self.Hkv * L * self.D * 2
         self.bytes_per_step = self.kv_bytes + 2 * self.B * self.H * self.D * 4 + self.B * 4
-        self.units_per_step = self.B
+        self.i = 0
+        self.graphs = None
 
     def config(self):
         return {"workload": "cfg2 isolated GQA decode attention",
@@ -187,9 +430,10 @@ class GQAWorkload:
                 "head_dim": self.D, "kv_lens": "U[128,2048] seed 1",
                 "sum_kv_len": int(self.lens.sum()),
                 "kv_dtype": "bf16", "kv_layout": "(B, n_kv, 2048, d) prealloc",
+                "parallelism": f"dp{self.ranks.world if self.ranks else 1}",
                 "timed": "K launches replayed as one CUDA graph",
-                "l2": f"{self.BENCH_COPIES} rotating cache copies "
-                      f"({self.BENCH_COPIES * self.kv_bytes / 1e6:.0f} MB touched > 126 MB L2)"}
+                "l2": f"{self.COPIES} rotating cache copies "
+                      f"({self.COPIES * self.kv_bytes / 1e6:.0f} MB touched > 126 MB L2)"}
 
     def setup(self):
         from triton_llm import gpu
@@ -209,7 +453,6 @@ class GQAWorkload:
         self.ld = gpu.to_device(self.lens)
         self.od = gpu.allocate(self.q.shape, np.float32)
         self.ws = DecodeWorkspace(self.B, self.H, self.Hkv, self.D, self.S)
-        # pinned host buffers for the end-to-end leg
         self.q_host = gpu.pinned_empty(self.q.shape, np.float32)
         self.q_host[...] = self.q
         self.l_host = gpu.pinned_empty(self.lens.shape, np.int32)
@@ -217,80 +460,366 @@ class GQAWorkload:
         self.o_host = gpu.pinned_empty(self.q.shape, np.float32)
         self.h2d = self.q.nbytes + self.lens.nbytes
         self.d2h = self.q.nbytes
+        self.launches_per_step = 1
 
-    def step(self, i):
+    def _launch(self):
         from triton_llm.kernels import gqa_decode
-        c = i % self.copies
+        c = self.i % self.copies
+        self.i += 1
         gqa_decode(self.qd, self.kd[c], self.vd[c], self.ld, self.od,
                    max_len=self.S, workspace=self.ws)
-        return 1  # kernel launches
 
-    def step_e2e(self, i):
+    def reset(self):
+        self.i = 0
+
+    def capture(self):
+        # one graph per cache copy; a step replays one launch
+        self.i = 0
+        graphs = []
+        for _ in range(self.copies):
+            g = self.gpu.Graph()
+            with g:
+                self._launch()
+            graphs.append(g)
+        self.graphs = graphs
+        self.i = 0
+
+    def step(self):
+        if self.graphs is None:
+            self._launch()
+            return
+        self.graphs[self.i % self.copies].launch()
+        self.i += 1
+
+    def units_per_step(self):
+        return self.B
+
+    def e2e_begin(self):
+        self.i = 0
+
+    def step_e2e(self):
         g = self.gpu
         g.copy_h2d_async(self.qd, self.q_host)
         g.copy_h2d_async(self.ld, self.l_host)
-        n = self.step(i)
+        self.step()
         g.copy_d2h_async(self.o_host, self.od)
         g.stream_synchronize()
-        return n
+
+    def kernel_roofline(self, gpu, peak):
+        ms = None
+        e0, e1 = gpu.Event(), gpu.Event()
+        reps = 30
+        for g in self.graphs:
+            g.launch()
+        gpu.device_synchronize()
+        e0.record()
+        for r in range(reps):
+            self.graphs[r % self.copies].launch()
+        e1.record()
+        gpu.device_synchronize()
+        ms = e0.elapsed_ms(e1) / reps
+        achieved = self.bytes_per_step / (ms / 1e3) / 1e9
+        return {"kernel": "gqa_decode_mma_kernel<64> (+ split merge)",
+                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "bound": "hbm",
+                "algorithmic_bytes_per_launch": self.bytes_per_step,
+                "launch_ms": round(ms, 5),
+                "timing": f"{reps} graph replays over {self.copies} rotating caches",
+                "traffic": profiled_traffic("gqa")}
+
+    def projection_roofline(self, gpu, peak):
+        return None
 
     def check(self):
-        """Result of the last step vs the oracle on the first sequences."""
         from oracle import ops
         out = self.od.to_numpy()
         n = 4
         ref = ops.gqa_decode(self.q[:n], self.kc[:n], self.vc[:n], self.lens[:n])
         return float(np.abs(out[:n] - ref).max())
 
-    # ---- CPU baseline: the oracle (numpy restatement) on a sample ----
-    def cpu_sample(self, nseq):
-        idx = np.arange(nseq) % self.B
-        return idx
-
+    # CPU baseline: the oracle on a sample of sequences
     def cpu_run(self, idx):
         from oracle import ops
         ops.gqa_decode(self.q[idx], self.kc[idx], self.vc[idx], self.lens[idx])
         return len(idx)
 
 
-WORKLOADS = {"gqa": GQAWorkload}
+class _IsolatedWorkload:
+    """An isolated kernel at config-4 geometry on device-filled inputs,
+    rotating over ``copies`` input sets so the working set exceeds L2.
+    A step replays one copy's captured launches."""
 
+    scaling = "weak"
+    dtype = "bf16"
+    copies = 2
+
+    def __init__(self, ranks=None, steps=0, warmup=0):
+        self.ranks = ranks
+        self.i = 0
+        self.graphs = None
+
+    def reset(self):
+        self.i = 0
+
+    def capture(self):
+        graphs = []
+        for c in range(self.copies):
+            g = self.gpu.Graph()
+            with g:
+                self.launch(c)
+            graphs.append(g)
+        self.graphs = graphs
+
+    def step(self):
+        c = self.i % self.copies
+        if self.graphs is None:
+            self.launch(c)
+        else:
+            self.graphs[c].launch()
+        self.i += 1
+
+    def e2e_begin(self):
+        self.i = 0
+
+    def kernel_roofline(self, gpu, peak):
+        reps = 20
+        for g in self.graphs:
+            g.launch()
+        gpu.device_synchronize()
+        e0, e1 = gpu.Event(), gpu.Event()
+        e0.record()
+        for r in range(reps):
+            self.graphs[r % self.copies].launch()
+        e1.record()
+        gpu.device_synchronize()
+        ms = e0.elapsed_ms(e1) / reps / self.launches_per_step
+        achieved = self.bytes_per_launch / (ms / 1e3) / 1e9
+        return {"kernel": self.kernel, "achieved": round(achieved, 1), "peak": peak,
+                "unit": "GB/s", "frac": round(achieved / peak, 4), "bound": "hbm",
+                "algorithmic_bytes_per_launch": self.bytes_per_launch,
+                "launch_ms": round(ms, 5),
+                "timing": f"{reps} graph replays over {self.copies} input copies",
+                "traffic": profiled_traffic(self.name)}
+
+    def projection_roofline(self, gpu, peak):
+        return None
+
+
+class GQALlamaLayerWorkload(_IsolatedWorkload):
+    """Split-KV decode attention alone at config-4 geometry: one layer of
+    64 sequences, contexts U[1024, 8192] (seed 4), 24 q / 8 kv heads,
+    head_dim 128, bf16 cache filled N(0, 1)."""
+
+    name = "gqa_llama3b"
+    kernel = "gqa_decode_mma_kernel<128> (+ split merge)"
+    copies = 1      # one launch reads ~1.2 GB, far above L2
+
+    def setup(self):
+        from triton_llm import gpu, _lib, shard
+        from triton_llm.kernels import DecodeWorkspace
+        self.gpu = gpu
+        self.B, self.H, self.Hkv, self.D, self.S = 64, 24, 8, 128, 8192
+        self.lens = shard.ragged_lengths(self.B, 1024, 8192, 4)
+        self.kd, self.vd = [], []
+        n = self.B * self.Hkv * self.S * self.D
+        for c in range(self.copies):
+            for lst, sd in ((self.kd, 2 * c), (self.vd, 2 * c + 1)):
+                t = gpu.allocate((self.B, self.Hkv, self.S, self.D), gpu.BFLOAT16)
+                _lib.call("tllm_fill_random", t.ptr, _lib.BF16, n, 500 + sd, 1.0, None)
+                lst.append(t)
+        q = np.random.default_rng(3).standard_normal((self.B, self.H, self.D), dtype=np.float32)
+        self.q = q
+        self.qd = gpu.to_device(q)
+        self.ld = gpu.to_device(self.lens)
+        self.od = gpu.allocate(q.shape, np.float32)
+        self.ws = DecodeWorkspace(self.B, self.H, self.Hkv, self.D, self.S)
+        self.bytes_per_launch = (2 * self.Hkv * self.D * 2 * int(self.lens.sum())
+                                 + 2 * q.nbytes + self.lens.nbytes)
+        self.launches_per_step = 1
+        self.q_host = gpu.pinned_empty(q.shape, np.float32)
+        self.q_host[...] = q
+        self.o_host = gpu.pinned_empty(q.shape, np.float32)
+        self.h2d, self.d2h = q.nbytes, q.nbytes
+
+    def launch(self, c):
+        from triton_llm.kernels import gqa_decode
+        gqa_decode(self.qd, self.kd[c], self.vd[c], self.ld, self.od,
+                   max_len=self.S, workspace=self.ws)
+
+    def units_per_step(self):
+        return self.B
+
+    def step_e2e(self):
+        g = self.gpu
+        g.copy_h2d_async(self.qd, self.q_host)
+        self.step()
+        g.copy_d2h_async(self.o_host, self.od)
+        g.stream_synchronize()
+
+    def config(self):
+        return {"workload": "isolated GQA decode attention at cfg4 geometry (one layer)",
+                "batch": self.B, "n_head": self.H, "n_kv_head": self.Hkv,
+                "head_dim": self.D, "ctx": "U[1024,8192] seed 4",
+                "sum_ctx": int(self.lens.sum()), "kv_dtype": "bf16",
+                "timed": "K graph replays of one launch",
+                "l2": f"{self.copies} rotating caches of "
+                      f"{self.bytes_per_launch / 1e9:.2f} GB read per launch"}
+
+    def check(self):
+        from oracle import ops
+        gpu = self.gpu
+        self.launch(0)
+        gpu.device_synchronize()
+        n = 2
+        shp = (n, self.Hkv, self.S, self.D)
+        kc = gpu.to_host(gpu.sub_view(self.kd[0], 0, shp))
+        vc = gpu.to_host(gpu.sub_view(self.vd[0], 0, shp))
+        ref = ops.gqa_decode(self.q[:n], kc, vc, self.lens[:n])
+        return float(np.abs(self.od.to_numpy()[:n] - ref).max())
+
+
+class ProjLlamaLayerWorkload(_IsolatedWorkload):
+    """The projection GEMMs of one config-4 decode layer at M = 64 rows:
+    qkv (5120 x 3072, RoPE + KV append epilogue), o (3072 x 3072, residual),
+    gate/up (16384 x 3072, SwiGLU), down (3072 x 8192, residual); bf16
+    weights N(0, 0.02), fp32 activations."""
+
+    name = "proj_llama3b"
+    kernel = "linear_tc_kernel<64, op>"
+    copies = 4
+
+    def setup(self):
+        from triton_llm import gpu, _lib
+        from triton_llm.kernels.linear import Linear, LinearWorkspace
+        from triton_llm.kernels.rope import precompute_cos_sin
+        self.gpu = gpu
+        B, n, H, Hkv, D, F = 64, 3072, 24, 8, 128, 8192
+        self.B = B
+        self.shapes = [(B, (H + 2 * Hkv) * D, n), (B, n, H * D), (B, 2 * F, n), (B, n, F)]
+
+        def lin(N, K, seed):
+            o = Linear.__new__(Linear)
+            o.N, o.K, o.bf16, o.b = N, K, True, None
+            o.w = gpu.allocate((N, K), gpu.BFLOAT16)
+            _lib.call("tllm_fill_random", o.w.ptr, _lib.BF16, N * K, seed, 0.02, None)
+            return o
+        self.layers = [[lin(N, K, 10 * c + j) for j, (_, N, K) in enumerate(self.shapes)]
+                       for c in range(self.copies)]
+        # projection inputs in the tensor-core operand format (bf16 planes)
+        self.x, self.attn, self.act = (gpu.split_empty(B, n), gpu.split_empty(B, H * D),
+                                       gpu.split_empty(B, F))
+        self.h = gpu.allocate((B, n), np.float32)
+        _lib.call("tllm_fill_random", self.h.ptr, _lib.F32, B * n, 2, 1.0, None)
+        for t, sd in ((self.x, 1), (self.attn, 3), (self.act, 4)):
+            src = gpu.allocate((t.shape[1], t.shape[2]), np.float32)
+            _lib.call("tllm_fill_random", src.ptr, _lib.F32, int(np.prod(src.shape)), sd,
+                      1.0, None)
+            _lib.call("tllm_split_bf16", src.ptr, t.ptr, t.shape[1], t.shape[2],
+                      t.shape[1], None)
+        self.q = gpu.allocate((B, H, D), np.float32)
+        self.kc = gpu.zeros((B, Hkv, 64, D), gpu.BFLOAT16)
+        self.vc = gpu.zeros((B, Hkv, 64, D), gpu.BFLOAT16)
+        cos, sin = precompute_cos_sin(64, D, 500000.0)
+        self.cos, self.sin = gpu.to_device(cos), gpu.to_device(sin)
+        self.row_seq = gpu.to_device(np.arange(B, dtype=np.int32))
+        self.pos = gpu.to_device(np.full(B, 7, np.int32))
+        self.H, self.Hkv, self.D = H, Hkv, D
+        self.ws = LinearWorkspace(self.shapes)
+        self.bytes_per_launch = sum(N * K * 2 + M * K * 4 + M * N * 4
+                                    for (M, N, K) in self.shapes) // 4
+        self.launches_per_step = 4
+        self.x_host = gpu.pinned_empty(self.x.shape, np.uint16)
+        self.x_host[...] = self.x.to_numpy()
+        self.h_host = gpu.pinned_empty((B, n), np.float32)
+        self.h2d, self.d2h = self.x.nbytes, B * n * 4
+
+    def launch(self, c):
+        from triton_llm import _lib
+        from triton_llm.kernels.linear import linear
+        qkv, o, gu, down = self.layers[c]
+        B = self.B
+        linear(self.x, qkv, op=_lib.EPI_QKV, ws=self.ws, M=B, qkv=dict(
+            cos=self.cos, sin=self.sin, row_seq=self.row_seq, row_pos=self.pos,
+            q_out=self.q, k_cache=self.kc, v_cache=self.vc, n_head=self.H,
+            n_kv_head=self.Hkv, head_dim=self.D))
+        linear(self.attn, o, out_dev=self.h, op=_lib.EPI_RESID, resid_dev=self.h,
+               ws=self.ws, M=B)
+        linear(self.x, gu, out_dev=self.act, op=_lib.EPI_SWIGLU, ws=self.ws, M=B)
+        linear(self.act, down, out_dev=self.h, op=_lib.EPI_RESID, resid_dev=self.h,
+               ws=self.ws, M=B)
+
+    def units_per_step(self):
+        return self.B
+
+    def step_e2e(self):
+        g = self.gpu
+        g.copy_h2d_async(self.x, self.x_host)
+        self.step()
+        g.copy_d2h_async(self.h_host, self.h)
+        g.stream_synchronize()
+
+    def config(self):
+        return {"workload": "isolated projection GEMMs of one cfg4 decode layer",
+                "rows": self.B, "shapes_MNK": self.shapes,
+                "weights": "bf16 N(0,0.02)",
+                "activations": "fp32 values as bf16 hi/lo planes (TLLM_SPLIT)",
+                "timed": "K graph replays of the 4 launches",
+                "l2": f"{self.copies} rotating weight sets of 201 MB"}
+
+    def check(self):
+        """The gate/up + SwiGLU projection of copy 0 vs numpy in fp64."""
+        from oracle import ops
+        gpu = self.gpu
+        self.launch(0)
+        gpu.device_synchronize()
+        gu = self.layers[0][2]
+        w = gpu.to_host(gu.w)[:64].astype(np.float64)     # first 4 blocks of 16 rows
+        x = gpu.split_to_host(self.x).astype(np.float64)
+        y = x @ w.T                                        # (B, 64) interleaved
+        g = np.concatenate([y[:, 16 * b:16 * b + 8] for b in range(4)], axis=1)
+        u = np.concatenate([y[:, 16 * b + 8:16 * b + 16] for b in range(4)], axis=1)
+        ref = ops.swiglu(g.astype(np.float32), u.astype(np.float32))
+        return float(np.abs(gpu.split_to_host(self.act)[:, :32] - ref).max())
+
+
+WORKLOADS = {"llama3b": LlamaDecodeWorkload, "gqa": GQAWorkload,
+             "gqa_llama3b": GQALlamaLayerWorkload, "proj_llama3b": ProjLlamaLayerWorkload}
 
 # ----------------------------------------------------------- CPU baseline ----
 _worker_wl: dict = {}
 
 
-def _make_cpu_workload(name):
-    return GQAWorkload(copies=0) if name == "gqa" else WORKLOADS[name]()
-
-
-def _cpu_worker(args):
-    """Pool worker: run the oracle on a list of sample indices."""
-    name, idx = args
-    if name not in _worker_wl:
-        _worker_wl[name] = _make_cpu_workload(name)
-    wl = _worker_wl[name]
+def _gqa_worker(idx):
+    if "gqa" not in _worker_wl:
+        _worker_wl["gqa"] = GQAWorkload(copies=0)
+    wl = _worker_wl["gqa"]
     t = time.perf_counter()
     n = wl.cpu_run(np.asarray(idx, dtype=np.int64))
     return n, time.perf_counter() - t
 
 
-def cpu_baseline(name, cores, pool, budget_s=15.0):
-    """Time the oracle (numpy restatement of the reference) on a bounded
-    sample spread over `cores` worker processes. Returns (units/s, text)."""
-    wl = _make_cpu_workload(name)
-    # warm every worker (input generation) and calibrate one unit
-    warm = pool.map(_cpu_worker, [(name, [0])] * cores)
+def gqa_cpu_baseline(cores, pool, budget_s=15.0):
+    """The oracle's attention on a bounded sample of the 64 sequences spread
+    over ``cores`` spawned worker processes."""
+    warm = pool.map(_gqa_worker, [[0]] * cores)
     per = max(min(r[1] for r in warm), 1e-4)
-    per_worker = max(1, int(budget_s / per))
-    nseq = min(per_worker * cores, 8 * wl.B)
-    idx = wl.cpu_sample(nseq)
+    nseq = min(max(1, int(budget_s / per)) * cores, 8 * 64)
+    idx = np.arange(nseq) % 64
     chunks = [idx[i::cores].tolist() for i in range(cores)]
     t = time.perf_counter()
-    res = pool.map(_cpu_worker, [(name, c) for c in chunks if c])
+    res = pool.map(_gqa_worker, [c for c in chunks if c])
     dt = time.perf_counter() - t
     done = sum(r[0] for r in res)
-    return done / dt, f"oracle on {done} sequences over {cores} processes ({dt:.1f} s)"
+    return done / dt, (f"oracle attention on {done} sequences over {cores} processes "
+                       f"({dt:.1f} s); numpy restatement of the reference kernel (oracle/)")
+
+
+def cpu_baseline(name, cores, steps, pool=None, ctx=None):
+    if name == "gqa":
+        return gqa_cpu_baseline(cores, pool)
+    if name == "llama3b":
+        return llama_cpu_sample(int(ctx), steps)
+    return None
 
 
 # ------------------------------------------------------------------ main ----
@@ -298,34 +827,32 @@ def run_b200(args, ranks):
     from triton_llm import gpu
     gpu.set_device(ranks.local)
     gpu.device_error(reset=True)
-    wl = WORKLOADS[args.workload]()
+    wl = WORKLOADS[args.workload](ranks, args.steps, args.warmup)
     wl.setup()
     gpu.device_synchronize()
 
-    # warm-up
-    for i in range(args.warmup):
-        wl.step(i)
+    # warm-up (eager), then capture the step as a CUDA graph
+    wl.reset()
+    for _ in range(args.warmup):
+        wl.step()
+    gpu.device_synchronize()
+    wl.capture()
+    wl.reset()
+    for _ in range(args.warmup):
+        wl.step()
+    gpu.device_synchronize()
+    wl.reset()
     gpu.device_synchronize()
 
-    # The K timed steps are captured once as a CUDA graph (the decode loop
-    # of a server is replayed the same way), so host launch cost stays off
-    # the device timeline; the graph is replayed once untimed first.
-    launches = 0
-    graph = gpu.Graph()
-    with graph:
-        for i in range(args.steps):
-            launches += wl.step(args.warmup + i)
-    graph.launch()
-    gpu.device_synchronize()
-
-    # timed region (device events on the library stream), clocks sampled
+    # timed region: K graph replays between device events, clocks sampled
     clocks = ClockSampler(ranks.local)
     clocks.start()
     ranks.barrier()
     gpu.device_synchronize()
     e0, e1 = gpu.Event(), gpu.Event()
     e0.record()
-    graph.launch()
+    for _ in range(args.steps):
+        wl.step()
     e1.record()
     gpu.device_synchronize()
     ranks.barrier()
@@ -333,59 +860,100 @@ def run_b200(args, ranks):
     clk = clocks.stop()
     ms_max = ranks.max(ms)
 
-    # end-to-end leg: host buffers, copies inside the timed region
-    for i in range(2):
-        wl.step_e2e(i)
+    # end-to-end: host token buffers, copies inside the timed region
+    wl.e2e_begin()
+    for _ in range(2):
+        wl.step_e2e()
+    wl.e2e_begin()
     ranks.barrier()
     gpu.device_synchronize()
     t0, t1 = gpu.Event(), gpu.Event()
     t0.record()
-    for i in range(args.steps):
-        wl.step_e2e(i)
+    for _ in range(args.steps):
+        wl.step_e2e()
     t1.record()
     gpu.device_synchronize()
     ranks.barrier()
     e2e_ms = ranks.max(t0.elapsed_ms(t1))
 
+    peak, peak_kind = measured_peaks()
+    roof = wl.kernel_roofline(gpu, peak)
+    proj = wl.projection_roofline(gpu, peak)
+    roof["peak_source"] = ("MEASURED_PEAKS.json hbm_gbs (of measured)"
+                           if peak_kind == "measured" else "fallback 6.65 TB/s (of fallback)")
+    # one more eager step so the check reads a consistent step
+    wl.reset()
+    wl.step()
+    gpu.device_synchronize()
     err = wl.check()
     dev_err = gpu.device_error()
-    units = ranks.sum(wl.units_per_step * args.steps)
+
+    units = ranks.sum(wl.units_per_step() * args.steps)
     value = units / (ms_max / 1e3)
     e2e_value = units / (e2e_ms / 1e3)
-
-    peak, peak_kind = measured_peaks()
-    per_launch_ms = ms / args.steps  # this rank, dominant kernel only
-    achieved = wl.bytes_per_step / (per_launch_ms / 1e3) / 1e9
     out = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s",
         "n_gpus": ranks.world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms_max / args.steps, 5),
         "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None,
-        "dtype": wl.dtype, "data": "synthetic (seeded, BASELINE config inputs)",
+        "dtype": wl.dtype, "data": "synthetic (seeded random weights, token ids and "
+                                   "KV contents; BASELINE config shapes)",
         "config": wl.config(),
-        "parallelism": f"dp{ranks.world} (independent replicas, no collective)",
-        "roofline": {"bound": "hbm", "kernel": wl.kernel,
-                     "achieved": round(achieved, 1), "peak": peak,
-                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"
-                     if peak_kind == "measured" else "fallback 6.65 TB/s",
-                     "unit": "GB/s", "frac": round(achieved / peak, 4),
-                     "algorithmic_bytes_per_launch": wl.bytes_per_step,
-                     "traffic": profiled_traffic(wl.name)},
+        "roofline": roof,
         "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": wl.h2d, "d2h_bytes_per_step": wl.d2h},
-        "gpu_launches": launches,
+        "gpu_launches": wl.launches_per_step * args.steps,
         "clocks": clk,
-        "check": {"max_abs_err_vs_oracle": err, "device_error": dev_err},
+        "check": {"attention_max_abs_err_vs_oracle": err, "device_error": dev_err},
     }
+    if proj:
+        out["roofline_projections"] = proj
+    out["_ctx_mean"] = float(np.mean(getattr(wl, "lens", [0])))
     return out
+
+
+def reference_arm(args, ranks, cores):
+    """Rank 0 times the oracle (the reference's math in numpy) on the host."""
+    if ranks.rank != 0:
+        return None
+    if args.workload == "gqa":
+        import multiprocessing as mp
+        wl = GQAWorkload(ranks, 0, 0, copies=0)
+        with mp.get_context("spawn").Pool(cores) as pool:
+            vals, sample = [], ""
+            for i in range(args.warmup + args.steps):
+                v, sample = gqa_cpu_baseline(cores, pool, budget_s=2.0)
+                if i >= args.warmup:
+                    vals.append(v)
+        value = statistics.median(vals)
+        cfg = wl.config()
+        scaling = wl.scaling
+    else:
+        from triton_llm import shard
+        lens = shard.ragged_lengths(64, LlamaDecodeWorkload.lo, LlamaDecodeWorkload.hi,
+                                    LlamaDecodeWorkload.len_seed)
+        value, sample = llama_cpu_sample(int(lens.mean()), max(args.steps, 3))
+        cfg = {"workload": "cfg4 Llama-3.2-3B ragged-batch greedy decode",
+               "model": LlamaDecodeWorkload.model, "batch": 64,
+               "ctx": "U[1024,8192] seed 4"}
+        scaling = "weak"
+    return {"impl": "reference", "metric": METRIC, "value": round(value, 4),
+            "unit": "tokens/s", "n_gpus": ranks.world, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "scaling": scaling,
+            "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded, BASELINE config shapes)", "config": cfg,
+            "cpu_baseline": {"value": round(value, 4), "unit": "tokens/s",
+                             "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": round(value, 4), "unit": "tokens/s",
+                    "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=128)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="gqa", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="llama3b", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -395,48 +963,28 @@ def main():
     cores = len(os.sched_getaffinity(0))
 
     if args.impl == "reference":
-        if ranks.rank != 0:
-            ranks.close()
-            return
-        import multiprocessing as mp
-        ctx = mp.get_context("spawn")
-        with ctx.Pool(cores) as pool:
-            wl = _make_cpu_workload(args.workload)
-            vals = []
-            for i in range(args.warmup + args.steps):
-                v, sample = cpu_baseline(args.workload, cores, pool, budget_s=2.0)
-                if i >= args.warmup:
-                    vals.append(v)
-        value = statistics.median(vals)
-        line = {"impl": "reference", "metric": METRIC, "value": round(value, 3),
-                "unit": "tokens/s", "n_gpus": ranks.world, "steps": args.steps,
-                "warmup": args.warmup, "higher_is_better": True,
-                "scaling": wl.scaling, "vs_baseline": None, "dtype": "f32",
-                "data": "synthetic (seeded, BASELINE config inputs)",
-                "config": wl.config(),
-                "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s",
-                                 "cores": cores, "kind": "port",
-                                 "sample": sample + " per step; numpy restatement "
-                                 "of the reference kernels (oracle/)"},
-                "e2e": {"value": round(value, 3), "unit": "tokens/s",
-                        "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-        print(json.dumps(line), flush=True)
+        line = reference_arm(args, ranks, cores)
+        if line is not None:
+            print(json.dumps(line), flush=True)
         ranks.close()
         return
 
     pool = None
-    if ranks.world == 1 and not args.no_cpu_baseline:
+    want_cpu = ranks.world == 1 and not args.no_cpu_baseline
+    if want_cpu and args.workload == "gqa":
         # spawn the CPU-baseline workers before the first GPU call
         import multiprocessing as mp
         pool = mp.get_context("spawn").Pool(cores)
     out = run_b200(args, ranks)
-    if pool is not None:
-        v, sample = cpu_baseline(args.workload, cores, pool)
-        pool.close()
-        out["cpu_baseline"] = {"value": round(v, 3), "unit": "tokens/s",
-                               "cores": cores, "kind": "port",
-                               "sample": sample + "; numpy restatement of the "
-                               "reference kernels (oracle/)"}
+    ctx = out.pop("_ctx_mean")
+    if want_cpu:
+        res = cpu_baseline(args.workload, cores, 5, pool, ctx)
+        if pool is not None:
+            pool.close()
+        if res is not None:
+            v, sample = res
+            out["cpu_baseline"] = {"value": round(v, 4), "unit": "tokens/s",
+                                   "cores": cores, "kind": "port", "sample": sample}
     if ranks.rank == 0:
         print(json.dumps(out), flush=True)
     ranks.close()

@@ -42,7 +42,13 @@ typedef enum {
 typedef enum {
   TLLM_F32 = 0,
   TLLM_BF16 = 1,
-  TLLM_I32 = 2
+  TLLM_I32 = 2,
+  /* An fp32 activation matrix stored as two bf16 planes of `plane_rows`
+   * rows each: hi = bf16(x) in plane 0, lo = bf16(x - hi) in plane 1, so
+   * hi + lo keeps ~16 mantissa bits of x. This is the operand format of the
+   * tensor-core projections; the kernels that produce their inputs (norms,
+   * attention, the SwiGLU / GELU epilogues) can write it directly. */
+  TLLM_SPLIT = 3
 } tllm_dtype;
 
 /* ------------------------------------------------------------------------ */
@@ -159,28 +165,37 @@ int tllm_gqa_decode(const float *q, const void *k_cache, const void *v_cache,
  * r * *_row_stride + h * *_head_stride elements. Used for the prefill
  * (causal: row_len = position + 1) and for the reference's flat layout
  * (Q as (n_head * seq_q, d_k) is row stride d_k, head stride seq_q * d_k).
- * Replaces triton_llm/kernels/attention_gqa.py:149-269 (causal branch) and
- * the prefill attention of smollm2_triton/model.py:341-343. Scratch as for
+ * out_dtype F32 writes fp32; TLLM_SPLIT writes the two bf16 planes at the
+ * same element offsets, planes out_plane_rows * out_row_stride elements
+ * apart (the operand format of tllm_linear). Replaces
+ * triton_llm/kernels/attention_gqa.py:149-269 (causal branch) and the
+ * prefill attention of smollm2_triton/model.py:341-343. Scratch as for
  * tllm_gqa_decode with batch = rows.
  */
 int tllm_gqa_rows(const float *q, long q_row_stride, long q_head_stride,
                   const void *k_cache, const void *v_cache, int kv_dtype,
-                  const int32_t *row_seq, const int32_t *row_len, float *out,
-                  long out_row_stride, long out_head_stride, int rows,
-                  int n_head, int n_kv_head, int head_dim, int cache_batch,
-                  int max_seq, int max_len, float sm_scale, void *partial,
-                  size_t partial_bytes, int32_t *counters,
-                  tllm_stream_t stream);
+                  const int32_t *row_seq, const int32_t *row_len, void *out,
+                  int out_dtype, long out_plane_rows, long out_row_stride,
+                  long out_head_stride, int rows, int n_head, int n_kv_head,
+                  int head_dim, int cache_batch, int max_seq, int max_len,
+                  float sm_scale, void *partial, size_t partial_bytes,
+                  int32_t *counters, tllm_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* Projections (GEMM with fused epilogues)                                   */
 /* ------------------------------------------------------------------------ */
 
 /*
- * y = epilogue(x @ W^T) for x (M, K) f32 and W (N, K) in w_dtype (F32 or
- * BF16; BF16 needs K % 64 == 0). Replaces triton_llm/kernels/gemm.py:53-109
- * plus the add / swiglu / gelu / apply_rope calls that follow it in
- * smollm2_triton/model.py:281-365 and gpt2_triton/model.py:319-361.
+ * y = epilogue(x @ W^T) for x (M, K) and W (N, K). Replaces
+ * triton_llm/kernels/gemm.py:53-109 plus the add / swiglu / gelu /
+ * apply_rope calls that follow it in smollm2_triton/model.py:281-365 and
+ * gpt2_triton/model.py:319-361.
+ *
+ * w_dtype BF16: tensor-core path; x must be TLLM_SPLIT (planes of
+ *   x_plane_rows >= M rows, see tllm_split_bf16) and K % 64 == 0.
+ * w_dtype F32 : CUDA-core fp32 path; x must be F32 (M, K), K % 4 == 0.
+ * out_dtype F32 or TLLM_SPLIT (planes of out_plane_rows rows of ld_out);
+ *   op RESID needs F32.
  *
  * op 0 STORE : out[m, n] = acc (+ bias[n])
  * op 1 RESID : out[m, n] = resid[m, n] + acc (+ bias[n]); resid may be out
@@ -195,12 +210,14 @@ int tllm_gqa_rows(const float *q, long q_row_stride, long q_head_stride,
  *              written into the caches (B, n_kv_head, max_seq, D) at
  *              row_pos[m] (rope.py:49-66 + smollm2_triton/model.py:296-302);
  *              if lens_out != NULL, lens_out[row_seq[m]] = row_pos[m] + 1.
- * Scratch for split-K: tllm_linear_workspace; counters zero-filled once.
+ * Scratch for split-K: tllm_linear_workspace; counters zero-filled once
+ * (the kernel leaves them at zero).
  */
 int tllm_linear_workspace(int M, int N, int K, size_t *partial_bytes,
                           size_t *counter_bytes);
-int tllm_linear(const float *x, const void *w, int w_dtype, int M, int N,
-                int K, int op, const float *bias, float *out, int ld_out,
+int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
+                int w_dtype, int M, int N, int K, int op, const float *bias,
+                void *out, int out_dtype, int out_plane_rows, int ld_out,
                 const float *resid, const float *cos_t, const float *sin_t,
                 const int32_t *row_seq, const int32_t *row_pos, float *q_out,
                 void *k_cache, void *v_cache, int kv_dtype, int max_seq,
@@ -217,12 +234,20 @@ int tllm_gemm_f32(const float *a, const float *b, float *c, int M, int N,
 /* Norms, embedding, sampling, elementwise                                   */
 /* ------------------------------------------------------------------------ */
 
-/* triton_llm/kernels/rms_norm.py:68-115: y = (x / sqrt(mean(x^2) + eps)) * w */
-int tllm_rmsnorm(const float *x, const float *w, float *y, int M, int N,
-                 float eps, tllm_stream_t stream);
-/* triton_llm/kernels/layernorm.py:79-152 (two-pass mean / variance) */
+/* triton_llm/kernels/rms_norm.py:68-115: y = (x / sqrt(mean(x^2) + eps)) * w
+ * y_dtype F32 (M, N), or TLLM_SPLIT with planes of y_plane_rows rows. */
+int tllm_rmsnorm(const float *x, const float *w, void *y, int y_dtype,
+                 int y_plane_rows, int M, int N, float eps,
+                 tllm_stream_t stream);
+/* triton_llm/kernels/layernorm.py:79-152 (two-pass mean / variance);
+ * output as for tllm_rmsnorm. */
 int tllm_layernorm(const float *x, const float *gamma, const float *beta,
-                   float *y, int M, int N, float eps, tllm_stream_t stream);
+                   void *y, int y_dtype, int y_plane_rows, int M, int N,
+                   float eps, tllm_stream_t stream);
+/* fp32 (rows, cols) -> TLLM_SPLIT with planes of plane_rows >= rows rows.
+ * No counterpart in the reference (its activations stay fp32). */
+int tllm_split_bf16(const float *x, void *y, int rows, int cols,
+                    int plane_rows, tllm_stream_t stream);
 /* out[m] = wte[ids[m]] (+ wpe[pos[m]] if wpe): triton_llm/kernels/
  * embedding.py:98-187 and smollm2_triton/model.py:547-560. Out-of-range ids
  * give a zero row and set bit 4 of the device error word. */

@@ -383,3 +383,101 @@ def test_gqa_rows_ragged_prefill(gpu, bf16):
     got = out.to_numpy().reshape(R, H, D)
     ref = ops.gqa_decode(q, kc[row_seq], vc[row_seq], row_len)
     np.testing.assert_allclose(got, ref, atol=1e-4)
+
+
+# ------------------------------------------------ split operand format --
+def test_split_conversion_bit_exact(gpu):
+    """tllm_split_bf16: plane 0 = bf16(x), plane 1 = bf16(x - hi), rows
+    beyond `rows` untouched."""
+    from triton_llm.kernels.linear import to_split
+    rng = np.random.default_rng(1)
+    x = (rng.standard_normal((7, 320)) * 10).astype(F32)
+    x[0, :4] = [0.0, -0.0, 1e-30, 3e38]
+    xs = gpu.split_empty(9, 320)
+    gpu.memset(xs, 0)
+    to_split(gpu.to_device(x), out=xs)
+    planes = xs.to_numpy()
+    hi, lo = gpu.split_host(x)
+    np.testing.assert_array_equal(planes[0, :7], hi)
+    np.testing.assert_array_equal(planes[1, :7], lo)
+    assert not planes[:, 7:].any()
+    rel = np.abs(gpu.split_to_host(xs, 7) - x) / np.maximum(np.abs(x), 1e-30)
+    assert rel.max() < 2 ** -16
+
+
+@pytest.mark.parametrize("norm", ["rms", "ln"])
+def test_norm_split_output_equals_split_of_fp32(gpu, norm):
+    from triton_llm.kernels.rms_norm import rms_norm_rows
+    from triton_llm.kernels.layernorm import layer_norm_dev
+    rng = np.random.default_rng(2)
+    M, N = 5, 576
+    x = rng.standard_normal((M, N), dtype=F32)
+    w = rng.standard_normal(N, dtype=F32)
+    b = rng.standard_normal(N, dtype=F32)
+    xd, wd, bd = gpu.to_device(x), gpu.to_device(w), gpu.to_device(b)
+    f = gpu.allocate((M, N), np.float32)
+    sp = gpu.split_empty(8, N)
+    if norm == "rms":
+        rms_norm_rows(xd, wd, f, M)
+        rms_norm_rows(xd, wd, sp, M)
+    else:
+        layer_norm_dev(xd, wd, bd, f, M=M)
+        layer_norm_dev(xd, wd, bd, sp, M=M)
+    hi, lo = gpu.split_host(f.to_numpy())
+    planes = sp.to_numpy()
+    np.testing.assert_array_equal(planes[0, :M], hi)
+    np.testing.assert_array_equal(planes[1, :M], lo)
+
+
+def test_linear_split_output_equals_split_of_fp32(gpu):
+    """SwiGLU epilogue writing the operand format of the next projection."""
+    from triton_llm import _lib
+    from triton_llm.kernels.linear import Linear, LinearWorkspace, linear, swiglu_rows
+    rng = np.random.default_rng(4)
+    F, K, M = 256, 576, 6
+    lin = Linear(swiglu_rows(rng.standard_normal((F, K), dtype=F32) * 0.05,
+                             rng.standard_normal((F, K), dtype=F32) * 0.05), "bfloat16")
+    xs = gpu.to_device_split(rng.standard_normal((M, K), dtype=F32), plane_rows=16)
+    ws = LinearWorkspace([(M, 2 * F, K)])
+    f = gpu.allocate((M, F), np.float32)
+    sp = gpu.split_empty(16, F)
+    linear(xs, lin, out_dev=f, op=_lib.EPI_SWIGLU, ws=ws, M=M)
+    linear(xs, lin, out_dev=sp, op=_lib.EPI_SWIGLU, ws=ws, M=M)
+    hi, lo = gpu.split_host(f.to_numpy())
+    planes = sp.to_numpy()
+    np.testing.assert_array_equal(planes[0, :M], hi)
+    np.testing.assert_array_equal(planes[1, :M], lo)
+
+
+@pytest.mark.parametrize("M", [1, 16, 17, 64, 65, 200, 300, 600])
+def test_linear_tile_shapes(gpu, M):
+    """Every activation tile width (16..256 columns), multiple row tiles,
+    and N not a multiple of the 128-row weight tile."""
+    from triton_llm.kernels.linear import LinearWorkspace, linear
+    N, K = 1000, 1024
+    lin, x, wd, ref, bound = _linear_case(gpu, M, N, K, True, seed=100 + M)
+    out = gpu.allocate((M, N), np.float32)
+    linear(gpu.to_device(x), lin, out_dev=out, ws=LinearWorkspace([(M, N, K)]), M=M)
+    _close(out.to_numpy(), ref, bound, msg=f"M={M}")
+
+
+def test_attention_split_output(gpu):
+    """gqa_rows writing the operand format of the o projection."""
+    from triton_llm.kernels import gqa_rows
+    H, Hkv, D, S, R = 24, 8, 128, 512, 5
+    rng = np.random.default_rng(8)
+    kc = ops.bf16_round(rng.standard_normal((R, Hkv, S, D), dtype=F32))
+    vc = ops.bf16_round(rng.standard_normal((R, Hkv, S, D), dtype=F32))
+    lens = np.array([1, 100, 512, 64, 300], np.int32)
+    q = rng.standard_normal((R, H, D), dtype=F32)
+    seq = np.arange(R, dtype=np.int32)
+    args = (gpu.to_device(q), gpu.to_device_bf16(kc), gpu.to_device_bf16(vc),
+            gpu.to_device(seq), gpu.to_device(lens))
+    f = gpu.allocate((R, H * D), np.float32)
+    sp = gpu.split_empty(8, H * D)
+    gqa_rows(*args, f, R, H, H * D, D, H * D, D, S)
+    gqa_rows(*args, sp, R, H, H * D, D, H * D, D, S)
+    hi, lo = gpu.split_host(f.to_numpy())
+    planes = sp.to_numpy()
+    np.testing.assert_array_equal(planes[0, :R], hi)
+    np.testing.assert_array_equal(planes[1, :R], lo)

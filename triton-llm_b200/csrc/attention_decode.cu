@@ -10,7 +10,7 @@
 //    query heads of its KV group, so each K/V byte is read from HBM once
 //    (the reference re-reads K/V once per query head);
 //  * a producer warp streams K and V tiles with 3-D tiled TMA loads
-//    (cp.async.bulk.tensor, no multicast) into a 4-stage shared-memory ring
+//    (cp.async.bulk.tensor into this CTA only) into a 4-stage shared-memory ring
 //    guarded by full/empty mbarriers; four consumer warps read 128-bit
 //    vectors from shared memory;
 //  * scores are reduced with warp shuffles and folded into a per-warp
@@ -75,6 +75,8 @@ __device__ __forceinline__ float fast_exp2(float x) {
 struct DecodeParams {
   const float *q;        // row b, head h at q + b * q_sb + h * q_sh
   float *out;            // row b, head h at out + b * o_sb + h * o_sh
+  uint16_t *out_split;   // or TLLM_SPLIT output at the same element offsets,
+  long out_plane;        //   planes out_plane elements apart
   const int *seq_lens;   // (B,) or null (every sequence has max_len keys)
   const int *row_seq;    // (B,) cache sequence of each row, or null (= row)
   long q_sb, q_sh, o_sb, o_sh;
@@ -86,6 +88,14 @@ struct DecodeParams {
   int max_seq, max_len, chunk, max_splits;
   float qscale;          // sm_scale * log2(e)
 };
+
+__device__ __forceinline__ void store_o(const DecodeParams &p, long idx,
+                                        float v) {
+  if (p.out_split)
+    store_split(p.out_split, (size_t)p.out_plane, (size_t)idx, v);
+  else
+    p.out[idx] = v;
+}
 
 // Shape constants of one instantiation.
 template <typename T, int D>
@@ -371,8 +381,7 @@ __global__ void __launch_bounds__(kThreads)
     }
     const size_t row = (size_t)b * p.n_head + head0 + g;
     if (single) {
-      p.out[b * p.o_sb + (long)(head0 + g) * p.o_sh + d] =
-          den > 0.f ? num / den : 0.f;
+      store_o(p, b * p.o_sb + (long)(head0 + g) * p.o_sh + d, den > 0.f ? num / den : 0.f);
     } else {
       const size_t slot = row * p.max_splits + j;
       p.part_acc[slot * D + d] = num;
@@ -428,7 +437,7 @@ __global__ void __launch_bounds__(kThreads)
     float o = 0.f;
     for (int s = 0; s < n_splits; ++s)
       o = fmaf(sw[g * kMaxSplits + s], __ldcg(&p.part_acc[(base + s) * D + d]), o);
-    p.out[b * p.o_sb + (long)(head0 + g) * p.o_sh + d] = o;
+    store_o(p, b * p.o_sb + (long)(head0 + g) * p.o_sh + d, o);
   }
 }
 
@@ -782,8 +791,7 @@ __global__ void __launch_bounds__(kThreads)
     }
     const size_t row = (size_t)b * p.n_head + head0 + g;
     if (single) {
-      p.out[b * p.o_sb + (long)(head0 + g) * p.o_sh + d] =
-          den > 0.f ? num / den : 0.f;
+      store_o(p, b * p.o_sb + (long)(head0 + g) * p.o_sh + d, den > 0.f ? num / den : 0.f);
     } else {
       const size_t slot = row * p.max_splits + j;
       p.part_acc[slot * D + d] = num;
@@ -839,7 +847,7 @@ __global__ void __launch_bounds__(kThreads)
     for (int s = 0; s < n_splits; ++s)
       o2 = fmaf(sw[g * kMaxSplits + s], __ldcg(&p.part_acc[(base + s) * D + d]),
                 o2);
-    p.out[b * p.o_sb + (long)(head0 + g) * p.o_sh + d] = o2;
+    store_o(p, b * p.o_sb + (long)(head0 + g) * p.o_sh + d, o2);
   }
 }
 
@@ -1018,8 +1026,8 @@ int pick_chunk(int rows, int batch, int ygrid, int max_len) {
 //   cache_batch = sequences in the cache.
 static int rows_impl(const float *q, long q_sb, long q_sh, const void *k_cache,
                      const void *v_cache, int kv_dtype, const int32_t *seq_lens,
-                     const int32_t *row_seq, float *out, long o_sb, long o_sh,
-                     int batch, int n_head, int n_kv_head, int head_dim,
+                     const int32_t *row_seq, void *out, int out_dtype,
+                     long out_plane_rows, long o_sb, long o_sh, int batch, int n_head, int n_kv_head, int head_dim,
                      int cache_batch, int max_seq, int max_len, float sm_scale,
                      void *partial, size_t partial_bytes, int32_t *counters,
                      int *err_word, tllm_stream_t stream) {
@@ -1031,6 +1039,10 @@ static int rows_impl(const float *q, long q_sb, long q_sh, const void *k_cache,
                  n_kv_head);
   TLLM_CHECK_ARG(kv_dtype == TLLM_F32 || kv_dtype == TLLM_BF16,
                  "kv_dtype must be F32 or BF16");
+  TLLM_CHECK_ARG(out_dtype == TLLM_F32 || out_dtype == TLLM_SPLIT,
+                 "out_dtype must be F32 or SPLIT");
+  TLLM_CHECK_ARG(out_dtype != TLLM_SPLIT || out_plane_rows >= batch,
+                 "out_plane_rows (%ld) < rows (%d)", out_plane_rows, batch);
   if (batch == 0) return TLLM_OK;
   TLLM_CHECK_ARG(q && out && k_cache && v_cache, "NULL tensor pointer");
   TLLM_CHECK_ARG(max_seq > 0, "max_seq must be > 0");
@@ -1081,7 +1093,9 @@ static int rows_impl(const float *q, long q_sb, long q_sh, const void *k_cache,
 
   DecodeParams p;
   p.q = q;
-  p.out = out;
+  p.out = out_dtype == TLLM_SPLIT ? nullptr : static_cast<float *>(out);
+  p.out_split = out_dtype == TLLM_SPLIT ? static_cast<uint16_t *>(out) : nullptr;
+  p.out_plane = out_dtype == TLLM_SPLIT ? out_plane_rows * o_sb : 0;
   p.seq_lens = seq_lens;
   p.row_seq = row_seq;
   p.q_sb = q_sb;
@@ -1148,23 +1162,23 @@ int tllm_gqa_decode(const float *q, const void *k_cache, const void *v_cache,
   TLLM_INJECT("launch");
   const long hd = (long)n_head * head_dim;
   return rows_impl(q, hd, head_dim, k_cache, v_cache, kv_dtype, seq_lens,
-                   nullptr, out, hd, head_dim, batch, n_head, n_kv_head,
-                   head_dim, batch, max_seq, max_len, sm_scale, partial,
-                   partial_bytes, counters, device_error_ptr(), stream);
+                   nullptr, out, TLLM_F32, 0, hd, head_dim, batch, n_head,
+                   n_kv_head, head_dim, batch, max_seq, max_len, sm_scale,
+                   partial, partial_bytes, counters, device_error_ptr(), stream);
 }
 
 int tllm_gqa_rows(const float *q, long q_row_stride, long q_head_stride,
                   const void *k_cache, const void *v_cache, int kv_dtype,
-                  const int32_t *row_seq, const int32_t *row_len, float *out,
-                  long out_row_stride, long out_head_stride, int rows,
-                  int n_head, int n_kv_head, int head_dim, int cache_batch,
-                  int max_seq, int max_len, float sm_scale, void *partial,
-                  size_t partial_bytes, int32_t *counters,
-                  tllm_stream_t stream) {
+                  const int32_t *row_seq, const int32_t *row_len, void *out,
+                  int out_dtype, long out_plane_rows, long out_row_stride,
+                  long out_head_stride, int rows, int n_head, int n_kv_head,
+                  int head_dim, int cache_batch, int max_seq, int max_len,
+                  float sm_scale, void *partial, size_t partial_bytes,
+                  int32_t *counters, tllm_stream_t stream) {
   TLLM_INJECT("launch");
   return rows_impl(q, q_row_stride, q_head_stride, k_cache, v_cache, kv_dtype,
-                   row_len, row_seq, out, out_row_stride, out_head_stride,
-                   rows, n_head, n_kv_head, head_dim, cache_batch, max_seq,
+                   row_len, row_seq, out, out_dtype, out_plane_rows,
+                   out_row_stride, out_head_stride, rows, n_head, n_kv_head, head_dim, cache_batch, max_seq,
                    max_len, sm_scale, partial, partial_bytes, counters,
                    device_error_ptr(), stream);
 }
@@ -1257,7 +1271,7 @@ extern "C" int tllm_gqa_decode_noalloc(
                             st));
   const long hd = (long)n_head * head_dim;
   return rows_impl(q, hd, head_dim, k_cache, v_cache, kv_dtype, seq_lens,
-                   nullptr, out, hd, head_dim, batch, n_head, n_kv_head,
-                   head_dim, batch, max_seq, max_len, sm_scale, base,
+                   nullptr, out, TLLM_F32, 0, hd, head_dim, batch, n_head,
+                   n_kv_head, head_dim, batch, max_seq, max_len, sm_scale, base,
                    kNoAllocPartialBytes, counters, err_word, st);
 }

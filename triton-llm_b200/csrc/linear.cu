@@ -6,32 +6,37 @@
 // (smollm2_triton/model.py:281-365, gpt2_triton/model.py:319-361).
 //
 // Two kernels:
-//  * linear_mma_kernel (bf16 weights): tensor cores via mma.sync m16n8k16.
-//    The weight rows are the MMA M dimension (128 rows per CTA, 32 per
-//    consumer warp) and the activation rows the N dimension (8..64 per
-//    tile), so each weight byte is streamed from HBM once whatever the
-//    batch. Weight tiles (128 x 64) and fp32 activation tiles (64 rows x 64)
-//    arrive by 2-D TMA with 128-byte swizzle into a 3-stage ring; each
-//    activation element is split into bf16 head + residual when it is
-//    loaded into a fragment, so the product keeps ~16 mantissa bits of x.
-//    K is split across CTAs when there are few weight tiles; the last CTA
-//    of a tile (atomic ticket) sums the splits in fixed order and runs the
-//    epilogue, so results do not depend on scheduling.
+//  * linear_tc_kernel (bf16 weights): 5th-generation tensor cores. Weight
+//    rows are the MMA's M dimension (128 per CTA) and activation rows its N
+//    dimension (16..256 per tile), so every weight byte streams from HBM
+//    once whatever the batch. One thread issues the TMA loads of 128 x 64
+//    weight tiles and of the activation tiles into a ring of shared-memory
+//    stages; one thread issues tcgen05.mma with the fp32 accumulator in
+//    TMEM and releases each stage with tcgen05.commit; after the last stage
+//    the four warps read the accumulator with tcgen05.ld and run the
+//    epilogue. Activations arrive in the TLLM_SPLIT format (bf16 hi and lo
+//    planes): each k-slice issues one MMA for hi and one for lo, so the
+//    product keeps ~16 mantissa bits of the fp32 activations while both
+//    operands are bf16. K is split across CTAs when there are too few
+//    weight tiles to occupy the GPU: the S CTAs of a tile form a thread-block
+//    cluster, each stages its accumulator tile in shared memory, and after a
+//    cluster barrier each reduces a slice of the tile over distributed shared
+//    memory (ranks summed in fixed order, so results do not depend on
+//    scheduling) and runs the epilogue for that slice.
 //  * linear_f32_kernel (fp32 weights, GPT-2 and the fp32 drop-in): one warp
-//    per weight row, 16-byte loads along K, fp32 FMA, same epilogues.
+//    per weight-row pair, 16-byte loads along K, fp32 FMA, same epilogues.
 //
-// Epilogue row pairing: a thread's accumulator holds weight rows r and r+8
-// of a 16-row block. SwiGLU weights are stored with gate and up rows
-// interleaved in blocks of 8 (gate 8i..8i+7, up 8i..8i+7), so gate and up of
-// one output sit in one thread. QKV weights are stored per head with dims
+// Epilogue row pairing: rows r and r + 8 of a 16-row block are handled by
+// one thread. SwiGLU weights are stored with gate and up rows interleaved in
+// blocks of 8 (gate 8i..8i+7, up 8i..8i+7), so gate and up of one output
+// meet in one thread. QKV weights are stored per head with dims
 // (8b..8b+7) followed by (D/2+8b..D/2+8b+7), so the RoPE pair (d, d+D/2) of
-// the reference's rotate-half (triton_llm/kernels/rope.py:49-66) sits in one
-// thread and is rotated before the store.
+// the reference's rotate-half (triton_llm/kernels/rope.py:49-66) meets in
+// one thread and is rotated before the store.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
 #include <cmath>
-#include <mutex>
 
 #include "common.cuh"
 
@@ -41,6 +46,9 @@ namespace tllm {
 int make_map_2d(CUtensorMap *m, const void *base, int dtype, long inner,
                 long outer, long stride_bytes, int box_inner, int box_outer,
                 bool swizzle128);
+int make_map(CUtensorMap *m, const void *base, int dtype, int rank,
+             const long *dims, const long *strides_bytes, const int *box,
+             bool swizzle128);
 
 namespace {
 
@@ -55,7 +63,9 @@ enum EpiOp : int {
 struct Epilogue {
   int op;
   const float *bias;   // [N] or null (in weight-row order)
-  float *out;          // [M, ld_out]
+  float *out;          // [M, ld_out] fp32, or null when out_split is set
+  uint16_t *out_split; // TLLM_SPLIT output, planes out_plane elements apart
+  size_t out_plane;
   const float *resid;  // [M, ld_out] (EPI_RESID)
   int ld_out;
   // EPI_QKV
@@ -84,314 +94,307 @@ __device__ __forceinline__ float silu_ref(float x) {
   return x * sig;
 }
 
+__device__ __forceinline__ void store_out(const Epilogue &e, size_t idx,
+                                          float v) {
+  if (e.out_split)
+    store_split(e.out_split, e.out_plane, idx, v);
+  else
+    e.out[idx] = v;
+}
+
 // Apply the epilogue to weight rows (r, r + 8) of one 16-row block at
 // activation row m. v0 = acc(r, m), v1 = acc(r + 8, m).
+template <int OP>
 __device__ __forceinline__ void epi_pair(const Epilogue &e, int N, int M,
                                          int r, int m, float v0, float v1) {
   if (m >= M) return;
   const int r1 = r + 8;
-  switch (e.op) {
-    case EPI_STORE:
-    case EPI_RESID:
-    case EPI_GELU: {
-      float *o = e.out + (size_t)m * e.ld_out;
-      if (r < N) {
-        float a = v0 + (e.bias ? e.bias[r] : 0.f);
-        if (e.op == EPI_RESID) a = e.resid[(size_t)m * e.ld_out + r] + a;
-        if (e.op == EPI_GELU) a = gelu_tanh(a);
-        o[r] = a;
-      }
-      if (r1 < N) {
-        float a = v1 + (e.bias ? e.bias[r1] : 0.f);
-        if (e.op == EPI_RESID) a = e.resid[(size_t)m * e.ld_out + r1] + a;
-        if (e.op == EPI_GELU) a = gelu_tanh(a);
-        o[r1] = a;
-      }
-      break;
+  if constexpr (OP == EPI_STORE || OP == EPI_RESID || OP == EPI_GELU) {
+    const size_t o = (size_t)m * e.ld_out;
+    if (r < N) {
+      float a = v0 + (e.bias ? e.bias[r] : 0.f);
+      if constexpr (OP == EPI_RESID) a = e.resid[o + r] + a;
+      if constexpr (OP == EPI_GELU) a = gelu_tanh(a);
+      store_out(e, o + r, a);
     }
-    case EPI_SWIGLU: {
-      if (r1 < N) {
-        const int j = (r >> 4) * 8 + (r & 7);
-        e.out[(size_t)m * e.ld_out + j] = silu_ref(v0) * v1;
-      }
-      break;
+    if (r1 < N) {
+      float a = v1 + (e.bias ? e.bias[r1] : 0.f);
+      if constexpr (OP == EPI_RESID) a = e.resid[o + r1] + a;
+      if constexpr (OP == EPI_GELU) a = gelu_tanh(a);
+      store_out(e, o + r1, a);
     }
-    case EPI_QKV: {
-      if (r1 >= N) break;
-      const int D = e.D;
-      const int head = r / D;
-      const int local = r - head * D;         // r is in the first 8 of a 16
-      const int blk = local >> 4;
-      const int d0 = blk * 8 + (local & 7);   // dim of v0; v1 is d0 + D/2
-      const int d1 = d0 + D / 2;
-      float x0 = v0 + (e.bias ? e.bias[r] : 0.f);
-      float x1 = v1 + (e.bias ? e.bias[r1] : 0.f);
-      const int pos = e.row_pos[m];
-      const int seq = e.row_seq[m];
-      const bool is_v = head >= e.H + e.Hkv;
-      if (e.cos && !is_v) {
-        // x0' = x0 c - x1 s, x1' = x0 s + x1 c with each product rounded
-        // (no FMA contraction), as numpy computes rope.py:65-66
-        const float c = e.cos[(size_t)pos * (D / 2) + d0];
-        const float s = e.sin[(size_t)pos * (D / 2) + d0];
-        const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-        const float y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
-        x0 = y0;
-        x1 = y1;
+  } else if constexpr (OP == EPI_SWIGLU) {
+    if (r1 < N) {
+      const int j = (r >> 4) * 8 + (r & 7);
+      store_out(e, (size_t)m * e.ld_out + j, silu_ref(v0) * v1);
+    }
+  } else {  // EPI_QKV
+    if (r1 >= N) return;
+    const int D = e.D;
+    const int head = r / D;
+    const int local = r - head * D;         // r is in the first 8 of a 16
+    const int blk = local >> 4;
+    const int d0 = blk * 8 + (local & 7);   // dim of v0; v1 is d0 + D/2
+    const int d1 = d0 + D / 2;
+    float x0 = v0 + (e.bias ? e.bias[r] : 0.f);
+    float x1 = v1 + (e.bias ? e.bias[r1] : 0.f);
+    const int pos = e.row_pos[m];
+    const int seq = e.row_seq[m];
+    const bool is_v = head >= e.H + e.Hkv;
+    if (e.cos && !is_v) {
+      // x0' = x0 c - x1 s, x1' = x0 s + x1 c with each product rounded
+      // (no FMA contraction), as numpy computes rope.py:65-66
+      const float c = e.cos[(size_t)pos * (D / 2) + d0];
+      const float s = e.sin[(size_t)pos * (D / 2) + d0];
+      const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+      const float y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+      x0 = y0;
+      x1 = y1;
+    }
+    if (head < e.H) {
+      float *q = e.q_out + ((size_t)m * e.H + head) * D;
+      q[d0] = x0;
+      q[d1] = x1;
+    } else {
+      const int kvh = is_v ? head - e.H - e.Hkv : head - e.H;
+      if (pos < 0 || pos >= e.max_seq || seq < 0) {
+        atomicOr(e.err, DEV_ERR_LEN_CLAMPED);
+        return;
       }
-      if (head < e.H) {
-        float *q = e.q_out + ((size_t)m * e.H + head) * D;
-        q[d0] = x0;
-        q[d1] = x1;
+      const size_t off = (((size_t)seq * e.Hkv + kvh) * e.max_seq + pos) * D;
+      void *cache = is_v ? e.v_cache : e.k_cache;
+      if (e.kv_bf16) {
+        uint16_t *c = static_cast<uint16_t *>(cache) + off;
+        c[d0] = f32_to_bf16_bits(x0);
+        c[d1] = f32_to_bf16_bits(x1);
       } else {
-        const int kvh = is_v ? head - e.H - e.Hkv : head - e.H;
-        if (pos < 0 || pos >= e.max_seq || seq < 0) {
-          atomicOr(e.err, DEV_ERR_LEN_CLAMPED);
-          break;
-        }
-        const size_t off =
-            (((size_t)seq * e.Hkv + kvh) * e.max_seq + pos) * D;
-        void *cache = is_v ? e.v_cache : e.k_cache;
-        if (e.kv_bf16) {
-          uint16_t *c = static_cast<uint16_t *>(cache) + off;
-          c[d0] = f32_to_bf16_bits(x0);
-          c[d1] = f32_to_bf16_bits(x1);
-        } else {
-          float *c = static_cast<float *>(cache) + off;
-          c[d0] = x0;
-          c[d1] = x1;
-        }
-        if (e.lens_out && head == e.H && local == 0) e.lens_out[seq] = pos + 1;
+        float *c = static_cast<float *>(cache) + off;
+        c[d0] = x0;
+        c[d1] = x1;
       }
-      break;
+      if (e.lens_out && head == e.H && local == 0) e.lens_out[seq] = pos + 1;
     }
   }
 }
 
-// ------------------------------------------------------------------------
-// bf16 weights, tensor cores
-// ------------------------------------------------------------------------
-constexpr int kLinThreads = 5 * 32;  // 4 consumer warps + 1 producer warp
-constexpr int kLinBN = 128;          // weight rows per CTA
-constexpr int kLinBK = 64;           // K per stage
-constexpr int kLinStages = 3;
-
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0,
-                                        uint32_t &r1, uint32_t &r2,
-                                        uint32_t &r3) {
-  asm volatile(
-      "ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-      : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-      : "r"(addr));
-}
-__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4],
-                                         uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
-      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ uint32_t pack_bf16x2(float x0, float x1) {
-  uint32_t r;
-  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(x1), "f"(x0));
-  return r;
-}
-__device__ __forceinline__ void split_bf16x2(float x0, float x1, uint32_t &hi,
-                                             uint32_t &lo) {
-  hi = pack_bf16x2(x0, x1);
-  lo = pack_bf16x2(x0 - bf16lo(hi), x1 - bf16hi(hi));
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-__device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap,
-                                            uint64_t *bar, int c0, int c1) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_"
-      "tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
-      "l"(tmap), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
-      : "memory");
+__device__ __forceinline__ void epi_pair_rt(const Epilogue &e, int N, int M,
+                                            int r, int m, float v0, float v1) {
+  switch (e.op) {
+    case EPI_STORE: epi_pair<EPI_STORE>(e, N, M, r, m, v0, v1); break;
+    case EPI_RESID: epi_pair<EPI_RESID>(e, N, M, r, m, v0, v1); break;
+    case EPI_GELU: epi_pair<EPI_GELU>(e, N, M, r, m, v0, v1); break;
+    case EPI_SWIGLU: epi_pair<EPI_SWIGLU>(e, N, M, r, m, v0, v1); break;
+    default: epi_pair<EPI_QKV>(e, N, M, r, m, v0, v1); break;
+  }
 }
 
-struct LinParams {
+// ------------------------------------------------------------------------
+// bf16 weights, tcgen05 tensor cores
+// ------------------------------------------------------------------------
+constexpr int kTcThreads = 128;       // 4 warps: TMA, MMA, then epilogue
+constexpr int kTcBN = 128;            // weight rows per CTA (MMA M)
+constexpr int kTcBK = 64;             // K per stage (one 128-byte row)
+constexpr int kTcW = kTcBN * kTcBK * 2;  // weight tile bytes (16 KB)
+
+constexpr int kTcMaxSplit = 8;        // portable cluster size
+
+struct TcParams {
   Epilogue e;
-  float *partial;   // [m_tiles][S][n_tiles * 128][MT] split-K partials
-  int *counters;    // [m_tiles][n_tiles]
-  int M, N, K, S, k_chunks, n_tiles;
+  int M, N, K, S, k_chunks, n_tiles, stages;
 };
 
-template <int MT>
-__global__ void __launch_bounds__(kLinThreads)
-    linear_mma_kernel(const LinParams p,
-                      const __grid_constant__ CUtensorMap tw,
-                      const __grid_constant__ CUtensorMap ta) {
-  constexpr int NT = MT / 8;                       // n8 tiles of activations
-  constexpr int W_BYTES = kLinBN * 128;            // 128 rows x 64 bf16
-  constexpr int A_BYTES = MT * 256;                // MT rows x 64 fp32
-  constexpr int STAGE = W_BYTES + A_BYTES;
-  extern __shared__ __align__(1024) uint8_t smem[];
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + kLinStages * STAGE);
-  uint64_t *empty = full + kLinStages;
-  __shared__ int s_last;
+__host__ __device__ constexpr int tc_stage_bytes(int MT) {
+  return kTcW + 2 * MT * kTcBK * 2;
+}
+__host__ __device__ constexpr int tc_tmem_cols(int MT) {
+  return MT < 32 ? 32 : MT;
+}
 
-  // 128-byte-swizzled TMA tiles need 1024-byte aligned stage buffers
+template <int MT, int OP>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    linear_tc_kernel(const TcParams p, const __grid_constant__ CUtensorMap tw,
+                     const __grid_constant__ CUtensorMap tx) {
+  constexpr int X_BYTES = MT * kTcBK * 2;    // one bf16 plane of the tile
+  constexpr int STAGE = tc_stage_bytes(MT);
+  constexpr uint32_t TCOLS = tc_tmem_cols(MT);
+  constexpr uint32_t IDESC = umma_idesc_bf16(kTcBN, MT);
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const int ST = p.stages;
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + ST * STAGE);
+  uint64_t *empty = full + ST;
+  uint64_t *accb = empty + ST;
+  __shared__ uint32_t s_tmem;
+  __shared__ int s_issued, s_consumed, s_fail;
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  // 128-byte-swizzled TMA tiles and UMMA descriptors need 1024-byte
+  // aligned stage buffers
   if (smem_u32(smem) & 1023) {
-    if (threadIdx.x == 0) atomicOr(p.e.err, DEV_ERR_SMEM_ALIGN);
+    if (tid == 0) atomicOr(p.e.err, DEV_ERR_SMEM_ALIGN);
     return;
   }
   const int nt = blockIdx.x;
   const int split = blockIdx.y;
   const int mt = blockIdx.z;
-  const int tid = threadIdx.x;
-  const int warp = tid >> 5;
-  const int lane = tid & 31;
   const int per = (p.k_chunks + p.S - 1) / p.S;
   const int kc0 = split * per;
   const int kc1 = min(kc0 + per, p.k_chunks);
   const int nch = kc1 > kc0 ? kc1 - kc0 : 0;
 
   if (tid == 0) {
-    for (int s = 0; s < kLinStages; ++s) {
+    for (int s = 0; s < ST; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 4);
+      mbar_init(&empty[s], 1);
     }
+    mbar_init(accb, 1);
+    s_issued = 0;
+    s_consumed = 0;
+    s_fail = 0;
     fence_mbar_init();
   }
+  if (warp == 1) tmem_alloc(&s_tmem, TCOLS);
+  tc_fence_before();
   __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = s_tmem;
 
-  bool failed = false;
-  float acc[2][NT][4];
-#pragma unroll
-  for (int a = 0; a < 2; ++a)
-#pragma unroll
-    for (int j = 0; j < NT; ++j)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) acc[a][j][e] = 0.f;
-
-  if (warp == 4) {
+  if (warp == 0) {
     if (lane == 0) {
-      for (int c = 0; c < nch; ++c) {
-        const int s = c % kLinStages;
-        if (c >= kLinStages &&
-            !mbar_wait_bounded(&empty[s], ((c / kLinStages) - 1) & 1)) {
-          failed = true;
+      // TMA producer: weights are read once (evict first), activation tiles
+      // are shared by every CTA of the grid (evict last)
+      const uint64_t pol_w = l2_policy_evict_first();
+      const uint64_t pol_x = l2_policy_evict_last();
+      int c = 0;
+      for (; c < nch; ++c) {
+        const int s = c % ST;
+        if (c >= ST && !mbar_wait_bounded(&empty[s], ((c / ST) - 1) & 1)) {
+          s_fail = 1;
           break;
         }
         uint8_t *st = smem + s * STAGE;
         mbar_expect_tx(&full[s], STAGE);
-        const int k0 = (kc0 + c) * kLinBK;
-        tma_load_2d(st, &tw, &full[s], k0, nt * kLinBN);
-        tma_load_2d(st + W_BYTES, &ta, &full[s], k0, mt * MT);
-        tma_load_2d(st + W_BYTES + MT * 128, &ta, &full[s], k0 + 32, mt * MT);
+        const int k0 = (kc0 + c) * kTcBK;
+        tma_load_2d_hint(st, &tw, &full[s], k0, nt * kTcBN, pol_w);
+        tma_load_3d_hint(st + kTcW, &tx, &full[s], k0, mt * MT, 0, pol_x);
+        tma_load_3d_hint(st + kTcW + X_BYTES, &tx, &full[s], k0, mt * MT, 1,
+                         pol_x);
       }
+      s_issued = c;
     }
-  } else {
-    // ldmatrix lane addressing for the weight (A operand) 16x16 blocks
-    const int w_row = (lane & 7) + ((lane >> 3) & 1) * 8;
-    const int w_kof = (lane >> 4) * 8;
-    const int ar = lane >> 2;        // activation row within an n8 tile
-    const int ak = (lane & 3) * 2;   // k pair within a 16-k step
-    for (int c = 0; c < nch; ++c) {
-      const int s = c % kLinStages;
-      if (!__all_sync(0xffffffffu,
-                      mbar_wait_bounded(&full[s], (c / kLinStages) & 1))) {
-        failed = true;
-        break;
-      }
-      const uint8_t *wt = smem + s * STAGE;
-      const uint8_t *at = wt + W_BYTES;
-#pragma unroll
-      for (int kk = 0; kk < kLinBK / 16; ++kk) {
-        uint32_t wa[2][4];
-#pragma unroll
-        for (int a = 0; a < 2; ++a) {
-          const int row = warp * 32 + a * 16 + w_row;
-          const int chunk = kk * 2 + (w_kof >> 3);
-          ldsm_x4(smem_u32(wt + row * 128 + ((chunk ^ (row & 7)) << 4)),
-                  wa[a][0], wa[a][1], wa[a][2], wa[a][3]);
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // MMA issuer: D[128 x MT] += W[128 x 16] . X[MT x 16]^T per k-slice,
+      // once for the hi plane and once for the lo plane
+      int c = 0;
+      for (; c < nch; ++c) {
+        const int s = c % ST;
+        if (!mbar_wait_bounded(&full[s], (c / ST) & 1)) {
+          s_fail = 1;
+          break;
         }
+        tc_fence_after();
+        const uint32_t st = smem_u32(smem + s * STAGE);
+        const uint64_t a = umma_desc_sw128(st);
+        const uint64_t bh = umma_desc_sw128(st + kTcW);
+        const uint64_t bl = umma_desc_sw128(st + kTcW + X_BYTES);
 #pragma unroll
-        for (int j = 0; j < NT; ++j) {
-          const int m = j * 8 + ar;
-          uint32_t bh[2], bl[2];
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int k = kk * 16 + h * 8 + ak;      // 0..63, even
-            const int box = k >> 5;
-            const int chunk = (k & 31) >> 2;
-            const float2 v = *reinterpret_cast<const float2 *>(
-                at + box * (MT * 128) + m * 128 + ((chunk ^ (m & 7)) << 4) +
-                (k & 3) * 4);
-            split_bf16x2(v.x, v.y, bh[h], bl[h]);
-          }
-#pragma unroll
-          for (int a = 0; a < 2; ++a) {
-            mma_bf16(acc[a][j], wa[a], bh[0], bh[1]);
-            mma_bf16(acc[a][j], wa[a], bl[0], bl[1]);
-          }
+        for (int kk = 0; kk < kTcBK / 16; ++kk) {
+          umma_bf16(tmem, a + 2 * kk, bh + 2 * kk, IDESC, (c | kk) != 0);
+          umma_bf16(tmem, a + 2 * kk, bl + 2 * kk, IDESC, 1);
         }
+        umma_commit(&empty[s]);   // stage free once these MMAs are done
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
+      s_consumed = c;
+      umma_commit(accb);          // accumulator complete (or nothing issued)
     }
+    __syncwarp();
   }
-  if (failed) atomicOr(p.e.err, DEV_ERR_WAIT_TIMEOUT);
-  if (warp == 4) return;
 
-  // accumulator element (a, j, e): weight row
-  //   nt*128 + warp*32 + a*16 + (lane>>2) + (e >= 2 ? 8 : 0)
-  // activation row mt*MT + j*8 + (lane&3)*2 + (e & 1)
-  const int row_base = nt * kLinBN + warp * 32 + (lane >> 2);
-  const int m_base = mt * MT + (lane & 3) * 2;
-  if (p.S > 1) {
-    // write this split's partial, take a ticket, the last CTA reduces
-    const size_t ldp = (size_t)p.n_tiles * kLinBN;
-    float *part = p.partial + ((size_t)mt * p.S + split) * ldp * MT;
+  // ---- epilogue ----
+  // 1. the four warps copy the accumulator (TMEM lanes 32*warp..+31) into
+  //    shared memory, column-major: tile[m * 128 + r] (the ring is free now)
+  const bool acc_ok = mbar_wait_bounded(accb, 0);
+  tc_fence_after();
+  __syncthreads();  // s_fail / s_consumed visible
+  const bool valid = acc_ok && !s_fail && nch > 0;
+  float *tile = reinterpret_cast<float *>(smem);
+  const int r_own = warp * 32 + lane;
+  const uint32_t t_lane = tmem + ((uint32_t)(warp * 32) << 16);
+#pragma unroll 1
+  for (int c0 = 0; c0 < MT; c0 += 16) {
+    float v[16];
+    if (valid) {
+      tmem_ld16(t_lane + c0, v);
+    } else {
 #pragma unroll
-    for (int a = 0; a < 2; ++a)
-#pragma unroll
-      for (int j = 0; j < NT; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int row = row_base + a * 16 + (e >= 2 ? 8 : 0);
-          const int mm = j * 8 + (lane & 3) * 2 + (e & 1);
-          part[(size_t)row * MT + mm] = acc[a][j][e];
-        }
-    __threadfence();
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    if (tid == 0) {
-      int *ctr = p.counters + (size_t)mt * p.n_tiles + nt;
-      const int ticket = atomicAdd(ctr, 1);
-      s_last = (ticket == p.S - 1);
-      if (s_last) *ctr = 0;
+      for (int j = 0; j < 16; ++j) v[j] = 0.f;
     }
-    asm volatile("bar.sync 1, 128;" ::: "memory");
-    if (!s_last) return;
-    __threadfence();
 #pragma unroll
-    for (int a = 0; a < 2; ++a)
-#pragma unroll
-      for (int j = 0; j < NT; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int row = row_base + a * 16 + (e >= 2 ? 8 : 0);
-          const int mm = j * 8 + (lane & 3) * 2 + (e & 1);
-          float sum = 0.f;
-          for (int sp = 0; sp < p.S; ++sp)  // fixed order: deterministic
-            sum += __ldcg(&p.partial[(((size_t)mt * p.S + sp) * ldp + row) * MT + mm]);
-          acc[a][j][e] = sum;
-        }
+    for (int j = 0; j < 16; ++j) tile[(c0 + j) * kTcBN + r_own] = v[j];
   }
+  // 2. every split of this tile has staged its partial
+  const int S = p.S;
+  if (S > 1)
+    cluster_sync();
+  else
+    __syncthreads();
+  // 3. this CTA reduces items rank, rank + S, ... of the tile: an item is
+  //    one row pair (r, r + 8) at one activation column m; the splits are
+  //    summed in rank order
+  const int rank = S > 1 ? (int)cluster_ctarank() : 0;
+  const uint32_t tile_s = smem_u32(tile);
+  const int n_items = (kTcBN / 2) * MT;
+#pragma unroll 2
+  for (int it = rank * kTcThreads + tid; it < n_items; it += S * kTcThreads) {
+    const int m = it >> 6;
+    const int pr = it & 63;
+    const int r = (pr >> 3) * 16 + (pr & 7);
+    const int idx = m * kTcBN + r;
+    float v0, v1;
+    if (S == 1) {
+      v0 = tile[idx];
+      v1 = tile[idx + 8];
+    } else {
+      float a0[kTcMaxSplit], a1[kTcMaxSplit];
 #pragma unroll
-  for (int a = 0; a < 2; ++a)
+      for (int q = 0; q < kTcMaxSplit; ++q) {
+        if (q < S) {
+          a0[q] = ld_dsmem_f32(tile_s + idx * 4, q);
+          a1[q] = ld_dsmem_f32(tile_s + (idx + 8) * 4, q);
+        }
+      }
+      v0 = a0[0];
+      v1 = a1[0];
 #pragma unroll
-    for (int j = 0; j < NT; ++j)
-#pragma unroll
-      for (int e = 0; e < 2; ++e)
-        epi_pair(p.e, p.N, p.M, row_base + a * 16, m_base + j * 8 + e,
-                 acc[a][j][e], acc[a][j][e + 2]);
+      for (int q = 1; q < kTcMaxSplit; ++q) {
+        if (q < S) {
+          v0 += a0[q];
+          v1 += a1[q];
+        }
+      }
+    }
+    epi_pair<OP>(p.e, p.N, p.M, nt * kTcBN + r, mt * MT + m, v0, v1);
+  }
+  if (!acc_ok || s_fail) {
+    if (tid == 0) atomicOr(p.e.err, DEV_ERR_WAIT_TIMEOUT);
+  }
+
+  // teardown: the other CTAs of the cluster are done reading this tile, no
+  // TMEM reads in flight, no TMA writes into this CTA's shared memory left
+  // (a failed wait may have left issued stages unconsumed)
+  tc_fence_before();
+  if (S > 1)
+    cluster_sync();
+  else
+    __syncthreads();
+  if (tid == 0) {
+    for (int c = s_consumed; c < s_issued; ++c)
+      mbar_wait_bounded(&full[c % ST], (c / ST) & 1);
+  }
+  if (warp == 1) tmem_free(tmem, TCOLS);
 }
 
 // ------------------------------------------------------------------------
@@ -452,44 +455,121 @@ __global__ void __launch_bounds__(kF32Warps * 32)
         v0 = acc0[i];
         v1 = acc1[i];
       }
-    epi_pair(e, N, M, r, m0 + lane, v0, v1);
+    epi_pair_rt(e, N, M, r, m0 + lane, v0, v1);
   }
 }
 
-template <int MT>
-int launch_mma(const LinParams &p, const CUtensorMap &tw, const CUtensorMap &ta,
-               dim3 grid, cudaStream_t st) {
-  const size_t smem = (size_t)kLinStages * (kLinBN * 128 + MT * 256) +
-                      2 * kLinStages * sizeof(uint64_t);
-  auto kern = linear_mma_kernel<MT>;
+// ------------------------------------------------------------------------
+// host side
+// ------------------------------------------------------------------------
+struct TcPlan {
+  int MT, m_tiles, n_tiles, k_chunks, S, stages;
+  size_t smem;
+};
+
+int tc_mt_for(int M) {
+  return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
+}
+
+// Stages: about 100 KB of ring per CTA (two CTAs per SM), 2 to 6; the ring
+// must also hold the fp32 accumulator tile staged by the epilogue.
+int tc_stages_for(int MT) {
+  int st = (100 * 1024) / tc_stage_bytes(MT);
+  st = st < 2 ? 2 : (st > 6 ? 6 : st);
+  while (st * tc_stage_bytes(MT) < kTcBN * MT * 4) ++st;
+  return st;
+}
+
+size_t tc_smem_for(int MT, int stages) {
+  return (size_t)stages * tc_stage_bytes(MT) +
+         (2 * stages + 1) * sizeof(uint64_t);
+}
+
+TcPlan tc_plan(int M, int N, int K) {
+  TcPlan pl{};
+  pl.MT = tc_mt_for(M);
+  pl.m_tiles = (M + pl.MT - 1) / pl.MT;
+  pl.n_tiles = (N + kTcBN - 1) / kTcBN;
+  pl.k_chunks = K / kTcBK;
+  pl.stages = tc_stages_for(pl.MT);
+  pl.smem = tc_smem_for(pl.MT, pl.stages);
+  // CTAs resident at once: shared memory allows two per SM up to ~113 KB
+  const int per_sm = pl.smem <= 113 * 1024 ? 2 : 1;
+  const long slots = (long)per_sm * sm_count();
+  const long base = (long)pl.m_tiles * pl.n_tiles;
+  int S = 1;
+  if (base < slots) {
+    long s = slots / base;
+    const long by_k = pl.k_chunks / 4;  // keep >= 4 k-chunks per split
+    if (s > by_k) s = by_k;
+    if (s > kTcMaxSplit) s = kTcMaxSplit;
+    S = s < 1 ? 1 : (int)s;
+  }
+  pl.S = S;
+  return pl;
+}
+
+template <int MT, int OP>
+int launch_tc(const TcParams &p, const CUtensorMap &tw, const CUtensorMap &tx,
+              dim3 grid, size_t smem, cudaStream_t st) {
+  auto kern = linear_tc_kernel<MT, OP>;
   static bool configured[64] = {};  // per instantiation and device
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !configured[dev]) {
     TLLM_CUDA(cudaFuncSetAttribute(
-        kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
-  kern<<<grid, kLinThreads, smem, st>>>(p, tw, ta);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = p.S;   // the splits of one weight tile
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = p.S > 1 ? 1 : 0;
+  TLLM_CUDA(cudaLaunchKernelEx(&cfg, kern, p, tw, tx));
   TLLM_LAUNCH_CHECK();
   return TLLM_OK;
+}
+
+template <int MT>
+int launch_tc_op(const TcParams &p, const CUtensorMap &tw,
+                 const CUtensorMap &tx, dim3 grid, size_t smem,
+                 cudaStream_t st) {
+  switch (p.e.op) {
+    case EPI_STORE: return launch_tc<MT, EPI_STORE>(p, tw, tx, grid, smem, st);
+    case EPI_RESID: return launch_tc<MT, EPI_RESID>(p, tw, tx, grid, smem, st);
+    case EPI_GELU: return launch_tc<MT, EPI_GELU>(p, tw, tx, grid, smem, st);
+    case EPI_SWIGLU:
+      return launch_tc<MT, EPI_SWIGLU>(p, tw, tx, grid, smem, st);
+    default: return launch_tc<MT, EPI_QKV>(p, tw, tx, grid, smem, st);
+  }
 }
 
 int check_epilogue(const Epilogue &e, int N) {
   TLLM_CHECK_ARG(e.op >= EPI_STORE && e.op <= EPI_QKV, "bad epilogue op %d",
                  e.op);
   if (e.op == EPI_QKV) {
-    TLLM_CHECK_ARG(e.D > 0 && e.D % 16 == 0, "head_dim must be a multiple of 16");
+    TLLM_CHECK_ARG(e.D > 0 && e.D % 16 == 0,
+                   "head_dim must be a multiple of 16");
     TLLM_CHECK_ARG(N == (e.H + 2 * e.Hkv) * e.D,
                    "QKV rows (%d) != (H + 2 Hkv) * D", N);
     TLLM_CHECK_ARG(e.q_out && e.k_cache && e.v_cache && e.row_seq && e.row_pos,
                    "QKV epilogue needs q_out, caches, row_seq, row_pos");
-  } else if (e.op == EPI_SWIGLU) {
-    TLLM_CHECK_ARG(N % 16 == 0, "SwiGLU rows must be a multiple of 16");
-    TLLM_CHECK_ARG(e.out, "NULL output");
   } else {
-    TLLM_CHECK_ARG(e.out, "NULL output");
-    if (e.op == EPI_RESID) TLLM_CHECK_ARG(e.resid, "residual is NULL");
+    if (e.op == EPI_SWIGLU)
+      TLLM_CHECK_ARG(N % 16 == 0, "SwiGLU rows must be a multiple of 16");
+    TLLM_CHECK_ARG(e.out || e.out_split, "NULL output");
+    if (e.op == EPI_RESID) {
+      TLLM_CHECK_ARG(e.resid, "residual is NULL");
+      TLLM_CHECK_ARG(!e.out_split, "the residual output must be fp32");
+    }
   }
   return TLLM_OK;
 }
@@ -503,20 +583,20 @@ extern "C" {
 
 int tllm_linear_workspace(int M, int N, int K, size_t *partial_bytes,
                           size_t *counter_bytes) {
+  // split-K partials are reduced on chip (distributed shared memory): no
+  // global scratch is needed; the entry point stays for callers that size
+  // buffers generically
   TLLM_CHECK_ARG(partial_bytes && counter_bytes, "NULL output");
   TLLM_CHECK_ARG(M >= 0 && N >= 0 && K >= 0, "negative shape");
-  const long n_tiles = (N + kLinBN - 1) / kLinBN;
-  const long mt = M <= 64 ? 1 : (M + 63) / 64;
-  const int mtile = M <= 8 ? 8 : M <= 16 ? 16 : M <= 32 ? 32 : 64;
-  // at most 16 splits
-  *partial_bytes = (size_t)mt * 16 * n_tiles * kLinBN * mtile * sizeof(float);
-  *counter_bytes = (size_t)mt * n_tiles * sizeof(int32_t);
+  *partial_bytes = 0;
+  *counter_bytes = 0;
   return TLLM_OK;
 }
 
-// y = epilogue(x @ W^T); see tllm.h for the epilogue encoding.
-int tllm_linear(const float *x, const void *w, int w_dtype, int M, int N,
-                int K, int op, const float *bias, float *out, int ld_out,
+// y = epilogue(x @ W^T); see tllm.h for the argument encoding.
+int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
+                int w_dtype, int M, int N, int K, int op, const float *bias,
+                void *out, int out_dtype, int out_plane_rows, int ld_out,
                 const float *resid, const float *cos_t, const float *sin_t,
                 const int32_t *row_seq, const int32_t *row_pos, float *q_out,
                 void *k_cache, void *v_cache, int kv_dtype, int max_seq,
@@ -527,17 +607,25 @@ int tllm_linear(const float *x, const void *w, int w_dtype, int M, int N,
   TLLM_CHECK_ARG(M >= 0 && N >= 0 && K >= 0, "negative shape");
   if (M == 0 || N == 0) return TLLM_OK;
   TLLM_CHECK_ARG(x && w, "NULL input");
-  TLLM_CHECK_ARG(K > 0 && K % 64 == 0 || w_dtype == TLLM_F32,
-                 "bf16 linear needs K %% 64 == 0 (K=%d)", K);
-  TLLM_CHECK_ARG(K % 4 == 0, "K must be a multiple of 4");
+  TLLM_CHECK_ARG(w_dtype == TLLM_F32 || w_dtype == TLLM_BF16,
+                 "w_dtype must be F32 or BF16");
+  TLLM_CHECK_ARG(out_dtype == TLLM_F32 || out_dtype == TLLM_SPLIT,
+                 "out_dtype must be F32 or SPLIT");
   TLLM_CHECK_ARG(((uintptr_t)x & 15) == 0 && ((uintptr_t)w & 15) == 0,
                  "x and W must be 16-byte aligned");
   Epilogue e{};
   e.op = op;
   e.bias = bias;
-  e.out = out;
-  e.resid = resid;
   e.ld_out = ld_out > 0 ? ld_out : (op == EPI_SWIGLU ? N / 2 : N);
+  if (out_dtype == TLLM_SPLIT) {
+    TLLM_CHECK_ARG(out_plane_rows >= M, "out_plane_rows (%d) < M (%d)",
+                   out_plane_rows, M);
+    e.out_split = static_cast<uint16_t *>(out);
+    e.out_plane = (size_t)out_plane_rows * e.ld_out;
+  } else {
+    e.out = static_cast<float *>(out);
+  }
+  e.resid = resid;
   e.cos = cos_t;
   e.sin = sin_t;
   e.row_seq = row_seq;
@@ -558,51 +646,54 @@ int tllm_linear(const float *x, const void *w, int w_dtype, int M, int N,
   cudaStream_t st = resolve(stream);
 
   if (w_dtype == TLLM_F32) {
+    TLLM_CHECK_ARG(x_dtype == TLLM_F32, "fp32 weights take fp32 activations");
+    TLLM_CHECK_ARG(K % 4 == 0, "K must be a multiple of 4");
     const int pairs = ((N + 15) / 16) * 8;
     const int blocks = (pairs + kF32Warps - 1) / kF32Warps;
     for (int m0 = 0; m0 < M; m0 += 8) {
       linear_f32_kernel<8><<<blocks, kF32Warps * 32, 0, st>>>(
-          x, static_cast<const float *>(w), e, M, N, K, m0);
+          static_cast<const float *>(x), static_cast<const float *>(w), e, M,
+          N, K, m0);
       TLLM_LAUNCH_CHECK();
     }
     return TLLM_OK;
   }
-  TLLM_CHECK_ARG(w_dtype == TLLM_BF16, "w_dtype must be F32 or BF16");
 
-  const int MT = M <= 8 ? 8 : M <= 16 ? 16 : M <= 32 ? 32 : 64;
-  const int m_tiles = (M + MT - 1) / MT;
-  const int n_tiles = (N + kLinBN - 1) / kLinBN;
-  const int k_chunks = K / kLinBK;
-  // split K until the grid covers the device twice, >= 4 chunks per split
-  int S = 1;
-  const long base = (long)m_tiles * n_tiles;
-  while (S < 16 && base * S < 2L * sm_count() && k_chunks / (S * 2) >= 4) S *= 2;
-  if (S > 1) {
-    const size_t need = (size_t)m_tiles * S * n_tiles * kLinBN * MT * sizeof(float);
-    const size_t cneed = (size_t)m_tiles * n_tiles * sizeof(int32_t);
-    if (!partial || !counters || partial_bytes < need || cneed == 0) S = 1;
-  }
-  CUtensorMap tw, ta;
-  rc = make_map_2d(&tw, w, TLLM_BF16, K, N, (long)K * 2, kLinBK, kLinBN, true);
+  TLLM_CHECK_ARG(x_dtype == TLLM_SPLIT,
+                 "bf16 weights take TLLM_SPLIT activations (tllm_split_bf16)");
+  TLLM_CHECK_ARG(K > 0 && K % kTcBK == 0, "bf16 linear needs K %% 64 == 0 (K=%d)",
+                 K);
+  TLLM_CHECK_ARG(x_plane_rows >= M, "x_plane_rows (%d) < M (%d)", x_plane_rows,
+                 M);
+  (void)partial;
+  (void)partial_bytes;
+  (void)counters;
+  const TcPlan pl = tc_plan(M, N, K);
+  const int S = pl.S;
+  CUtensorMap tw, tx;
+  rc = make_map_2d(&tw, w, TLLM_BF16, K, N, (long)K * 2, kTcBK, kTcBN, true);
   if (rc) return rc;
-  rc = make_map_2d(&ta, x, TLLM_F32, K, M, (long)K * 4, 32, MT, true);
+  const long xd[3] = {K, x_plane_rows, 2};
+  const long xs[2] = {(long)K * 2, (long)x_plane_rows * K * 2};
+  const int xb[3] = {kTcBK, pl.MT, 1};
+  rc = make_map(&tx, x, TLLM_BF16, 3, xd, xs, xb, true);
   if (rc) return rc;
-  LinParams p;
+  TcParams p;
   p.e = e;
-  p.partial = static_cast<float *>(partial);
-  p.counters = counters;
   p.M = M;
   p.N = N;
   p.K = K;
   p.S = S;
-  p.k_chunks = k_chunks;
-  p.n_tiles = n_tiles;
-  dim3 grid(n_tiles, S, m_tiles);
-  switch (MT) {
-    case 8: return launch_mma<8>(p, tw, ta, grid, st);
-    case 16: return launch_mma<16>(p, tw, ta, grid, st);
-    case 32: return launch_mma<32>(p, tw, ta, grid, st);
-    default: return launch_mma<64>(p, tw, ta, grid, st);
+  p.k_chunks = pl.k_chunks;
+  p.n_tiles = pl.n_tiles;
+  p.stages = pl.stages;
+  dim3 grid(pl.n_tiles, S, pl.m_tiles);
+  switch (pl.MT) {
+    case 16: return launch_tc_op<16>(p, tw, tx, grid, pl.smem, st);
+    case 32: return launch_tc_op<32>(p, tw, tx, grid, pl.smem, st);
+    case 64: return launch_tc_op<64>(p, tw, tx, grid, pl.smem, st);
+    case 128: return launch_tc_op<128>(p, tw, tx, grid, pl.smem, st);
+    default: return launch_tc_op<256>(p, tw, tx, grid, pl.smem, st);
   }
 }
 

@@ -30,24 +30,37 @@ __device__ float block_sum(float v, float *red) {
 }
 
 // y = (x / sqrt(sum(x^2) / N + eps)) * w   (triton_llm/kernels/rms_norm.py:50-55)
-__global__ void rmsnorm_kernel(const float *x, const float *w, float *y, int N,
+// Row output of the norms: fp32, or TLLM_SPLIT planes `plane` elements apart.
+struct RowOut {
+  float *f;
+  uint16_t *s;
+  size_t plane;
+  __device__ __forceinline__ void put(size_t i, float v) const {
+    if (s)
+      store_split(s, plane, i, v);
+    else
+      f[i] = v;
+  }
+};
+
+__global__ void rmsnorm_kernel(const float *x, const float *w, RowOut y, int N,
                                float eps) {
   __shared__ float red[32];
   const float *xr = x + (size_t)blockIdx.x * N;
-  float *yr = y + (size_t)blockIdx.x * N;
+  const size_t o = (size_t)blockIdx.x * N;
   float ss = 0.f;
   for (int i = threadIdx.x; i < N; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
   ss = block_sum(ss, red);
   const float rms = sqrtf(ss / (float)N + eps);
-  for (int i = threadIdx.x; i < N; i += blockDim.x) yr[i] = (xr[i] / rms) * w[i];
+  for (int i = threadIdx.x; i < N; i += blockDim.x) y.put(o + i, (xr[i] / rms) * w[i]);
 }
 
 // two-pass LayerNorm (triton_llm/kernels/layernorm.py:56-66)
 __global__ void layernorm_kernel(const float *x, const float *g, const float *b,
-                                 float *y, int N, float eps) {
+                                 RowOut y, int N, float eps) {
   __shared__ float red[32];
   const float *xr = x + (size_t)blockIdx.x * N;
-  float *yr = y + (size_t)blockIdx.x * N;
+  const size_t o = (size_t)blockIdx.x * N;
   float s = 0.f;
   for (int i = threadIdx.x; i < N; i += blockDim.x) s += xr[i];
   const float mean = block_sum(s, red) / (float)N;
@@ -59,7 +72,14 @@ __global__ void layernorm_kernel(const float *x, const float *g, const float *b,
   const float var = block_sum(v, red) / (float)N;
   const float rstd = 1.f / sqrtf(var + eps);
   for (int i = threadIdx.x; i < N; i += blockDim.x)
-    yr[i] = (xr[i] - mean) * rstd * g[i] + b[i];
+    y.put(o + i, (xr[i] - mean) * rstd * g[i] + b[i]);
+}
+
+// fp32 (rows, cols) -> TLLM_SPLIT planes of plane_rows rows
+__global__ void split_kernel(const float *x, uint16_t *y, long n, size_t plane) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n;
+       i += (long)gridDim.x * blockDim.x)
+    store_split(y, plane, (size_t)i, x[i]);
 }
 
 // out[m] = wte[ids[m]] (+ wpe[pos[m]])   (triton_llm/kernels/embedding.py:75-94,
@@ -306,27 +326,68 @@ using namespace tllm;
 
 extern "C" {
 
-int tllm_rmsnorm(const float *x, const float *w, float *y, int M, int N,
-                 float eps, tllm_stream_t stream) {
+static int row_out(RowOut *o, void *y, int y_dtype, int y_plane_rows, int M,
+                   int N) {
+  TLLM_CHECK_ARG(y_dtype == TLLM_F32 || y_dtype == TLLM_SPLIT,
+                 "y_dtype must be F32 or SPLIT");
+  o->f = nullptr;
+  o->s = nullptr;
+  o->plane = 0;
+  if (y_dtype == TLLM_SPLIT) {
+    TLLM_CHECK_ARG(y_plane_rows >= M, "y_plane_rows (%d) < M (%d)",
+                   y_plane_rows, M);
+    o->s = static_cast<uint16_t *>(y);
+    o->plane = (size_t)y_plane_rows * N;
+  } else {
+    o->f = static_cast<float *>(y);
+  }
+  return TLLM_OK;
+}
+
+int tllm_rmsnorm(const float *x, const float *w, void *y, int y_dtype,
+                 int y_plane_rows, int M, int N, float eps,
+                 tllm_stream_t stream) {
   TLLM_INJECT("launch");
   TLLM_CHECK_ARG(M >= 0 && N >= 0, "negative shape");
   if (M == 0) return TLLM_OK;
   TLLM_CHECK_ARG(N > 0, "RMSNorm requires the last dimension N > 0");
   TLLM_CHECK_ARG(x && w && y, "NULL pointer");
+  RowOut o;
+  int rc = row_out(&o, y, y_dtype, y_plane_rows, M, N);
+  if (rc) return rc;
   rmsnorm_kernel<<<M, row_threads(N) > 256 ? 256 : row_threads(N), 0,
-                   resolve(stream)>>>(x, w, y, N, eps);
+                   resolve(stream)>>>(x, w, o, N, eps);
   TLLM_LAUNCH_CHECK();
   return TLLM_OK;
 }
 
-int tllm_layernorm(const float *x, const float *g, const float *b, float *y,
-                   int M, int N, float eps, tllm_stream_t stream) {
+int tllm_layernorm(const float *x, const float *g, const float *b, void *y,
+                   int y_dtype, int y_plane_rows, int M, int N, float eps,
+                   tllm_stream_t stream) {
   TLLM_INJECT("launch");
   TLLM_CHECK_ARG(M >= 0 && N >= 0, "negative shape");
   if (M == 0) return TLLM_OK;
   TLLM_CHECK_ARG(N > 0, "LayerNorm requires the last dimension N > 0");
   TLLM_CHECK_ARG(x && g && b && y, "NULL pointer");
-  layernorm_kernel<<<M, 256, 0, resolve(stream)>>>(x, g, b, y, N, eps);
+  RowOut o;
+  int rc = row_out(&o, y, y_dtype, y_plane_rows, M, N);
+  if (rc) return rc;
+  layernorm_kernel<<<M, 256, 0, resolve(stream)>>>(x, g, b, o, N, eps);
+  TLLM_LAUNCH_CHECK();
+  return TLLM_OK;
+}
+
+int tllm_split_bf16(const float *x, void *y, int rows, int cols,
+                    int plane_rows, tllm_stream_t stream) {
+  TLLM_INJECT("launch");
+  TLLM_CHECK_ARG(rows >= 0 && cols >= 0, "negative shape");
+  if (rows == 0 || cols == 0) return TLLM_OK;
+  TLLM_CHECK_ARG(x && y, "NULL pointer");
+  TLLM_CHECK_ARG(plane_rows >= rows, "plane_rows (%d) < rows (%d)", plane_rows,
+                 rows);
+  const long n = (long)rows * cols;
+  split_kernel<<<grid_for(n, 256), 256, 0, resolve(stream)>>>(
+      x, static_cast<uint16_t *>(y), n, (size_t)plane_rows * cols);
   TLLM_LAUNCH_CHECK();
   return TLLM_OK;
 }

@@ -55,4 +55,38 @@ int make_map_2d(CUtensorMap *m, const void *base, int dtype, long inner,
   return TLLM_OK;
 }
 
+// N-d tiled map (rank 2..5): dims[0] innermost, strides_bytes[i] = stride of
+// dim i+1.
+int make_map(CUtensorMap *m, const void *base, int dtype, int rank,
+             const long *dims, const long *strides_bytes, const int *box,
+             bool swizzle128) {
+  auto fn = tensor_map_encoder();
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled is not available from the driver");
+    return TLLM_ERR_CUDA;
+  }
+  cuuint64_t d[5], st[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = (cuuint64_t)dims[i];
+    b[i] = (cuuint32_t)box[i];
+    e[i] = 1;
+    if (i + 1 < rank) st[i] = (cuuint64_t)strides_bytes[i];
+  }
+  CUtensorMapDataType t = dtype == TLLM_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                             : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  CUresult r = fn(m, t, rank, const_cast<void *>(base), d, st, b, e,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                             : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled(%dd) failed (%d): dims %ld x %ld box %d x %d",
+              rank, (int)r, dims[0], dims[1], box[0], box[1]);
+    return TLLM_ERR_CUDA;
+  }
+  return TLLM_OK;
+}
+
 }  // namespace tllm

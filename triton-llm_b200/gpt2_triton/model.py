@@ -20,7 +20,7 @@ import time
 import numpy as np
 
 from triton_llm import gpu, _lib
-from triton_llm.kernels import gqa_decode, gqa_rows, DecodeWorkspace, softmax
+from triton_llm.kernels import gqa_rows, DecodeWorkspace, softmax
 from triton_llm.kernels.embedding import embedding_dev
 from triton_llm.kernels.layernorm import layer_norm_dev
 from triton_llm.kernels.linear import Linear, LinearWorkspace, linear, qkv_rows
@@ -72,9 +72,11 @@ class GPT2Model:
             return
         c, n = self.config, self.n
         f = lambda *s: gpu.allocate(s, np.float32)  # noqa: E731
-        self.h, self.x = f(M, n), f(M, n)
-        self.q, self.attn = f(M, self.H, self.D), f(M, n)
-        self.act, self.logits = f(M, 4 * n), f(M, c.vocab_size)
+        # projection inputs in the tensor-core operand format for bf16 weights
+        a = (lambda r, k: gpu.split_empty(r, k)) if self.bf16 else f  # noqa: E731
+        self.h, self.x = f(M, n), a(M, n)
+        self.q, self.attn = f(M, self.H, self.D), a(M, n)
+        self.act, self.logits = a(M, 4 * n), f(M, c.vocab_size)
         self.ids_d = gpu.allocate((M,), np.int32)
         self.pos_d = gpu.allocate((M,), np.int32)
         self.len_d = gpu.allocate((M,), np.int32)
@@ -116,8 +118,7 @@ class GPT2Model:
             self.attn_ws = DecodeWorkspace(max(M, 1), H, H, D, self._max_seq, kvd)
         for i, L in enumerate(self.layers):
             kv = self.kv_cache[i]
-            layer_norm_dev(gpu.sub_view(h, 0, (M, n)), L["ln1"][0], L["ln1"][1],
-                           gpu.sub_view(x, 0, (M, n)), c.layer_norm_epsilon)
+            layer_norm_dev(h, L["ln1"][0], L["ln1"][1], x, c.layer_norm_epsilon, M=M)
             linear(x, L["qkv"], op=_lib.EPI_QKV, ws=self.lin_ws, M=M, qkv=dict(
                 row_seq=self.seq_d, row_pos=self.pos_d, q_out=self.q,
                 k_cache=kv["k"], v_cache=kv["v"], n_head=H, n_kv_head=H, head_dim=D))
@@ -125,13 +126,11 @@ class GPT2Model:
                      H * D, D, H * D, D, prev + M, workspace=self.attn_ws)
             linear(self.attn, L["proj"], out_dev=h, op=_lib.EPI_RESID, resid_dev=h,
                    ws=self.lin_ws, M=M)
-            layer_norm_dev(gpu.sub_view(h, 0, (M, n)), L["ln2"][0], L["ln2"][1],
-                           gpu.sub_view(x, 0, (M, n)), c.layer_norm_epsilon)
+            layer_norm_dev(h, L["ln2"][0], L["ln2"][1], x, c.layer_norm_epsilon, M=M)
             linear(x, L["fc"], out_dev=self.act, op=_lib.EPI_GELU, ws=self.lin_ws, M=M)
             linear(self.act, L["mproj"], out_dev=h, op=_lib.EPI_RESID, resid_dev=h,
                    ws=self.lin_ws, M=M)
-        layer_norm_dev(gpu.sub_view(h, 0, (M, n)), self.ln_f[0], self.ln_f[1],
-                       gpu.sub_view(x, 0, (M, n)), c.layer_norm_epsilon)
+        layer_norm_dev(h, self.ln_f[0], self.ln_f[1], x, c.layer_norm_epsilon, M=M)
         linear(x, self.lm_head, out_dev=self.logits, ws=self.lin_ws, M=M)
         return gpu.sub_view(self.logits, 0, (M, c.vocab_size)).to_numpy()
 

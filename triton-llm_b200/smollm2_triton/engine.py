@@ -22,6 +22,12 @@ can be captured as one CUDA graph.
 
 KV cache layout: per layer k and v (B, n_kv_head, max_seq, head_dim), the
 reference's (n_kv_head, max_seq, d_k) (model.py:219-225) with a batch axis.
+
+Activation buffers that only feed projections (the normed x, the attention
+output, the SwiGLU output) are kept in the tensor-core operand format
+(TLLM_SPLIT, two bf16 planes) when the weights are bf16: the kernels that
+produce them write that format directly. The residual stream h, q and the
+logits stay fp32.
 """
 
 from __future__ import annotations
@@ -29,9 +35,10 @@ from __future__ import annotations
 import numpy as np
 
 from triton_llm import gpu, _lib
-from triton_llm.kernels import gqa_decode, gqa_rows, DecodeWorkspace
+from triton_llm.kernels import gqa_rows, DecodeWorkspace
 from triton_llm.kernels.linear import (Linear, LinearWorkspace, linear, qkv_rows,
                                        swiglu_rows)
+from triton_llm.kernels.rms_norm import rms_norm_rows
 from triton_llm.kernels.rope import precompute_cos_sin
 from triton_llm.kernels.embedding import embedding_dev
 
@@ -184,25 +191,31 @@ class LlamaSession:
             self._prefill_buffers(max_prefill_rows, attn_budget_bytes)
         self.graph = None
 
+    def _act(self, rows, cols):
+        """A projection-input buffer: TLLM_SPLIT for bf16 weights, else fp32."""
+        if self.w.bf16:
+            return gpu.split_empty(rows, cols)
+        return gpu.allocate((rows, cols), np.float32)
+
     def _buffers(self, M):
         w = self.w
         f = lambda *s: gpu.allocate(s, np.float32)  # noqa: E731
-        self.h, self.x = f(M, w.n), f(M, w.n)
-        self.q, self.attn = f(M, w.H, w.D), f(M, w.H * w.D)
-        self.act, self.logits = f(M, w.F), f(M, w.V)
+        self.h, self.x = f(M, w.n), self._act(M, w.n)
+        self.q, self.attn = f(M, w.H, w.D), self._act(M, w.H * w.D)
+        self.act, self.logits = self._act(M, w.F), f(M, w.V)
 
     def _prefill_buffers(self, M, attn_budget):
         w = self.w
         f = lambda *s: gpu.allocate(s, np.float32)  # noqa: E731
-        self.p_h, self.p_x = f(M, w.n), f(M, w.n)
-        self.p_q, self.p_attn = f(M, w.H, w.D), f(M, w.H * w.D)
-        self.p_act = f(M, w.F)
+        self.p_h, self.p_x = f(M, w.n), self._act(M, w.n)
+        self.p_q, self.p_attn = f(M, w.H, w.D), self._act(M, w.H * w.D)
+        self.p_act = self._act(M, w.F)
         self.p_ids = gpu.allocate((M,), np.int32)
         self.p_seq = gpu.allocate((M,), np.int32)
         self.p_pos = gpu.allocate((M,), np.int32)
         self.p_len = gpu.allocate((M,), np.int32)
         self.p_last = gpu.allocate((self.B,), np.int32)
-        self.p_lin_ws = LinearWorkspace(w.linear_shapes(M)[:4])
+        self.p_lin_ws = LinearWorkspace(w.linear_shapes(M))
         ws = DecodeWorkspace.__new__(DecodeWorkspace)
         ws.partial_bytes = int(attn_budget)
         ws.partial = gpu.allocate((max(attn_budget // 4, 1),), np.float32)
@@ -216,19 +229,18 @@ class LlamaSession:
         w = self.w
         L = w.layers[i]
         k, v = self.kv[i]
-        _lib.call("tllm_rmsnorm", h.ptr, L["ln1"].ptr, x.ptr, M, w.n, w.eps, None)
+        rms_norm_rows(h, L["ln1"], x, M, w.eps)
         linear(x, L["qkv"], op=_lib.EPI_QKV, ws=ws, M=M, qkv=dict(
             cos=w.cos, sin=w.sin, row_seq=row_seq, row_pos=row_pos, q_out=q,
             k_cache=k, v_cache=v, n_head=w.H, n_kv_head=w.Hkv, head_dim=w.D,
             lens_out=lens if decode else None))
-        if decode:
-            gqa_decode(q, k, v, lens, gpu.view(attn, (M, w.H, w.D)), max_len=self.S,
-                       workspace=attn_ws)
-        else:
-            gqa_rows(q, k, v, row_seq, row_len, attn, M, w.H, w.H * w.D, w.D,
-                     w.H * w.D, w.D, max_len or self.S, workspace=attn_ws)
+        # decode: row b reads its own sequence for lens[b] keys (set by the
+        # QKV epilogue); prefill: row r reads its sequence's causal prefix
+        gqa_rows(q, k, v, row_seq, lens if decode else row_len, attn, M, w.H,
+                 w.H * w.D, w.D, w.H * w.D, w.D, self.S if decode else (max_len or self.S),
+                 workspace=attn_ws)
         linear(attn, L["o"], out_dev=h, op=_lib.EPI_RESID, resid_dev=h, ws=ws, M=M)
-        _lib.call("tllm_rmsnorm", h.ptr, L["ln2"].ptr, x.ptr, M, w.n, w.eps, None)
+        rms_norm_rows(h, L["ln2"], x, M, w.eps)
         linear(x, L["gu"], out_dev=act, op=_lib.EPI_SWIGLU, ws=ws, M=M)
         linear(act, L["down"], out_dev=h, op=_lib.EPI_RESID, resid_dev=h, ws=ws, M=M)
 
@@ -269,7 +281,7 @@ class LlamaSession:
                         row_len=self.p_len, max_len=int(lens.max()))
         if all_logits:
             logits = gpu.allocate((M, w.V), np.float32)
-            _lib.call("tllm_rmsnorm", h.ptr, w.norm.ptr, x.ptr, M, w.n, w.eps, None)
+            rms_norm_rows(h, w.norm, x, M, w.eps)
             linear(x, w.lm_head, out_dev=logits, ws=self.p_lin_ws, M=M)
             host = logits.to_numpy()
             last_rows = np.cumsum(lens) - 1
@@ -280,8 +292,7 @@ class LlamaSession:
             for b, r in enumerate(last_rows):
                 gpu.copy_d2d(gpu.sub_view(self.h, b * w.n * 4, (w.n,)),
                              gpu.sub_view(h, int(r) * w.n * 4, (w.n,)))
-            _lib.call("tllm_rmsnorm", self.h.ptr, w.norm.ptr, self.x.ptr, nseq, w.n,
-                      w.eps, None)
+            rms_norm_rows(self.h, w.norm, self.x, nseq, w.eps)
             linear(self.x, w.lm_head, out_dev=self.logits, ws=self.lin_ws, M=nseq)
             host = self.logits.to_numpy()[:nseq]
             next_ids = np.argmax(host, axis=-1).astype(np.int32)
@@ -314,7 +325,7 @@ class LlamaSession:
             self._layer(i, B, self.h, self.x, self.q, self.attn, self.act,
                         self.row_seq, self.pos, self.lens, self.lin_ws, True,
                         self.attn_ws)
-        _lib.call("tllm_rmsnorm", self.h.ptr, w.norm.ptr, self.x.ptr, B, w.n, w.eps, None)
+        rms_norm_rows(self.h, w.norm, self.x, B, w.eps)
         linear(self.x, w.lm_head, out_dev=self.logits, ws=self.lin_ws, M=B)
         n = 1 + 7 * w.L + 2
         if sample:
@@ -337,6 +348,20 @@ class LlamaSession:
             self.graph.launch()
         else:
             self.decode_step(True)
+
+    def step_host(self, ids_in: np.ndarray | None, ids_out: np.ndarray) -> None:
+        """One serving-loop step with host token buffers.
+
+        Copies ``ids_in`` (B int32, pinned host memory, or None to keep the
+        device's own next tokens) to the device, runs one greedy decode step
+        (the captured graph when there is one) and copies the sampled tokens
+        into ``ids_out`` (B int32, pinned), then waits for the copy.
+        """
+        if ids_in is not None:
+            gpu.copy_h2d_async(self.ids, ids_in)
+        self.step()
+        gpu.copy_d2h_async(ids_out, self.ids)
+        gpu.stream_synchronize()
 
     def kv_bytes_per_step(self, lens: np.ndarray) -> int:
         w = self.w

@@ -34,6 +34,7 @@ ERR_INJECTED = 7
 F32 = 0
 BF16 = 1
 I32 = 2
+SPLIT = 3   # fp32 values as two bf16 planes (hi, lo): tensor-core operand format
 
 _vp = ctypes.c_void_p
 _i = ctypes.c_int
@@ -86,17 +87,18 @@ SIGNATURES: dict[str, list] = {
                         _f, _vp, _sz, _vp, _vp],
     "tllm_gqa_decode_noalloc": [_vp, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _i,
                                 _i, _i, _f, _vp],
-    "tllm_gqa_rows": [_vp, _l, _l, _vp, _vp, _i, _vp, _vp, _vp, _l, _l, _i, _i,
-                      _i, _i, _i, _i, _i, _f, _vp, _sz, _vp, _vp],
+    "tllm_gqa_rows": [_vp, _l, _l, _vp, _vp, _i, _vp, _vp, _vp, _i, _l, _l, _l,
+                      _i, _i, _i, _i, _i, _i, _i, _f, _vp, _sz, _vp, _vp],
     # projections
     "tllm_linear_workspace": [_i, _i, _i, _psz, _psz],
-    "tllm_linear": [_vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _i, _vp, _vp, _vp,
-                    _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _sz,
-                    _vp, _vp],
+    "tllm_linear": [_vp, _i, _i, _vp, _i, _i, _i, _i, _i, _vp, _vp, _i, _i, _i,
+                    _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i,
+                    _vp, _vp, _sz, _vp, _vp],
     "tllm_gemm_f32": [_vp, _vp, _vp, _i, _i, _i, _vp],
     # rows / elementwise
-    "tllm_rmsnorm": [_vp, _vp, _vp, _i, _i, _f, _vp],
-    "tllm_layernorm": [_vp, _vp, _vp, _vp, _i, _i, _f, _vp],
+    "tllm_rmsnorm": [_vp, _vp, _vp, _i, _i, _i, _i, _f, _vp],
+    "tllm_layernorm": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp],
+    "tllm_split_bf16": [_vp, _vp, _i, _i, _i, _vp],
     "tllm_embedding": [_vp, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _vp],
     "tllm_argmax": [_vp, _i, _i, _i, _vp, _vp, _vp],
     "tllm_rope": [_vp, _vp, _vp, _i, _i, _i, _i, _vp],

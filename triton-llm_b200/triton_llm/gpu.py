@@ -98,6 +98,7 @@ class DeviceTensor:
         self._defer_free = defer_free
         self._base = base
         self.device = device
+        self.is_split = False   # TLLM_SPLIT activation buffer (split_empty)
 
     def __del__(self):
         if not getattr(self, "_defer_free", False):
@@ -213,6 +214,53 @@ def to_host(tensor: DeviceTensor):
     if tensor.is_bf16:
         return bf16_bits_to_f32(out)
     return out
+
+
+def split_empty(rows: int, cols: int) -> DeviceTensor:
+    """An activation buffer in the tensor-core operand format (TLLM_SPLIT):
+    shape (2, rows, cols) of bf16, plane 0 = bf16(x), plane 1 = bf16(x - hi).
+    Kernels that take activations accept it wherever they accept fp32."""
+    t = allocate((2, int(rows), int(cols)), BFLOAT16)
+    t.is_split = True
+    return t
+
+
+def split_host(arr: np.ndarray):
+    """(hi, lo) bf16 bit planes of an fp32 array, as the device computes them."""
+    a = np.ascontiguousarray(arr, dtype=np.float32)
+    hi = f32_to_bf16_bits(a)
+    lo = f32_to_bf16_bits(a - bf16_bits_to_f32(hi))
+    return hi, lo
+
+
+def to_device_split(arr: np.ndarray, plane_rows: int | None = None) -> DeviceTensor:
+    """Upload an fp32 (rows, cols) array in the TLLM_SPLIT format."""
+    a = np.ascontiguousarray(arr, dtype=np.float32)
+    rows, cols = a.shape
+    pr = rows if plane_rows is None else int(plane_rows)
+    hi, lo = split_host(a)
+    planes = np.zeros((2, pr, cols), np.uint16)
+    planes[0, :rows], planes[1, :rows] = hi, lo
+    t = split_empty(pr, cols)
+    t.from_numpy(planes)
+    return t
+
+
+def split_to_host(t: DeviceTensor, rows: int | None = None) -> np.ndarray:
+    """hi + lo of a TLLM_SPLIT buffer as fp32 (rows, cols)."""
+    planes = t.to_numpy()
+    n = planes.shape[1] if rows is None else int(rows)
+    hi = bf16_bits_to_f32(planes[0, :n])
+    lo = bf16_bits_to_f32(planes[1, :n])
+    return (hi + lo).astype(np.float32)
+
+
+def act_args(t: DeviceTensor):
+    """(pointer, dtype code, rows per plane) of an activation buffer: fp32
+    (rows, cols) or TLLM_SPLIT (2, rows, cols)."""
+    if getattr(t, "is_split", False):
+        return t.ptr, _lib.SPLIT, int(t.shape[1])
+    return t.ptr, _lib.F32, int(t.shape[0])
 
 
 def synchronize():
@@ -335,12 +383,18 @@ def pinned_empty(shape, dtype=np.float32) -> np.ndarray:
 
 def copy_h2d_async(dst: DeviceTensor, src: np.ndarray, stream=None, nbytes=None):
     n = dst.nbytes if nbytes is None else int(nbytes)
+    if n > dst.nbytes or n > src.nbytes or not src.flags["C_CONTIGUOUS"]:
+        raise ValueError(f"copy of {n} bytes: device buffer {dst.nbytes}, "
+                         f"host buffer {src.nbytes} (contiguous required)")
     _lib.call("tllm_memcpy_h2d_async", dst.ptr,
               src.ctypes.data_as(ctypes.c_void_p), n, stream)
 
 
 def copy_d2h_async(dst: np.ndarray, src: DeviceTensor, stream=None, nbytes=None):
     n = src.nbytes if nbytes is None else int(nbytes)
+    if n > dst.nbytes or n > src.nbytes or not dst.flags["C_CONTIGUOUS"]:
+        raise ValueError(f"copy of {n} bytes: device buffer {src.nbytes}, "
+                         f"host buffer {dst.nbytes} (contiguous required)")
     _lib.call("tllm_memcpy_d2h_async", dst.ctypes.data_as(ctypes.c_void_p),
               src.ptr, n, stream)
 

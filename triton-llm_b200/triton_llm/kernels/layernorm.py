@@ -11,10 +11,14 @@ import numpy as np
 from triton_llm import gpu, _lib
 
 
-def layer_norm_dev(x_dev, g_dev, b_dev, out_dev, eps=1e-5):
-    M, N = x_dev.shape
-    _lib.call("tllm_layernorm", x_dev.ptr, g_dev.ptr, b_dev.ptr, out_dev.ptr, M, N,
-              float(eps), None)
+def layer_norm_dev(x_dev, g_dev, b_dev, out_dev, eps=1e-5, M=None):
+    """LayerNorm of the first M rows of x (all rows by default); the output
+    is fp32 or in the tensor-core operand format (``gpu.split_empty``)."""
+    N = int(x_dev.shape[-1])
+    M = int(x_dev.shape[0]) if M is None else int(M)
+    ptr, dt, plane = gpu.act_args(out_dev)
+    _lib.call("tllm_layernorm", x_dev.ptr, g_dev.ptr, b_dev.ptr, ptr, dt, plane, M,
+              N, float(eps), None)
     return out_dev
 
 

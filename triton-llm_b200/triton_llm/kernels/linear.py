@@ -82,20 +82,43 @@ class LinearWorkspace:
         self.counters = gpu.zeros((max(cb_max // 4, 1),), np.int32)
 
 
+def to_split(x_dev, M=None, out=None):
+    """fp32 (rows, K) -> TLLM_SPLIT buffer (the bf16 tensor-core operand)."""
+    rows, K = int(x_dev.shape[0]), int(x_dev.shape[-1])
+    M = rows if M is None else int(M)
+    if out is None:
+        out = gpu.split_empty(rows, K)
+    _lib.call("tllm_split_bf16", x_dev.ptr, out.ptr, M, K, int(out.shape[1]), None)
+    return out
+
+
 def linear(x_dev, lin: Linear, out_dev=None, op=_lib.EPI_STORE, resid_dev=None,
            ws: LinearWorkspace | None = None, M=None, ld_out=0, qkv=None,
            stream=None):
-    """Run one projection. ``qkv`` = dict(cos, sin, row_seq, row_pos, q_out,
-    k_cache, v_cache, n_head, n_kv_head, head_dim, lens_out) for op QKV."""
-    M = int(x_dev.shape[0]) if M is None else int(M)
+    """Run one projection on the first M rows of ``x_dev``.
+
+    ``x_dev``: fp32 (rows, K) or TLLM_SPLIT (2, rows, K) (``gpu.split_empty``);
+    bf16 weights take TLLM_SPLIT, and fp32 input is converted first.
+    ``out_dev``: fp32 or TLLM_SPLIT. ``qkv`` = dict(cos, sin, row_seq,
+    row_pos, q_out, k_cache, v_cache, n_head, n_kv_head, head_dim, lens_out)
+    for op QKV.
+    """
+    split_in = getattr(x_dev, "is_split", False)
+    rows = int(x_dev.shape[1] if split_in else x_dev.shape[0])
+    M = rows if M is None else int(M)
     K = int(x_dev.shape[-1])
     if K != lin.K:
         raise ValueError(f"linear: x has K={K}, weight has K={lin.K}")
+    if lin.bf16 and not split_in:
+        x_dev = to_split(x_dev, M)
+    xptr, xdt, xplane = gpu.act_args(x_dev)
+    optr, odt, oplane = (gpu.act_args(out_dev) if out_dev is not None
+                         else (None, _lib.F32, 0))
     q = qkv or {}
     kc = q.get("k_cache")
     _lib.call(
-        "tllm_linear", x_dev.ptr, lin.w.ptr, lin.dtype, M, lin.N, lin.K, int(op),
-        _lib.ptr(lin.b), _lib.ptr(out_dev), int(ld_out), _lib.ptr(resid_dev),
+        "tllm_linear", xptr, xdt, xplane, lin.w.ptr, lin.dtype, M, lin.N, lin.K,
+        int(op), _lib.ptr(lin.b), optr, odt, oplane, int(ld_out), _lib.ptr(resid_dev),
         _lib.ptr(q.get("cos")), _lib.ptr(q.get("sin")), _lib.ptr(q.get("row_seq")),
         _lib.ptr(q.get("row_pos")), _lib.ptr(q.get("q_out")), _lib.ptr(kc),
         _lib.ptr(q.get("v_cache")),

@@ -1,4 +1,9 @@
-"""RMSNorm (drop-in for triton_llm/kernels/rms_norm.py:68-115)."""
+"""RMSNorm (drop-in for triton_llm/kernels/rms_norm.py:68-115).
+
+``rms_norm`` keeps the reference signature (fp32 device tensors);
+``rms_norm_rows`` is the model entry: the first M rows of x, output fp32 or
+in the tensor-core operand format (``gpu.split_empty``).
+"""
 
 from __future__ import annotations
 
@@ -16,5 +21,14 @@ def rms_norm(x_dev: "gpu.DeviceTensor", w_dev: "gpu.DeviceTensor",
         return out_dev
     if N == 0:
         raise ValueError("RMSNorm requires the last dimension N > 0")
-    _lib.call("tllm_rmsnorm", x_dev.ptr, w_dev.ptr, out_dev.ptr, M, N, float(eps), None)
+    _lib.call("tllm_rmsnorm", x_dev.ptr, w_dev.ptr, out_dev.ptr, _lib.F32, M, M, N,
+              float(eps), None)
+    return out_dev
+
+
+def rms_norm_rows(x_dev, w_dev, out_dev, M: int, eps: float = 1e-5, stream=None):
+    N = int(x_dev.shape[-1])
+    ptr, dt, plane = gpu.act_args(out_dev)
+    _lib.call("tllm_rmsnorm", x_dev.ptr, w_dev.ptr, ptr, dt, plane, int(M), N,
+              float(eps), stream)
     return out_dev
