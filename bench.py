@@ -199,6 +199,7 @@ class LlamaDecodeWorkload:
     name = "llama3b"
     scaling = "weak"
     dtype = "bf16"
+    act = "bfloat16"
     model = "Llama-3.2-3B-Instruct"
     per_rank = 64
     lo, hi = 1024, 8192
@@ -227,6 +228,7 @@ class LlamaDecodeWorkload:
                        "partitioned by total context",
                 "sum_ctx_this_rank": int(self.lens.sum()),
                 "weights": "random N(0,0.02) bf16 (seed 0), tied embeddings",
+                "projection_inputs": ("bf16 hi/lo planes" if self.act == "split" else "bf16"),
                 "kv_cache": f"bf16 (B, 8, {self.S}, 128) per layer, filled N(0,1)",
                 "parallelism": f"dp{self.ranks.world} (independent replicas, no collective)",
                 "timed": "K steps, each one CUDA-graph replay of the full decode step "
@@ -243,7 +245,7 @@ class LlamaDecodeWorkload:
         cfg = SmolLM2Config.from_pretrained(self.model)
         self.cfg = cfg
         self.wts = LlamaWeights(cfg, None, "bfloat16", seed=0, std=0.02, max_pos=self.S)
-        self.sess = LlamaSession(self.wts, self.B, self.S)
+        self.sess = LlamaSession(self.wts, self.B, self.S, act_dtype=self.act)
         s = self.sess
         _lib.call("tllm_fill_random", s.kv_arena.ptr, _lib.BF16,
                   int(np.prod(s.kv_arena.shape)), 1000 + self.ranks.rank, 1.0, None)
@@ -685,8 +687,9 @@ class ProjLlamaLayerWorkload(_IsolatedWorkload):
     weights N(0, 0.02), fp32 activations."""
 
     name = "proj_llama3b"
-    kernel = "linear_tc_kernel<64, op>"
+    kernel = "linear_tc_kernel<64, op, planes>"
     copies = 4
+    planes = 1
 
     def setup(self):
         from triton_llm import gpu, _lib
@@ -698,24 +701,24 @@ class ProjLlamaLayerWorkload(_IsolatedWorkload):
         self.shapes = [(B, (H + 2 * Hkv) * D, n), (B, n, H * D), (B, 2 * F, n), (B, n, F)]
 
         def lin(N, K, seed):
-            o = Linear.__new__(Linear)
-            o.N, o.K, o.bf16, o.b = N, K, True, None
-            o.w = gpu.allocate((N, K), gpu.BFLOAT16)
-            _lib.call("tllm_fill_random", o.w.ptr, _lib.BF16, N * K, seed, 0.02, None)
+            o = Linear.empty_bf16(N, K)
+            _lib.call("tllm_fill_random", o.w.ptr, _lib.BF16, int(o.w.shape[0]), seed,
+                      0.02, None)
             return o
         self.layers = [[lin(N, K, 10 * c + j) for j, (_, N, K) in enumerate(self.shapes)]
                        for c in range(self.copies)]
-        # projection inputs in the tensor-core operand format (bf16 planes)
-        self.x, self.attn, self.act = (gpu.split_empty(B, n), gpu.split_empty(B, H * D),
-                                       gpu.split_empty(B, F))
+        # projection inputs in the tensor-core operand format
+        pl = self.planes
+        self.x, self.attn, self.act = (gpu.act_empty(B, n, pl), gpu.act_empty(B, H * D, pl),
+                                       gpu.act_empty(B, F, pl))
         self.h = gpu.allocate((B, n), np.float32)
         _lib.call("tllm_fill_random", self.h.ptr, _lib.F32, B * n, 2, 1.0, None)
         for t, sd in ((self.x, 1), (self.attn, 3), (self.act, 4)):
             src = gpu.allocate((t.shape[1], t.shape[2]), np.float32)
             _lib.call("tllm_fill_random", src.ptr, _lib.F32, int(np.prod(src.shape)), sd,
                       1.0, None)
-            _lib.call("tllm_split_bf16", src.ptr, t.ptr, t.shape[1], t.shape[2],
-                      t.shape[1], None)
+            _lib.call("tllm_split_bf16", src.ptr, t.ptr, gpu.act_args(t)[1], t.shape[1],
+                      t.shape[2], t.shape[1], None)
         self.q = gpu.allocate((B, H, D), np.float32)
         self.kc = gpu.zeros((B, Hkv, 64, D), gpu.BFLOAT16)
         self.vc = gpu.zeros((B, Hkv, 64, D), gpu.BFLOAT16)
@@ -759,10 +762,13 @@ class ProjLlamaLayerWorkload(_IsolatedWorkload):
         g.stream_synchronize()
 
     def config(self):
+        from triton_llm.kernels.linear import plan
         return {"workload": "isolated projection GEMMs of one cfg4 decode layer",
                 "rows": self.B, "shapes_MNK": self.shapes,
+                "plans": [plan(*sh, planes=self.planes) for sh in self.shapes],
                 "weights": "bf16 N(0,0.02)",
-                "activations": "fp32 values as bf16 hi/lo planes (TLLM_SPLIT)",
+                "activations": ("bf16 hi/lo planes (TLLM_SPLIT)" if self.planes == 2
+                                else "bf16 (TLLM_BF16)"),
                 "timed": "K graph replays of the 4 launches",
                 "l2": f"{self.copies} rotating weight sets of 201 MB"}
 
@@ -773,7 +779,7 @@ class ProjLlamaLayerWorkload(_IsolatedWorkload):
         self.launch(0)
         gpu.device_synchronize()
         gu = self.layers[0][2]
-        w = gpu.to_host(gu.w)[:64].astype(np.float64)     # first 4 blocks of 16 rows
+        w = gu.to_numpy()[:64].astype(np.float64)         # first 4 blocks of 16 rows
         x = gpu.split_to_host(self.x).astype(np.float64)
         y = x @ w.T                                        # (B, 64) interleaved
         g = np.concatenate([y[:, 16 * b:16 * b + 8] for b in range(4)], axis=1)
@@ -956,7 +962,11 @@ def main():
     ap.add_argument("--workload", default="llama3b", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--act", default="bfloat16", choices=["bfloat16", "split"],
+                    help="projection input format of the bf16 path")
     args = ap.parse_args()
+    LlamaDecodeWorkload.act = args.act
+    ProjLlamaLayerWorkload.planes = 2 if args.act == "split" else 1
     args.warmup = max(args.warmup, 3)
 
     ranks = Ranks()

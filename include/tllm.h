@@ -48,7 +48,13 @@ typedef enum {
    * hi + lo keeps ~16 mantissa bits of x. This is the operand format of the
    * tensor-core projections; the kernels that produce their inputs (norms,
    * attention, the SwiGLU / GELU epilogues) can write it directly. */
-  TLLM_SPLIT = 3
+  TLLM_SPLIT = 3,
+  /* A bf16 weight matrix (N, K) stored as contiguous 128 x 64 tiles so that
+   * every tile the projection streams is one 16 KB block of HBM: tile
+   * (n / 128, k / 64) starts at element ((n / 128) * (K / 64) + k / 64) * 8192
+   * and holds its 128 rows of 64 elements row-major. N is padded to a
+   * multiple of 128 with zero rows. K % 64 == 0. */
+  TLLM_BF16_TILED = 4
 } tllm_dtype;
 
 /* ------------------------------------------------------------------------ */
@@ -165,9 +171,9 @@ int tllm_gqa_decode(const float *q, const void *k_cache, const void *v_cache,
  * r * *_row_stride + h * *_head_stride elements. Used for the prefill
  * (causal: row_len = position + 1) and for the reference's flat layout
  * (Q as (n_head * seq_q, d_k) is row stride d_k, head stride seq_q * d_k).
- * out_dtype F32 writes fp32; TLLM_SPLIT writes the two bf16 planes at the
- * same element offsets, planes out_plane_rows * out_row_stride elements
- * apart (the operand format of tllm_linear). Replaces
+ * out_dtype F32 writes fp32; TLLM_SPLIT / TLLM_BF16 write the bf16 planes
+ * at the same element offsets, planes out_plane_rows * out_row_stride
+ * elements apart (the operand formats of tllm_linear). Replaces
  * triton_llm/kernels/attention_gqa.py:149-269 (causal branch) and the
  * prefill attention of smollm2_triton/model.py:341-343. Scratch as for
  * tllm_gqa_decode with batch = rows.
@@ -191,11 +197,13 @@ int tllm_gqa_rows(const float *q, long q_row_stride, long q_head_stride,
  * apply_rope calls that follow it in smollm2_triton/model.py:281-365 and
  * gpt2_triton/model.py:319-361.
  *
- * w_dtype BF16: tensor-core path; x must be TLLM_SPLIT (planes of
- *   x_plane_rows >= M rows, see tllm_split_bf16) and K % 64 == 0.
+ * w_dtype BF16 or BF16_TILED: tensor-core path; x is TLLM_BF16 (one
+ *   bf16 plane) or TLLM_SPLIT (hi and lo planes, ~16 mantissa bits), planes
+ *   of x_plane_rows >= M rows (see tllm_split_bf16), K % 64 == 0.
+ *   BF16_TILED streams each weight tile as one 16 KB block.
  * w_dtype F32 : CUDA-core fp32 path; x must be F32 (M, K), K % 4 == 0.
- * out_dtype F32 or TLLM_SPLIT (planes of out_plane_rows rows of ld_out);
- *   op RESID needs F32.
+ * out_dtype F32, TLLM_SPLIT or TLLM_BF16 (planes of out_plane_rows rows of
+ *   ld_out); op RESID needs F32.
  *
  * op 0 STORE : out[m, n] = acc (+ bias[n])
  * op 1 RESID : out[m, n] = resid[m, n] + acc (+ bias[n]); resid may be out
@@ -215,6 +223,11 @@ int tllm_gqa_rows(const float *q, long q_row_stride, long q_head_stride,
  */
 int tllm_linear_workspace(int M, int N, int K, size_t *partial_bytes,
                           size_t *counter_bytes);
+/* Launch plan of the bf16 path for (M, N, K) and activation format x_dtype
+ * (SPLIT or BF16): plan[0..7] = activation tile width, activation tiles,
+ * 128-row weight tiles, K splits (cluster size), weight ring stages, dynamic
+ * shared memory bytes, activation ring stages, CTAs resident at once. */
+int tllm_linear_plan(int M, int N, int K, int x_dtype, int *plan);
 int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
                 int w_dtype, int M, int N, int K, int op, const float *bias,
                 void *out, int out_dtype, int out_plane_rows, int ld_out,
@@ -235,7 +248,8 @@ int tllm_gemm_f32(const float *a, const float *b, float *c, int M, int N,
 /* ------------------------------------------------------------------------ */
 
 /* triton_llm/kernels/rms_norm.py:68-115: y = (x / sqrt(mean(x^2) + eps)) * w
- * y_dtype F32 (M, N), or TLLM_SPLIT with planes of y_plane_rows rows. */
+ * y_dtype F32 (M, N), or TLLM_SPLIT / TLLM_BF16 with planes of y_plane_rows
+ * rows (the projection operand formats). */
 int tllm_rmsnorm(const float *x, const float *w, void *y, int y_dtype,
                  int y_plane_rows, int M, int N, float eps,
                  tllm_stream_t stream);
@@ -244,9 +258,10 @@ int tllm_rmsnorm(const float *x, const float *w, void *y, int y_dtype,
 int tllm_layernorm(const float *x, const float *gamma, const float *beta,
                    void *y, int y_dtype, int y_plane_rows, int M, int N,
                    float eps, tllm_stream_t stream);
-/* fp32 (rows, cols) -> TLLM_SPLIT with planes of plane_rows >= rows rows.
- * No counterpart in the reference (its activations stay fp32). */
-int tllm_split_bf16(const float *x, void *y, int rows, int cols,
+/* fp32 (rows, cols) -> the projection operand format: y_dtype TLLM_SPLIT
+ * (hi and lo planes) or TLLM_BF16 (one plane), planes of plane_rows >= rows
+ * rows. No counterpart in the reference (its activations stay fp32). */
+int tllm_split_bf16(const float *x, void *y, int y_dtype, int rows, int cols,
                     int plane_rows, tllm_stream_t stream);
 /* out[m] = wte[ids[m]] (+ wpe[pos[m]] if wpe): triton_llm/kernels/
  * embedding.py:98-187 and smollm2_triton/model.py:547-560. Out-of-range ids

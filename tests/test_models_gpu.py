@@ -35,10 +35,10 @@ def gpu():
     assert g.device_error(reset=True) == 0, "kernel reported a device error"
 
 
-def _smol(shape, weights, dtype=None, kv_dtype=None):
+def _smol(shape, weights, dtype=None, kv_dtype=None, act_dtype="bfloat16"):
     from smollm2_triton import SmolLM2Config, SmolLM2ForCausalLM
     return SmolLM2ForCausalLM(SmolLM2Config(**shape.config_kwargs()), weights,
-                              dtype=dtype, kv_dtype=kv_dtype)
+                              dtype=dtype, kv_dtype=kv_dtype, act_dtype=act_dtype)
 
 
 def _smol_run(model, prompt, n_new):
@@ -93,10 +93,11 @@ def test_smol_tiny_generate_matches_reference(gpu, golden):
     np.testing.assert_array_equal(streamed, g["tokens"][3:])
 
 
+@pytest.mark.parametrize("act", ["bfloat16", "split"])
 @pytest.mark.parametrize("kv", ["float32", "bfloat16"])
-def test_smol_tiny_bf16_vs_oracle(gpu, kv):
+def test_smol_tiny_bf16_vs_oracle(gpu, kv, act):
     w = inputs.llama_weights_legacy(inputs.SMOL_TINY, 42)
-    m = _smol(inputs.SMOL_TINY, w, dtype="bfloat16", kv_dtype=kv)
+    m = _smol(inputs.SMOL_TINY, w, dtype="bfloat16", kv_dtype=kv, act_dtype=act)
     from smollm2_triton import SmolLM2Config
     o = omodels.SmolLM2Oracle(SmolLM2Config(**inputs.SMOL_TINY.config_kwargs()), w,
                               weight_dtype="bfloat16", kv_dtype=kv)
@@ -107,14 +108,20 @@ def test_smol_tiny_bf16_vs_oracle(gpu, kv):
     np.testing.assert_allclose(logits[:steps], wl[:steps], atol=2e-2)
 
 
-@pytest.mark.parametrize("mode", ["float32", "bf16w"])
+@pytest.mark.parametrize("mode", ["float32", "bf16w-split", "bf16w"])
 def test_smol135m_slice_matches_reference(gpu, golden, mode):
-    """SmolLM2-135M geometry (config 3): fp32, and bf16 weights with an fp32
-    cache (exact weights), both against the reference's own logits."""
+    """SmolLM2-135M geometry (config 3) against the reference's own logits:
+    fp32; bf16 weights (exact, the slice's weights are bf16 values) with an
+    fp32 cache and hi + lo activations (near fp32); the same with bf16
+    activations (the serving default)."""
     g = golden("smol135m_slice")
     w = inputs.round_linear_weights_bf16(inputs.llama_weights(inputs.SMOL_135M, 0))
     if mode == "float32":
         m = _smol(inputs.SMOL_135M, w)
+        tol = 1e-4
+    elif mode == "bf16w-split":
+        m = _smol(inputs.SMOL_135M, w, dtype="bfloat16", kv_dtype="float32",
+                  act_dtype="split")
         tol = 1e-4
     else:
         m = _smol(inputs.SMOL_135M, w, dtype="bfloat16", kv_dtype="float32")
@@ -141,13 +148,17 @@ def test_smol135m_bf16_32_steps_vs_oracle(gpu):
     np.testing.assert_allclose(logits[:steps], wl[:steps], atol=2e-2)
 
 
-@pytest.mark.parametrize("mode", ["float32", "bf16w"])
+@pytest.mark.parametrize("mode", ["float32", "bf16w-split", "bf16w"])
 def test_llama3b_slice_matches_reference(gpu, golden, mode):
     """Llama-3.2-3B geometry (24/8/128, 2 layers, 128256 vocab)."""
     g = golden("llama3b_2l_slice")
     w = inputs.round_linear_weights_bf16(inputs.llama_weights(inputs.LLAMA3B_2L, 0))
     if mode == "float32":
         m = _smol(inputs.LLAMA3B_2L, w)
+        tol = 1e-4
+    elif mode == "bf16w-split":
+        m = _smol(inputs.LLAMA3B_2L, w, dtype="bfloat16", kv_dtype="float32",
+                  act_dtype="split")
         tol = 1e-4
     else:
         m = _smol(inputs.LLAMA3B_2L, w, dtype="bfloat16", kv_dtype="float32")

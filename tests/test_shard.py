@@ -77,3 +77,20 @@ def test_two_ranks_select_disjoint_shards():
     idx, tot, want = got
     assert idx == list(range(128))
     assert tot == want
+
+
+def test_weight_tiling_round_trip():
+    """TLLM_BF16_TILED layout: tile (n // 128, k // 64) is one contiguous
+    block of 128 x 64 elements; N padded with zero rows."""
+    from triton_llm.kernels.linear import tile_bf16, untile_bf16
+    rng = np.random.default_rng(0)
+    for N, K in ((200, 192), (128, 64), (5, 64)):
+        bits = rng.integers(0, 65535, (N, K)).astype(np.uint16)
+        flat = tile_bf16(bits)
+        n_pad = -(-N // 128) * 128
+        assert flat.size == n_pad * K
+        np.testing.assert_array_equal(untile_bf16(flat, N, K), bits)
+        k_chunks = K // 64
+        for (n, k) in ((0, 0), (N - 1, K - 1), (min(N - 1, 130), 65 % K)):
+            idx = ((n // 128) * k_chunks + k // 64) * 8192 + (n % 128) * 64 + k % 64
+            assert flat[idx] == bits[n, k]

@@ -75,8 +75,9 @@ __device__ __forceinline__ float fast_exp2(float x) {
 struct DecodeParams {
   const float *q;        // row b, head h at q + b * q_sb + h * q_sh
   float *out;            // row b, head h at out + b * o_sb + h * o_sh
-  uint16_t *out_split;   // or TLLM_SPLIT output at the same element offsets,
-  long out_plane;        //   planes out_plane elements apart
+  uint16_t *out_split;   // or operand-format output (TLLM_SPLIT / TLLM_BF16)
+  long out_plane;        //   at the same element offsets, planes out_plane
+  int out_planes;        //   elements apart, 2 or 1 planes
   const int *seq_lens;   // (B,) or null (every sequence has max_len keys)
   const int *row_seq;    // (B,) cache sequence of each row, or null (= row)
   long q_sb, q_sh, o_sb, o_sh;
@@ -92,7 +93,7 @@ struct DecodeParams {
 __device__ __forceinline__ void store_o(const DecodeParams &p, long idx,
                                         float v) {
   if (p.out_split)
-    store_split(p.out_split, (size_t)p.out_plane, (size_t)idx, v);
+    store_act(p.out_split, (size_t)p.out_plane, (size_t)idx, v, p.out_planes);
   else
     p.out[idx] = v;
 }
@@ -122,6 +123,7 @@ __global__ void __launch_bounds__(kThreads)
     gqa_decode_kernel(const DecodeParams p,
                       const __grid_constant__ CUtensorMap tmk,
                       const __grid_constant__ CUtensorMap tmv) {
+  griddep_launch();
   using S = Shape<T, D>;
   extern __shared__ __align__(1024) uint8_t smem[];
   T *k_st = reinterpret_cast<T *>(smem);
@@ -512,6 +514,7 @@ __global__ void __launch_bounds__(kThreads)
     gqa_decode_mma_kernel(const DecodeParams p, const int G,
                           const __grid_constant__ CUtensorMap tmk,
                           const __grid_constant__ CUtensorMap tmv) {
+  griddep_launch();
   using S = MmaShape<D>;
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t *k_st = smem;
@@ -1039,9 +1042,10 @@ static int rows_impl(const float *q, long q_sb, long q_sh, const void *k_cache,
                  n_kv_head);
   TLLM_CHECK_ARG(kv_dtype == TLLM_F32 || kv_dtype == TLLM_BF16,
                  "kv_dtype must be F32 or BF16");
-  TLLM_CHECK_ARG(out_dtype == TLLM_F32 || out_dtype == TLLM_SPLIT,
-                 "out_dtype must be F32 or SPLIT");
-  TLLM_CHECK_ARG(out_dtype != TLLM_SPLIT || out_plane_rows >= batch,
+  TLLM_CHECK_ARG(out_dtype == TLLM_F32 || out_dtype == TLLM_SPLIT ||
+                     out_dtype == TLLM_BF16,
+                 "out_dtype must be F32, SPLIT or BF16");
+  TLLM_CHECK_ARG(out_dtype == TLLM_F32 || out_plane_rows >= batch,
                  "out_plane_rows (%ld) < rows (%d)", out_plane_rows, batch);
   if (batch == 0) return TLLM_OK;
   TLLM_CHECK_ARG(q && out && k_cache && v_cache, "NULL tensor pointer");
@@ -1093,9 +1097,11 @@ static int rows_impl(const float *q, long q_sb, long q_sh, const void *k_cache,
 
   DecodeParams p;
   p.q = q;
-  p.out = out_dtype == TLLM_SPLIT ? nullptr : static_cast<float *>(out);
-  p.out_split = out_dtype == TLLM_SPLIT ? static_cast<uint16_t *>(out) : nullptr;
-  p.out_plane = out_dtype == TLLM_SPLIT ? out_plane_rows * o_sb : 0;
+  const bool act_out = out_dtype != TLLM_F32;
+  p.out = act_out ? nullptr : static_cast<float *>(out);
+  p.out_split = act_out ? static_cast<uint16_t *>(out) : nullptr;
+  p.out_plane = act_out ? out_plane_rows * o_sb : 0;
+  p.out_planes = out_dtype == TLLM_SPLIT ? 2 : 1;
   p.seq_lens = seq_lens;
   p.row_seq = row_seq;
   p.q_sb = q_sb;

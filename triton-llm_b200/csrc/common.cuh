@@ -35,11 +35,15 @@ inline int dtype_size(int dt) {
     case TLLM_BF16: return 2;
     case TLLM_I32: return 4;
     case TLLM_SPLIT: return 4;   // two bf16 planes
+    case TLLM_BF16_TILED: return 2;
     default: return 0;
   }
 }
 
 int sm_count();  // multiprocessors of the current device (cached)
+// Programmatic dependent launch of the projection kernels (TLLM_NO_PDL=1
+// turns it off, for comparisons).
+bool pdl_enabled();
 
 // Device-side error word (one int per device, allocated on first use).
 // Kernels receive its address and OR a code into it instead of trapping when
@@ -119,6 +123,12 @@ __host__ __device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
   return (uint16_t)(u >> 16);
 }
 
+// Element (n, k) of a TLLM_BF16_TILED (N, K) matrix.
+__host__ __device__ __forceinline__ size_t tiled_index(size_t n, size_t k,
+                                                      size_t K) {
+  return ((n >> 7) * (K >> 6) + (k >> 6)) * 8192 + (n & 127) * 64 + (k & 63);
+}
+
 __host__ __device__ __forceinline__ float bf16_bits_to_f32(uint16_t h) {
 #ifdef __CUDA_ARCH__
   return __uint_as_float((uint32_t)h << 16);
@@ -137,6 +147,14 @@ __device__ __forceinline__ void store_split(uint16_t *base, size_t plane,
   const uint16_t h = f32_to_bf16_bits(v);
   base[idx] = h;
   base[plane + idx] = f32_to_bf16_bits(v - bf16_bits_to_f32(h));
+}
+// Activation store in the tensor-core operand format: TLLM_SPLIT (two
+// planes) or TLLM_BF16 (the hi plane only).
+__device__ __forceinline__ void store_act(uint16_t *base, size_t plane,
+                                          size_t idx, float v, int planes) {
+  const uint16_t h = f32_to_bf16_bits(v);
+  base[idx] = h;
+  if (planes == 2) base[plane + idx] = f32_to_bf16_bits(v - bf16_bits_to_f32(h));
 }
 
 // Load 16 bytes that are read once (bypass L1 allocation).
@@ -290,6 +308,25 @@ __device__ __forceinline__ void tmem_free(uint32_t taddr, uint32_t ncols) {
                "r"(ncols)
                : "memory");
 }
+// 32 consecutive fp32 columns of this thread's TMEM lane (warp-wide).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,"
+      "%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,"
+      "%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]),
+        "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]),
+        "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
+        "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
 // 16 consecutive fp32 columns of this thread's TMEM lane (warp-wide).
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
   uint32_t r[16];
@@ -318,6 +355,18 @@ __device__ __forceinline__ void cluster_sync() {
       "barrier.cluster.arrive.release.aligned;\n\t"
       "barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// 4 consecutive fp32 at shared address `saddr` (16-byte aligned) of CTA
+// `rank` of this cluster.
+__device__ __forceinline__ float4 ld_dsmem_f32x4(uint32_t saddr, uint32_t rank) {
+  uint32_t a;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(a) : "r"(saddr), "r"(rank));
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(a)
+               : "memory");
+  return v;
+}
 // fp32 at shared address `saddr` of CTA `rank` of this cluster.
 __device__ __forceinline__ float ld_dsmem_f32(uint32_t saddr, uint32_t rank) {
   uint32_t a;
@@ -325,6 +374,19 @@ __device__ __forceinline__ float ld_dsmem_f32(uint32_t saddr, uint32_t rank) {
   float v;
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
   return v;
+}
+
+// ---- programmatic dependent launch ----------------------------------------
+// A kernel launched with the programmatic-serialization attribute may start
+// before the previous kernel on the stream has finished; it must call
+// griddep_wait() before touching anything that kernel writes or reads.
+// Every kernel calls griddep_launch() once all its CTAs are resident, so a
+// dependent kernel can fill the SMs freed by the last wave.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" :::);
 }
 
 }  // namespace tllm

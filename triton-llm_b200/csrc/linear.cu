@@ -14,10 +14,10 @@
 //    stages; one thread issues tcgen05.mma with the fp32 accumulator in
 //    TMEM and releases each stage with tcgen05.commit; after the last stage
 //    the four warps read the accumulator with tcgen05.ld and run the
-//    epilogue. Activations arrive in the TLLM_SPLIT format (bf16 hi and lo
-//    planes): each k-slice issues one MMA for hi and one for lo, so the
-//    product keeps ~16 mantissa bits of the fp32 activations while both
-//    operands are bf16. K is split across CTAs when there are too few
+//    epilogue. Activations arrive as bf16 (TLLM_BF16, one MMA per k-slice)
+//    or in the TLLM_SPLIT format (bf16 hi and lo planes, one MMA for each:
+//    the product keeps ~16 mantissa bits of the fp32 activations while both
+//    operands are bf16). K is split across CTAs when there are too few
 //    weight tiles to occupy the GPU: the S CTAs of a tile form a thread-block
 //    cluster, each stages its accumulator tile in shared memory, and after a
 //    cluster barrier each reduces a slice of the tile over distributed shared
@@ -37,6 +37,7 @@
 #include <cudaTypedefs.h>
 
 #include <cmath>
+#include <cstdlib>
 
 #include "common.cuh"
 
@@ -64,8 +65,9 @@ struct Epilogue {
   int op;
   const float *bias;   // [N] or null (in weight-row order)
   float *out;          // [M, ld_out] fp32, or null when out_split is set
-  uint16_t *out_split; // TLLM_SPLIT output, planes out_plane elements apart
-  size_t out_plane;
+  uint16_t *out_split; // bf16 operand-format output (TLLM_SPLIT or TLLM_BF16)
+  size_t out_plane;    //   planes out_plane elements apart
+  int out_planes;      //   2 (SPLIT) or 1 (BF16)
   const float *resid;  // [M, ld_out] (EPI_RESID)
   int ld_out;
   // EPI_QKV
@@ -97,7 +99,7 @@ __device__ __forceinline__ float silu_ref(float x) {
 __device__ __forceinline__ void store_out(const Epilogue &e, size_t idx,
                                           float v) {
   if (e.out_split)
-    store_split(e.out_split, e.out_plane, idx, v);
+    store_act(e.out_split, e.out_plane, idx, v, e.out_planes);
   else
     e.out[idx] = v;
 }
@@ -195,36 +197,61 @@ constexpr int kTcThreads = 128;       // 4 warps: TMA, MMA, then epilogue
 constexpr int kTcBN = 128;            // weight rows per CTA (MMA M)
 constexpr int kTcBK = 64;             // K per stage (one 128-byte row)
 constexpr int kTcW = kTcBN * kTcBK * 2;  // weight tile bytes (16 KB)
-
 constexpr int kTcMaxSplit = 8;        // portable cluster size
+constexpr int kTcMaxWS = 12;          // weight ring stages (at most)
+constexpr int kTcMaxXS = 8;           // activation ring stages (at most)
 
 struct TcParams {
   Epilogue e;
-  int M, N, K, S, k_chunks, n_tiles, stages;
+  int M, N, K, S, k_chunks, n_tiles, wstages, xstages;
+  int nacc;      // independent TMEM accumulators (even, 2..8)
+  uint32_t tcols;  // TMEM columns allocated (power of two >= 32)
+  int w_tiled;   // TLLM_BF16_TILED weights: tile (nt, kc) = rows
+                 // (nt * k_chunks + kc) * 128 .. +127 of a (., 64) view
 };
 
-__host__ __device__ constexpr int tc_stage_bytes(int MT) {
-  return kTcW + 2 * MT * kTcBK * 2;
+// one activation stage: the bf16 planes (1 or 2) of an MT x 64 tile
+__host__ __device__ constexpr int tc_x_bytes(int MT, int PL) {
+  return PL * MT * kTcBK * 2;
 }
-__host__ __device__ constexpr int tc_tmem_cols(int MT) {
-  return MT < 32 ? 32 : MT;
+// activation ring depth (default): up to 8 stages in at most 128 KB
+__host__ __device__ constexpr int tc_xs_default(int MT, int PL) {
+  return (128 * 1024) / tc_x_bytes(MT, PL) >= kTcMaxXS
+             ? kTcMaxXS
+             : ((128 * 1024) / tc_x_bytes(MT, PL) < 2
+                    ? 2
+                    : (128 * 1024) / tc_x_bytes(MT, PL));
 }
+// TMEM accumulators: one per MMA-issuing thread by default (the epilogue
+// sums them in fixed order); TLLM_LINEAR_NACC (even) gives each issuer more,
+// rotated over the MMAs of a chunk.
+__host__ __device__ constexpr int tc_nacc(int) { return 2; }
 
-template <int MT, int OP>
+// Weight tiles and activation tiles travel in two rings: the weights are
+// the HBM stream (a deep ring keeps many bytes in flight per SM), the
+// activation tiles are L2 hits shared by every CTA (a 2-stage ring suffices).
+// The producer of the weight ring starts before the previous kernel has
+// finished (programmatic dependent launch); the activation producer waits
+// for it.
+template <int MT, int OP, int PL>
 __global__ void __launch_bounds__(kTcThreads, 1)
     linear_tc_kernel(const TcParams p, const __grid_constant__ CUtensorMap tw,
                      const __grid_constant__ CUtensorMap tx) {
-  constexpr int X_BYTES = MT * kTcBK * 2;    // one bf16 plane of the tile
-  constexpr int STAGE = tc_stage_bytes(MT);
-  constexpr uint32_t TCOLS = tc_tmem_cols(MT);
+  constexpr int X_PLANE = MT * kTcBK * 2;    // one bf16 plane of the tile
+  constexpr int X_BYTES = tc_x_bytes(MT, PL);
+  const uint32_t TCOLS = p.tcols;
+  const int NACC = p.nacc;
   constexpr uint32_t IDESC = umma_idesc_bf16(kTcBN, MT);
   extern __shared__ __align__(1024) uint8_t smem[];
-  const int ST = p.stages;
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + ST * STAGE);
-  uint64_t *empty = full + ST;
-  uint64_t *accb = empty + ST;
+  __shared__ uint64_t wfull[kTcMaxWS], wempty[kTcMaxWS];
+  const int kTcXS = p.xstages;
+  __shared__ uint64_t xfull[kTcMaxXS], xempty[kTcMaxXS], accb[1];
   __shared__ uint32_t s_tmem;
-  __shared__ int s_issued, s_consumed, s_fail;
+  __shared__ int s_wissued, s_xissued, s_consumed, s_fail;
+  __shared__ int s_empty_acc[2];   // an issuer whose accumulators were never written
+  const int WS = p.wstages;
+  uint8_t *wring = smem;
+  uint8_t *xring = smem + WS * kTcW;
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -235,6 +262,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (tid == 0) atomicOr(p.e.err, DEV_ERR_SMEM_ALIGN);
     return;
   }
+  griddep_launch();
   const int nt = blockIdx.x;
   const int split = blockIdx.y;
   const int mt = blockIdx.z;
@@ -244,14 +272,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int nch = kc1 > kc0 ? kc1 - kc0 : 0;
 
   if (tid == 0) {
-    for (int s = 0; s < ST; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < WS; ++s) {
+      mbar_init(&wfull[s], 1);
+      mbar_init(&wempty[s], 1);
     }
-    mbar_init(accb, 1);
-    s_issued = 0;
+    for (int s = 0; s < kTcXS; ++s) {
+      mbar_init(&xfull[s], 1);
+      mbar_init(&xempty[s], 1);
+    }
+    mbar_init(accb, 2);   // one arrival per MMA issuer
+    s_wissued = 0;
+    s_xissued = 0;
     s_consumed = 0;
     s_fail = 0;
+    s_empty_acc[0] = 0;
+    s_empty_acc[1] = 0;
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(&s_tmem, TCOLS);
@@ -262,78 +297,131 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      // TMA producer: weights are read once (evict first), activation tiles
-      // are shared by every CTA of the grid (evict last)
-      const uint64_t pol_w = l2_policy_evict_first();
-      const uint64_t pol_x = l2_policy_evict_last();
+      // weight producer: read once, evict first; needs nothing from the
+      // previous kernel
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&tw) : "memory");
+      const uint64_t pol = l2_policy_evict_first();
       int c = 0;
       for (; c < nch; ++c) {
-        const int s = c % ST;
-        if (c >= ST && !mbar_wait_bounded(&empty[s], ((c / ST) - 1) & 1)) {
+        const int s = c % WS;
+        if (c >= WS && !mbar_wait_bounded(&wempty[s], ((c / WS) - 1) & 1)) {
           s_fail = 1;
           break;
         }
-        uint8_t *st = smem + s * STAGE;
-        mbar_expect_tx(&full[s], STAGE);
-        const int k0 = (kc0 + c) * kTcBK;
-        tma_load_2d_hint(st, &tw, &full[s], k0, nt * kTcBN, pol_w);
-        tma_load_3d_hint(st + kTcW, &tx, &full[s], k0, mt * MT, 0, pol_x);
-        tma_load_3d_hint(st + kTcW + X_BYTES, &tx, &full[s], k0, mt * MT, 1,
-                         pol_x);
+        mbar_expect_tx(&wfull[s], kTcW);
+        if (p.w_tiled)
+          tma_load_2d_hint(wring + s * kTcW, &tw, &wfull[s], 0,
+                           (nt * p.k_chunks + kc0 + c) * kTcBN, pol);
+        else
+          tma_load_2d_hint(wring + s * kTcW, &tw, &wfull[s], (kc0 + c) * kTcBK,
+                           nt * kTcBN, pol);
       }
-      s_issued = c;
+      s_wissued = c;
     }
     __syncwarp();
-  } else if (warp == 1) {
+  } else if (warp == 2) {
     if (lane == 0) {
-      // MMA issuer: D[128 x MT] += W[128 x 16] . X[MT x 16]^T per k-slice,
-      // once for the hi plane and once for the lo plane
+      // activation producer: the tiles are written by the previous kernel
+      asm volatile("prefetch.tensormap [%0];" ::"l"(&tx) : "memory");
+      const uint64_t pol = l2_policy_evict_last();
+      griddep_wait();
       int c = 0;
       for (; c < nch; ++c) {
-        const int s = c % ST;
-        if (!mbar_wait_bounded(&full[s], (c / ST) & 1)) {
+        const int s = c % kTcXS;
+        if (c >= kTcXS &&
+            !mbar_wait_bounded(&xempty[s], ((c / kTcXS) - 1) & 1)) {
+          s_fail = 1;
+          break;
+        }
+        uint8_t *st = xring + s * X_BYTES;
+        const int k0 = (kc0 + c) * kTcBK;
+        mbar_expect_tx(&xfull[s], X_BYTES);
+        tma_load_3d_hint(st, &tx, &xfull[s], k0, mt * MT, 0, pol);
+        if (PL == 2)
+          tma_load_3d_hint(st + X_PLANE, &tx, &xfull[s], k0, mt * MT, 1, pol);
+      }
+      s_xissued = c;
+    }
+    __syncwarp();
+  } else if (warp == 1 || warp == 3) {
+    if (lane == 0) {
+      // MMA issuers: two threads (warps 1 and 3) take alternate k-chunks,
+      // each with its own half of the accumulators, so one thread's barrier
+      // waits and MMA issue overlap the other's. Per chunk and plane:
+      // D[128 x MT] += W[128 x 16] . X[MT x 16]^T for each k-slice.
+      const int who = warp == 1 ? 0 : 1;
+      const int nacc = NACC / 2;                    // accumulators per issuer
+      const uint32_t tacc = tmem + who * nacc * MT;
+      int c = who;
+      bool first = true;
+      for (; c < nch; c += 2) {
+        const int ws = c % WS;
+        const int xs = c % kTcXS;
+        if (!mbar_wait_bounded(&wfull[ws], (c / WS) & 1) ||
+            !mbar_wait_bounded(&xfull[xs], (c / kTcXS) & 1)) {
           s_fail = 1;
           break;
         }
         tc_fence_after();
-        const uint32_t st = smem_u32(smem + s * STAGE);
-        const uint64_t a = umma_desc_sw128(st);
-        const uint64_t bh = umma_desc_sw128(st + kTcW);
-        const uint64_t bl = umma_desc_sw128(st + kTcW + X_BYTES);
+        const uint64_t a = umma_desc_sw128(smem_u32(wring + ws * kTcW));
+        const uint32_t xa = smem_u32(xring + xs * X_BYTES);
+        const uint64_t bh = umma_desc_sw128(xa);
+        const uint64_t bl = umma_desc_sw128(xa + X_PLANE);
 #pragma unroll
-        for (int kk = 0; kk < kTcBK / 16; ++kk) {
-          umma_bf16(tmem, a + 2 * kk, bh + 2 * kk, IDESC, (c | kk) != 0);
-          umma_bf16(tmem, a + 2 * kk, bl + 2 * kk, IDESC, 1);
+        for (int j = 0; j < PL * (kTcBK / 16); ++j) {
+          const int kk = j / PL;        // k-slice
+          const int acc = j % nacc;     // accumulator of this MMA
+          // the first MMA into an accumulator initialises it
+          const uint32_t accumulate = (!first || j >= nacc) ? 1u : 0u;
+          umma_bf16(tacc + acc * MT, a + 2 * kk,
+                    ((PL == 2 && (j & 1)) ? bl : bh) + 2 * kk, IDESC, accumulate);
         }
-        umma_commit(&empty[s]);   // stage free once these MMAs are done
+        umma_commit(&wempty[ws]);   // slots free once these MMAs are done
+        umma_commit(&xempty[xs]);
+        first = false;
       }
-      s_consumed = c;
-      umma_commit(accb);          // accumulator complete (or nothing issued)
+      if (who == 0) s_consumed = c < nch ? c : nch;
+      // an issuer that got no chunk zeroes its accumulators by marking them
+      if (first) s_empty_acc[who] = 1;
+      umma_commit(accb);            // this issuer's MMAs complete
     }
     __syncwarp();
   }
 
   // ---- epilogue ----
   // 1. the four warps copy the accumulator (TMEM lanes 32*warp..+31) into
-  //    shared memory, column-major: tile[m * 128 + r] (the ring is free now)
+  //    shared memory, column-major: tile[m * 128 + r] (the rings are free)
   const bool acc_ok = mbar_wait_bounded(accb, 0);
   tc_fence_after();
+  griddep_wait();   // the epilogue reads / writes buffers of earlier kernels
   __syncthreads();  // s_fail / s_consumed visible
   const bool valid = acc_ok && !s_fail && nch > 0;
   float *tile = reinterpret_cast<float *>(smem);
   const int r_own = warp * 32 + lane;
   const uint32_t t_lane = tmem + ((uint32_t)(warp * 32) << 16);
+  // 32 columns per TMEM load (16 for the narrowest tile), one wait each
+  constexpr int CW = MT >= 32 ? 32 : 16;
 #pragma unroll 1
-  for (int c0 = 0; c0 < MT; c0 += 16) {
-    float v[16];
-    if (valid) {
-      tmem_ld16(t_lane + c0, v);
-    } else {
+  for (int c0 = 0; c0 < MT; c0 += CW) {
+    float v[CW];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) v[j] = 0.f;
+    for (int j = 0; j < CW; ++j) v[j] = 0.f;
+    if (valid) {
+      const int nacc = NACC / 2;
+#pragma unroll 1
+      for (int acc = 0; acc < NACC; ++acc) {   // fixed order: deterministic
+        if (s_empty_acc[acc / nacc]) continue;
+        float u[CW];
+        if constexpr (CW == 32)
+          tmem_ld32(t_lane + acc * MT + c0, u);
+        else
+          tmem_ld16(t_lane + acc * MT + c0, u);
+#pragma unroll
+        for (int j = 0; j < CW; ++j) v[j] += u[j];
+      }
     }
 #pragma unroll
-    for (int j = 0; j < 16; ++j) tile[(c0 + j) * kTcBN + r_own] = v[j];
+    for (int j = 0; j < CW; ++j) tile[(c0 + j) * kTcBN + r_own] = v[j];
   }
   // 2. every split of this tile has staged its partial
   const int S = p.S;
@@ -341,42 +429,81 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     cluster_sync();
   else
     __syncthreads();
-  // 3. this CTA reduces items rank, rank + S, ... of the tile: an item is
-  //    one row pair (r, r + 8) at one activation column m; the splits are
-  //    summed in rank order
+  // 3. this CTA finishes activation rows m = rank, rank + S, ... of the
+  //    tile, one warp per row: the splits are summed in rank order and the
+  //    epilogue stores whole output rows (lane l covers weight rows
+  //    4l .. 4l + 3 of the tile)
   const int rank = S > 1 ? (int)cluster_ctarank() : 0;
   const uint32_t tile_s = smem_u32(tile);
-  const int n_items = (kTcBN / 2) * MT;
-#pragma unroll 2
-  for (int it = rank * kTcThreads + tid; it < n_items; it += S * kTcThreads) {
-    const int m = it >> 6;
-    const int pr = it & 63;
-    const int r = (pr >> 3) * 16 + (pr & 7);
-    const int idx = m * kTcBN + r;
-    float v0, v1;
-    if (S == 1) {
-      v0 = tile[idx];
-      v1 = tile[idx + 8];
-    } else {
-      float a0[kTcMaxSplit], a1[kTcMaxSplit];
+  const int row0 = nt * kTcBN;
+#pragma unroll 1
+  for (int ml = rank + warp * S; ml < MT; ml += 4 * S) {
+    const int m = mt * MT + ml;
+    if (m >= p.M) break;
+    if constexpr (OP == EPI_STORE || OP == EPI_RESID || OP == EPI_GELU) {
+      // this lane's 4 accumulator values (weight rows 4*lane .. +3)
+      const int r4 = lane * 4;
+      float4 v;
+      if (S == 1) {
+        v = *reinterpret_cast<const float4 *>(&tile[ml * kTcBN + r4]);
+      } else {
+        v = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int q = 0; q < kTcMaxSplit; ++q) {
-        if (q < S) {
-          a0[q] = ld_dsmem_f32(tile_s + idx * 4, q);
-          a1[q] = ld_dsmem_f32(tile_s + (idx + 8) * 4, q);
+        for (int q = 0; q < kTcMaxSplit; ++q) {
+          if (q < S) {
+            const float4 u = ld_dsmem_f32x4(tile_s + (ml * kTcBN + r4) * 4, q);
+            v.x += u.x;
+            v.y += u.y;
+            v.z += u.z;
+            v.w += u.w;
+          }
         }
       }
-      v0 = a0[0];
-      v1 = a1[0];
+      const Epilogue &e = p.e;
+      const int n = row0 + r4;
+      const size_t o = (size_t)m * e.ld_out + n;
+      float a[4] = {v.x, v.y, v.z, v.w};
+      const bool full = n + 3 < p.N;
 #pragma unroll
-      for (int q = 1; q < kTcMaxSplit; ++q) {
-        if (q < S) {
-          v0 += a0[q];
-          v1 += a1[q];
+      for (int i = 0; i < 4; ++i) {
+        if (!full && n + i >= p.N) continue;
+        if (e.bias) a[i] += e.bias[n + i];
+        if constexpr (OP == EPI_RESID) a[i] += e.resid[o + i];
+        if constexpr (OP == EPI_GELU) a[i] = gelu_tanh(a[i]);
+      }
+      if (full && !e.out_split && ((o & 3) == 0)) {
+        *reinterpret_cast<float4 *>(&e.out[o]) = make_float4(a[0], a[1], a[2], a[3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (n + i < p.N) store_out(e, o + i, a[i]);
+      }
+    } else {
+      // SwiGLU / QKV combine weight rows r and r + 8 of each 16-row block:
+      // lane l takes row pairs 2l and 2l + 1 of the 64 in this tile row
+      const int pr0 = lane * 2;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int pr = pr0 + h;
+        const int r = (pr >> 3) * 16 + (pr & 7);
+        float v0, v1;
+        if (S == 1) {
+          v0 = tile[ml * kTcBN + r];
+          v1 = tile[ml * kTcBN + r + 8];
+        } else {
+          v0 = 0.f;
+          v1 = 0.f;
+#pragma unroll
+          for (int q = 0; q < kTcMaxSplit; ++q) {
+            if (q < S) {
+              v0 += ld_dsmem_f32(tile_s + (ml * kTcBN + r) * 4, q);
+              v1 += ld_dsmem_f32(tile_s + (ml * kTcBN + r + 8) * 4, q);
+            }
+          }
         }
+        epi_pair<OP>(p.e, p.N, p.M, row0 + r, m, v0, v1);
       }
     }
-    epi_pair<OP>(p.e, p.N, p.M, nt * kTcBN + r, mt * MT + m, v0, v1);
   }
   if (!acc_ok || s_fail) {
     if (tid == 0) atomicOr(p.e.err, DEV_ERR_WAIT_TIMEOUT);
@@ -391,8 +518,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   else
     __syncthreads();
   if (tid == 0) {
-    for (int c = s_consumed; c < s_issued; ++c)
-      mbar_wait_bounded(&full[c % ST], (c / ST) & 1);
+    for (int c = s_consumed; c < s_wissued; ++c)
+      mbar_wait_bounded(&wfull[c % WS], (c / WS) & 1);
+    for (int c = s_consumed; c < s_xissued; ++c)
+      mbar_wait_bounded(&xfull[c % kTcXS], (c / kTcXS) & 1);
   }
   if (warp == 1) tmem_free(tmem, TCOLS);
 }
@@ -406,6 +535,7 @@ template <int MB>
 __global__ void __launch_bounds__(kF32Warps * 32)
     linear_f32_kernel(const float *x, const float *w, Epilogue e, int M,
                       int N, int K, int m0) {
+  griddep_launch();
   const int warp = (blockIdx.x * kF32Warps) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   // pair index -> rows r (first 8 of a 16-block) and r + 8
@@ -463,7 +593,7 @@ __global__ void __launch_bounds__(kF32Warps * 32)
 // host side
 // ------------------------------------------------------------------------
 struct TcPlan {
-  int MT, m_tiles, n_tiles, k_chunks, S, stages;
+  int MT, PL, m_tiles, n_tiles, k_chunks, S, wstages;
   size_t smem;
 };
 
@@ -471,84 +601,213 @@ int tc_mt_for(int M) {
   return M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
 }
 
-// Stages: about 100 KB of ring per CTA (two CTAs per SM), 2 to 6; the ring
-// must also hold the fp32 accumulator tile staged by the epilogue.
-int tc_stages_for(int MT) {
-  int st = (100 * 1024) / tc_stage_bytes(MT);
-  st = st < 2 ? 2 : (st > 6 ? 6 : st);
-  while (st * tc_stage_bytes(MT) < kTcBN * MT * 4) ++st;
-  return st;
+int env_int(const char *name, int dflt) {
+  const char *v = getenv(name);
+  return v && v[0] ? atoi(v) : dflt;
 }
 
-size_t tc_smem_for(int MT, int stages) {
-  return (size_t)stages * tc_stage_bytes(MT) +
-         (2 * stages + 1) * sizeof(uint64_t);
+// Activation ring depth (TLLM_LINEAR_XS overrides, for tuning).
+int tc_xs_for(int MT, int PL) {
+  static const int forced = env_int("TLLM_LINEAR_XS", 0);
+  if (forced >= 2 && forced <= kTcMaxXS) return forced;
+  return tc_xs_default(MT, PL);
 }
 
-TcPlan tc_plan(int M, int N, int K) {
-  TcPlan pl{};
-  pl.MT = tc_mt_for(M);
-  pl.m_tiles = (M + pl.MT - 1) / pl.MT;
-  pl.n_tiles = (N + kTcBN - 1) / kTcBN;
-  pl.k_chunks = K / kTcBK;
-  pl.stages = tc_stages_for(pl.MT);
-  pl.smem = tc_smem_for(pl.MT, pl.stages);
-  // CTAs resident at once: shared memory allows two per SM up to ~113 KB
-  const int per_sm = pl.smem <= 113 * 1024 ? 2 : 1;
-  const long slots = (long)per_sm * sm_count();
-  const long base = (long)pl.m_tiles * pl.n_tiles;
-  int S = 1;
-  if (base < slots) {
-    long s = slots / base;
-    const long by_k = pl.k_chunks / 4;  // keep >= 4 k-chunks per split
-    if (s > by_k) s = by_k;
-    if (s > kTcMaxSplit) s = kTcMaxSplit;
-    S = s < 1 ? 1 : (int)s;
-  }
-  pl.S = S;
-  return pl;
+// Weight ring depth: one CTA per SM with ~224 KB of rings (the activation
+// ring first); the rings also hold the fp32 accumulator tile staged by the
+// epilogue.
+int tc_wstages_for(int MT, int PL) {
+  static const int forced = [] {  // TLLM_LINEAR_WS: ring depth for tuning
+    const char *v = getenv("TLLM_LINEAR_WS");
+    return v ? atoi(v) : 0;
+  }();
+  if (forced >= 2 && forced <= kTcMaxWS) return forced;
+  static const int budget_kb = env_int("TLLM_LINEAR_RING_KB", 224);
+  const int xb = tc_xs_for(MT, PL) * tc_x_bytes(MT, PL);
+  int ws = (budget_kb * 1024 - xb) / kTcW;
+  ws = ws < 2 ? 2 : (ws > kTcMaxWS ? kTcMaxWS : ws);
+  return ws;
 }
 
-template <int MT, int OP>
-int launch_tc(const TcParams &p, const CUtensorMap &tw, const CUtensorMap &tx,
-              dim3 grid, size_t smem, cudaStream_t st) {
-  auto kern = linear_tc_kernel<MT, OP>;
+size_t tc_smem_for(int MT, int PL, int wstages) {
+  return (size_t)wstages * kTcW + (size_t)tc_xs_for(MT, PL) * tc_x_bytes(MT, PL);
+}
+
+template <int MT, int OP, int PL>
+int configure_tc() {
+  auto kern = linear_tc_kernel<MT, OP, PL>;
   static bool configured[64] = {};  // per instantiation and device
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !configured[dev]) {
     TLLM_CUDA(cudaFuncSetAttribute(
-        kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 226 * 1024));
+    TLLM_CUDA(cudaFuncSetAttribute(
+        kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+        cudaSharedmemCarveoutMaxShared));
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
+  return TLLM_OK;
+}
+
+int tc_cluster_policy() {   // TLLM_LINEAR_CLUSTER_POLICY: 1 spread, 2 balance
+  static const int pol = [] {
+    const char *v = getenv("TLLM_LINEAR_CLUSTER_POLICY");
+    return v ? atoi(v) : 2;
+  }();
+  return pol;
+}
+
+// Clusters of S CTAs resident at once (cached per device and S).
+template <int MT, int PL>
+int tc_active_clusters(int S, size_t smem) {
+  static int cached[64][kTcMaxSplit + 1] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && cached[dev][S]) return cached[dev][S] - 1;
+  int n = 0;
+  if (configure_tc<MT, EPI_STORE, PL>() == TLLM_OK) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, S, 1);
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = S;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeClusterSchedulingPolicyPreference;
+    attr[1].val.clusterSchedulingPolicyPreference =
+        tc_cluster_policy() == 1 ? cudaClusterSchedulingPolicySpread
+                                 : cudaClusterSchedulingPolicyLoadBalancing;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    if (cudaOccupancyMaxActiveClusters(&n, linear_tc_kernel<MT, EPI_STORE, PL>,
+                                       &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+  }
+  if (dev >= 0 && dev < 64) cached[dev][S] = n + 1;
+  return n;
+}
+
+// CTAs that can run at once with S splits: one CTA per SM (the rings take
+// ~224 KB of shared memory); clusters of S CTAs as the device places them.
+int tc_active_ctas(int MT, int PL, int S, size_t smem) {
+  static const int per_sm = env_int("TLLM_LINEAR_PER_SM", 0);
+  if (per_sm > 0) return per_sm * sm_count();
+  if (S == 1) return sm_count();
+  int c = 0;
+  if (PL == 2) {
+    switch (MT) {
+      case 16: c = tc_active_clusters<16, 2>(S, smem); break;
+      case 32: c = tc_active_clusters<32, 2>(S, smem); break;
+      case 64: c = tc_active_clusters<64, 2>(S, smem); break;
+      case 128: c = tc_active_clusters<128, 2>(S, smem); break;
+      default: c = tc_active_clusters<256, 2>(S, smem); break;
+    }
+  } else {
+    switch (MT) {
+      case 16: c = tc_active_clusters<16, 1>(S, smem); break;
+      case 32: c = tc_active_clusters<32, 1>(S, smem); break;
+      case 64: c = tc_active_clusters<64, 1>(S, smem); break;
+      case 128: c = tc_active_clusters<128, 1>(S, smem); break;
+      default: c = tc_active_clusters<256, 1>(S, smem); break;
+    }
+  }
+  return c * S;
+}
+
+TcPlan tc_plan(int M, int N, int K, int PL) {
+  TcPlan pl{};
+  pl.MT = tc_mt_for(M);
+  pl.PL = PL;
+  pl.m_tiles = (M + pl.MT - 1) / pl.MT;
+  pl.n_tiles = (N + kTcBN - 1) / kTcBN;
+  pl.k_chunks = K / kTcBK;
+  pl.wstages = tc_wstages_for(pl.MT, PL);
+  pl.smem = tc_smem_for(pl.MT, PL, pl.wstages);
+  // the largest split count (cluster size) whose whole grid is resident at
+  // once, keeping >= 4 k-chunks per split
+  const long base = (long)pl.m_tiles * pl.n_tiles;
+  int s_max = pl.k_chunks / 4;
+  if (s_max > kTcMaxSplit) s_max = kTcMaxSplit;
+  int S = 1;
+  for (int s = s_max; s >= 2; --s) {
+    if (base * s <= tc_active_ctas(pl.MT, PL, s, pl.smem)) {
+      S = s;
+      break;
+    }
+  }
+  pl.S = S;
+  return pl;
+}
+
+template <int MT, int OP, int PL>
+int launch_tc(const TcParams &p, const CUtensorMap &tw, const CUtensorMap &tx,
+              dim3 grid, size_t smem, cudaStream_t st) {
+  auto kern = linear_tc_kernel<MT, OP, PL>;
+  int rc = configure_tc<MT, OP, PL>();
+  if (rc) return rc;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = p.S;   // the splits of one weight tile
-  attr[0].val.clusterDim.z = 1;
+  cudaLaunchAttribute attr[3];
+  int na = 0;
+  if (p.S > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = p.S;   // the splits of one weight tile
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+    attr[na].id = cudaLaunchAttributeClusterSchedulingPolicyPreference;
+    attr[na].val.clusterSchedulingPolicyPreference =
+        tc_cluster_policy() == 1 ? cudaClusterSchedulingPolicySpread
+                                 : cudaClusterSchedulingPolicyLoadBalancing;
+    ++na;
+  }
+  if (pdl_enabled()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = p.S > 1 ? 1 : 0;
+  cfg.numAttrs = na;
   TLLM_CUDA(cudaLaunchKernelEx(&cfg, kern, p, tw, tx));
   TLLM_LAUNCH_CHECK();
   return TLLM_OK;
 }
 
-template <int MT>
+template <int MT, int PL>
 int launch_tc_op(const TcParams &p, const CUtensorMap &tw,
                  const CUtensorMap &tx, dim3 grid, size_t smem,
                  cudaStream_t st) {
   switch (p.e.op) {
-    case EPI_STORE: return launch_tc<MT, EPI_STORE>(p, tw, tx, grid, smem, st);
-    case EPI_RESID: return launch_tc<MT, EPI_RESID>(p, tw, tx, grid, smem, st);
-    case EPI_GELU: return launch_tc<MT, EPI_GELU>(p, tw, tx, grid, smem, st);
+    case EPI_STORE:
+      return launch_tc<MT, EPI_STORE, PL>(p, tw, tx, grid, smem, st);
+    case EPI_RESID:
+      return launch_tc<MT, EPI_RESID, PL>(p, tw, tx, grid, smem, st);
+    case EPI_GELU:
+      return launch_tc<MT, EPI_GELU, PL>(p, tw, tx, grid, smem, st);
     case EPI_SWIGLU:
-      return launch_tc<MT, EPI_SWIGLU>(p, tw, tx, grid, smem, st);
-    default: return launch_tc<MT, EPI_QKV>(p, tw, tx, grid, smem, st);
+      return launch_tc<MT, EPI_SWIGLU, PL>(p, tw, tx, grid, smem, st);
+    default: return launch_tc<MT, EPI_QKV, PL>(p, tw, tx, grid, smem, st);
+  }
+}
+
+template <int PL>
+int launch_tc_mt(const TcParams &p, int MT, const CUtensorMap &tw,
+                 const CUtensorMap &tx, dim3 grid, size_t smem,
+                 cudaStream_t st) {
+  switch (MT) {
+    case 16: return launch_tc_op<16, PL>(p, tw, tx, grid, smem, st);
+    case 32: return launch_tc_op<32, PL>(p, tw, tx, grid, smem, st);
+    case 64: return launch_tc_op<64, PL>(p, tw, tx, grid, smem, st);
+    case 128: return launch_tc_op<128, PL>(p, tw, tx, grid, smem, st);
+    default: return launch_tc_op<256, PL>(p, tw, tx, grid, smem, st);
   }
 }
 
@@ -593,6 +852,25 @@ int tllm_linear_workspace(int M, int N, int K, size_t *partial_bytes,
   return TLLM_OK;
 }
 
+int tllm_linear_plan(int M, int N, int K, int x_dtype, int *plan) {
+  TLLM_CHECK_ARG(plan, "NULL output");
+  TLLM_CHECK_ARG(M > 0 && N > 0 && K >= kTcBK && K % kTcBK == 0,
+                 "plan needs M, N > 0 and K a positive multiple of 64");
+  TLLM_CHECK_ARG(x_dtype == TLLM_SPLIT || x_dtype == TLLM_BF16,
+                 "x_dtype must be SPLIT or BF16");
+  const int PL = x_dtype == TLLM_SPLIT ? 2 : 1;
+  const TcPlan pl = tc_plan(M, N, K, PL);
+  plan[0] = pl.MT;
+  plan[1] = pl.m_tiles;
+  plan[2] = pl.n_tiles;
+  plan[3] = pl.S;
+  plan[4] = pl.wstages;
+  plan[5] = (int)pl.smem;
+  plan[6] = tc_xs_for(pl.MT, PL);
+  plan[7] = tc_active_ctas(pl.MT, PL, pl.S, pl.smem);
+  return TLLM_OK;
+}
+
 // y = epilogue(x @ W^T); see tllm.h for the argument encoding.
 int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
                 int w_dtype, int M, int N, int K, int op, const float *bias,
@@ -607,21 +885,24 @@ int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
   TLLM_CHECK_ARG(M >= 0 && N >= 0 && K >= 0, "negative shape");
   if (M == 0 || N == 0) return TLLM_OK;
   TLLM_CHECK_ARG(x && w, "NULL input");
-  TLLM_CHECK_ARG(w_dtype == TLLM_F32 || w_dtype == TLLM_BF16,
-                 "w_dtype must be F32 or BF16");
-  TLLM_CHECK_ARG(out_dtype == TLLM_F32 || out_dtype == TLLM_SPLIT,
-                 "out_dtype must be F32 or SPLIT");
+  TLLM_CHECK_ARG(w_dtype == TLLM_F32 || w_dtype == TLLM_BF16 ||
+                     w_dtype == TLLM_BF16_TILED,
+                 "w_dtype must be F32, BF16 or BF16_TILED");
+  TLLM_CHECK_ARG(out_dtype == TLLM_F32 || out_dtype == TLLM_SPLIT ||
+                     out_dtype == TLLM_BF16,
+                 "out_dtype must be F32, SPLIT or BF16");
   TLLM_CHECK_ARG(((uintptr_t)x & 15) == 0 && ((uintptr_t)w & 15) == 0,
                  "x and W must be 16-byte aligned");
   Epilogue e{};
   e.op = op;
   e.bias = bias;
   e.ld_out = ld_out > 0 ? ld_out : (op == EPI_SWIGLU ? N / 2 : N);
-  if (out_dtype == TLLM_SPLIT) {
+  if (out_dtype != TLLM_F32) {
     TLLM_CHECK_ARG(out_plane_rows >= M, "out_plane_rows (%d) < M (%d)",
                    out_plane_rows, M);
     e.out_split = static_cast<uint16_t *>(out);
     e.out_plane = (size_t)out_plane_rows * e.ld_out;
+    e.out_planes = out_dtype == TLLM_SPLIT ? 2 : 1;
   } else {
     e.out = static_cast<float *>(out);
   }
@@ -659,8 +940,10 @@ int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
     return TLLM_OK;
   }
 
-  TLLM_CHECK_ARG(x_dtype == TLLM_SPLIT,
-                 "bf16 weights take TLLM_SPLIT activations (tllm_split_bf16)");
+  TLLM_CHECK_ARG(x_dtype == TLLM_SPLIT || x_dtype == TLLM_BF16,
+                 "bf16 weights take TLLM_SPLIT or TLLM_BF16 activations "
+                 "(tllm_split_bf16)");
+  const int PL = x_dtype == TLLM_SPLIT ? 2 : 1;
   TLLM_CHECK_ARG(K > 0 && K % kTcBK == 0, "bf16 linear needs K %% 64 == 0 (K=%d)",
                  K);
   TLLM_CHECK_ARG(x_plane_rows >= M, "x_plane_rows (%d) < M (%d)", x_plane_rows,
@@ -668,12 +951,18 @@ int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
   (void)partial;
   (void)partial_bytes;
   (void)counters;
-  const TcPlan pl = tc_plan(M, N, K);
+  const TcPlan pl = tc_plan(M, N, K, PL);
   const int S = pl.S;
   CUtensorMap tw, tx;
-  rc = make_map_2d(&tw, w, TLLM_BF16, K, N, (long)K * 2, kTcBK, kTcBN, true);
+  const bool tiled = w_dtype == TLLM_BF16_TILED;
+  if (tiled)  // (n_tiles * k_chunks * 128, 64) rows of 128 bytes
+    rc = make_map_2d(&tw, w, TLLM_BF16, kTcBK,
+                     (long)pl.n_tiles * pl.k_chunks * kTcBN, kTcBK * 2, kTcBK,
+                     kTcBN, true);
+  else
+    rc = make_map_2d(&tw, w, TLLM_BF16, K, N, (long)K * 2, kTcBK, kTcBN, true);
   if (rc) return rc;
-  const long xd[3] = {K, x_plane_rows, 2};
+  const long xd[3] = {K, x_plane_rows, PL};
   const long xs[2] = {(long)K * 2, (long)x_plane_rows * K * 2};
   const int xb[3] = {kTcBK, pl.MT, 1};
   rc = make_map(&tx, x, TLLM_BF16, 3, xd, xs, xb, true);
@@ -686,15 +975,24 @@ int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
   p.S = S;
   p.k_chunks = pl.k_chunks;
   p.n_tiles = pl.n_tiles;
-  p.stages = pl.stages;
-  dim3 grid(pl.n_tiles, S, pl.m_tiles);
-  switch (pl.MT) {
-    case 16: return launch_tc_op<16>(p, tw, tx, grid, pl.smem, st);
-    case 32: return launch_tc_op<32>(p, tw, tx, grid, pl.smem, st);
-    case 64: return launch_tc_op<64>(p, tw, tx, grid, pl.smem, st);
-    case 128: return launch_tc_op<128>(p, tw, tx, grid, pl.smem, st);
-    default: return launch_tc_op<256>(p, tw, tx, grid, pl.smem, st);
+  p.wstages = pl.wstages;
+  p.xstages = tc_xs_for(pl.MT, PL);
+  {
+    static const int forced = env_int("TLLM_LINEAR_NACC", 0);
+    // two MMA issuers, each with half of the accumulators (>= 1 each)
+    int nacc = forced > 0 ? forced : tc_nacc(pl.MT);
+    if (nacc > 2 * PL * (kTcBK / 16)) nacc = 2 * PL * (kTcBK / 16);
+    while (nacc > 2 && nacc * pl.MT > 512) nacc -= 2;
+    nacc = nacc < 2 ? 2 : (nacc & ~1);
+    uint32_t cols = 32;
+    while (cols < (uint32_t)(nacc * pl.MT)) cols <<= 1;
+    p.nacc = nacc;
+    p.tcols = cols;
   }
+  p.w_tiled = tiled ? 1 : 0;
+  dim3 grid(pl.n_tiles, S, pl.m_tiles);
+  if (PL == 2) return launch_tc_mt<2>(p, pl.MT, tw, tx, grid, pl.smem, st);
+  return launch_tc_mt<1>(p, pl.MT, tw, tx, grid, pl.smem, st);
 }
 
 }  // extern "C"

@@ -35,9 +35,10 @@ struct RowOut {
   float *f;
   uint16_t *s;
   size_t plane;
+  int planes;
   __device__ __forceinline__ void put(size_t i, float v) const {
     if (s)
-      store_split(s, plane, i, v);
+      store_act(s, plane, i, v, planes);
     else
       f[i] = v;
   }
@@ -45,6 +46,7 @@ struct RowOut {
 
 __global__ void rmsnorm_kernel(const float *x, const float *w, RowOut y, int N,
                                float eps) {
+  griddep_launch();
   __shared__ float red[32];
   const float *xr = x + (size_t)blockIdx.x * N;
   const size_t o = (size_t)blockIdx.x * N;
@@ -58,6 +60,7 @@ __global__ void rmsnorm_kernel(const float *x, const float *w, RowOut y, int N,
 // two-pass LayerNorm (triton_llm/kernels/layernorm.py:56-66)
 __global__ void layernorm_kernel(const float *x, const float *g, const float *b,
                                  RowOut y, int N, float eps) {
+  griddep_launch();
   __shared__ float red[32];
   const float *xr = x + (size_t)blockIdx.x * N;
   const size_t o = (size_t)blockIdx.x * N;
@@ -75,19 +78,22 @@ __global__ void layernorm_kernel(const float *x, const float *g, const float *b,
     y.put(o + i, (xr[i] - mean) * rstd * g[i] + b[i]);
 }
 
-// fp32 (rows, cols) -> TLLM_SPLIT planes of plane_rows rows
-__global__ void split_kernel(const float *x, uint16_t *y, long n, size_t plane) {
+// fp32 (rows, cols) -> operand-format planes of plane_rows rows
+__global__ void split_kernel(const float *x, uint16_t *y, long n, size_t plane,
+                             int planes) {
+  griddep_launch();
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n;
        i += (long)gridDim.x * blockDim.x)
-    store_split(y, plane, (size_t)i, x[i]);
+    store_act(y, plane, (size_t)i, x[i], planes);
 }
 
 // out[m] = wte[ids[m]] (+ wpe[pos[m]])   (triton_llm/kernels/embedding.py:75-94,
 // smollm2_triton/model.py:547-560)
-template <bool BF16>
+template <int DT>
 __global__ void embedding_kernel(const int *ids, const void *wte,
                                  const float *wpe, const int *pos, float *out,
                                  int n, int vocab, int max_pos, int *err) {
+  griddep_launch();
   const int m = blockIdx.x;
   const int id = ids[m];
   const bool ok = id >= 0 && id < vocab;
@@ -99,9 +105,13 @@ __global__ void embedding_kernel(const int *ids, const void *wte,
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     float v = 0.f;
     if (ok) {
-      if (BF16)
+      if (DT == TLLM_BF16)
         v = __uint_as_float(
             (uint32_t)static_cast<const uint16_t *>(wte)[(size_t)id * n + i] << 16);
+      else if (DT == TLLM_BF16_TILED)
+        v = __uint_as_float((uint32_t)static_cast<const uint16_t *>(
+                                wte)[tiled_index(id, i, n)]
+                            << 16);
       else
         v = static_cast<const float *>(wte)[(size_t)id * n + i];
     }
@@ -328,12 +338,14 @@ extern "C" {
 
 static int row_out(RowOut *o, void *y, int y_dtype, int y_plane_rows, int M,
                    int N) {
-  TLLM_CHECK_ARG(y_dtype == TLLM_F32 || y_dtype == TLLM_SPLIT,
-                 "y_dtype must be F32 or SPLIT");
+  TLLM_CHECK_ARG(y_dtype == TLLM_F32 || y_dtype == TLLM_SPLIT ||
+                     y_dtype == TLLM_BF16,
+                 "y_dtype must be F32, SPLIT or BF16");
   o->f = nullptr;
   o->s = nullptr;
   o->plane = 0;
-  if (y_dtype == TLLM_SPLIT) {
+  o->planes = y_dtype == TLLM_SPLIT ? 2 : 1;
+  if (y_dtype != TLLM_F32) {
     TLLM_CHECK_ARG(y_plane_rows >= M, "y_plane_rows (%d) < M (%d)",
                    y_plane_rows, M);
     o->s = static_cast<uint16_t *>(y);
@@ -377,17 +389,20 @@ int tllm_layernorm(const float *x, const float *g, const float *b, void *y,
   return TLLM_OK;
 }
 
-int tllm_split_bf16(const float *x, void *y, int rows, int cols,
+int tllm_split_bf16(const float *x, void *y, int y_dtype, int rows, int cols,
                     int plane_rows, tllm_stream_t stream) {
   TLLM_INJECT("launch");
   TLLM_CHECK_ARG(rows >= 0 && cols >= 0, "negative shape");
+  TLLM_CHECK_ARG(y_dtype == TLLM_SPLIT || y_dtype == TLLM_BF16,
+                 "y_dtype must be SPLIT or BF16");
   if (rows == 0 || cols == 0) return TLLM_OK;
   TLLM_CHECK_ARG(x && y, "NULL pointer");
   TLLM_CHECK_ARG(plane_rows >= rows, "plane_rows (%d) < rows (%d)", plane_rows,
                  rows);
   const long n = (long)rows * cols;
   split_kernel<<<grid_for(n, 256), 256, 0, resolve(stream)>>>(
-      x, static_cast<uint16_t *>(y), n, (size_t)plane_rows * cols);
+      x, static_cast<uint16_t *>(y), n, (size_t)plane_rows * cols,
+      y_dtype == TLLM_SPLIT ? 2 : 1);
   TLLM_LAUNCH_CHECK();
   return TLLM_OK;
 }
@@ -402,11 +417,19 @@ int tllm_embedding(const int32_t *ids, const void *wte, int wte_dtype,
   TLLM_CHECK_ARG(!wpe || pos, "positions are required with wpe");
   int *err = device_error_ptr();
   TLLM_CHECK_ARG(err, "device error word unavailable");
+  TLLM_CHECK_ARG(wte_dtype == TLLM_F32 || wte_dtype == TLLM_BF16 ||
+                     wte_dtype == TLLM_BF16_TILED,
+                 "wte dtype must be F32, BF16 or BF16_TILED");
+  TLLM_CHECK_ARG(wte_dtype != TLLM_BF16_TILED || n_embd % 64 == 0,
+                 "a tiled table needs n_embd %% 64 == 0");
   if (wte_dtype == TLLM_BF16)
-    embedding_kernel<true><<<M, 256, 0, resolve(stream)>>>(
+    embedding_kernel<TLLM_BF16><<<M, 256, 0, resolve(stream)>>>(
+        ids, wte, wpe, pos, out, n_embd, vocab, max_pos, err);
+  else if (wte_dtype == TLLM_BF16_TILED)
+    embedding_kernel<TLLM_BF16_TILED><<<M, 256, 0, resolve(stream)>>>(
         ids, wte, wpe, pos, out, n_embd, vocab, max_pos, err);
   else
-    embedding_kernel<false><<<M, 256, 0, resolve(stream)>>>(
+    embedding_kernel<TLLM_F32><<<M, 256, 0, resolve(stream)>>>(
         ids, wte, wpe, pos, out, n_embd, vocab, max_pos, err);
   TLLM_LAUNCH_CHECK();
   return TLLM_OK;

@@ -106,6 +106,14 @@ int sm_count() {
   return g_sms[d];
 }
 
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char *v = getenv("TLLM_NO_PDL");
+    return !(v && v[0] && v[0] != '0');
+  }();
+  return on;
+}
+
 static int *g_err_word[kMaxDevices];
 
 int *device_error_ptr() {
@@ -329,6 +337,9 @@ int tllm_device_error(int *code, int reset) {
 }
 
 int tllm_graph_capture_begin(tllm_stream_t stream) {
+  // Per-device state that kernels reach lazily (the device error word, the
+  // library stream) is created now: allocation is not allowed during capture.
+  TLLM_CHECK_ARG(device_error_ptr(), "device error word unavailable");
   TLLM_CUDA(cudaStreamBeginCapture(resolve(stream),
                                    cudaStreamCaptureModeThreadLocal));
   return TLLM_OK;

@@ -59,7 +59,7 @@ class GPT2Model:
             ))
         self.ln_f = (f32(g("ln_f.weight")), f32(g("ln_f.bias")))
         self.lm_head = Linear(self.wte, dt)              # tied (model.py:60-65)
-        self.wte_dev = self.lm_head.w
+        self.wte_dev = self.lm_head                      # embedding reads the same copy
         self.wpe_dev = f32(self.wpe)
         self.kv_cache = None
         self._cache_len = 0
@@ -73,7 +73,7 @@ class GPT2Model:
         c, n = self.config, self.n
         f = lambda *s: gpu.allocate(s, np.float32)  # noqa: E731
         # projection inputs in the tensor-core operand format for bf16 weights
-        a = (lambda r, k: gpu.split_empty(r, k)) if self.bf16 else f  # noqa: E731
+        a = (lambda r, k: gpu.act_empty(r, k, 1)) if self.bf16 else f  # noqa: E731
         self.h, self.x = f(M, n), a(M, n)
         self.q, self.attn = f(M, self.H, self.D), a(M, n)
         self.act, self.logits = a(M, 4 * n), f(M, c.vocab_size)

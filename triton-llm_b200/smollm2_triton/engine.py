@@ -24,10 +24,11 @@ KV cache layout: per layer k and v (B, n_kv_head, max_seq, head_dim), the
 reference's (n_kv_head, max_seq, d_k) (model.py:219-225) with a batch axis.
 
 Activation buffers that only feed projections (the normed x, the attention
-output, the SwiGLU output) are kept in the tensor-core operand format
-(TLLM_SPLIT, two bf16 planes) when the weights are bf16: the kernels that
-produce them write that format directly. The residual stream h, q and the
-logits stay fp32.
+output, the SwiGLU output) are kept in the tensor-core operand format when
+the weights are bf16 -- bf16 (default) or hi + lo bf16 planes
+(act_dtype="split", ~16 mantissa bits) -- and the kernels that produce them
+write that format directly. The residual stream h, q and the logits stay
+fp32.
 """
 
 from __future__ import annotations
@@ -96,12 +97,12 @@ class LlamaWeights:
         emb = w["model.embed_tokens.weight"]
         self.lm_head = Linear(w["lm_head.weight"] if "lm_head.weight" in w else emb, dt)
         if "lm_head.weight" in w:
-            self.embed = Linear(emb, dt).w
+            self.embed = Linear(emb, dt)
         else:
             if not getattr(self.config, "tie_word_embeddings", True):
                 raise KeyError("lm_head.weight is missing from weights and "
                                "tie_word_embeddings is False")
-            self.embed = self.lm_head.w        # tied: one device copy
+            self.embed = self.lm_head          # tied: one device copy
 
     # -- random-init N(0, std) on the device (benchmarks)
     def _random(self, seed, std):
@@ -116,8 +117,14 @@ class LlamaWeights:
             return t
 
         def lin(N, K):
+            if self.bf16:
+                obj = Linear.empty_bf16(N, K)
+                counter[0] += 1
+                _lib.call("tllm_fill_random", obj.w.ptr, _lib.BF16,
+                          int(obj.w.shape[0]), counter[0], float(std), None)
+                return obj
             obj = Linear.__new__(Linear)
-            obj.N, obj.K, obj.bf16, obj.b = N, K, self.bf16, None
+            obj.N, obj.K, obj.bf16, obj.b = N, K, False, None
             obj.w = rnd((N, K))
             return obj
 
@@ -136,7 +143,7 @@ class LlamaWeights:
                                     down=lin(n, self.F), ln1=norm_w(), ln2=norm_w()))
         self.norm = norm_w()
         self.lm_head = lin(self.V, n)
-        self.embed = self.lm_head.w
+        self.embed = self.lm_head
 
     def linear_shapes(self, M):
         n, D = self.n, self.D
@@ -156,8 +163,13 @@ class LlamaSession:
 
     def __init__(self, wts: LlamaWeights, batch: int, max_seq: int,
                  max_prefill_rows: int = 0, attn_budget_bytes: int = 256 << 20,
-                 kv_dtype: str | None = None):
+                 kv_dtype: str | None = None, act_dtype: str = "bfloat16"):
         self.w = wts
+        # projection inputs: "bfloat16" (one bf16 plane) or "split" (bf16
+        # hi + lo, ~16 mantissa bits); fp32 weights take fp32 activations
+        if act_dtype not in ("bfloat16", "bf16", "split"):
+            raise ValueError(f"act_dtype must be 'bfloat16' or 'split', got {act_dtype!r}")
+        self.act_planes = 2 if act_dtype == "split" else 1
         self.B = int(batch)
         self.S = int(max_seq)
         if self.S > wts.max_pos:
@@ -192,9 +204,10 @@ class LlamaSession:
         self.graph = None
 
     def _act(self, rows, cols):
-        """A projection-input buffer: TLLM_SPLIT for bf16 weights, else fp32."""
+        """A projection-input buffer: bf16 operand format for bf16 weights,
+        else fp32."""
         if self.w.bf16:
-            return gpu.split_empty(rows, cols)
+            return gpu.act_empty(rows, cols, self.act_planes)
         return gpu.allocate((rows, cols), np.float32)
 
     def _buffers(self, M):

@@ -37,10 +37,13 @@ class SmolLM2ForCausalLM:
         ``config.torch_dtype``). Activations and accumulation are fp32.
     kv_dtype : "float32" | "bfloat16" | None
         KV cache precision when it should differ from ``dtype``.
+    act_dtype : "bfloat16" | "split"
+        Projection inputs of the bf16 path: bf16, or hi + lo bf16 planes
+        (~16 mantissa bits, twice the tensor-core work).
     """
 
     def __init__(self, config: SmolLM2Config, weights: dict, dtype: str | None = None,
-                 kv_dtype: str | None = None):
+                 kv_dtype: str | None = None, act_dtype: str = "bfloat16"):
         self.config = config
         if config.n_head % config.n_kv_head != 0:
             raise ValueError(
@@ -52,6 +55,7 @@ class SmolLM2ForCausalLM:
         self._weights = weights
         self._dtype = dtype
         self._kv_dtype = kv_dtype
+        self._act_dtype = act_dtype
         self._gpu_initialized = False
         self.dev: LlamaWeights | None = None
         self.session: LlamaSession | None = None
@@ -78,7 +82,8 @@ class SmolLM2ForCausalLM:
                 f"max_position_embeddings ({self.config.max_position_embeddings})")
         self._init_gpu_weights()
         if self.session is None or self.session.S != max_seq or self.session.B != 1:
-            self.session = LlamaSession(self.dev, 1, max_seq, kv_dtype=self._kv_dtype)
+            self.session = LlamaSession(self.dev, 1, max_seq, kv_dtype=self._kv_dtype,
+                                        act_dtype=self._act_dtype)
         else:
             gpu.memset(self.session.kv_arena, 0)
         d = self.dev
@@ -218,7 +223,8 @@ class SmolLM2ForCausalLM:
             raise ValueError(f"{longest} tokens exceed max_position_embeddings "
                              f"({self.config.max_position_embeddings})")
         self._init_gpu_weights()
-        sess = LlamaSession(self.dev, len(prompts), longest, kv_dtype=self._kv_dtype)
+        sess = LlamaSession(self.dev, len(prompts), longest, kv_dtype=self._kv_dtype,
+                            act_dtype=self._act_dtype)
         logits = sess.prefill(prompts)
         gen = [[int(np.argmax(logits[b]))] for b in range(len(prompts))]
         if use_graph and max_new_tokens > 1:

@@ -35,6 +35,7 @@ F32 = 0
 BF16 = 1
 I32 = 2
 SPLIT = 3   # fp32 values as two bf16 planes (hi, lo): tensor-core operand format
+BF16_TILED = 4  # bf16 weights as contiguous 128 x 64 tiles (16 KB per tile)
 
 _vp = ctypes.c_void_p
 _i = ctypes.c_int
@@ -91,6 +92,7 @@ SIGNATURES: dict[str, list] = {
                       _i, _i, _i, _i, _i, _i, _i, _f, _vp, _sz, _vp, _vp],
     # projections
     "tllm_linear_workspace": [_i, _i, _i, _psz, _psz],
+    "tllm_linear_plan": [_i, _i, _i, _i, _pi],
     "tllm_linear": [_vp, _i, _i, _vp, _i, _i, _i, _i, _i, _vp, _vp, _i, _i, _i,
                     _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i,
                     _vp, _vp, _sz, _vp, _vp],
@@ -98,7 +100,7 @@ SIGNATURES: dict[str, list] = {
     # rows / elementwise
     "tllm_rmsnorm": [_vp, _vp, _vp, _i, _i, _i, _i, _f, _vp],
     "tllm_layernorm": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp],
-    "tllm_split_bf16": [_vp, _vp, _i, _i, _i, _vp],
+    "tllm_split_bf16": [_vp, _vp, _i, _i, _i, _i, _vp],
     "tllm_embedding": [_vp, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _vp],
     "tllm_argmax": [_vp, _i, _i, _i, _vp, _vp, _vp],
     "tllm_rope": [_vp, _vp, _vp, _i, _i, _i, _i, _vp],

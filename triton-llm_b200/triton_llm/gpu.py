@@ -216,13 +216,21 @@ def to_host(tensor: DeviceTensor):
     return out
 
 
-def split_empty(rows: int, cols: int) -> DeviceTensor:
-    """An activation buffer in the tensor-core operand format (TLLM_SPLIT):
-    shape (2, rows, cols) of bf16, plane 0 = bf16(x), plane 1 = bf16(x - hi).
-    Kernels that take activations accept it wherever they accept fp32."""
-    t = allocate((2, int(rows), int(cols)), BFLOAT16)
+def act_empty(rows: int, cols: int, planes: int = 1) -> DeviceTensor:
+    """An activation buffer in a tensor-core operand format: shape
+    (planes, rows, cols) of bf16 with plane 0 = bf16(x) and, for planes=2
+    (TLLM_SPLIT), plane 1 = bf16(x - hi); planes=1 is TLLM_BF16. Kernels
+    that take activations accept it wherever they accept fp32."""
+    if planes not in (1, 2):
+        raise ValueError(f"planes must be 1 or 2, got {planes}")
+    t = allocate((int(planes), int(rows), int(cols)), BFLOAT16)
     t.is_split = True
     return t
+
+
+def split_empty(rows: int, cols: int) -> DeviceTensor:
+    """TLLM_SPLIT activation buffer (hi and lo planes)."""
+    return act_empty(rows, cols, 2)
 
 
 def split_host(arr: np.ndarray):
@@ -233,33 +241,38 @@ def split_host(arr: np.ndarray):
     return hi, lo
 
 
-def to_device_split(arr: np.ndarray, plane_rows: int | None = None) -> DeviceTensor:
-    """Upload an fp32 (rows, cols) array in the TLLM_SPLIT format."""
+def to_device_split(arr: np.ndarray, plane_rows: int | None = None,
+                    planes: int = 2) -> DeviceTensor:
+    """Upload an fp32 (rows, cols) array in an operand format (TLLM_SPLIT
+    for planes=2, TLLM_BF16 for planes=1)."""
     a = np.ascontiguousarray(arr, dtype=np.float32)
     rows, cols = a.shape
     pr = rows if plane_rows is None else int(plane_rows)
     hi, lo = split_host(a)
-    planes = np.zeros((2, pr, cols), np.uint16)
-    planes[0, :rows], planes[1, :rows] = hi, lo
-    t = split_empty(pr, cols)
-    t.from_numpy(planes)
+    buf = np.zeros((planes, pr, cols), np.uint16)
+    buf[0, :rows] = hi
+    if planes == 2:
+        buf[1, :rows] = lo
+    t = act_empty(pr, cols, planes)
+    t.from_numpy(buf)
     return t
 
 
 def split_to_host(t: DeviceTensor, rows: int | None = None) -> np.ndarray:
-    """hi + lo of a TLLM_SPLIT buffer as fp32 (rows, cols)."""
+    """The fp32 values (hi + lo, or hi) of an operand-format buffer."""
     planes = t.to_numpy()
     n = planes.shape[1] if rows is None else int(rows)
-    hi = bf16_bits_to_f32(planes[0, :n])
-    lo = bf16_bits_to_f32(planes[1, :n])
-    return (hi + lo).astype(np.float32)
+    out = bf16_bits_to_f32(planes[0, :n])
+    if planes.shape[0] == 2:
+        out = out + bf16_bits_to_f32(planes[1, :n])
+    return out.astype(np.float32)
 
 
 def act_args(t: DeviceTensor):
     """(pointer, dtype code, rows per plane) of an activation buffer: fp32
-    (rows, cols) or TLLM_SPLIT (2, rows, cols)."""
+    (rows, cols), TLLM_SPLIT (2, rows, cols) or TLLM_BF16 (1, rows, cols)."""
     if getattr(t, "is_split", False):
-        return t.ptr, _lib.SPLIT, int(t.shape[1])
+        return t.ptr, (_lib.SPLIT if t.shape[0] == 2 else _lib.BF16), int(t.shape[1])
     return t.ptr, _lib.F32, int(t.shape[0])
 
 

@@ -12,12 +12,18 @@ import numpy as np
 from triton_llm import gpu, _lib
 
 
-def embedding_dev(ids_dev, wte_dev, out_dev, wpe_dev=None, pos_dev=None):
+def embedding_dev(ids_dev, wte, out_dev, wpe_dev=None, pos_dev=None):
+    """out[m] = wte[ids[m]] (+ wpe[pos[m]]). ``wte`` is a (V, n) DeviceTensor
+    (fp32 or bf16) or a ``Linear`` (the table tied to the lm_head, tiled when
+    bf16)."""
     M = int(np.prod(ids_dev.shape))
-    V, n = wte_dev.shape
+    if hasattr(wte, "dtype") and hasattr(wte, "K") and hasattr(wte, "w"):
+        V, n, ptr, dt = wte.N, wte.K, wte.w.ptr, wte.dtype
+    else:
+        V, n = wte.shape
+        ptr, dt = wte.ptr, (_lib.BF16 if wte.is_bf16 else _lib.F32)
     P = wpe_dev.shape[0] if wpe_dev is not None else 0
-    _lib.call("tllm_embedding", ids_dev.ptr, wte_dev.ptr,
-              _lib.BF16 if wte_dev.is_bf16 else _lib.F32,
+    _lib.call("tllm_embedding", ids_dev.ptr, ptr, dt,
               wpe_dev.ptr if wpe_dev is not None else None,
               pos_dev.ptr if pos_dev is not None else None, out_dev.ptr, M, n, V,
               P, None)

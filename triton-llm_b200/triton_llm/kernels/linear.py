@@ -12,6 +12,7 @@ shared by every projection of a model.
 from __future__ import annotations
 
 import ctypes
+import os
 
 import numpy as np
 
@@ -51,19 +52,83 @@ def qkv_rows(wq, wk, wv, D, bq=None, bk=None, bv=None):
     return w, b
 
 
+TILE_N, TILE_K = 128, 64
+
+
+def tile_bf16(bits: np.ndarray) -> np.ndarray:
+    """(N, K) bf16 bits -> the TLLM_BF16_TILED layout: contiguous 128 x 64
+    tiles in (row tile, k chunk) order, N padded to 128 with zero rows."""
+    N, K = bits.shape
+    if K % TILE_K:
+        raise ValueError(f"bf16 weights need K % {TILE_K} == 0 (K={K})")
+    n_pad = -(-N // TILE_N) * TILE_N
+    padded = np.zeros((n_pad, K), np.uint16)
+    padded[:N] = bits
+    t = padded.reshape(n_pad // TILE_N, TILE_N, K // TILE_K, TILE_K).transpose(0, 2, 1, 3)
+    return np.ascontiguousarray(t).reshape(-1)
+
+
+def untile_bf16(flat: np.ndarray, N: int, K: int) -> np.ndarray:
+    n_pad = -(-N // TILE_N) * TILE_N
+    t = flat.reshape(n_pad // TILE_N, K // TILE_K, TILE_N, TILE_K).transpose(0, 2, 1, 3)
+    return np.ascontiguousarray(t).reshape(n_pad, K)[:N]
+
+
 class Linear:
-    """A projection y = x W^T (+ b) with W (N, K) on the device."""
+    """A projection y = x W^T (+ b) with W (N, K) on the device.
+
+    bf16 weights are stored tiled (TLLM_BF16_TILED: every 128 x 64 tile the
+    tensor-core projection streams is one contiguous 16 KB block); fp32
+    weights stay row-major (N, K).
+    """
+
+    # TLLM_TILE_WEIGHTS=0 keeps bf16 weights row-major (comparisons)
+    tiled_default = os.environ.get("TLLM_TILE_WEIGHTS", "1") != "0"
 
     def __init__(self, w: np.ndarray, dtype: str = "bfloat16", bias=None):
         w = np.ascontiguousarray(w, np.float32)
         self.N, self.K = w.shape
         self.bf16 = dtype in ("bfloat16", "bf16")
-        self.w = gpu.to_device_bf16(w) if self.bf16 else gpu.to_device(w)
+        self.tiled = self.bf16 and self.tiled_default
+        if self.bf16:
+            bits = gpu.f32_to_bf16_bits(w)
+            if self.tiled:
+                flat = tile_bf16(bits)
+            else:
+                if self.K % TILE_K:
+                    raise ValueError(f"bf16 weights need K % {TILE_K} == 0 (K={self.K})")
+                flat = bits.reshape(-1)
+            self.w = gpu.allocate(flat.shape, gpu.BFLOAT16)
+            self.w.from_numpy(flat)
+        else:
+            self.w = gpu.to_device(w)
         self.b = gpu.to_device(np.ascontiguousarray(bias, np.float32)) if bias is not None else None
+
+    @classmethod
+    def empty_bf16(cls, N: int, K: int):
+        """Uninitialised bf16 weights (filled on the device)."""
+        if K % TILE_K:
+            raise ValueError(f"bf16 weights need K % {TILE_K} == 0 (K={K})")
+        obj = cls.__new__(cls)
+        obj.N, obj.K, obj.bf16, obj.b = int(N), int(K), True, None
+        obj.tiled = cls.tiled_default
+        n_pad = -(-obj.N // TILE_N) * TILE_N if obj.tiled else obj.N
+        obj.w = gpu.allocate((n_pad * obj.K,), gpu.BFLOAT16)
+        return obj
 
     @property
     def dtype(self):
-        return _lib.BF16 if self.bf16 else _lib.F32
+        if not self.bf16:
+            return _lib.F32
+        return _lib.BF16_TILED if self.tiled else _lib.BF16
+
+    def to_numpy(self) -> np.ndarray:
+        """The (N, K) weights as fp32 on the host."""
+        if not self.bf16:
+            return self.w.to_numpy()
+        flat = self.w.to_numpy()
+        bits = untile_bf16(flat, self.N, self.K) if self.tiled else flat.reshape(self.N, self.K)
+        return gpu.bf16_bits_to_f32(bits)
 
 
 class LinearWorkspace:
@@ -82,13 +147,26 @@ class LinearWorkspace:
         self.counters = gpu.zeros((max(cb_max // 4, 1),), np.int32)
 
 
-def to_split(x_dev, M=None, out=None):
-    """fp32 (rows, K) -> TLLM_SPLIT buffer (the bf16 tensor-core operand)."""
+def plan(M: int, N: int, K: int, planes: int = 1) -> dict:
+    """Launch plan of the bf16 tensor-core path (tllm_linear_plan) for
+    activations with 1 (TLLM_BF16) or 2 (TLLM_SPLIT) planes."""
+    arr = (ctypes.c_int * 8)()
+    _lib.call("tllm_linear_plan", int(M), int(N), int(K),
+              _lib.SPLIT if planes == 2 else _lib.BF16, arr)
+    keys = ("tile_m", "m_tiles", "n_tiles", "splits", "weight_stages", "smem_bytes",
+            "act_stages", "resident_ctas")
+    return dict(zip(keys, list(arr)))
+
+
+def to_split(x_dev, M=None, out=None, planes=2):
+    """fp32 (rows, K) -> operand-format buffer (TLLM_SPLIT by default)."""
     rows, K = int(x_dev.shape[0]), int(x_dev.shape[-1])
     M = rows if M is None else int(M)
     if out is None:
-        out = gpu.split_empty(rows, K)
-    _lib.call("tllm_split_bf16", x_dev.ptr, out.ptr, M, K, int(out.shape[1]), None)
+        out = gpu.act_empty(rows, K, planes)
+    _lib.call("tllm_split_bf16", x_dev.ptr, out.ptr,
+              _lib.SPLIT if out.shape[0] == 2 else _lib.BF16, M, K, int(out.shape[1]),
+              None)
     return out
 
 
