@@ -46,7 +46,14 @@ import tempfile
 import time
 from pathlib import Path
 
-import numpy as np
+# The reference arm times numpy on every host core; torchrun pins
+# OMP_NUM_THREADS=1, so the BLAS thread counts are set before numpy loads.
+if "reference" in sys.argv:
+    _n = str(len(os.sched_getaffinity(0)))
+    for _v in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
+        os.environ[_v] = _n
+
+import numpy as np  # noqa: E402
 
 REPO = Path(__file__).resolve().parent
 for _p in (REPO / "triton-llm_b200", REPO, REPO / "tests" / "golden"):
