@@ -2,7 +2,7 @@
 
     python tests/golden/gen_golden.py [--only NAME ...] [--slow]
 
-The reference (read-only checkout, default /root/reference, or
+The reference (a read-only checkout whose path is given in
 $TLLM_REFERENCE) is imported with its GPU allocator replaced by a host-memory
 stand-in and its Triton kernels run under TRITON_INTERPRET=1 (see
 ref_shim.py). Inputs come from inputs.py. Every output is the reference's

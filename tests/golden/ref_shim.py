@@ -21,7 +21,6 @@ import sys
 
 import numpy as np
 
-REF_ROOT_DEFAULT = "/root/reference"
 
 
 class HostTensor:
@@ -86,7 +85,9 @@ def install(ref_root: str | None = None):
 
     Returns the reference's ``triton_llm.gpu`` module.
     """
-    ref_root = ref_root or os.environ.get("TLLM_REFERENCE", REF_ROOT_DEFAULT)
+    ref_root = ref_root or os.environ.get("TLLM_REFERENCE")
+    if not ref_root:
+        raise RuntimeError("set TLLM_REFERENCE to the reference triton-llm checkout")
     os.environ["TRITON_INTERPRET"] = "1"
     if ref_root not in sys.path:
         sys.path.insert(0, ref_root)
