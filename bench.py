@@ -363,6 +363,83 @@ class LlamaDecodeWorkload:
         return float(np.abs(out - ref).max())
 
 
+class LlamaTPWorkload(LlamaDecodeWorkload):
+    """Llama-3.2-3B long-context decode, 8 sequences at a
+    32768-token cached context (K/V N(0, 1)), tensor-parallel by KV head over
+    the N ranks (each holds 8/N KV heads, 24/N query heads and 8192/N of the
+    FFN; o_proj and down_proj partial sums are all-reduced with NCCL and
+    added to the residual by the next RMSNorm). Every rank serves the same
+    sequences, so the total work is fixed as N grows (strong scaling)."""
+
+    name = "llama3b_tp"
+    scaling = "strong"
+    per_rank = 8
+    ctx = 32768
+
+    def __init__(self, ranks, steps, warmup):
+        self.ranks = ranks
+        self.steps, self.warmup = steps, warmup
+        self.B = 8
+        self.lens = np.full(self.B, self.ctx, np.int32)
+        self.S = ((self.ctx + steps + warmup + 2 + 63) // 64) * 64
+        self.graph_note = ""
+
+    def config(self):
+        n = self.ranks.world
+        return {"workload": "cfg5 Llama-3.2-3B long-context greedy decode, KV-head TP",
+                "model": self.model, "layers": 28, "hidden": 3072,
+                "heads": "24 q / 8 kv, head_dim 128", "ffn": 8192, "vocab": 128256,
+                "batch": self.B, "global_batch": self.B, "ctx": self.ctx,
+                "parallelism": f"tp{n} by KV head ({8 // n} kv / {24 // n} q heads, "
+                               f"ffn {8192 // n} per rank), NCCL all-reduce after "
+                               "o_proj and down_proj, replicated embedding / lm_head",
+                "weights": "random N(0,0.02) bf16 (seed 0)",
+                "kv_cache": f"bf16 (8, {8 // n}, {self.S}, 128) per layer per rank, N(0,1)",
+                "timed": "K steps, each one CUDA-graph replay of the full decode step "
+                         "including the all-reduces" + self.graph_note,
+                "l2": "inputs larger than L2"}
+
+    def setup(self):
+        from triton_llm import gpu, _lib
+        from triton_llm.tp import TPGroup
+        from smollm2_triton import SmolLM2Config
+        from smollm2_triton.engine import LlamaSession, LlamaWeights
+        self.gpu = gpu
+        r = self.ranks
+        self.tp = TPGroup(r.rank, r.world, r.local)
+        cfg = SmolLM2Config.from_pretrained(self.model)
+        self.cfg = cfg
+        self.wts = LlamaWeights(cfg, None, "bfloat16", seed=0, std=0.02, max_pos=self.S,
+                                tp_rank=r.rank, tp_size=r.world)
+        self.sess = LlamaSession(self.wts, self.B, self.S, act_dtype=self.act, tp=self.tp)
+        s = self.sess
+        _lib.call("tllm_fill_random", s.kv_arena.ptr, _lib.BF16,
+                  int(np.prod(s.kv_arena.shape)), 2000 + r.rank, 1.0, None)
+        self.ids0 = np.random.default_rng(100).integers(0, cfg.vocab_size, self.B).astype(np.int32)
+        self.reset()
+        self.launches_per_step = s.decode_step(True)
+        gpu.device_synchronize()
+        self.reset()
+        self.ids_host = gpu.pinned_empty((self.B,), np.int32)
+        self.out_host = gpu.pinned_empty((self.B,), np.int32)
+        self.h2d = self.B * 4
+        self.d2h = self.B * 4
+
+    def capture(self):
+        try:
+            self.sess.capture()
+        except Exception as e:  # NCCL inside a graph needs a capturable stream
+            self.sess.graph = None
+            self.graph_note = f" (graph capture failed, eager launches: {str(e)[:80]})"
+
+    def projection_roofline(self, gpu, peak):
+        return None
+
+    def units_per_step(self):
+        # every rank serves the same sequences: count them once per job
+        return self.B / self.ranks.world
+
+
 def llama_cpu_sample(ctx: int, steps: int, model="Llama-3.2-3B-Instruct", log=None):
     """The oracle's decode step for ONE sequence at context ``ctx`` through
     2 of the model's layers and the lm_head, timed with numpy using every
@@ -795,7 +872,8 @@ class ProjLlamaLayerWorkload(_IsolatedWorkload):
         return float(np.abs(gpu.split_to_host(self.act)[:, :32] - ref).max())
 
 
-WORKLOADS = {"llama3b": LlamaDecodeWorkload, "gqa": GQAWorkload,
+WORKLOADS = {"llama3b": LlamaDecodeWorkload, "llama3b_tp": LlamaTPWorkload,
+             "gqa": GQAWorkload,
              "gqa_llama3b": GQALlamaLayerWorkload, "proj_llama3b": ProjLlamaLayerWorkload}
 
 # ----------------------------------------------------------- CPU baseline ----
@@ -830,7 +908,7 @@ def gqa_cpu_baseline(cores, pool, budget_s=15.0):
 def cpu_baseline(name, cores, steps, pool=None, ctx=None):
     if name == "gqa":
         return gqa_cpu_baseline(cores, pool)
-    if name == "llama3b":
+    if name in ("llama3b", "llama3b_tp"):
         return llama_cpu_sample(int(ctx), steps)
     return None
 
@@ -922,6 +1000,12 @@ def run_b200(args, ranks):
     if proj:
         out["roofline_projections"] = proj
     out["_ctx_mean"] = float(np.mean(getattr(wl, "lens", [0])))
+    # graphs that hold NCCL calls go before the process group does
+    if hasattr(wl, "sess"):
+        wl.sess.graph = None
+    import gc
+    gc.collect()
+    gpu.device_synchronize()
     return out
 
 
@@ -941,6 +1025,11 @@ def reference_arm(args, ranks, cores):
         value = statistics.median(vals)
         cfg = wl.config()
         scaling = wl.scaling
+    elif args.workload == "llama3b_tp":
+        value, sample = llama_cpu_sample(LlamaTPWorkload.ctx, max(args.steps, 3))
+        cfg = {"workload": "cfg5 Llama-3.2-3B long-context greedy decode, KV-head TP",
+               "model": LlamaTPWorkload.model, "batch": 8, "ctx": LlamaTPWorkload.ctx}
+        scaling = "strong"
     else:
         from triton_llm import shard
         lens = shard.ragged_lengths(64, LlamaDecodeWorkload.lo, LlamaDecodeWorkload.hi,
@@ -973,6 +1062,7 @@ def main():
                     help="projection input format of the bf16 path")
     args = ap.parse_args()
     LlamaDecodeWorkload.act = args.act
+    LlamaTPWorkload.act = args.act
     ProjLlamaLayerWorkload.planes = 2 if args.act == "split" else 1
     args.warmup = max(args.warmup, 3)
 

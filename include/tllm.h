@@ -253,6 +253,13 @@ int tllm_gemm_f32(const float *a, const float *b, float *c, int M, int N,
 int tllm_rmsnorm(const float *x, const float *w, void *y, int y_dtype,
                  int y_plane_rows, int M, int N, float eps,
                  tllm_stream_t stream);
+/* h += add in place, then y = RMSNorm(h): the residual add of a row-sharded
+ * projection (its all-reduced partial sums) fused into the next norm
+ * (smollm2_triton/model.py:351-357: add, then rms_norm). Output as for
+ * tllm_rmsnorm. */
+int tllm_rmsnorm_add(float *h, const float *add, const float *w, void *y,
+                     int y_dtype, int y_plane_rows, int M, int N, float eps,
+                     tllm_stream_t stream);
 /* triton_llm/kernels/layernorm.py:79-152 (two-pass mean / variance);
  * output as for tllm_rmsnorm. */
 int tllm_layernorm(const float *x, const float *gamma, const float *beta,

@@ -1,0 +1,166 @@
+"""Tensor parallelism by KV head (config 5).
+
+* CPU, world size 2 (gloo): the engine's sharding (``shard_llama_layer``)
+  plus an all-reduce of the o / down partial sums reproduces the oracle's
+  full forward pass -- the TP math, independent of the GPU.
+* GPU, 2 ranks (skipped with fewer than 2 GPUs): the TP engine on the
+  Llama-3.2-3B 2-layer slice against the reference's own logits and tokens.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import inputs
+
+REPO = Path(__file__).resolve().parent.parent
+SMALL = inputs.LlamaShape(100, 128, 2, 8, 4, 256, 64)
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _tp_forward_rank(rank, world, port, out_q):
+    import torch
+    import torch.distributed as dist
+    from oracle import ops
+    from triton_llm import shard
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    shp = SMALL
+    w = inputs.llama_weights(shp, 3)
+    n, H, Hkv, F = shp.hidden_size, shp.num_attention_heads, shp.num_key_value_heads, shp.intermediate_size
+    D = n // H
+    ids = np.array([5, 17, 3, 99, 42, 7])
+    T = len(ids)
+    cos, sin = ops.precompute_cos_sin(shp.max_position_embeddings, D, shp.rope_theta)
+    h = np.asarray(w["model.embed_tokens.weight"], np.float32)[ids]
+    Hl, Hkvl, _ = shard.tp_dims(H, Hkv, F, world)
+
+    def allreduce(a):
+        t = torch.from_numpy(np.ascontiguousarray(a, np.float32))
+        dist.all_reduce(t)
+        return t.numpy()
+
+    for i in range(shp.num_hidden_layers):
+        lw = shard.shard_llama_layer(w, f"model.layers.{i}.", D, H, Hkv, F, rank, world)
+        x = ops.rms_norm(h, lw["ln1"], shp.rms_norm_eps)
+        q = ops.gemm(x, lw["q"].T).reshape(T, Hl, D).transpose(1, 0, 2).reshape(-1, D)
+        k = ops.gemm(x, lw["k"].T).reshape(T, Hkvl, D).transpose(1, 0, 2).reshape(-1, D)
+        v = ops.gemm(x, lw["v"].T).reshape(T, Hkvl, D).transpose(1, 0, 2).reshape(-1, D)
+        q = ops.apply_rope(q, cos, sin, T, 0)
+        k = ops.apply_rope(k, cos, sin, T, 0)
+        o = ops.gqa_attention(q, k, v, Hl, Hkvl, causal=True)
+        o = o.reshape(Hl, T, D).transpose(1, 0, 2).reshape(T, Hl * D)
+        h = h + allreduce(ops.gemm(o, lw["o"].T))
+        x = ops.rms_norm(h, lw["ln2"], shp.rms_norm_eps)
+        act = ops.swiglu(ops.gemm(x, lw["gate"].T), ops.gemm(x, lw["up"].T))
+        h = h + allreduce(ops.gemm(act, lw["down"].T))
+    x = ops.rms_norm(h, np.asarray(w["model.norm.weight"], np.float32), shp.rms_norm_eps)
+    logits = ops.gemm(x, np.asarray(w["model.embed_tokens.weight"], np.float32).T)
+    dist.destroy_process_group()
+    if rank == 0:
+        out_q.put(logits)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_sharding_matches_full_model(world):
+    import multiprocessing as mp
+    from oracle.models import SmolLM2Oracle
+    from smollm2_triton import SmolLM2Config
+    ctx = mp.get_context("spawn")
+    qu = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_tp_forward_rank, args=(r, world, port, qu))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    got = qu.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    w = inputs.llama_weights(SMALL, 3)
+    o = SmolLM2Oracle(SmolLM2Config(**SMALL.config_kwargs()), w)
+    o.init_cache(16)
+    ref = o.forward_cached(np.array([[5, 17, 3, 99, 42, 7]]))[0]
+    np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-5)
+
+
+def test_tp_dims_reject_uneven():
+    from triton_llm import shard
+    assert shard.tp_dims(24, 8, 8192, 8) == (3, 1, 1024)
+    with pytest.raises(ValueError):
+        shard.tp_dims(9, 3, 1536, 2)
+
+
+_GPU_TP = r"""
+import os, sys, json
+import numpy as np
+sys.path[:0] = [os.path.join(os.getcwd(), p) for p in ("triton-llm_b200", ".", "tests/golden")]
+import torch, torch.distributed as dist
+import inputs
+rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+dist.init_process_group("nccl", device_id=torch.device("cuda", rank))
+from triton_llm import gpu
+from triton_llm.tp import TPGroup
+from smollm2_triton import SmolLM2Config
+from smollm2_triton.engine import LlamaSession, LlamaWeights
+tp = TPGroup(rank, world, rank)
+g = np.load("tests/golden/llama3b_2l_slice.npz")
+w = inputs.round_linear_weights_bf16(inputs.llama_weights(inputs.LLAMA3B_2L, 0))
+cfg = SmolLM2Config(**inputs.LLAMA3B_2L.config_kwargs())
+wts = LlamaWeights(cfg, w, "bfloat16", max_pos=64, tp_rank=rank, tp_size=world)
+prompt = g["tokens"][:4].tolist()
+sess = LlamaSession(wts, 1, 8, kv_dtype="float32", act_dtype="split", tp=tp)
+logits = [sess.prefill([prompt])[0]]
+toks = prompt + [int(np.argmax(logits[0]))]
+sess.decode_step(sample=True)
+gpu.device_synchronize()
+logits.append(sess.logits.to_numpy()[0])
+toks.append(int(sess.ids.to_numpy()[0]))
+err = float(np.abs(np.stack(logits) - g["logits"]).max())
+if rank == 0:
+    print(json.dumps({"tokens": toks, "want": g["tokens"].tolist(), "err": err}))
+tp.barrier()
+del sess
+dist.destroy_process_group()
+"""
+
+
+def _gpu_count():
+    try:
+        out = subprocess.run(["nvidia-smi", "-L"], capture_output=True, text=True, timeout=30)
+        return len([l for l in out.stdout.splitlines() if l.startswith("GPU")])
+    except Exception:
+        return 0
+
+
+@pytest.mark.gpu
+def test_tp2_engine_matches_reference(tmp_path):
+    if _gpu_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import json
+    script = tmp_path / "tp2.py"
+    script.write_text(_GPU_TP)
+    cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run",
+           "--nnodes=1", "--nproc-per-node=2", "--master-addr", "127.0.0.1",
+           "--master-port", str(_free_port()), str(script)]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run(cmd, cwd=str(REPO), capture_output=True, text=True, env=env)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+    line = [ln for ln in r.stdout.splitlines() if ln.startswith("{")][-1]
+    d = json.loads(line)
+    assert d["tokens"] == d["want"], d
+    assert d["err"] < 1e-3, d

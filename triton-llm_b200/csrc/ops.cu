@@ -57,6 +57,27 @@ __global__ void rmsnorm_kernel(const float *x, const float *w, RowOut y, int N,
   for (int i = threadIdx.x; i < N; i += blockDim.x) y.put(o + i, (xr[i] / rms) * w[i]);
 }
 
+// h += add (in place; the residual add of a row-sharded projection whose
+// partial sums were all-reduced), then y = RMSNorm(h) -- the residual add
+// fused into the norm that follows it.
+__global__ void rmsnorm_add_kernel(float *h, const float *add, const float *w,
+                                   RowOut y, int N, float eps) {
+  griddep_launch();
+  __shared__ float red[32];
+  float *hr = h + (size_t)blockIdx.x * N;
+  const float *ar = add + (size_t)blockIdx.x * N;
+  const size_t o = (size_t)blockIdx.x * N;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < N; i += blockDim.x) {
+    const float v = hr[i] + ar[i];
+    hr[i] = v;
+    ss = fmaf(v, v, ss);
+  }
+  ss = block_sum(ss, red);
+  const float rms = sqrtf(ss / (float)N + eps);
+  for (int i = threadIdx.x; i < N; i += blockDim.x) y.put(o + i, (hr[i] / rms) * w[i]);
+}
+
 // two-pass LayerNorm (triton_llm/kernels/layernorm.py:56-66)
 __global__ void layernorm_kernel(const float *x, const float *g, const float *b,
                                  RowOut y, int N, float eps) {
@@ -369,6 +390,23 @@ int tllm_rmsnorm(const float *x, const float *w, void *y, int y_dtype,
   if (rc) return rc;
   rmsnorm_kernel<<<M, row_threads(N) > 256 ? 256 : row_threads(N), 0,
                    resolve(stream)>>>(x, w, o, N, eps);
+  TLLM_LAUNCH_CHECK();
+  return TLLM_OK;
+}
+
+int tllm_rmsnorm_add(float *h, const float *add, const float *w, void *y,
+                     int y_dtype, int y_plane_rows, int M, int N, float eps,
+                     tllm_stream_t stream) {
+  TLLM_INJECT("launch");
+  TLLM_CHECK_ARG(M >= 0 && N >= 0, "negative shape");
+  if (M == 0) return TLLM_OK;
+  TLLM_CHECK_ARG(N > 0, "RMSNorm requires the last dimension N > 0");
+  TLLM_CHECK_ARG(h && add && w && y, "NULL pointer");
+  RowOut o;
+  int rc = row_out(&o, y, y_dtype, y_plane_rows, M, N);
+  if (rc) return rc;
+  rmsnorm_add_kernel<<<M, row_threads(N) > 256 ? 256 : row_threads(N), 0,
+                       resolve(stream)>>>(h, add, w, o, N, eps);
   TLLM_LAUNCH_CHECK();
   return TLLM_OK;
 }

@@ -35,11 +35,11 @@ from __future__ import annotations
 
 import numpy as np
 
-from triton_llm import gpu, _lib
+from triton_llm import gpu, _lib, shard
 from triton_llm.kernels import gqa_rows, DecodeWorkspace
 from triton_llm.kernels.linear import (Linear, LinearWorkspace, linear, qkv_rows,
                                        swiglu_rows)
-from triton_llm.kernels.rms_norm import rms_norm_rows
+from triton_llm.kernels.rms_norm import rms_norm_add_rows, rms_norm_rows
 from triton_llm.kernels.rope import precompute_cos_sin
 from triton_llm.kernels.embedding import embedding_dev
 
@@ -53,20 +53,23 @@ class LlamaWeights:
     """All weights of a Llama-family model on the device, in kernel layout."""
 
     def __init__(self, config, weights=None, dtype=None, seed=None, std=0.02,
-                 max_pos=None):
+                 max_pos=None, tp_rank=0, tp_size=1):
         c = self.config = config
         self.dtype = _dtype_of(config, dtype)
         self.bf16 = self.dtype == "bfloat16"
-        self.H = c.num_attention_heads
-        self.Hkv = c.num_key_value_heads
         self.n = c.hidden_size
-        self.D = self.n // self.H
-        self.F = c.intermediate_size
+        self.D = self.n // c.num_attention_heads
         self.V = c.vocab_size
         self.L = c.num_hidden_layers
         self.eps = float(c.rms_norm_eps)
-        if self.H % self.Hkv:
-            raise ValueError(f"n_head ({self.H}) must be divisible by n_kv_head ({self.Hkv})")
+        if c.num_attention_heads % c.num_key_value_heads:
+            raise ValueError(f"n_head ({c.num_attention_heads}) must be divisible by "
+                             f"n_kv_head ({c.num_key_value_heads})")
+        # tensor parallelism by KV head: H, Hkv, F are this rank's shares
+        self.tp_rank, self.tp_size = int(tp_rank), int(tp_size)
+        self.H, self.Hkv, self.F = shard.tp_dims(
+            c.num_attention_heads, c.num_key_value_heads, c.intermediate_size,
+            self.tp_size)
         self.max_pos = int(max_pos or c.max_position_embeddings)
         cos, sin = precompute_cos_sin(self.max_pos, self.D, c.rope_theta)
         self.cos, self.sin = gpu.to_device(cos), gpu.to_device(sin)
@@ -79,19 +82,21 @@ class LlamaWeights:
     def _from_state_dict(self, w):
         dt = self.dtype
         f32 = lambda a: gpu.to_device(np.ascontiguousarray(a, np.float32))  # noqa: E731
+        c = self.config
         self.layers = []
         for i in range(self.L):
-            p = f"model.layers.{i}."
-            wqkv, _ = qkv_rows(w[p + "self_attn.q_proj.weight"], w[p + "self_attn.k_proj.weight"],
-                               w[p + "self_attn.v_proj.weight"], self.D)
+            lw = shard.shard_llama_layer(w, f"model.layers.{i}.", self.D,
+                                         c.num_attention_heads, c.num_key_value_heads,
+                                         c.intermediate_size, self.tp_rank, self.tp_size)
+            wqkv, _ = qkv_rows(lw["q"], lw["k"], lw["v"], self.D)
             self.layers.append(dict(
                 qkv=Linear(wqkv, dt),
-                o=Linear(w[p + "self_attn.o_proj.weight"], dt),
-                gu=Linear(swiglu_rows(np.asarray(w[p + "mlp.gate_proj.weight"], np.float32),
-                                      np.asarray(w[p + "mlp.up_proj.weight"], np.float32)), dt),
-                down=Linear(w[p + "mlp.down_proj.weight"], dt),
-                ln1=f32(w[p + "input_layernorm.weight"]),
-                ln2=f32(w[p + "post_attention_layernorm.weight"]),
+                o=Linear(lw["o"], dt),
+                gu=Linear(swiglu_rows(np.asarray(lw["gate"], np.float32),
+                                      np.asarray(lw["up"], np.float32)), dt),
+                down=Linear(lw["down"], dt),
+                ln1=f32(lw["ln1"]),
+                ln2=f32(lw["ln2"]),
             ))
         self.norm = f32(w["model.norm.weight"])
         emb = w["model.embed_tokens.weight"]
@@ -163,8 +168,16 @@ class LlamaSession:
 
     def __init__(self, wts: LlamaWeights, batch: int, max_seq: int,
                  max_prefill_rows: int = 0, attn_budget_bytes: int = 256 << 20,
-                 kv_dtype: str | None = None, act_dtype: str = "bfloat16"):
+                 kv_dtype: str | None = None, act_dtype: str = "bfloat16",
+                 tp=None):
         self.w = wts
+        # tensor parallelism: o / down produce partial sums that ``tp``
+        # (a triton_llm.tp.TPGroup) all-reduces; the residual add moves into
+        # the next RMSNorm
+        self.tp = tp
+        tp_size = tp.size if tp is not None else 1
+        if tp_size != wts.tp_size:
+            raise ValueError(f"weights are sharded {wts.tp_size}-way, group has {tp_size}")
         # projection inputs: "bfloat16" (one bf16 plane) or "split" (bf16
         # hi + lo, ~16 mantissa bits); fp32 weights take fp32 activations
         if act_dtype not in ("bfloat16", "bf16", "split"):
@@ -216,6 +229,7 @@ class LlamaSession:
         self.h, self.x = f(M, w.n), self._act(M, w.n)
         self.q, self.attn = f(M, w.H, w.D), self._act(M, w.H * w.D)
         self.act, self.logits = self._act(M, w.F), f(M, w.V)
+        self.part = f(M, w.n) if self.tp is not None and self.tp.size > 1 else None
 
     def _prefill_buffers(self, M, attn_budget):
         w = self.w
@@ -223,6 +237,7 @@ class LlamaSession:
         self.p_h, self.p_x = f(M, w.n), self._act(M, w.n)
         self.p_q, self.p_attn = f(M, w.H, w.D), self._act(M, w.H * w.D)
         self.p_act = self._act(M, w.F)
+        self.p_part = f(M, w.n) if self.part is not None else None
         self.p_ids = gpu.allocate((M,), np.int32)
         self.p_seq = gpu.allocate((M,), np.int32)
         self.p_pos = gpu.allocate((M,), np.int32)
@@ -238,11 +253,18 @@ class LlamaSession:
 
     # ------------------------------------------------------------------
     def _layer(self, i, M, h, x, q, attn, act, row_seq, row_pos, lens, ws,
-               decode, attn_ws, row_len=None, max_len=None):
+               decode, attn_ws, row_len=None, max_len=None, part=None):
+        """One layer on rows 0..M-1. With tensor parallelism (``part`` set)
+        o / down write partial sums into ``part``, which is all-reduced and
+        added to h by the next RMSNorm (this layer's second one, the next
+        layer's first, or the final norm)."""
         w = self.w
         L = w.layers[i]
         k, v = self.kv[i]
-        rms_norm_rows(h, L["ln1"], x, M, w.eps)
+        if part is not None and i > 0:
+            rms_norm_add_rows(h, part, L["ln1"], x, M, w.eps)
+        else:
+            rms_norm_rows(h, L["ln1"], x, M, w.eps)
         linear(x, L["qkv"], op=_lib.EPI_QKV, ws=ws, M=M, qkv=dict(
             cos=w.cos, sin=w.sin, row_seq=row_seq, row_pos=row_pos, q_out=q,
             k_cache=k, v_cache=v, n_head=w.H, n_kv_head=w.Hkv, head_dim=w.D,
@@ -252,10 +274,30 @@ class LlamaSession:
         gqa_rows(q, k, v, row_seq, lens if decode else row_len, attn, M, w.H,
                  w.H * w.D, w.D, w.H * w.D, w.D, self.S if decode else (max_len or self.S),
                  workspace=attn_ws)
-        linear(attn, L["o"], out_dev=h, op=_lib.EPI_RESID, resid_dev=h, ws=ws, M=M)
-        rms_norm_rows(h, L["ln2"], x, M, w.eps)
+        if part is None:
+            linear(attn, L["o"], out_dev=h, op=_lib.EPI_RESID, resid_dev=h, ws=ws, M=M)
+            rms_norm_rows(h, L["ln2"], x, M, w.eps)
+        else:
+            pm = self._rows_view(part, M)
+            linear(attn, L["o"], out_dev=part, op=_lib.EPI_STORE, ws=ws, M=M)
+            self.tp.all_reduce(pm)
+            rms_norm_add_rows(h, part, L["ln2"], x, M, w.eps)
         linear(x, L["gu"], out_dev=act, op=_lib.EPI_SWIGLU, ws=ws, M=M)
-        linear(act, L["down"], out_dev=h, op=_lib.EPI_RESID, resid_dev=h, ws=ws, M=M)
+        if part is None:
+            linear(act, L["down"], out_dev=h, op=_lib.EPI_RESID, resid_dev=h, ws=ws, M=M)
+        else:
+            linear(act, L["down"], out_dev=part, op=_lib.EPI_STORE, ws=ws, M=M)
+            self.tp.all_reduce(self._rows_view(part, M))
+
+    def _rows_view(self, t, M):
+        return t if int(t.shape[0]) == M else gpu.sub_view(t, 0, (M, int(t.shape[1])))
+
+    def _final_norm(self, h, x, M, part):
+        w = self.w
+        if part is None:
+            rms_norm_rows(h, w.norm, x, M, w.eps)
+        else:
+            rms_norm_add_rows(h, part, w.norm, x, M, w.eps)
 
     def prefill(self, prompts, all_logits=False):
         """Run the prompts of sequences 0..len(prompts)-1 through the model.
@@ -291,7 +333,11 @@ class LlamaSession:
         for i in range(w.L):
             self._layer(i, M, h, x, self.p_q, self.p_attn, self.p_act, self.p_seq,
                         self.p_pos, None, self.p_lin_ws, False, self.p_attn_ws,
-                        row_len=self.p_len, max_len=int(lens.max()))
+                        row_len=self.p_len, max_len=int(lens.max()), part=self.p_part)
+        if self.p_part is not None:
+            # complete the residual stream before it is read row by row
+            _lib.call("tllm_elementwise", _lib.EL_ADD, h.ptr, self.p_part.ptr, h.ptr,
+                      M * w.n, None)
         if all_logits:
             logits = gpu.allocate((M, w.V), np.float32)
             rms_norm_rows(h, w.norm, x, M, w.eps)
@@ -337,8 +383,8 @@ class LlamaSession:
         for i in range(w.L):
             self._layer(i, B, self.h, self.x, self.q, self.attn, self.act,
                         self.row_seq, self.pos, self.lens, self.lin_ws, True,
-                        self.attn_ws)
-        rms_norm_rows(self.h, w.norm, self.x, B, w.eps)
+                        self.attn_ws, part=self.part)
+        self._final_norm(self.h, self.x, B, self.part)
         linear(self.x, w.lm_head, out_dev=self.logits, ws=self.lin_ws, M=B)
         n = 1 + 7 * w.L + 2
         if sample:

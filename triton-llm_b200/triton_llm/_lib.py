@@ -99,6 +99,7 @@ SIGNATURES: dict[str, list] = {
     "tllm_gemm_f32": [_vp, _vp, _vp, _i, _i, _i, _vp],
     # rows / elementwise
     "tllm_rmsnorm": [_vp, _vp, _vp, _i, _i, _i, _i, _f, _vp],
+    "tllm_rmsnorm_add": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp],
     "tllm_layernorm": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp],
     "tllm_split_bf16": [_vp, _vp, _i, _i, _i, _i, _vp],
     "tllm_embedding": [_vp, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _vp],

@@ -32,3 +32,13 @@ def rms_norm_rows(x_dev, w_dev, out_dev, M: int, eps: float = 1e-5, stream=None)
     _lib.call("tllm_rmsnorm", x_dev.ptr, w_dev.ptr, ptr, dt, plane, int(M), N,
               float(eps), stream)
     return out_dev
+
+
+def rms_norm_add_rows(h_dev, add_dev, w_dev, out_dev, M: int, eps: float = 1e-5,
+                      stream=None):
+    """h += add (first M rows, in place), then out = RMSNorm(h)."""
+    N = int(h_dev.shape[-1])
+    ptr, dt, plane = gpu.act_args(out_dev)
+    _lib.call("tllm_rmsnorm_add", h_dev.ptr, add_dev.ptr, w_dev.ptr, ptr, dt, plane,
+              int(M), N, float(eps), stream)
+    return out_dev

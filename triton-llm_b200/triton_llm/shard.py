@@ -49,3 +49,42 @@ def partition(lens, n_parts: int, per_part: int | None = None) -> list[np.ndarra
 def ragged_lengths(n: int, lo: int, hi: int, seed: int) -> np.ndarray:
     """Context lengths uniform in [lo, hi] from ``np.random.default_rng(seed)``."""
     return np.random.default_rng(seed).integers(lo, hi + 1, n).astype(np.int32)
+
+
+# ---------------------------------------------------------------------------
+# Tensor parallelism by KV head (long-context decode: all ranks serve the same
+# sequences, each holds a slice of every layer and of the KV cache).
+# ---------------------------------------------------------------------------
+def tp_dims(n_head: int, n_kv_head: int, ffn: int, size: int):
+    """Per-rank head and FFN counts; rank r holds KV heads
+    [r * Hkv/size, (r + 1) * Hkv/size) and exactly the query heads that read
+    them (head h reads KV head h // (H / Hkv), attention_gqa.py:76)."""
+    if n_kv_head % size or ffn % size:
+        raise ValueError(f"{n_kv_head} KV heads / FFN {ffn} do not split over {size} ranks")
+    return n_head // size, n_kv_head // size, ffn // size
+
+
+def shard_llama_layer(w: dict, prefix: str, head_dim: int, n_head: int,
+                      n_kv_head: int, ffn: int, rank: int, size: int) -> dict:
+    """One layer's HF-layout weights for rank ``rank`` of ``size``:
+
+    q / k / v and gate / up are column-parallel (their output rows are
+    sliced), o and down are row-parallel (their input columns are sliced),
+    so rank r's o / down outputs are partial sums that an all-reduce
+    completes. Norm weights are replicated."""
+    H, Hkv, F = tp_dims(n_head, n_kv_head, ffn, size)
+    D = head_dim
+    q0, k0, f0 = rank * H * D, rank * Hkv * D, rank * F
+    p = prefix
+    g = lambda k: np.asarray(w[p + k])  # noqa: E731
+    return {
+        "q": g("self_attn.q_proj.weight")[q0:q0 + H * D],
+        "k": g("self_attn.k_proj.weight")[k0:k0 + Hkv * D],
+        "v": g("self_attn.v_proj.weight")[k0:k0 + Hkv * D],
+        "o": g("self_attn.o_proj.weight")[:, q0:q0 + H * D],
+        "gate": g("mlp.gate_proj.weight")[f0:f0 + F],
+        "up": g("mlp.up_proj.weight")[f0:f0 + F],
+        "down": g("mlp.down_proj.weight")[:, f0:f0 + F],
+        "ln1": g("input_layernorm.weight"),
+        "ln2": g("post_attention_layernorm.weight"),
+    }
