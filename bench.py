@@ -367,8 +367,10 @@ class LlamaTPWorkload(LlamaDecodeWorkload):
     """Llama-3.2-3B long-context decode, 8 sequences at a
     32768-token cached context (K/V N(0, 1)), tensor-parallel by KV head over
     the N ranks (each holds 8/N KV heads, 24/N query heads and 8192/N of the
-    FFN; o_proj and down_proj partial sums are all-reduced with NCCL and
-    added to the residual by the next RMSNorm). Every rank serves the same
+    FFN; o_proj and down_proj partial sums are all-reduced and added to the
+    residual by the next RMSNorm: by default the projection epilogue scatters
+    its rows to every rank over NVLink and the RMSNorm sums them,
+    TLLM_TP_P2P=0 uses NCCL instead). Every rank serves the same
     sequences, so the total work is fixed as N grows (strong scaling)."""
 
     name = "llama3b_tp"
@@ -383,6 +385,7 @@ class LlamaTPWorkload(LlamaDecodeWorkload):
         self.lens = np.full(self.B, self.ctx, np.int32)
         self.S = ((self.ctx + steps + warmup + 2 + 63) // 64) * 64
         self.graph_note = ""
+        self.comm = ""
 
     def config(self):
         n = self.ranks.world
@@ -391,8 +394,9 @@ class LlamaTPWorkload(LlamaDecodeWorkload):
                 "heads": "24 q / 8 kv, head_dim 128", "ffn": 8192, "vocab": 128256,
                 "batch": self.B, "global_batch": self.B, "ctx": self.ctx,
                 "parallelism": f"tp{n} by KV head ({8 // n} kv / {24 // n} q heads, "
-                               f"ffn {8192 // n} per rank), NCCL all-reduce after "
-                               "o_proj and down_proj, replicated embedding / lm_head",
+                               f"ffn {8192 // n} per rank), all-reduce after "
+                               "o_proj and down_proj: " + self.comm + ", replicated "
+                               "embedding / lm_head",
                 "weights": "random N(0,0.02) bf16 (seed 0)",
                 "kv_cache": f"bf16 (8, {8 // n}, {self.S}, 128) per layer per rank, N(0,1)",
                 "timed": "K steps, each one CUDA-graph replay of the full decode step "
@@ -413,6 +417,9 @@ class LlamaTPWorkload(LlamaDecodeWorkload):
                                 tp_rank=r.rank, tp_size=r.world)
         self.sess = LlamaSession(self.wts, self.B, self.S, act_dtype=self.act, tp=self.tp)
         s = self.sess
+        self.comm = ("fused peer-to-peer (projection epilogue stores to every rank over "
+                     "NVLink, next RMSNorm sums)" if s.peer is not None else
+                     ("NCCL" if r.world > 1 else "none (1 rank)"))
         _lib.call("tllm_fill_random", s.kv_arena.ptr, _lib.BF16,
                   int(np.prod(s.kv_arena.shape)), 2000 + r.rank, 1.0, None)
         self.ids0 = np.random.default_rng(100).integers(0, cfg.vocab_size, self.B).astype(np.int32)
@@ -1003,6 +1010,10 @@ def run_b200(args, ranks):
     # graphs that hold NCCL calls go before the process group does
     if hasattr(wl, "sess"):
         wl.sess.graph = None
+        if getattr(wl.sess, "peer", None) is not None:
+            gpu.device_synchronize()
+            ranks.barrier()   # no peer still writes into the slots
+            wl.sess.close()
     import gc
     gc.collect()
     gpu.device_synchronize()

@@ -517,3 +517,83 @@ def test_first_call_inside_graph_capture(gpu):
     r = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True,
                        cwd=str(Path(__file__).resolve().parent.parent), timeout=300)
     assert r.returncode == 0 and "ok" in r.stdout, r.stdout + r.stderr
+
+
+# ------------------------------------------------- fused peer all-reduce --
+def _peer_group_1(rows, cols):
+    """A one-rank peer group (the scatter writes this GPU's own slots)."""
+    from types import SimpleNamespace
+    from triton_llm.tp import PeerGroup
+    return PeerGroup(SimpleNamespace(rank=0, size=1, group=None, _dist=None), rows, cols)
+
+
+@pytest.mark.parametrize("planes", [2, 1])
+def test_scatter_then_rmsnorm_p2p_equals_store_then_rmsnorm_add(gpu, planes):
+    """SCATTER + tllm_rmsnorm_p2p on a one-rank group computes what STORE +
+    tllm_rmsnorm_add computes, over several calls (both slot parities) and
+    inside a replayed CUDA graph."""
+    from triton_llm import _lib
+    from triton_llm.kernels.linear import Linear, LinearWorkspace, linear
+    from triton_llm.kernels.rms_norm import rms_norm_add_rows, rms_norm_p2p_rows
+    M, N, K = 5, 576, 1536
+    rng = np.random.default_rng(31)
+    lin = Linear((rng.standard_normal((N, K), dtype=F32) * 0.05).astype(F32), "bfloat16")
+    wn = gpu.to_device(rng.standard_normal(N, dtype=F32))
+    ws = LinearWorkspace([(M, N, K)])
+    peer = _peer_group_1(8, N)
+    h0 = rng.standard_normal((M, N), dtype=F32)
+    h_ref, h_p2p = gpu.to_device(h0), gpu.to_device(h0)
+    part = gpu.allocate((M, N), np.float32)
+    y_ref, y_p2p = gpu.act_empty(M, N, planes), gpu.act_empty(M, N, planes)
+    x = gpu.act_empty(M, K, planes)
+
+    def check(tag):
+        assert np.array_equal(h_p2p.to_numpy(), h_ref.to_numpy()), tag
+        a, b = gpu.split_to_host(y_p2p), gpu.split_to_host(y_ref)
+        np.testing.assert_allclose(a, b, rtol=2e-6, atol=1e-6, err_msg=tag)
+
+    xs = [rng.standard_normal((M, K), dtype=F32) for _ in range(3)]
+    for it, xv in enumerate(xs):
+        gpu.copy_d2d(x, gpu.to_device_split(xv, planes=planes))
+        linear(x, lin, out_dev=part, op=_lib.EPI_STORE, ws=ws, M=M)
+        rms_norm_add_rows(h_ref, part, wn, y_ref, M)
+        linear(x, lin, op=_lib.EPI_SCATTER, ws=ws, M=M, p2p=peer)
+        rms_norm_p2p_rows(h_p2p, peer, wn, y_p2p, M)
+        gpu.device_synchronize()
+        check(f"call {it}")
+    g = gpu.Graph()
+    with g:
+        linear(x, lin, op=_lib.EPI_SCATTER, ws=ws, M=M, p2p=peer)
+        rms_norm_p2p_rows(h_p2p, peer, wn, y_p2p, M)
+    for it in range(3):
+        linear(x, lin, out_dev=part, op=_lib.EPI_STORE, ws=ws, M=M)
+        rms_norm_add_rows(h_ref, part, wn, y_ref, M)
+        g.launch()
+        gpu.device_synchronize()
+        check(f"replay {it}")
+    del g
+    peer.close()
+
+
+def test_scatter_rejects_bad_arguments(gpu):
+    from triton_llm import _lib
+    from triton_llm.kernels.linear import Linear, LinearWorkspace, linear
+    from triton_llm.kernels.rms_norm import rms_norm_p2p_rows
+    N, K = 256, 128
+    rng = np.random.default_rng(3)
+    w = rng.standard_normal((N, K), dtype=F32)
+    peer = _peer_group_1(4, N)
+    x = gpu.act_empty(8, K, 2)
+    ws = LinearWorkspace([(8, N, K)])
+    with pytest.raises(ValueError):      # more rows than the slots hold
+        linear(x, Linear(w, "bfloat16"), op=_lib.EPI_SCATTER, ws=ws, M=5, p2p=peer)
+    with pytest.raises(ValueError):      # fp32 weights
+        linear(gpu.to_device(np.zeros((4, K), F32)), Linear(w, "float32"),
+               op=_lib.EPI_SCATTER, ws=ws, M=4, p2p=peer)
+    with pytest.raises(ValueError):      # no group
+        linear(x, Linear(w, "bfloat16"), op=_lib.EPI_SCATTER, ws=ws, M=4)
+    with pytest.raises(ValueError):      # wider rows than the slots
+        rms_norm_p2p_rows(gpu.allocate((4, 2 * N), np.float32), peer,
+                          gpu.allocate((2 * N,), np.float32),
+                          gpu.allocate((4, 2 * N), np.float32), 4)
+    peer.close()

@@ -131,9 +131,30 @@ gpu.device_synchronize()
 logits.append(sess.logits.to_numpy()[0])
 toks.append(int(sess.ids.to_numpy()[0]))
 err = float(np.abs(np.stack(logits) - g["logits"]).max())
+# graph-captured steps: fused peer all-reduce (default) against NCCL
+runs = []
+for p2p in (True, False):
+    s2 = LlamaSession(wts, 2, 16, kv_dtype="float32", act_dtype="split", tp=tp, p2p=p2p)
+    s2.prefill([prompt, prompt[:3]])
+    s2.capture()
+    tk, lg = [], []
+    for _ in range(4):
+        s2.step()
+        gpu.device_synchronize()
+        tk.append(s2.ids.to_numpy().tolist())
+        lg.append(s2.logits.to_numpy())
+    runs.append((tk, np.stack(lg)))
+    s2.graph = None
+    tp.barrier()
+    s2.close()
+same = runs[0][0] == runs[1][0]
+p2p_err = float(np.abs(runs[0][1] - runs[1][1]).max())
 if rank == 0:
-    print(json.dumps({"tokens": toks, "want": g["tokens"].tolist(), "err": err}))
+    print(json.dumps({"tokens": toks, "want": g["tokens"].tolist(), "err": err,
+                      "p2p_same_tokens": same, "p2p_err": p2p_err,
+                      "dev_err": gpu.device_error()}))
 tp.barrier()
+sess.close()
 del sess
 dist.destroy_process_group()
 """
@@ -164,3 +185,5 @@ def test_tp2_engine_matches_reference(tmp_path):
     d = json.loads(line)
     assert d["tokens"] == d["want"], d
     assert d["err"] < 1e-3, d
+    assert d["p2p_same_tokens"] and d["p2p_err"] < 1e-3, d
+    assert d["dev_err"] == 0, d

@@ -40,6 +40,7 @@
 #include <cstdlib>
 
 #include "common.cuh"
+#include "p2p.cuh"
 
 namespace tllm {
 
@@ -59,6 +60,7 @@ enum EpiOp : int {
   EPI_GELU = 2,    // out[m, n] = gelu_tanh(acc + bias)
   EPI_SWIGLU = 3,  // out[m, j] = silu(gate_j) * up_j  (rows interleaved by 8)
   EPI_QKV = 4,     // q / k / v heads, optional RoPE, K/V into the cache
+  EPI_SCATTER = 5, // partial rows into every rank's receive slot (p2p.cu)
 };
 
 struct Epilogue {
@@ -79,6 +81,8 @@ struct Epilogue {
   int kv_bf16, max_seq, H, Hkv, D;
   int *lens_out;           // optional [B]: lens_out[seq] = pos + 1
   int *err;
+  // EPI_SCATTER
+  const P2PDev *p2p;
 };
 
 __device__ __forceinline__ float gelu_tanh(float x) {
@@ -249,6 +253,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __shared__ uint32_t s_tmem;
   __shared__ int s_wissued, s_xissued, s_consumed, s_fail;
   __shared__ int s_empty_acc[2];   // an issuer whose accumulators were never written
+  __shared__ int s_par;            // EPI_SCATTER: receive-slot parity of this call
   const int WS = p.wstages;
   uint8_t *wring = smem;
   uint8_t *xring = smem + WS * kTcW;
@@ -394,6 +399,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const bool acc_ok = mbar_wait_bounded(accb, 0);
   tc_fence_after();
   griddep_wait();   // the epilogue reads / writes buffers of earlier kernels
+  if constexpr (OP == EPI_SCATTER) {
+    if (tid == 0)
+      s_par = (*reinterpret_cast<volatile const int *>(&p.e.p2p->state[0]) + 1) & 1;
+  }
   __syncthreads();  // s_fail / s_consumed visible
   const bool valid = acc_ok && !s_fail && nch > 0;
   float *tile = reinterpret_cast<float *>(smem);
@@ -440,7 +449,34 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   for (int ml = rank + warp * S; ml < MT; ml += 4 * S) {
     const int m = mt * MT + ml;
     if (m >= p.M) break;
-    if constexpr (OP == EPI_STORE || OP == EPI_RESID || OP == EPI_GELU) {
+    if constexpr (OP == EPI_SCATTER) {
+      // this lane's 4 values, to every rank's slot (this rank's source row)
+      const int r4 = lane * 4;
+      float4 v;
+      if (S == 1) {
+        v = *reinterpret_cast<const float4 *>(&tile[ml * kTcBN + r4]);
+      } else {
+        v = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int q = 0; q < kTcMaxSplit; ++q) {
+          if (q < S) {
+            const float4 u = ld_dsmem_f32x4(tile_s + (ml * kTcBN + r4) * 4, q);
+            v.x += u.x;
+            v.y += u.y;
+            v.z += u.z;
+            v.w += u.w;
+          }
+        }
+      }
+      const P2PDev *P = p.e.p2p;
+      const int n = row0 + r4;
+      if (n < p.N) {
+        const size_t off = (((size_t)s_par * P->size + P->rank) * P->mmax + m) *
+                               P->ncols + n;
+        for (int q = 0; q < P->size; ++q)
+          *reinterpret_cast<float4 *>(P->peer_recv[q] + off) = v;
+      }
+    } else if constexpr (OP == EPI_STORE || OP == EPI_RESID || OP == EPI_GELU) {
       // this lane's 4 accumulator values (weight rows 4*lane .. +3)
       const int r4 = lane * 4;
       float4 v;
@@ -502,6 +538,28 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
         }
         epi_pair<OP>(p.e, p.N, p.M, row0 + r, m, v0, v1);
+      }
+    }
+  }
+  if constexpr (OP == EPI_SCATTER) {
+    // every CTA's rows are out; the last CTA of the grid publishes the new
+    // epoch to every rank (release, system scope)
+    __threadfence_system();
+    __syncthreads();
+    if (tid == 0) {
+      const P2PDev *P = p.e.p2p;
+      const int total = gridDim.x * gridDim.y * gridDim.z;
+      const int ticket = atomicAdd(&P->state[1], 1);
+      if (ticket == total - 1) {
+        __threadfence_system();
+        P->state[1] = 0;
+        const int e = P->state[0] + 1;
+        P->state[0] = e;
+        __threadfence_system();
+        for (int q = 0; q < P->size; ++q) {
+          int *f = P->peer_flags[q] + P->rank;
+          asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(f), "r"(e) : "memory");
+        }
       }
     }
   }
@@ -794,6 +852,8 @@ int launch_tc_op(const TcParams &p, const CUtensorMap &tw,
       return launch_tc<MT, EPI_GELU, PL>(p, tw, tx, grid, smem, st);
     case EPI_SWIGLU:
       return launch_tc<MT, EPI_SWIGLU, PL>(p, tw, tx, grid, smem, st);
+    case EPI_SCATTER:
+      return launch_tc<MT, EPI_SCATTER, PL>(p, tw, tx, grid, smem, st);
     default: return launch_tc<MT, EPI_QKV, PL>(p, tw, tx, grid, smem, st);
   }
 }
@@ -812,9 +872,12 @@ int launch_tc_mt(const TcParams &p, int MT, const CUtensorMap &tw,
 }
 
 int check_epilogue(const Epilogue &e, int N) {
-  TLLM_CHECK_ARG(e.op >= EPI_STORE && e.op <= EPI_QKV, "bad epilogue op %d",
+  TLLM_CHECK_ARG(e.op >= EPI_STORE && e.op <= EPI_SCATTER, "bad epilogue op %d",
                  e.op);
-  if (e.op == EPI_QKV) {
+  if (e.op == EPI_SCATTER) {
+    TLLM_CHECK_ARG(e.p2p, "EPI_SCATTER needs a peer group (tllm_p2p_create)");
+    TLLM_CHECK_ARG(!e.bias, "EPI_SCATTER takes no bias");
+  } else if (e.op == EPI_QKV) {
     TLLM_CHECK_ARG(e.D > 0 && e.D % 16 == 0,
                    "head_dim must be a multiple of 16");
     TLLM_CHECK_ARG(N == (e.H + 2 * e.Hkv) * e.D,
@@ -879,8 +942,8 @@ int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
                 const int32_t *row_seq, const int32_t *row_pos, float *q_out,
                 void *k_cache, void *v_cache, int kv_dtype, int max_seq,
                 int n_head, int n_kv_head, int head_dim, int32_t *lens_out,
-                void *partial, size_t partial_bytes, int32_t *counters,
-                tllm_stream_t stream) {
+                const void *p2p, void *partial, size_t partial_bytes,
+                int32_t *counters, tllm_stream_t stream) {
   TLLM_INJECT("launch");
   TLLM_CHECK_ARG(M >= 0 && N >= 0 && K >= 0, "negative shape");
   if (M == 0 || N == 0) return TLLM_OK;
@@ -920,6 +983,10 @@ int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
   e.Hkv = n_kv_head;
   e.D = head_dim;
   e.lens_out = lens_out;
+  if (op == EPI_SCATTER) {
+    e.p2p = p2p_table(p2p, M, N);
+    if (!e.p2p) return TLLM_ERR_INVALID_ARG;
+  }
   e.err = device_error_ptr();
   TLLM_CHECK_ARG(e.err, "device error word unavailable");
   int rc = check_epilogue(e, N);
@@ -927,6 +994,7 @@ int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
   cudaStream_t st = resolve(stream);
 
   if (w_dtype == TLLM_F32) {
+    TLLM_CHECK_ARG(op != EPI_SCATTER, "EPI_SCATTER needs bf16 weights");
     TLLM_CHECK_ARG(x_dtype == TLLM_F32, "fp32 weights take fp32 activations");
     TLLM_CHECK_ARG(K % 4 == 0, "K must be a multiple of 4");
     const int pairs = ((N + 15) / 16) * 8;

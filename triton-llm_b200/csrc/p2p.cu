@@ -1,0 +1,252 @@
+// Peer-to-peer all-reduce of the tensor-parallel decode, fused into the
+// kernels around it.
+//
+// The row-parallel projections of a KV-head-sharded model (o_proj,
+// down_proj) end with partial sums that every rank needs in full; the
+// reference has no multi-GPU path (its decode is batch-1 on one device,
+// smollm2_triton/model.py:351-365). Here the projection's epilogue
+// (tllm_linear op EPI_SCATTER) stores its partial rows straight into a
+// receive slot on every rank of the group over NVLink (plain stores
+// through CUDA IPC mappings) and the last CTA publishes an epoch flag to
+// every rank; the RMSNorm that follows (tllm_rmsnorm_p2p) waits for all
+// ranks' flags, sums the slots in rank order -- identical on every rank --
+// adds the sum to the residual stream and normalises.
+//
+// Buffers (one cudaMalloc per rank, exported with cudaIpcGetMemHandle):
+//   recv  [2][size][mmax][ncols] fp32   slot (parity, source rank, row)
+//   flags [size] int                    epoch last published by each rank
+// and a local state {epoch, ticket}. A call's slots have parity
+// (epoch + 1) & 1; a rank overwrites a parity two calls later only after
+// its own reader of the previous call has seen every rank's flag, which each
+// rank publishes after finishing its reader of the call before, so a slot is
+// never overwritten while someone still reads it. Every wait is bounded and
+// reports through the device error word.
+#include <cstring>
+
+#include "common.cuh"
+#include "p2p.cuh"
+
+namespace tllm {
+
+struct P2PHost {
+  P2PDev *dev;          // device copy of the table below
+  P2PDev table;
+  void *base;           // this rank's exported allocation
+  void *peer_base[kP2PMaxRanks];
+  cudaIpcMemHandle_t handle;
+  bool opened;
+};
+
+const P2PDev *p2p_table(const void *ctx, int rows, int cols) {
+  if (!ctx) {
+    set_error("NULL peer group");
+    return nullptr;
+  }
+  const P2PHost *h = static_cast<const P2PHost *>(ctx);
+  if (!h->opened) {
+    set_error("peer group not opened (tllm_p2p_open)");
+    return nullptr;
+  }
+  if (rows > h->table.mmax || cols > h->table.ncols || cols % 4 != 0) {
+    set_error("%d x %d rows do not fit the peer slots (%d x %d, cols %% 4 == 0)",
+              rows, cols, h->table.mmax, h->table.ncols);
+    return nullptr;
+  }
+  return h->dev;
+}
+
+}  // namespace tllm
+
+using namespace tllm;
+
+namespace {
+
+constexpr uint64_t kP2PWaitNs = 2000000000ull;
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__global__ void rmsnorm_p2p_kernel(float *h, const P2PDev *P, const float *w,
+                                   uint16_t *ys, float *yf, size_t yplane,
+                                   int planes, int N, float eps, int *err) {
+  griddep_launch();
+  __shared__ float red[32];
+  __shared__ int s_epoch;
+  const int m = blockIdx.x;
+  if (threadIdx.x == 0) {
+    const int e = *reinterpret_cast<volatile const int *>(&P->state[0]);
+    // after one wait has run out the group is broken: do not wait again
+    bool ok = !(*reinterpret_cast<volatile int *>(err) & DEV_ERR_WAIT_TIMEOUT);
+    for (int q = 0; q < P->size && ok; ++q) {
+      const int *f = P->flags_local + q;
+      const uint64_t t0 = globaltimer_ns();
+      for (uint32_t i = 0;; ++i) {
+        int v;
+        asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+        if (v >= e) break;
+        // bounded: ~2 s, or 2^26 polls if the timer does not advance
+        if (((i & 1023) == 1023 && globaltimer_ns() - t0 > kP2PWaitNs) ||
+            i == (1u << 26)) {
+          ok = false;
+          break;
+        }
+      }
+    }
+    if (!ok) atomicOr(err, DEV_ERR_WAIT_TIMEOUT);
+    s_epoch = e;
+  }
+  __syncthreads();
+  const int par = s_epoch & 1;
+  float *hr = h + (size_t)m * N;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < N; i += blockDim.x) {
+    float v = hr[i];
+    for (int q = 0; q < P->size; ++q)   // rank order: identical on every rank
+      v += __ldcg(&P->recv_local[(((size_t)par * P->size + q) * P->mmax + m) *
+                                     P->ncols + i]);
+    hr[i] = v;
+    ss = fmaf(v, v, ss);
+  }
+  // block sum of squares
+  for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    for (int off = 16; off > 0; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float rms = sqrtf(red[0] / (float)N + eps);
+  const size_t o = (size_t)m * N;
+  for (int i = threadIdx.x; i < N; i += blockDim.x) {
+    const float y = (hr[i] / rms) * w[i];
+    if (ys)
+      store_act(ys, yplane, o + i, y, planes);
+    else
+      yf[o + i] = y;
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int tllm_p2p_create(int size, int mmax, int ncols, void **ctx,
+                    void *ipc_handle) {
+  TLLM_CHECK_ARG(ctx && ipc_handle, "NULL output");
+  TLLM_CHECK_ARG(size >= 1 && size <= kP2PMaxRanks, "group size %d not in [1, %d]",
+                 size, kP2PMaxRanks);
+  TLLM_CHECK_ARG(mmax > 0 && ncols > 0 && ncols % 4 == 0, "bad slot shape");
+  P2PHost *h = new P2PHost();
+  memset(h, 0, sizeof(*h));
+  const size_t recv_bytes = (size_t)2 * size * mmax * ncols * sizeof(float);
+  const size_t bytes = recv_bytes + 256;   // + flags
+  void *base = nullptr;
+  cudaError_t e = cudaMalloc(&base, bytes);
+  if (e != cudaSuccess) {
+    delete h;
+    set_error("cudaMalloc of the peer buffers failed: %s", cudaGetErrorString(e));
+    return TLLM_ERR_CUDA;
+  }
+  cudaMemset(base, 0, bytes);
+  int *state = nullptr;
+  cudaMalloc(&state, 2 * sizeof(int));
+  cudaMemset(state, 0, 2 * sizeof(int));
+  P2PDev *dev = nullptr;
+  cudaMalloc(&dev, sizeof(P2PDev));
+  e = cudaIpcGetMemHandle(&h->handle, base);
+  cudaDeviceSynchronize();
+  if (e != cudaSuccess || !state || !dev) {
+    set_error("peer buffer setup failed: %s", cudaGetErrorString(e));
+    cudaFree(base);
+    delete h;
+    return TLLM_ERR_CUDA;
+  }
+  h->base = base;
+  h->dev = dev;
+  h->table.size = size;
+  h->table.mmax = mmax;
+  h->table.ncols = ncols;
+  h->table.recv_local = static_cast<float *>(base);
+  h->table.flags_local = reinterpret_cast<int *>(static_cast<char *>(base) + recv_bytes);
+  h->table.state = state;
+  memcpy(ipc_handle, &h->handle, sizeof(cudaIpcMemHandle_t));
+  *ctx = h;
+  return TLLM_OK;
+}
+
+int tllm_p2p_handle_bytes(void) { return (int)sizeof(cudaIpcMemHandle_t); }
+
+// handles: size consecutive IPC handles (tllm_p2p_handle_bytes each), in
+// rank order; this rank's own entry is ignored.
+int tllm_p2p_open(void *ctx, int rank, const void *handles) {
+  TLLM_CHECK_ARG(ctx && handles, "NULL argument");
+  P2PHost *h = static_cast<P2PHost *>(ctx);
+  P2PDev &t = h->table;
+  TLLM_CHECK_ARG(rank >= 0 && rank < t.size, "rank %d not in [0, %d)", rank, t.size);
+  t.rank = rank;
+  const size_t recv_bytes = (size_t)2 * t.size * t.mmax * t.ncols * sizeof(float);
+  for (int q = 0; q < t.size; ++q) {
+    void *p = nullptr;
+    if (q == rank) {
+      p = h->base;
+    } else {
+      cudaIpcMemHandle_t hq;
+      memcpy(&hq, static_cast<const char *>(handles) + q * sizeof(cudaIpcMemHandle_t),
+             sizeof(hq));
+      cudaError_t e = cudaIpcOpenMemHandle(&p, hq, cudaIpcMemLazyEnablePeerAccess);
+      if (e != cudaSuccess) {
+        set_error("cudaIpcOpenMemHandle(rank %d) failed: %s", q, cudaGetErrorString(e));
+        return TLLM_ERR_CUDA;
+      }
+      h->peer_base[q] = p;
+    }
+    t.peer_recv[q] = static_cast<float *>(p);
+    t.peer_flags[q] = reinterpret_cast<int *>(static_cast<char *>(p) + recv_bytes);
+  }
+  TLLM_CUDA(cudaMemcpy(h->dev, &t, sizeof(P2PDev), cudaMemcpyHostToDevice));
+  h->opened = true;
+  return TLLM_OK;
+}
+
+int tllm_p2p_destroy(void *ctx) {
+  if (!ctx) return TLLM_OK;
+  P2PHost *h = static_cast<P2PHost *>(ctx);
+  cudaDeviceSynchronize();
+  for (int q = 0; q < kP2PMaxRanks; ++q)
+    if (h->peer_base[q]) cudaIpcCloseMemHandle(h->peer_base[q]);
+  cudaFree(h->table.state);
+  cudaFree(h->dev);
+  cudaFree(h->base);
+  delete h;
+  return TLLM_OK;
+}
+
+int tllm_rmsnorm_p2p(float *h, const void *p2p, const float *w, void *y,
+                     int y_dtype, int y_plane_rows, int M, int N, float eps,
+                     tllm_stream_t stream) {
+  TLLM_INJECT("launch");
+  TLLM_CHECK_ARG(M >= 0 && N > 0, "invalid shape");
+  if (M == 0) return TLLM_OK;
+  TLLM_CHECK_ARG(h && w && y, "NULL pointer");
+  const P2PDev *P = p2p_table(p2p, M, N);
+  if (!P) return TLLM_ERR_INVALID_ARG;
+  TLLM_CHECK_ARG(y_dtype == TLLM_F32 || y_dtype == TLLM_SPLIT || y_dtype == TLLM_BF16,
+                 "y_dtype must be F32, SPLIT or BF16");
+  int *err = device_error_ptr();
+  TLLM_CHECK_ARG(err, "device error word unavailable");
+  const bool act = y_dtype != TLLM_F32;
+  TLLM_CHECK_ARG(!act || y_plane_rows >= M, "y_plane_rows < M");
+  rmsnorm_p2p_kernel<<<M, 256, 0, resolve(stream)>>>(
+      h, P, w,
+      act ? static_cast<uint16_t *>(y) : nullptr, act ? nullptr : static_cast<float *>(y),
+      act ? (size_t)y_plane_rows * N : 0, y_dtype == TLLM_SPLIT ? 2 : 1, N, eps, err);
+  TLLM_LAUNCH_CHECK();
+  return TLLM_OK;
+}
+
+}  // extern "C"

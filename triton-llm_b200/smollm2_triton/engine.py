@@ -33,15 +33,19 @@ fp32.
 
 from __future__ import annotations
 
+import os
+
 import numpy as np
 
 from triton_llm import gpu, _lib, shard
 from triton_llm.kernels import gqa_rows, DecodeWorkspace
 from triton_llm.kernels.linear import (Linear, LinearWorkspace, linear, qkv_rows,
                                        swiglu_rows)
-from triton_llm.kernels.rms_norm import rms_norm_add_rows, rms_norm_rows
+from triton_llm.kernels.rms_norm import (rms_norm_add_rows, rms_norm_p2p_rows,
+                                         rms_norm_rows)
 from triton_llm.kernels.rope import precompute_cos_sin
 from triton_llm.kernels.embedding import embedding_dev
+from triton_llm.tp import PeerGroup
 
 
 def _dtype_of(config, dtype):
@@ -169,12 +173,16 @@ class LlamaSession:
     def __init__(self, wts: LlamaWeights, batch: int, max_seq: int,
                  max_prefill_rows: int = 0, attn_budget_bytes: int = 256 << 20,
                  kv_dtype: str | None = None, act_dtype: str = "bfloat16",
-                 tp=None):
+                 tp=None, p2p: bool | None = None):
         self.w = wts
         # tensor parallelism: o / down produce partial sums that ``tp``
         # (a triton_llm.tp.TPGroup) all-reduces; the residual add moves into
-        # the next RMSNorm
+        # the next RMSNorm. Decode rows reduce through the fused peer-to-peer
+        # path (p2p=True, the default; TLLM_TP_P2P=0 turns it off), prefill
+        # rows through NCCL.
         self.tp = tp
+        if p2p is None:
+            p2p = os.environ.get("TLLM_TP_P2P", "1") != "0"
         tp_size = tp.size if tp is not None else 1
         if tp_size != wts.tp_size:
             raise ValueError(f"weights are sharded {wts.tp_size}-way, group has {tp_size}")
@@ -207,6 +215,7 @@ class LlamaSession:
         self.lens = gpu.zeros((B,), np.int32)    # keys attended in the current step
         self.ids = gpu.zeros((B,), np.int32)     # tokens fed to the next step
         self.row_seq = gpu.to_device(np.arange(B, dtype=np.int32))
+        self._p2p = bool(p2p)
         self._buffers(B)
         self.attn_ws = DecodeWorkspace(B, wts.H, Hkv, D, S,
                                        _lib.BF16 if self.kv_bf16 else _lib.F32)
@@ -230,6 +239,9 @@ class LlamaSession:
         self.q, self.attn = f(M, w.H, w.D), self._act(M, w.H * w.D)
         self.act, self.logits = self._act(M, w.F), f(M, w.V)
         self.part = f(M, w.n) if self.tp is not None and self.tp.size > 1 else None
+        self.peer = None
+        if self.part is not None and self._p2p:
+            self.peer = self.tp.peer_group(M, w.n)
 
     def _prefill_buffers(self, M, attn_budget):
         w = self.w
@@ -262,7 +274,7 @@ class LlamaSession:
         L = w.layers[i]
         k, v = self.kv[i]
         if part is not None and i > 0:
-            rms_norm_add_rows(h, part, L["ln1"], x, M, w.eps)
+            self._norm_add(h, part, L["ln1"], x, M)
         else:
             rms_norm_rows(h, L["ln1"], x, M, w.eps)
         linear(x, L["qkv"], op=_lib.EPI_QKV, ws=ws, M=M, qkv=dict(
@@ -278,16 +290,39 @@ class LlamaSession:
             linear(attn, L["o"], out_dev=h, op=_lib.EPI_RESID, resid_dev=h, ws=ws, M=M)
             rms_norm_rows(h, L["ln2"], x, M, w.eps)
         else:
-            pm = self._rows_view(part, M)
-            linear(attn, L["o"], out_dev=part, op=_lib.EPI_STORE, ws=ws, M=M)
-            self.tp.all_reduce(pm)
-            rms_norm_add_rows(h, part, L["ln2"], x, M, w.eps)
+            self._reduce(attn, L["o"], part, M, ws)
+            self._norm_add(h, part, L["ln2"], x, M)
         linear(x, L["gu"], out_dev=act, op=_lib.EPI_SWIGLU, ws=ws, M=M)
         if part is None:
             linear(act, L["down"], out_dev=h, op=_lib.EPI_RESID, resid_dev=h, ws=ws, M=M)
         else:
-            linear(act, L["down"], out_dev=part, op=_lib.EPI_STORE, ws=ws, M=M)
+            self._reduce(act, L["down"], part, M, ws)
+
+    def _reduce(self, src, lin, part, M, ws):
+        """A row-parallel projection whose partial sums the group adds:
+        ``part`` is a PeerGroup (fused: the epilogue scatters to every rank)
+        or an fp32 buffer (stored, then NCCL all-reduce)."""
+        if isinstance(part, PeerGroup):
+            linear(src, lin, op=_lib.EPI_SCATTER, ws=ws, M=M, p2p=part)
+        else:
+            linear(src, lin, out_dev=part, op=_lib.EPI_STORE, ws=ws, M=M)
             self.tp.all_reduce(self._rows_view(part, M))
+
+    def _norm_add(self, h, part, wn, x, M):
+        """h += the group's sum of the last partial rows; x = RMSNorm(h)."""
+        if isinstance(part, PeerGroup):
+            rms_norm_p2p_rows(h, part, wn, x, M, self.w.eps)
+        else:
+            rms_norm_add_rows(h, part, wn, x, M, self.w.eps)
+
+    def close(self):
+        """Release the peer group (every rank, after a barrier)."""
+        if getattr(self, "peer", None) is not None:
+            self.peer.close()
+            self.peer = None
+
+    def _decode_part(self):
+        return self.peer if self.peer is not None else self.part
 
     def _rows_view(self, t, M):
         return t if int(t.shape[0]) == M else gpu.sub_view(t, 0, (M, int(t.shape[1])))
@@ -297,7 +332,7 @@ class LlamaSession:
         if part is None:
             rms_norm_rows(h, w.norm, x, M, w.eps)
         else:
-            rms_norm_add_rows(h, part, w.norm, x, M, w.eps)
+            self._norm_add(h, part, w.norm, x, M)
 
     def prefill(self, prompts, all_logits=False):
         """Run the prompts of sequences 0..len(prompts)-1 through the model.
@@ -383,8 +418,8 @@ class LlamaSession:
         for i in range(w.L):
             self._layer(i, B, self.h, self.x, self.q, self.attn, self.act,
                         self.row_seq, self.pos, self.lens, self.lin_ws, True,
-                        self.attn_ws, part=self.part)
-        self._final_norm(self.h, self.x, B, self.part)
+                        self.attn_ws, part=self._decode_part())
+        self._final_norm(self.h, self.x, B, self._decode_part())
         linear(self.x, w.lm_head, out_dev=self.logits, ws=self.lin_ws, M=B)
         n = 1 + 7 * w.L + 2
         if sample:

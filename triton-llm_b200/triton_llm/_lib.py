@@ -95,11 +95,17 @@ SIGNATURES: dict[str, list] = {
     "tllm_linear_plan": [_i, _i, _i, _i, _pi],
     "tllm_linear": [_vp, _i, _i, _vp, _i, _i, _i, _i, _i, _vp, _vp, _i, _i, _i,
                     _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i,
-                    _vp, _vp, _sz, _vp, _vp],
+                    _vp, _vp, _vp, _sz, _vp, _vp],
     "tllm_gemm_f32": [_vp, _vp, _vp, _i, _i, _i, _vp],
     # rows / elementwise
     "tllm_rmsnorm": [_vp, _vp, _vp, _i, _i, _i, _i, _f, _vp],
     "tllm_rmsnorm_add": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp],
+    "tllm_rmsnorm_p2p": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp],
+    # peer group
+    "tllm_p2p_handle_bytes": [],
+    "tllm_p2p_create": [_i, _i, _i, ctypes.POINTER(_vp), _vp],
+    "tllm_p2p_open": [_vp, _i, _vp],
+    "tllm_p2p_destroy": [_vp],
     "tllm_layernorm": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp],
     "tllm_split_bf16": [_vp, _vp, _i, _i, _i, _i, _vp],
     "tllm_embedding": [_vp, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _vp],
@@ -110,7 +116,7 @@ SIGNATURES: dict[str, list] = {
     "tllm_fill_random": [_vp, _i, _l, ctypes.c_uint64, _f, _vp],
 }
 
-EPI_STORE, EPI_RESID, EPI_GELU, EPI_SWIGLU, EPI_QKV = 0, 1, 2, 3, 4
+EPI_STORE, EPI_RESID, EPI_GELU, EPI_SWIGLU, EPI_QKV, EPI_SCATTER = 0, 1, 2, 3, 4, 5
 EL_SWIGLU, EL_ADD, EL_GELU = 0, 1, 2
 
 _lib = None

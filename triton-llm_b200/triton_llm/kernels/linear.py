@@ -172,14 +172,14 @@ def to_split(x_dev, M=None, out=None, planes=2):
 
 def linear(x_dev, lin: Linear, out_dev=None, op=_lib.EPI_STORE, resid_dev=None,
            ws: LinearWorkspace | None = None, M=None, ld_out=0, qkv=None,
-           stream=None):
+           p2p=None, stream=None):
     """Run one projection on the first M rows of ``x_dev``.
 
     ``x_dev``: fp32 (rows, K) or TLLM_SPLIT (2, rows, K) (``gpu.split_empty``);
     bf16 weights take TLLM_SPLIT, and fp32 input is converted first.
     ``out_dev``: fp32 or TLLM_SPLIT. ``qkv`` = dict(cos, sin, row_seq,
     row_pos, q_out, k_cache, v_cache, n_head, n_kv_head, head_dim, lens_out)
-    for op QKV.
+    for op QKV. ``p2p``: a ``triton_llm.tp.PeerGroup`` for op SCATTER.
     """
     split_in = getattr(x_dev, "is_split", False)
     rows = int(x_dev.shape[1] if split_in else x_dev.shape[0])
@@ -203,7 +203,7 @@ def linear(x_dev, lin: Linear, out_dev=None, op=_lib.EPI_STORE, resid_dev=None,
         _lib.BF16 if (kc is not None and kc.is_bf16) else _lib.F32,
         int(kc.shape[2]) if kc is not None else 0, int(q.get("n_head", 0)),
         int(q.get("n_kv_head", 0)), int(q.get("head_dim", 0)),
-        _lib.ptr(q.get("lens_out")),
+        _lib.ptr(q.get("lens_out")), p2p.ctx if p2p is not None else None,
         ws.partial.ptr if ws else None, ws.partial_bytes if ws else 0,
         ws.counters.ptr if ws else None, stream)
     return out_dev

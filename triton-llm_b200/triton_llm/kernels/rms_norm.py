@@ -42,3 +42,15 @@ def rms_norm_add_rows(h_dev, add_dev, w_dev, out_dev, M: int, eps: float = 1e-5,
     _lib.call("tllm_rmsnorm_add", h_dev.ptr, add_dev.ptr, w_dev.ptr, ptr, dt, plane,
               int(M), N, float(eps), stream)
     return out_dev
+
+
+def rms_norm_p2p_rows(h_dev, peer, w_dev, out_dev, M: int, eps: float = 1e-5,
+                      stream=None):
+    """h += the sum over the peer group of the rows that the last SCATTER
+    projection sent (first M rows, in place, rank order), then
+    out = RMSNorm(h). ``peer`` is a ``triton_llm.tp.PeerGroup``."""
+    N = int(h_dev.shape[-1])
+    ptr, dt, plane = gpu.act_args(out_dev)
+    _lib.call("tllm_rmsnorm_p2p", h_dev.ptr, peer.ctx, w_dev.ptr, ptr, dt, plane,
+              int(M), N, float(eps), stream)
+    return out_dev

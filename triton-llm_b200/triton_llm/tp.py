@@ -7,11 +7,18 @@ library stream like the kernels around it (torch's current stream is set to
 the library stream, so NCCL waits for the projection and the next kernel
 waits for NCCL); it can be captured in the decode step's CUDA graph.
 torch.distributed is used only for this plumbing.
+
+``PeerGroup`` is the fused alternative for the decode rows: the projection
+epilogue (tllm_linear op SCATTER) writes its partial rows into every rank's
+receive slots over NVLink and the next RMSNorm (tllm_rmsnorm_p2p) sums them,
+so the all-reduce costs no kernel of its own and no NCCL call.
 """
 
 from __future__ import annotations
 
-from triton_llm import gpu
+import ctypes
+
+from triton_llm import _lib, gpu
 
 
 class _CudaArray:
@@ -67,3 +74,45 @@ class TPGroup:
     def barrier(self):
         if self.size > 1:
             self._dist.barrier(group=self.group, device_ids=[self.device])
+
+    def peer_group(self, rows: int, cols: int) -> "PeerGroup":
+        return PeerGroup(self, rows, cols)
+
+
+class PeerGroup:
+    """Receive slots of the fused peer-to-peer all-reduce for up to ``rows``
+    rows of ``cols`` fp32 values (tllm_p2p_create / tllm_p2p_open). The CUDA
+    IPC handles are exchanged with ``all_gather_object``; every rank of
+    ``tp`` must construct it, in the same order as its other collectives."""
+
+    def __init__(self, tp: TPGroup, rows: int, cols: int):
+        lib = _lib.load()
+        self.rows, self.cols, self.size = int(rows), int(cols), tp.size
+        handle = ctypes.create_string_buffer(lib.tllm_p2p_handle_bytes())
+        ctx = ctypes.c_void_p()
+        _lib.call("tllm_p2p_create", tp.size, self.rows, self.cols, ctypes.byref(ctx),
+                  handle)
+        self.ctx = ctx.value
+        try:
+            handles = [handle.raw]
+            if tp.size > 1:
+                handles = [None] * tp.size
+                tp._dist.all_gather_object(handles, handle.raw, group=tp.group)
+            _lib.call("tllm_p2p_open", self.ctx, tp.rank, b"".join(handles))
+        except Exception:
+            self.close()
+            raise
+        self._tp = tp
+
+    def close(self):
+        """Unmap the peers' slots and free this rank's. Call on every rank
+        after the last use (a barrier first keeps a peer from still writing)."""
+        if self.ctx is not None:
+            _lib.call("tllm_p2p_destroy", self.ctx)
+            self.ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
