@@ -442,20 +442,61 @@ class LlamaTPWorkload(LlamaDecodeWorkload):
     def projection_roofline(self, gpu, peak):
         return None
 
+    def kernel_roofline(self, gpu, peak):
+        r = super().kernel_roofline(gpu, peak)
+        r["traffic"] = None   # the committed capture is of the config-4 cache
+        return r
+
     def units_per_step(self):
         # every rank serves the same sequences: count them once per job
         return self.B / self.ranks.world
+
+
+class SmolDecodeWorkload(LlamaDecodeWorkload):
+    """SmolLM2-135M decode, 32 sequences per GPU (bf16).
+    The configuration's run is a 512-token prompt and 256 greedy steps per
+    sequence (mean context 640); here every sequence starts at context 640
+    with its K/V filled N(0, 1), and the K timed steps continue from there."""
+
+    name = "smol135m"
+    model = "SmolLM2-135M"
+    per_rank = 32
+    lo, hi = 640, 640
+
+    def config(self):
+        w = self.ranks.world
+        return {"workload": "cfg3 SmolLM2-135M batched greedy decode",
+                "model": self.model, "layers": 30, "hidden": 576,
+                "heads": "9 q / 3 kv, head_dim 64", "ffn": 1536, "vocab": 49152,
+                "batch_per_gpu": self.B, "global_batch": self.B * w,
+                "ctx": "640 for every sequence (the mean of a 512-token prompt + 256 steps)",
+                "weights": "random N(0,0.02) bf16 (seed 0), tied embeddings",
+                "projection_inputs": ("bf16 hi/lo planes" if self.act == "split" else "bf16"),
+                "kv_cache": f"bf16 (B, 3, {self.S}, 64) per layer, filled N(0,1)",
+                "parallelism": f"dp{w} (independent replicas, no collective)",
+                "timed": "K steps, each one CUDA-graph replay of the full decode step "
+                         "(embedding, 30 layers, norm, lm_head, argmax)",
+                "l2": "inputs smaller than L2 (269 MB weights + ~0.5 GB KV per step "
+                      "exceed it together; no flush)"}
+
+    def kernel_roofline(self, gpu, peak):
+        r = super().kernel_roofline(gpu, peak)
+        r["kernel"] = "gqa_decode_mma_kernel<64> (+ split merge)"
+        r["traffic"] = None
+        return r
 
 
 def llama_cpu_sample(ctx: int, steps: int, model="Llama-3.2-3B-Instruct", log=None):
     """The oracle's decode step for ONE sequence at context ``ctx`` through
     2 of the model's layers and the lm_head, timed with numpy using every
     host core, extrapolated to the full depth. Returns (tokens/s, text)."""
+    import dataclasses
     import inputs
     from oracle.models import SmolLM2Oracle
     from smollm2_triton import SmolLM2Config
     full = SmolLM2Config.from_pretrained(model)
-    shape = inputs.LLAMA3B_2L
+    shape = (inputs.LLAMA3B_2L if model.startswith("Llama")
+             else dataclasses.replace(inputs.SMOL_135M, num_hidden_layers=2))
     w = inputs.llama_weights(shape, 0)
     cfg = SmolLM2Config(**shape.config_kwargs())
     cfg.max_position_embeddings = ctx + steps + 8
@@ -880,6 +921,7 @@ class ProjLlamaLayerWorkload(_IsolatedWorkload):
 
 
 WORKLOADS = {"llama3b": LlamaDecodeWorkload, "llama3b_tp": LlamaTPWorkload,
+             "smol135m": SmolDecodeWorkload,
              "gqa": GQAWorkload,
              "gqa_llama3b": GQALlamaLayerWorkload, "proj_llama3b": ProjLlamaLayerWorkload}
 
@@ -917,6 +959,8 @@ def cpu_baseline(name, cores, steps, pool=None, ctx=None):
         return gqa_cpu_baseline(cores, pool)
     if name in ("llama3b", "llama3b_tp"):
         return llama_cpu_sample(int(ctx), steps)
+    if name == "smol135m":
+        return llama_cpu_sample(int(ctx), steps, model=SmolDecodeWorkload.model)
     return None
 
 
@@ -1041,6 +1085,12 @@ def reference_arm(args, ranks, cores):
         cfg = {"workload": "cfg5 Llama-3.2-3B long-context greedy decode, KV-head TP",
                "model": LlamaTPWorkload.model, "batch": 8, "ctx": LlamaTPWorkload.ctx}
         scaling = "strong"
+    elif args.workload == "smol135m":
+        value, sample = llama_cpu_sample(640, max(args.steps, 3),
+                                         model=SmolDecodeWorkload.model)
+        cfg = {"workload": "cfg3 SmolLM2-135M batched greedy decode",
+               "model": SmolDecodeWorkload.model, "batch": 32, "ctx": 640}
+        scaling = "weak"
     else:
         from triton_llm import shard
         lens = shard.ragged_lengths(64, LlamaDecodeWorkload.lo, LlamaDecodeWorkload.hi,

@@ -108,6 +108,61 @@ __device__ __forceinline__ void store_out(const Epilogue &e, size_t idx,
     e.out[idx] = v;
 }
 
+// Where weight row r of a QKV projection goes (r is the first row of a
+// pair r, r + 8): head, dims d0 and d1 = d0 + D/2 within the head.
+struct QkvGeom {
+  int head, local, d0, d1;
+  bool is_q, is_v;
+};
+__device__ __forceinline__ QkvGeom qkv_geom(const Epilogue &e, int r) {
+  QkvGeom g;
+  const int D = e.D;
+  g.head = r / D;
+  g.local = r - g.head * D;                      // in the first 8 of a 16
+  g.d0 = (g.local >> 4) * 8 + (g.local & 7);
+  g.d1 = g.d0 + D / 2;
+  g.is_q = g.head < e.H;
+  g.is_v = g.head >= e.H + e.Hkv;
+  return g;
+}
+// x0' = x0 c - x1 s, x1' = x0 s + x1 c with each product rounded (no FMA
+// contraction), as numpy computes rope.py:65-66
+__device__ __forceinline__ void rope_pair(float c, float s, float &x0, float &x1) {
+  const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+  const float y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+  x0 = y0;
+  x1 = y1;
+}
+// q heads to q_out (M, H, D); k / v heads into the caches at (seq, pos)
+__device__ __forceinline__ void qkv_store(const Epilogue &e, const QkvGeom &g,
+                                          int m, int pos, int seq, float x0,
+                                          float x1) {
+  const int D = e.D;
+  if (g.is_q) {
+    float *q = e.q_out + ((size_t)m * e.H + g.head) * D;
+    q[g.d0] = x0;
+    q[g.d1] = x1;
+    return;
+  }
+  const int kvh = g.is_v ? g.head - e.H - e.Hkv : g.head - e.H;
+  if (pos < 0 || pos >= e.max_seq || seq < 0) {
+    atomicOr(e.err, DEV_ERR_LEN_CLAMPED);
+    return;
+  }
+  const size_t off = (((size_t)seq * e.Hkv + kvh) * e.max_seq + pos) * D;
+  void *cache = g.is_v ? e.v_cache : e.k_cache;
+  if (e.kv_bf16) {
+    uint16_t *c = static_cast<uint16_t *>(cache) + off;
+    c[g.d0] = f32_to_bf16_bits(x0);
+    c[g.d1] = f32_to_bf16_bits(x1);
+  } else {
+    float *c = static_cast<float *>(cache) + off;
+    c[g.d0] = x0;
+    c[g.d1] = x1;
+  }
+  if (e.lens_out && g.head == e.H && g.local == 0) e.lens_out[seq] = pos + 1;
+}
+
 // Apply the epilogue to weight rows (r, r + 8) of one 16-row block at
 // activation row m. v0 = acc(r, m), v1 = acc(r + 8, m).
 template <int OP>
@@ -136,50 +191,15 @@ __device__ __forceinline__ void epi_pair(const Epilogue &e, int N, int M,
     }
   } else {  // EPI_QKV
     if (r1 >= N) return;
-    const int D = e.D;
-    const int head = r / D;
-    const int local = r - head * D;         // r is in the first 8 of a 16
-    const int blk = local >> 4;
-    const int d0 = blk * 8 + (local & 7);   // dim of v0; v1 is d0 + D/2
-    const int d1 = d0 + D / 2;
+    const QkvGeom g = qkv_geom(e, r);
     float x0 = v0 + (e.bias ? e.bias[r] : 0.f);
     float x1 = v1 + (e.bias ? e.bias[r1] : 0.f);
     const int pos = e.row_pos[m];
     const int seq = e.row_seq[m];
-    const bool is_v = head >= e.H + e.Hkv;
-    if (e.cos && !is_v) {
-      // x0' = x0 c - x1 s, x1' = x0 s + x1 c with each product rounded
-      // (no FMA contraction), as numpy computes rope.py:65-66
-      const float c = e.cos[(size_t)pos * (D / 2) + d0];
-      const float s = e.sin[(size_t)pos * (D / 2) + d0];
-      const float y0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-      const float y1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
-      x0 = y0;
-      x1 = y1;
-    }
-    if (head < e.H) {
-      float *q = e.q_out + ((size_t)m * e.H + head) * D;
-      q[d0] = x0;
-      q[d1] = x1;
-    } else {
-      const int kvh = is_v ? head - e.H - e.Hkv : head - e.H;
-      if (pos < 0 || pos >= e.max_seq || seq < 0) {
-        atomicOr(e.err, DEV_ERR_LEN_CLAMPED);
-        return;
-      }
-      const size_t off = (((size_t)seq * e.Hkv + kvh) * e.max_seq + pos) * D;
-      void *cache = is_v ? e.v_cache : e.k_cache;
-      if (e.kv_bf16) {
-        uint16_t *c = static_cast<uint16_t *>(cache) + off;
-        c[d0] = f32_to_bf16_bits(x0);
-        c[d1] = f32_to_bf16_bits(x1);
-      } else {
-        float *c = static_cast<float *>(cache) + off;
-        c[d0] = x0;
-        c[d1] = x1;
-      }
-      if (e.lens_out && head == e.H && local == 0) e.lens_out[seq] = pos + 1;
-    }
+    if (e.cos && !g.is_v && pos >= 0 && pos < e.max_seq)
+      rope_pair(e.cos[(size_t)pos * (e.D / 2) + g.d0],
+                e.sin[(size_t)pos * (e.D / 2) + g.d0], x0, x1);
+    qkv_store(e, g, m, pos, seq, x0, x1);
   }
 }
 
@@ -198,6 +218,7 @@ __device__ __forceinline__ void epi_pair_rt(const Epilogue &e, int N, int M,
 // bf16 weights, tcgen05 tensor cores
 // ------------------------------------------------------------------------
 constexpr int kTcThreads = 128;       // 4 warps: TMA, MMA, then epilogue
+constexpr int kTcRB = 4;              // epilogue rows a warp finishes at once
 constexpr int kTcBN = 128;            // weight rows per CTA (MMA M)
 constexpr int kTcBK = 64;             // K per stage (one 128-byte row)
 constexpr int kTcW = kTcBN * kTcBK * 2;  // weight tile bytes (16 KB)
@@ -446,116 +467,216 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t tile_s = smem_u32(tile);
   const int row0 = nt * kTcBN;
 #pragma unroll 1
-  for (int ml = rank + warp * S; ml < MT; ml += 4 * S) {
-    const int m = mt * MT + ml;
-    if (m >= p.M) break;
-    if constexpr (OP == EPI_SCATTER) {
-      // this lane's 4 values, to every rank's slot (this rank's source row)
-      const int r4 = lane * 4;
-      float4 v;
-      if (S == 1) {
-        v = *reinterpret_cast<const float4 *>(&tile[ml * kTcBN + r4]);
-      } else {
-        v = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int mlb = rank + warp * S; mlb < MT; mlb += 4 * S * kTcRB) {
+    int mrow[kTcRB];
+    bool in_tile[kTcRB], ok[kTcRB];
 #pragma unroll
-        for (int q = 0; q < kTcMaxSplit; ++q) {
-          if (q < S) {
-            const float4 u = ld_dsmem_f32x4(tile_s + (ml * kTcBN + r4) * 4, q);
-            v.x += u.x;
-            v.y += u.y;
-            v.z += u.z;
-            v.w += u.w;
+    for (int i = 0; i < kTcRB; ++i) {
+      const int ml = mlb + i * 4 * S;
+      mrow[i] = mt * MT + ml;
+      in_tile[i] = ml < MT;
+      ok[i] = in_tile[i] && mrow[i] < p.M;
+    }
+    if constexpr (OP == EPI_SCATTER || OP == EPI_STORE || OP == EPI_RESID ||
+                  OP == EPI_GELU) {
+      // lane l: weight rows 4l .. 4l + 3 of the tile, every row of the group
+      const int r4 = lane * 4;
+      const int n = row0 + r4;
+      float4 v[kTcRB];
+#pragma unroll
+      for (int i = 0; i < kTcRB; ++i) {
+        const int ml = mlb + i * 4 * S;
+        v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (!in_tile[i]) continue;
+        if (S == 1) {
+          v[i] = *reinterpret_cast<const float4 *>(&tile[ml * kTcBN + r4]);
+        } else {
+#pragma unroll
+          for (int q = 0; q < kTcMaxSplit; ++q) {
+            if (q < S) {
+              const float4 u = ld_dsmem_f32x4(tile_s + (ml * kTcBN + r4) * 4, q);
+              v[i].x += u.x;
+              v[i].y += u.y;
+              v[i].z += u.z;
+              v[i].w += u.w;
+            }
           }
         }
       }
-      const P2PDev *P = p.e.p2p;
-      const int n = row0 + r4;
-      if (n < p.N) {
-        const size_t off = (((size_t)s_par * P->size + P->rank) * P->mmax + m) *
-                               P->ncols + n;
-        for (int q = 0; q < P->size; ++q)
-          *reinterpret_cast<float4 *>(P->peer_recv[q] + off) = v;
-      }
-    } else if constexpr (OP == EPI_STORE || OP == EPI_RESID || OP == EPI_GELU) {
-      // this lane's 4 accumulator values (weight rows 4*lane .. +3)
-      const int r4 = lane * 4;
-      float4 v;
-      if (S == 1) {
-        v = *reinterpret_cast<const float4 *>(&tile[ml * kTcBN + r4]);
-      } else {
-        v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if constexpr (OP == EPI_SCATTER) {
+        const P2PDev *P = p.e.p2p;
+        if (n < p.N) {
 #pragma unroll
-        for (int q = 0; q < kTcMaxSplit; ++q) {
-          if (q < S) {
-            const float4 u = ld_dsmem_f32x4(tile_s + (ml * kTcBN + r4) * 4, q);
-            v.x += u.x;
-            v.y += u.y;
-            v.z += u.z;
-            v.w += u.w;
+          for (int i = 0; i < kTcRB; ++i) {
+            if (!ok[i]) continue;
+            const size_t off =
+                (((size_t)s_par * P->size + P->rank) * P->mmax + mrow[i]) * P->ncols + n;
+            for (int q = 0; q < P->size; ++q)
+              *reinterpret_cast<float4 *>(P->peer_recv[q] + off) = v[i];
           }
         }
-      }
-      const Epilogue &e = p.e;
-      const int n = row0 + r4;
-      const size_t o = (size_t)m * e.ld_out + n;
-      float a[4] = {v.x, v.y, v.z, v.w};
-      const bool full = n + 3 < p.N;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        if (!full && n + i >= p.N) continue;
-        if (e.bias) a[i] += e.bias[n + i];
-        if constexpr (OP == EPI_RESID) a[i] += e.resid[o + i];
-        if constexpr (OP == EPI_GELU) a[i] = gelu_tanh(a[i]);
-      }
-      if (full && !e.out_split && ((o & 3) == 0)) {
-        *reinterpret_cast<float4 *>(&e.out[o]) = make_float4(a[0], a[1], a[2], a[3]);
       } else {
+        const Epilogue &e = p.e;
+        const bool full = n + 3 < p.N;
+        float bias[4] = {0.f, 0.f, 0.f, 0.f};
+        if (e.bias) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          if (n + i < p.N) store_out(e, o + i, a[i]);
+          for (int k = 0; k < 4; ++k)
+            if (n + k < p.N) bias[k] = e.bias[n + k];
+        }
+        // residual rows of the whole group before the first use
+        float rv[kTcRB][4];
+#pragma unroll
+        for (int i = 0; i < kTcRB; ++i) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) rv[i][k] = 0.f;
+          if constexpr (OP == EPI_RESID) {
+            const size_t o = (size_t)mrow[i] * e.ld_out + n;
+            if (!ok[i]) continue;
+            if (full && (o & 3) == 0) {
+              const float4 t = *reinterpret_cast<const float4 *>(&e.resid[o]);
+              rv[i][0] = t.x;
+              rv[i][1] = t.y;
+              rv[i][2] = t.z;
+              rv[i][3] = t.w;
+            } else {
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                if (n + k < p.N) rv[i][k] = e.resid[o + k];
+            }
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < kTcRB; ++i) {
+          if (!ok[i]) continue;
+          const size_t o = (size_t)mrow[i] * e.ld_out + n;
+          float a[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            if (e.bias) a[k] += bias[k];
+            if constexpr (OP == EPI_RESID) a[k] = rv[i][k] + a[k];
+            if constexpr (OP == EPI_GELU) a[k] = gelu_tanh(a[k]);
+          }
+          if (full && !e.out_split && ((o & 3) == 0)) {
+            *reinterpret_cast<float4 *>(&e.out[o]) = make_float4(a[0], a[1], a[2], a[3]);
+          } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              if (n + k < p.N) store_out(e, o + k, a[k]);
+          }
+        }
       }
     } else {
       // SwiGLU / QKV combine weight rows r and r + 8 of each 16-row block:
       // lane l takes row pairs 2l and 2l + 1 of the 64 in this tile row
-      const int pr0 = lane * 2;
+      const Epilogue &e = p.e;
+      int rr[2];
+      bool live[2];
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        const int pr = pr0 + h;
-        const int r = (pr >> 3) * 16 + (pr & 7);
-        float v0, v1;
-        if (S == 1) {
-          v0 = tile[ml * kTcBN + r];
-          v1 = tile[ml * kTcBN + r + 8];
-        } else {
-          v0 = 0.f;
-          v1 = 0.f;
+        const int pr = lane * 2 + h;
+        rr[h] = (pr >> 3) * 16 + (pr & 7);
+        live[h] = row0 + rr[h] + 8 < p.N;
+      }
+      float v0[kTcRB][2], v1[kTcRB][2];
 #pragma unroll
-          for (int q = 0; q < kTcMaxSplit; ++q) {
-            if (q < S) {
-              v0 += ld_dsmem_f32(tile_s + (ml * kTcBN + r) * 4, q);
-              v1 += ld_dsmem_f32(tile_s + (ml * kTcBN + r + 8) * 4, q);
+      for (int i = 0; i < kTcRB; ++i) {
+        const int ml = mlb + i * 4 * S;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          v0[i][h] = 0.f;
+          v1[i][h] = 0.f;
+          if (!in_tile[i]) continue;
+          const int r = rr[h];
+          if (S == 1) {
+            v0[i][h] = tile[ml * kTcBN + r];
+            v1[i][h] = tile[ml * kTcBN + r + 8];
+          } else {
+#pragma unroll
+            for (int q = 0; q < kTcMaxSplit; ++q) {
+              if (q < S) {
+                v0[i][h] += ld_dsmem_f32(tile_s + (ml * kTcBN + r) * 4, q);
+                v1[i][h] += ld_dsmem_f32(tile_s + (ml * kTcBN + r + 8) * 4, q);
+              }
             }
           }
         }
-        epi_pair<OP>(p.e, p.N, p.M, row0 + r, m, v0, v1);
+      }
+      if constexpr (OP == EPI_SWIGLU) {
+#pragma unroll
+        for (int i = 0; i < kTcRB; ++i) {
+          if (!ok[i]) continue;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            if (!live[h]) continue;
+            const int r = row0 + rr[h];
+            const int j = (r >> 4) * 8 + (r & 7);
+            store_out(e, (size_t)mrow[i] * e.ld_out + j, silu_ref(v0[i][h]) * v1[i][h]);
+          }
+        }
+      } else {  // EPI_QKV
+        QkvGeom g[2];
+        float b0[2], b1[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int r = row0 + rr[h];
+          g[h] = qkv_geom(e, r);
+          b0[h] = (e.bias && live[h]) ? e.bias[r] : 0.f;
+          b1[h] = (e.bias && live[h]) ? e.bias[r + 8] : 0.f;
+        }
+        int pos[kTcRB], seq[kTcRB];
+#pragma unroll
+        for (int i = 0; i < kTcRB; ++i) {
+          pos[i] = ok[i] ? e.row_pos[mrow[i]] : -1;
+          seq[i] = ok[i] ? e.row_seq[mrow[i]] : -1;
+        }
+        float cs[kTcRB][2], sn[kTcRB][2];
+#pragma unroll
+        for (int i = 0; i < kTcRB; ++i) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            cs[i][h] = 1.f;
+            sn[i][h] = 0.f;
+            if (ok[i] && live[h] && e.cos && !g[h].is_v && pos[i] >= 0 &&
+                pos[i] < e.max_seq) {
+              const size_t t = (size_t)pos[i] * (e.D / 2) + g[h].d0;
+              cs[i][h] = e.cos[t];
+              sn[i][h] = e.sin[t];
+            }
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < kTcRB; ++i) {
+          if (!ok[i]) continue;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            if (!live[h]) continue;
+            float x0 = v0[i][h] + b0[h];
+            float x1 = v1[i][h] + b1[h];
+            if (e.cos && !g[h].is_v && pos[i] >= 0 && pos[i] < e.max_seq)
+              rope_pair(cs[i][h], sn[i][h], x0, x1);
+            qkv_store(e, g[h], mrow[i], pos[i], seq[i], x0, x1);
+          }
+        }
       }
     }
   }
   if constexpr (OP == EPI_SCATTER) {
     // every CTA's rows are out; the last CTA of the grid publishes the new
-    // epoch to every rank (release, system scope)
-    __threadfence_system();
+    // epoch to every rank (release, system scope). One fence per CTA after
+    // the barrier orders all of the CTA's stores (fences are cumulative).
     __syncthreads();
     if (tid == 0) {
       const P2PDev *P = p.e.p2p;
       const int total = gridDim.x * gridDim.y * gridDim.z;
+      asm volatile("fence.acq_rel.sys;" ::: "memory");
       const int ticket = atomicAdd(&P->state[1], 1);
       if (ticket == total - 1) {
-        __threadfence_system();
+        // every other CTA's stores before the flags
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
         P->state[1] = 0;
         const int e = P->state[0] + 1;
         P->state[0] = e;
-        __threadfence_system();
         for (int q = 0; q < P->size; ++q) {
           int *f = P->peer_flags[q] + P->rank;
           asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(f), "r"(e) : "memory");
