@@ -111,8 +111,10 @@ int tllm_stream_wait_event(tllm_stream_t stream, void *event);
 
 /* Device-side error word of the current device (bit set: 1 = a bounded
  * wait ran out, 2 = a device-side length exceeded its bound, 4 = a token id
- * was out of range). Waits for the library stream first; reset != 0 clears
- * the word. Kernels report through it instead of trapping. */
+ * was out of range, 8 = dynamic shared memory misaligned, 16 = a projection
+ * launch with an invalid pipeline layout). Waits for the library stream
+ * first; reset != 0 clears the word. Kernels report through it instead of
+ * trapping. */
 int tllm_device_error(int *code, int reset);
 
 /* CUDA graphs of the library's work (decode steps are replayed as graphs so

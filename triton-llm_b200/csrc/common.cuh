@@ -54,6 +54,7 @@ enum DeviceError : int {
   DEV_ERR_LEN_CLAMPED = 2,    // a device-side length exceeded its bound
   DEV_ERR_TOKEN_RANGE = 4,    // a token id outside [0, vocab)
   DEV_ERR_SMEM_ALIGN = 8,     // dynamic shared memory not 1024-byte aligned
+  DEV_ERR_LAYOUT = 16,        // a launch whose ring / issuer layout is invalid
 };
 int *device_error_ptr();
 

@@ -94,9 +94,13 @@ __device__ __forceinline__ float gelu_tanh(float x) {
   return 0.5f * x * (1.f + t);
 }
 __device__ __forceinline__ float silu_ref(float x) {
-  // x * sigmoid(x), sigmoid from exp(-|x|) (triton_llm/kernels/swiglu.py:51-54)
+  // x * sigmoid(x), sigmoid from exp(-|x|) (triton_llm/kernels/swiglu.py:51-54):
+  // 1 / (1 + e) for x >= 0 (the correctly rounded reciprocal, equal to the
+  // IEEE quotient), e / (1 + e) as e times it for x < 0 (within 1 ulp); no
+  // division, so the epilogue's many independent evaluations overlap
   const float e = expf(-fabsf(x));
-  const float sig = x >= 0.f ? 1.f / (1.f + e) : e / (1.f + e);
+  const float r = __frcp_rn(1.f + e);
+  const float sig = x >= 0.f ? r : e * r;
   return x * sig;
 }
 
@@ -106,6 +110,23 @@ __device__ __forceinline__ void store_out(const Epilogue &e, size_t idx,
     store_act(e.out_split, e.out_plane, idx, v, e.out_planes);
   else
     e.out[idx] = v;
+}
+
+// Two adjacent outputs idx, idx + 1 (idx even) with one store per plane.
+__device__ __forceinline__ void store_out2(const Epilogue &e, size_t idx,
+                                           float a0, float a1) {
+  if (e.out_split) {
+    const uint16_t h0 = f32_to_bf16_bits(a0), h1 = f32_to_bf16_bits(a1);
+    *reinterpret_cast<uint32_t *>(e.out_split + idx) = (uint32_t)h0 | ((uint32_t)h1 << 16);
+    if (e.out_planes == 2) {
+      const uint16_t l0 = f32_to_bf16_bits(a0 - bf16_bits_to_f32(h0));
+      const uint16_t l1 = f32_to_bf16_bits(a1 - bf16_bits_to_f32(h1));
+      *reinterpret_cast<uint32_t *>(e.out_split + e.out_plane + idx) =
+          (uint32_t)l0 | ((uint32_t)l1 << 16);
+    }
+  } else {
+    *reinterpret_cast<float2 *>(e.out + idx) = make_float2(a0, a1);
+  }
 }
 
 // Where weight row r of a QKV projection goes (r is the first row of a
@@ -217,8 +238,23 @@ __device__ __forceinline__ void epi_pair_rt(const Epilogue &e, int N, int M,
 // ------------------------------------------------------------------------
 // bf16 weights, tcgen05 tensor cores
 // ------------------------------------------------------------------------
-constexpr int kTcThreads = 128;       // 4 warps: TMA, MMA, then epilogue
+// 8 warps: warps 0-3 stream and issue (one thread each), all 8 share the
+// epilogue, where a single warp per scheduler would leave the latency of
+// TMEM, distributed shared memory and global accesses exposed
+constexpr int kTcWarps = 8;
+constexpr int kTcThreads = kTcWarps * 32;
 constexpr int kTcRB = 4;              // epilogue rows a warp finishes at once
+// MMA-issuing threads: 4 (warps 1, 3, 5, 7, two per odd scheduler), 2 when
+// four accumulators of the tile do not fit in TMEM's 512 columns. Issuer i
+// takes the chunks c = i (mod issuers), so each ring depth is a multiple of
+// the issuer count: every ring slot then belongs to one issuer, which waits
+// for the slot's fills strictly in order (an issuer may otherwise run a whole
+// ring ahead of another and pass a parity wait on a fill two phases old).
+constexpr int kTcMaxIssuers = 4;
+__host__ __device__ constexpr int tc_issuer_index(int warp) {
+  return warp == 1 ? 0 : warp == 3 ? 1 : warp == 5 ? 2 : warp == 7 ? 3
+       : kTcMaxIssuers;
+}
 constexpr int kTcBN = 128;            // weight rows per CTA (MMA M)
 constexpr int kTcBK = 64;             // K per stage (one 128-byte row)
 constexpr int kTcW = kTcBN * kTcBK * 2;  // weight tile bytes (16 KB)
@@ -229,7 +265,8 @@ constexpr int kTcMaxXS = 8;           // activation ring stages (at most)
 struct TcParams {
   Epilogue e;
   int M, N, K, S, k_chunks, n_tiles, wstages, xstages;
-  int nacc;      // independent TMEM accumulators (even, 2..8)
+  int nacc;      // independent TMEM accumulators (a multiple of issuers)
+  int issuers;   // MMA-issuing threads (2 or 4; divides both ring depths)
   uint32_t tcols;  // TMEM columns allocated (power of two >= 32)
   int w_tiled;   // TLLM_BF16_TILED weights: tile (nt, kc) = rows
                  // (nt * k_chunks + kc) * 128 .. +127 of a (., 64) view
@@ -240,13 +277,7 @@ __host__ __device__ constexpr int tc_x_bytes(int MT, int PL) {
   return PL * MT * kTcBK * 2;
 }
 // activation ring depth (default): up to 8 stages in at most 128 KB
-__host__ __device__ constexpr int tc_xs_default(int MT, int PL) {
-  return (128 * 1024) / tc_x_bytes(MT, PL) >= kTcMaxXS
-             ? kTcMaxXS
-             : ((128 * 1024) / tc_x_bytes(MT, PL) < 2
-                    ? 2
-                    : (128 * 1024) / tc_x_bytes(MT, PL));
-}
+
 // TMEM accumulators: one per MMA-issuing thread by default (the epilogue
 // sums them in fixed order); TLLM_LINEAR_NACC (even) gives each issuer more,
 // rotated over the MMAs of a chunk.
@@ -266,14 +297,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   constexpr int X_BYTES = tc_x_bytes(MT, PL);
   const uint32_t TCOLS = p.tcols;
   const int NACC = p.nacc;
+  const int NI = p.issuers;
   constexpr uint32_t IDESC = umma_idesc_bf16(kTcBN, MT);
   extern __shared__ __align__(1024) uint8_t smem[];
   __shared__ uint64_t wfull[kTcMaxWS], wempty[kTcMaxWS];
   const int kTcXS = p.xstages;
   __shared__ uint64_t xfull[kTcMaxXS], xempty[kTcMaxXS], accb[1];
   __shared__ uint32_t s_tmem;
-  __shared__ int s_wissued, s_xissued, s_consumed, s_fail;
-  __shared__ int s_empty_acc[2];   // an issuer whose accumulators were never written
+  __shared__ int s_wissued, s_xissued, s_fail;
+  __shared__ int s_empty_acc[kTcMaxIssuers];   // an issuer whose accumulators were never written
   __shared__ int s_par;            // EPI_SCATTER: receive-slot parity of this call
   const int WS = p.wstages;
   uint8_t *wring = smem;
@@ -286,6 +318,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // aligned stage buffers
   if (smem_u32(smem) & 1023) {
     if (tid == 0) atomicOr(p.e.err, DEV_ERR_SMEM_ALIGN);
+    return;
+  }
+  // every ring slot must belong to one MMA issuer (the host plans it so)
+  if (WS % NI != 0 || p.xstages % NI != 0 || NI > kTcMaxIssuers) {
+    if (tid == 0) atomicOr(p.e.err, DEV_ERR_LAYOUT);
     return;
   }
   griddep_launch();
@@ -306,13 +343,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&xfull[s], 1);
       mbar_init(&xempty[s], 1);
     }
-    mbar_init(accb, 2);   // one arrival per MMA issuer
+    mbar_init(accb, NI);   // one arrival per MMA issuer
     s_wissued = 0;
     s_xissued = 0;
-    s_consumed = 0;
     s_fail = 0;
-    s_empty_acc[0] = 0;
-    s_empty_acc[1] = 0;
+    for (int i = 0; i < kTcMaxIssuers; ++i) s_empty_acc[i] = 0;
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(&s_tmem, TCOLS);
@@ -369,18 +404,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       s_xissued = c;
     }
     __syncwarp();
-  } else if (warp == 1 || warp == 3) {
+  } else if (tc_issuer_index(warp) < NI) {
     if (lane == 0) {
-      // MMA issuers: two threads (warps 1 and 3) take alternate k-chunks,
-      // each with its own half of the accumulators, so one thread's barrier
-      // waits and MMA issue overlap the other's. Per chunk and plane:
+      // MMA issuers: NI threads (warps 1, 3, 5, 7, 4, 6 in that order,
+      // spread over the four schedulers) take k-chunks in turn, each with
+      // its own share of the accumulators, so one thread's barrier waits and
+      // MMA issue overlap the others'. Per chunk and plane:
       // D[128 x MT] += W[128 x 16] . X[MT x 16]^T for each k-slice.
-      const int who = warp == 1 ? 0 : 1;
-      const int nacc = NACC / 2;                    // accumulators per issuer
+      const int who = tc_issuer_index(warp);
+      const int nacc = NACC / NI;                   // accumulators per issuer
       const uint32_t tacc = tmem + who * nacc * MT;
       int c = who;
       bool first = true;
-      for (; c < nch; c += 2) {
+      for (; c < nch; c += NI) {
         const int ws = c % WS;
         const int xs = c % kTcXS;
         if (!mbar_wait_bounded(&wfull[ws], (c / WS) & 1) ||
@@ -406,7 +442,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         umma_commit(&xempty[xs]);
         first = false;
       }
-      if (who == 0) s_consumed = c < nch ? c : nch;
       // an issuer that got no chunk zeroes its accumulators by marking them
       if (first) s_empty_acc[who] = 1;
       umma_commit(accb);            // this issuer's MMAs complete
@@ -424,20 +459,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (tid == 0)
       s_par = (*reinterpret_cast<volatile const int *>(&p.e.p2p->state[0]) + 1) & 1;
   }
-  __syncthreads();  // s_fail / s_consumed visible
+  __syncthreads();  // s_fail visible
   const bool valid = acc_ok && !s_fail && nch > 0;
   float *tile = reinterpret_cast<float *>(smem);
-  const int r_own = warp * 32 + lane;
-  const uint32_t t_lane = tmem + ((uint32_t)(warp * 32) << 16);
+  // a warp reads the TMEM lane quarter warp % 4; warps w and w + 4 take
+  // alternate column chunks
+  const int r_own = (warp & 3) * 32 + lane;
+  const uint32_t t_lane = tmem + ((uint32_t)((warp & 3) * 32) << 16);
   // 32 columns per TMEM load (16 for the narrowest tile), one wait each
   constexpr int CW = MT >= 32 ? 32 : 16;
 #pragma unroll 1
-  for (int c0 = 0; c0 < MT; c0 += CW) {
+  for (int c0 = (warp >> 2) * CW; c0 < MT; c0 += 2 * CW) {
     float v[CW];
 #pragma unroll
     for (int j = 0; j < CW; ++j) v[j] = 0.f;
     if (valid) {
-      const int nacc = NACC / 2;
+      const int nacc = NACC / NI;
 #pragma unroll 1
       for (int acc = 0; acc < NACC; ++acc) {   // fixed order: deterministic
         if (s_empty_acc[acc / nacc]) continue;
@@ -467,12 +504,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t tile_s = smem_u32(tile);
   const int row0 = nt * kTcBN;
 #pragma unroll 1
-  for (int mlb = rank + warp * S; mlb < MT; mlb += 4 * S * kTcRB) {
+  for (int mlb = rank + warp * S; mlb < MT; mlb += kTcWarps * S * kTcRB) {
     int mrow[kTcRB];
     bool in_tile[kTcRB], ok[kTcRB];
 #pragma unroll
     for (int i = 0; i < kTcRB; ++i) {
-      const int ml = mlb + i * 4 * S;
+      const int ml = mlb + i * kTcWarps * S;
       mrow[i] = mt * MT + ml;
       in_tile[i] = ml < MT;
       ok[i] = in_tile[i] && mrow[i] < p.M;
@@ -485,7 +522,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       float4 v[kTcRB];
 #pragma unroll
       for (int i = 0; i < kTcRB; ++i) {
-        const int ml = mlb + i * 4 * S;
+        const int ml = mlb + i * kTcWarps * S;
         v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
         if (!in_tile[i]) continue;
         if (S == 1) {
@@ -581,7 +618,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       float v0[kTcRB][2], v1[kTcRB][2];
 #pragma unroll
       for (int i = 0; i < kTcRB; ++i) {
-        const int ml = mlb + i * 4 * S;
+        const int ml = mlb + i * kTcWarps * S;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           v0[i][h] = 0.f;
@@ -603,15 +640,28 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
       if constexpr (OP == EPI_SWIGLU) {
+        // pairs 2l and 2l + 1 give adjacent outputs j0, j0 + 1
+        const int r = row0 + rr[0];
+        const int j0 = (r >> 4) * 8 + (r & 7);
+        const bool pack =
+            e.out_split ? ((reinterpret_cast<uintptr_t>(e.out_split) & 3) == 0 &&
+                           (e.out_plane & 1) == 0)
+                        : (reinterpret_cast<uintptr_t>(e.out) & 7) == 0;
+        float a[kTcRB][2];
+#pragma unroll
+        for (int i = 0; i < kTcRB; ++i)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) a[i][h] = silu_ref(v0[i][h]) * v1[i][h];
 #pragma unroll
         for (int i = 0; i < kTcRB; ++i) {
           if (!ok[i]) continue;
+          const size_t o = (size_t)mrow[i] * e.ld_out + j0;
+          if (pack && live[0] && live[1] && (o & 1) == 0) {
+            store_out2(e, o, a[i][0], a[i][1]);
+          } else {
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            if (!live[h]) continue;
-            const int r = row0 + rr[h];
-            const int j = (r >> 4) * 8 + (r & 7);
-            store_out(e, (size_t)mrow[i] * e.ld_out + j, silu_ref(v0[i][h]) * v1[i][h]);
+            for (int h = 0; h < 2; ++h)
+              if (live[h]) store_out(e, o + h, a[i][h]);
           }
         }
       } else {  // EPI_QKV
@@ -696,10 +746,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     cluster_sync();
   else
     __syncthreads();
-  if (tid == 0) {
-    for (int c = s_consumed; c < s_wissued; ++c)
+  if (tid == 0 && (s_fail || !acc_ok)) {
+    // a failed wait may have left fills in flight: wait (bounded) for the
+    // last fill issued into every slot; without a failure every issued
+    // fill was consumed
+    for (int c = s_wissued > WS ? s_wissued - WS : 0; c < s_wissued; ++c)
       mbar_wait_bounded(&wfull[c % WS], (c / WS) & 1);
-    for (int c = s_consumed; c < s_xissued; ++c)
+    for (int c = s_xissued > kTcXS ? s_xissued - kTcXS : 0; c < s_xissued; ++c)
       mbar_wait_bounded(&xfull[c % kTcXS], (c / kTcXS) & 1);
   }
   if (warp == 1) tmem_free(tmem, TCOLS);
@@ -786,10 +839,38 @@ int env_int(const char *name, int dflt) {
 }
 
 // Activation ring depth (TLLM_LINEAR_XS overrides, for tuning).
+int tc_issuers_for(int MT, int PL) {
+  static const int forced = env_int("TLLM_LINEAR_ISSUERS", 0);
+  int ni = forced == 2 || forced == 4 ? forced : kTcMaxIssuers;
+  // one accumulator of MT columns per issuer in TMEM's 512 columns, and
+  // two activation stages per issuer must leave room for the weight ring
+  if (ni * MT > 512 || ni * tc_x_bytes(MT, PL) > 64 * 1024) ni = 2;
+  return ni;
+}
+
+// a ring depth rounded down to a multiple of the issuer count
+int tc_ring_for_issuers(int depth, int MT, int PL) {
+  const int ni = tc_issuers_for(MT, PL);
+  depth -= depth % ni;
+  return depth < ni ? ni : depth;
+}
+
+static int tc_ring_budget() {
+  static const int budget_kb = env_int("TLLM_LINEAR_RING_KB", 224);
+  return budget_kb * 1024;
+}
+
+// Activation ring depth: the deepest multiple of the issuer count (<= 8)
+// that leaves >= 8 weight stages; the activation tiles are L2 hits, so two
+// stages per issuer keep its next tile on the way.
 int tc_xs_for(int MT, int PL) {
   static const int forced = env_int("TLLM_LINEAR_XS", 0);
-  if (forced >= 2 && forced <= kTcMaxXS) return forced;
-  return tc_xs_default(MT, PL);
+  if (forced >= 2 && forced <= kTcMaxXS) return tc_ring_for_issuers(forced, MT, PL);
+  const int ni = tc_issuers_for(MT, PL);
+  const int xb = tc_x_bytes(MT, PL);
+  int xs = kTcMaxXS - kTcMaxXS % ni;
+  while (xs > ni && (tc_ring_budget() - xs * xb) / kTcW < 8) xs -= ni;
+  return xs;
 }
 
 // Weight ring depth: one CTA per SM with ~224 KB of rings (the activation
@@ -800,16 +881,19 @@ int tc_wstages_for(int MT, int PL) {
     const char *v = getenv("TLLM_LINEAR_WS");
     return v ? atoi(v) : 0;
   }();
-  if (forced >= 2 && forced <= kTcMaxWS) return forced;
-  static const int budget_kb = env_int("TLLM_LINEAR_RING_KB", 224);
+  if (forced >= 2 && forced <= kTcMaxWS) return tc_ring_for_issuers(forced, MT, PL);
   const int xb = tc_xs_for(MT, PL) * tc_x_bytes(MT, PL);
-  int ws = (budget_kb * 1024 - xb) / kTcW;
+  int ws = (tc_ring_budget() - xb) / kTcW;
   ws = ws < 2 ? 2 : (ws > kTcMaxWS ? kTcMaxWS : ws);
-  return ws;
+  return tc_ring_for_issuers(ws, MT, PL);
 }
 
 size_t tc_smem_for(int MT, int PL, int wstages) {
-  return (size_t)wstages * kTcW + (size_t)tc_xs_for(MT, PL) * tc_x_bytes(MT, PL);
+  const size_t rings =
+      (size_t)wstages * kTcW + (size_t)tc_xs_for(MT, PL) * tc_x_bytes(MT, PL);
+  // the epilogue stages the fp32 accumulator tile (MT x 128) in the rings
+  const size_t tile = (size_t)MT * kTcBN * 4;
+  return rings > tile ? rings : tile;
 }
 
 template <int MT, int OP, int PL>
@@ -1168,14 +1252,17 @@ int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
   p.xstages = tc_xs_for(pl.MT, PL);
   {
     static const int forced = env_int("TLLM_LINEAR_NACC", 0);
-    // two MMA issuers, each with half of the accumulators (>= 1 each)
+    // MMA issuers, each with its own accumulators (>= 1 each, 512 TMEM
+    // columns in all)
+    const int ni = tc_issuers_for(pl.MT, PL);
     int nacc = forced > 0 ? forced : tc_nacc(pl.MT);
-    if (nacc > 2 * PL * (kTcBK / 16)) nacc = 2 * PL * (kTcBK / 16);
-    while (nacc > 2 && nacc * pl.MT > 512) nacc -= 2;
-    nacc = nacc < 2 ? 2 : (nacc & ~1);
+    if (nacc > ni * PL * (kTcBK / 16)) nacc = ni * PL * (kTcBK / 16);
+    while (nacc > ni && nacc * pl.MT > 512) nacc -= ni;
+    nacc = nacc < ni ? ni : nacc - nacc % ni;
     uint32_t cols = 32;
     while (cols < (uint32_t)(nacc * pl.MT)) cols <<= 1;
     p.nacc = nacc;
+    p.issuers = ni;
     p.tcols = cols;
   }
   p.w_tiled = tiled ? 1 : 0;
