@@ -124,6 +124,7 @@ __global__ void __launch_bounds__(kThreads)
                       const __grid_constant__ CUtensorMap tmk,
                       const __grid_constant__ CUtensorMap tmv) {
   griddep_launch();
+  griddep_wait();   // q, lengths and the cache come from earlier kernels
   using S = Shape<T, D>;
   extern __shared__ __align__(1024) uint8_t smem[];
   T *k_st = reinterpret_cast<T *>(smem);
@@ -515,6 +516,7 @@ __global__ void __launch_bounds__(kThreads)
                           const __grid_constant__ CUtensorMap tmk,
                           const __grid_constant__ CUtensorMap tmv) {
   griddep_launch();
+  griddep_wait();   // q, lengths and the cache come from earlier kernels
   using S = MmaShape<D>;
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t *k_st = smem;
@@ -918,8 +920,7 @@ int launch_t(const DecodeParams &p, const CUtensorMap &mk, const CUtensorMap &mv
         kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
-  kern<<<grid, kThreads, smem, st>>>(p, mk, mv);
-  TLLM_LAUNCH_CHECK();
+  TLLM_CUDA(launch_pdl(kern, grid, dim3(kThreads), smem, st, p, mk, mv));
   return TLLM_OK;
 }
 
@@ -972,8 +973,7 @@ int launch_mma(const DecodeParams &p, int G, const CUtensorMap &mk,
         kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     if (dev >= 0 && dev < 64) configured[dev] = true;
   }
-  kern<<<grid, kThreads, smem, st>>>(p, G, mk, mv);
-  TLLM_LAUNCH_CHECK();
+  TLLM_CUDA(launch_pdl(kern, grid, dim3(kThreads), smem, st, p, G, mk, mv));
   return TLLM_OK;
 }
 

@@ -47,6 +47,7 @@ struct RowOut {
 __global__ void rmsnorm_kernel(const float *x, const float *w, RowOut y, int N,
                                float eps) {
   griddep_launch();
+  griddep_wait();
   __shared__ float red[32];
   const float *xr = x + (size_t)blockIdx.x * N;
   const size_t o = (size_t)blockIdx.x * N;
@@ -63,6 +64,7 @@ __global__ void rmsnorm_kernel(const float *x, const float *w, RowOut y, int N,
 __global__ void rmsnorm_add_kernel(float *h, const float *add, const float *w,
                                    RowOut y, int N, float eps) {
   griddep_launch();
+  griddep_wait();
   __shared__ float red[32];
   float *hr = h + (size_t)blockIdx.x * N;
   const float *ar = add + (size_t)blockIdx.x * N;
@@ -82,6 +84,7 @@ __global__ void rmsnorm_add_kernel(float *h, const float *add, const float *w,
 __global__ void layernorm_kernel(const float *x, const float *g, const float *b,
                                  RowOut y, int N, float eps) {
   griddep_launch();
+  griddep_wait();
   __shared__ float red[32];
   const float *xr = x + (size_t)blockIdx.x * N;
   const size_t o = (size_t)blockIdx.x * N;
@@ -115,6 +118,7 @@ __global__ void embedding_kernel(const int *ids, const void *wte,
                                  const float *wpe, const int *pos, float *out,
                                  int n, int vocab, int max_pos, int *err) {
   griddep_launch();
+  griddep_wait();
   const int m = blockIdx.x;
   const int id = ids[m];
   const bool ok = id >= 0 && id < vocab;
@@ -388,9 +392,9 @@ int tllm_rmsnorm(const float *x, const float *w, void *y, int y_dtype,
   RowOut o;
   int rc = row_out(&o, y, y_dtype, y_plane_rows, M, N);
   if (rc) return rc;
-  rmsnorm_kernel<<<M, row_threads(N) > 256 ? 256 : row_threads(N), 0,
-                   resolve(stream)>>>(x, w, o, N, eps);
-  TLLM_LAUNCH_CHECK();
+  TLLM_CUDA(launch_pdl(rmsnorm_kernel, dim3(M),
+                       dim3(row_threads(N) > 256 ? 256 : row_threads(N)), 0,
+                       resolve(stream), x, w, o, N, eps));
   return TLLM_OK;
 }
 
@@ -405,9 +409,9 @@ int tllm_rmsnorm_add(float *h, const float *add, const float *w, void *y,
   RowOut o;
   int rc = row_out(&o, y, y_dtype, y_plane_rows, M, N);
   if (rc) return rc;
-  rmsnorm_add_kernel<<<M, row_threads(N) > 256 ? 256 : row_threads(N), 0,
-                       resolve(stream)>>>(h, add, w, o, N, eps);
-  TLLM_LAUNCH_CHECK();
+  TLLM_CUDA(launch_pdl(rmsnorm_add_kernel, dim3(M),
+                       dim3(row_threads(N) > 256 ? 256 : row_threads(N)), 0,
+                       resolve(stream), h, add, w, o, N, eps));
   return TLLM_OK;
 }
 
@@ -422,8 +426,8 @@ int tllm_layernorm(const float *x, const float *g, const float *b, void *y,
   RowOut o;
   int rc = row_out(&o, y, y_dtype, y_plane_rows, M, N);
   if (rc) return rc;
-  layernorm_kernel<<<M, 256, 0, resolve(stream)>>>(x, g, b, o, N, eps);
-  TLLM_LAUNCH_CHECK();
+  TLLM_CUDA(launch_pdl(layernorm_kernel, dim3(M), dim3(256), 0, resolve(stream), x,
+                       g, b, o, N, eps));
   return TLLM_OK;
 }
 
