@@ -221,12 +221,18 @@ int tllm_gqa_rows(const float *q, long q_row_stride, long q_head_stride,
  *              row_pos[m] (rope.py:49-66 + smollm2_triton/model.py:296-302);
  *              if lens_out != NULL, lens_out[row_seq[m]] = row_pos[m] + 1.
  * op 5 SCATTER: row m of acc goes to the receive slot of this rank on every
- *              rank of the peer group p2p (tllm_p2p_create), over NVLink;
- *              the last CTA publishes the call's epoch to every rank.
+ *              rank of the peer group p2p (tllm_p2p_create), over NVLink,
+ *              each value tagged with the call's number in one 64-bit word.
  *              M <= the group's rows, N <= its columns, no bias, out unused.
  *              tllm_rmsnorm_p2p completes the all-reduce. No counterpart in
  *              the reference (single-GPU); it replaces the all-reduce of a
  *              row-parallel o_proj / down_proj.
+ * next_w (optional, TLLM_BF16_TILED, next_N x next_K): the weights of the
+ *   projection that runs next on these rows (same M and activation format).
+ *   Once a CTA has requested its own weights it prefetches into L2 up to
+ *   next_bytes of the chunks that projection's CTAs read first, so HBM keeps
+ *   streaming through this kernel's drain and epilogue. Only a hint: results
+ *   do not depend on it. No counterpart in the reference.
  * Scratch for split-K: tllm_linear_workspace; counters zero-filled once
  * (the kernel leaves them at zero).
  */
@@ -244,8 +250,9 @@ int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
                 const int32_t *row_seq, const int32_t *row_pos, float *q_out,
                 void *k_cache, void *v_cache, int kv_dtype, int max_seq,
                 int n_head, int n_kv_head, int head_dim, int32_t *lens_out,
-                const void *p2p, void *partial, size_t partial_bytes,
-                int32_t *counters, tllm_stream_t stream);
+                const void *p2p, const void *next_w, int next_w_dtype,
+                int next_N, int next_K, size_t next_bytes, void *partial,
+                size_t partial_bytes, int32_t *counters, tllm_stream_t stream);
 
 /* C = A @ B, fp32, A (M, K), B (K, N) row-major: the reference's weight
  * layout (triton_llm/kernels/gemm.py:53-109). */
@@ -273,16 +280,16 @@ int tllm_rmsnorm_add(float *h, const float *add, const float *w, void *y,
 /*
  * Peer-to-peer all-reduce of a tensor-parallel group, one rank per GPU
  * (no counterpart in the reference, whose decode runs on one device).
- * Each rank allocates receive slots [2][size][rows][cols] fp32 plus flags
- * and exports them as a CUDA IPC handle (tllm_p2p_handle_bytes bytes);
- * after exchanging the handles (any host channel), tllm_p2p_open maps every
- * peer's slots. A projection with op SCATTER writes its partial rows into
- * every rank's slot; tllm_rmsnorm_p2p then waits (bounded, ~2 s, reported
- * as TLLM_ERR_TIMEOUT by the next synchronize) for every rank's epoch flag,
- * adds the slots in rank order to h (identical on every rank), and
- * normalises: h += sum_q part_q; y = RMSNorm(h). Calls alternate between
- * two slot sets, so consecutive SCATTER / rmsnorm_p2p pairs need no
- * barrier. All ranks must issue the same sequence of pairs.
+ * Each rank allocates receive slots [2][size][rows][cols] of 64-bit words
+ * (fp32 bits | call number << 32) and exports them as a CUDA IPC handle
+ * (tllm_p2p_handle_bytes bytes); after exchanging the handles (any host
+ * channel), tllm_p2p_open maps every peer's slots. A projection with op
+ * SCATTER writes its partial rows into every rank's slot; tllm_rmsnorm_p2p
+ * then waits (bounded, ~2 s, device error bit 1) until every word carries
+ * the current call number, adds the slots in rank order to h (identical on
+ * every rank), and normalises: h += sum_q part_q; y = RMSNorm(h). Calls
+ * alternate between two slot sets, so consecutive SCATTER / rmsnorm_p2p
+ * pairs need no barrier. All ranks must issue the same sequence of pairs.
  */
 int tllm_p2p_handle_bytes(void);
 int tllm_p2p_create(int size, int rows, int cols, void **ctx, void *ipc_handle);

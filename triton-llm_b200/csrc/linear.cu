@@ -267,6 +267,12 @@ struct TcParams {
   int M, N, K, S, k_chunks, n_tiles, wstages, xstages;
   int nacc;      // independent TMEM accumulators (a multiple of issuers)
   int issuers;   // MMA-issuing threads (2 or 4; divides both ring depths)
+  // L2 prefetch of the next projection's first weight chunks (tiled
+  // weights; pf == nullptr: none): its CTAs (tile, split) start at chunk
+  // split * pf_per of pf_k_chunks; the first pf_chunks of each of pf_units
+  // = tiles x splits CTAs are fetched
+  const uint8_t *pf;
+  int pf_units, pf_splits, pf_per, pf_k_chunks, pf_chunks;
   uint32_t tcols;  // TMEM columns allocated (power of two >= 32)
   int w_tiled;   // TLLM_BF16_TILED weights: tile (nt, kc) = rows
                  // (nt * k_chunks + kc) * 128 .. +127 of a (., 64) view
@@ -306,7 +312,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __shared__ uint32_t s_tmem;
   __shared__ int s_wissued, s_xissued, s_fail;
   __shared__ int s_empty_acc[kTcMaxIssuers];   // an issuer whose accumulators were never written
-  __shared__ int s_par;            // EPI_SCATTER: receive-slot parity of this call
+  __shared__ unsigned s_epoch;     // EPI_SCATTER: this call's number
   const int WS = p.wstages;
   uint8_t *wring = smem;
   uint8_t *xring = smem + WS * kTcW;
@@ -378,6 +384,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                            nt * kTcBN, pol);
       }
       s_wissued = c;
+      if (p.pf) {
+        // this CTA's weights are all requested: spend the rest of its life
+        // (the MMA drain and the epilogue, when HBM would idle) pulling the
+        // next projection's first chunks into L2, spread over the grid
+        const int G = gridDim.x * gridDim.y * gridDim.z;
+        const int me = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+        const int total = p.pf_units * p.pf_chunks;
+        for (int t = me; t < total; t += G) {
+          const int j = t / p.pf_units;
+          const int u = t - j * p.pf_units;
+          const int tile = u / p.pf_splits;
+          const int sp = u - tile * p.pf_splits;
+          const int kc = sp * p.pf_per + j;
+          const int kend = (sp + 1) * p.pf_per < p.pf_k_chunks ? (sp + 1) * p.pf_per
+                                                              : p.pf_k_chunks;
+          if (kc >= kend) continue;
+          const uint8_t *a = p.pf + ((size_t)tile * p.pf_k_chunks + kc) * kTcW;
+          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"(kTcW)
+                       : "memory");
+        }
+      }
     }
     __syncwarp();
   } else if (warp == 2) {
@@ -456,8 +483,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   tc_fence_after();
   griddep_wait();   // the epilogue reads / writes buffers of earlier kernels
   if constexpr (OP == EPI_SCATTER) {
+    // calls completed so far (this rank's reader of the previous call has
+    // finished): this call's number
     if (tid == 0)
-      s_par = (*reinterpret_cast<volatile const int *>(&p.e.p2p->state[0]) + 1) & 1;
+      s_epoch = (unsigned)*reinterpret_cast<volatile const int *>(&p.e.p2p->state[0]) + 1u;
   }
   __syncthreads();  // s_fail visible
   const bool valid = acc_ok && !s_fail && nch > 0;
@@ -541,15 +570,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
       if constexpr (OP == EPI_SCATTER) {
+        // each value with this call's number, as 64-bit words, into this
+        // rank's slot on every rank
         const P2PDev *P = p.e.p2p;
+        const unsigned ep = s_epoch;
         if (n < p.N) {
 #pragma unroll
           for (int i = 0; i < kTcRB; ++i) {
             if (!ok[i]) continue;
             const size_t off =
-                (((size_t)s_par * P->size + P->rank) * P->mmax + mrow[i]) * P->ncols + n;
-            for (int q = 0; q < P->size; ++q)
-              *reinterpret_cast<float4 *>(P->peer_recv[q] + off) = v[i];
+                (((size_t)(ep & 1) * P->size + P->rank) * P->mmax + mrow[i]) * P->ncols + n;
+            const unsigned long long w0 = p2p_word(v[i].x, ep), w1 = p2p_word(v[i].y, ep);
+            const unsigned long long w2 = p2p_word(v[i].z, ep), w3 = p2p_word(v[i].w, ep);
+            for (int q = 0; q < P->size; ++q) {
+              unsigned long long *d = P->peer_recv[q] + off;
+              asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(d), "l"(w0),
+                           "l"(w1) : "memory");
+              asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(d + 2),
+                           "l"(w2), "l"(w3) : "memory");
+            }
           }
         }
       } else {
@@ -707,29 +746,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               rope_pair(cs[i][h], sn[i][h], x0, x1);
             qkv_store(e, g[h], mrow[i], pos[i], seq[i], x0, x1);
           }
-        }
-      }
-    }
-  }
-  if constexpr (OP == EPI_SCATTER) {
-    // every CTA's rows are out; the last CTA of the grid publishes the new
-    // epoch to every rank (release, system scope). One fence per CTA after
-    // the barrier orders all of the CTA's stores (fences are cumulative).
-    __syncthreads();
-    if (tid == 0) {
-      const P2PDev *P = p.e.p2p;
-      const int total = gridDim.x * gridDim.y * gridDim.z;
-      asm volatile("fence.acq_rel.sys;" ::: "memory");
-      const int ticket = atomicAdd(&P->state[1], 1);
-      if (ticket == total - 1) {
-        // every other CTA's stores before the flags
-        asm volatile("fence.acq_rel.sys;" ::: "memory");
-        P->state[1] = 0;
-        const int e = P->state[0] + 1;
-        P->state[0] = e;
-        for (int q = 0; q < P->size; ++q) {
-          int *f = P->peer_flags[q] + P->rank;
-          asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(f), "r"(e) : "memory");
         }
       }
     }
@@ -1147,8 +1163,9 @@ int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
                 const int32_t *row_seq, const int32_t *row_pos, float *q_out,
                 void *k_cache, void *v_cache, int kv_dtype, int max_seq,
                 int n_head, int n_kv_head, int head_dim, int32_t *lens_out,
-                const void *p2p, void *partial, size_t partial_bytes,
-                int32_t *counters, tllm_stream_t stream) {
+                const void *p2p, const void *next_w, int next_w_dtype,
+                int next_N, int next_K, size_t next_bytes, void *partial,
+                size_t partial_bytes, int32_t *counters, tllm_stream_t stream) {
   TLLM_INJECT("launch");
   TLLM_CHECK_ARG(M >= 0 && N >= 0 && K >= 0, "negative shape");
   if (M == 0 || N == 0) return TLLM_OK;
@@ -1266,6 +1283,25 @@ int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
     p.tcols = cols;
   }
   p.w_tiled = tiled ? 1 : 0;
+  p.pf = nullptr;
+  p.pf_units = p.pf_splits = p.pf_per = p.pf_k_chunks = p.pf_chunks = 0;
+  if (next_w && next_w_dtype == TLLM_BF16_TILED && next_bytes >= (size_t)kTcW &&
+      next_N > 0 && next_K > 0 && next_K % kTcBK == 0) {
+    // the next projection's plan for the same rows and activation format
+    const TcPlan nx = tc_plan(M, next_N, next_K, PL);
+    const int per = (nx.k_chunks + nx.S - 1) / nx.S;
+    const long units = (long)nx.n_tiles * nx.S;
+    long chunks = (long)(next_bytes / kTcW) / units;
+    if (chunks > per) chunks = per;
+    if (chunks > 0) {
+      p.pf = static_cast<const uint8_t *>(next_w);
+      p.pf_units = (int)units;
+      p.pf_splits = nx.S;
+      p.pf_per = per;
+      p.pf_k_chunks = nx.k_chunks;
+      p.pf_chunks = (int)chunks;
+    }
+  }
   dim3 grid(pl.n_tiles, S, pl.m_tiles);
   if (PL == 2) return launch_tc_mt<2>(p, pl.MT, tw, tx, grid, pl.smem, st);
   return launch_tc_mt<1>(p, pl.MT, tw, tx, grid, pl.smem, st);

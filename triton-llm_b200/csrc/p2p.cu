@@ -7,20 +7,24 @@
 // smollm2_triton/model.py:351-365). Here the projection's epilogue
 // (tllm_linear op EPI_SCATTER) stores its partial rows straight into a
 // receive slot on every rank of the group over NVLink (plain stores
-// through CUDA IPC mappings) and the last CTA publishes an epoch flag to
-// every rank; the RMSNorm that follows (tllm_rmsnorm_p2p) waits for all
-// ranks' flags, sums the slots in rank order -- identical on every rank --
-// adds the sum to the residual stream and normalises.
+// through CUDA IPC mappings), and the RMSNorm that follows
+// (tllm_rmsnorm_p2p) waits for every rank's rows, sums the slots in rank
+// order -- identical on every rank -- adds the sum to the residual stream
+// and normalises.
+//
+// Every value travels as one 64-bit word: fp32 bits | call number << 32.
+// A single aligned 64-bit store is seen whole or not at all, so the reader
+// knows a value has arrived when its word carries the current call number:
+// the writer needs no fence, no flag and no grid-wide ticket.
 //
 // Buffers (one cudaMalloc per rank, exported with cudaIpcGetMemHandle):
-//   recv  [2][size][mmax][ncols] fp32   slot (parity, source rank, row)
-//   flags [size] int                    epoch last published by each rank
-// and a local state {epoch, ticket}. A call's slots have parity
-// (epoch + 1) & 1; a rank overwrites a parity two calls later only after
-// its own reader of the previous call has seen every rank's flag, which each
-// rank publishes after finishing its reader of the call before, so a slot is
-// never overwritten while someone still reads it. Every wait is bounded and
-// reports through the device error word.
+//   recv  [2][size][mmax][ncols] words   slot (parity, source rank, row)
+// and a local state {calls done, reader ticket}. Call c (1, 2, ...) writes
+// parity c & 1. A rank writes call c + 2 into a peer only after its own
+// reader of call c + 1 has seen that peer's rows of call c + 1, which the
+// peer wrote after its reader of call c had finished, so a slot is never
+// overwritten while it is read. Every wait is bounded and reports through
+// the device error word.
 #include <cstring>
 
 #include "common.cuh"
@@ -36,6 +40,10 @@ struct P2PHost {
   cudaIpcMemHandle_t handle;
   bool opened;
 };
+
+size_t p2p_recv_bytes(int size, int mmax, int ncols) {
+  return (size_t)2 * size * mmax * ncols * sizeof(unsigned long long);
+}
 
 const P2PDev *p2p_table(const void *ctx, int rows, int cols) {
   if (!ctx) {
@@ -73,40 +81,38 @@ __global__ void rmsnorm_p2p_kernel(float *h, const P2PDev *P, const float *w,
                                    uint16_t *ys, float *yf, size_t yplane,
                                    int planes, int N, float eps, int *err) {
   griddep_launch();
+  // the projection that scatters has finished on this rank, and with it
+  // this rank's reader of the previous call: state[0] is final
+  griddep_wait();
   __shared__ float red[32];
-  __shared__ int s_epoch;
+  __shared__ int s_broken;
   const int m = blockIdx.x;
-  if (threadIdx.x == 0) {
-    const int e = *reinterpret_cast<volatile const int *>(&P->state[0]);
-    // after one wait has run out the group is broken: do not wait again
-    bool ok = !(*reinterpret_cast<volatile int *>(err) & DEV_ERR_WAIT_TIMEOUT);
-    for (int q = 0; q < P->size && ok; ++q) {
-      const int *f = P->flags_local + q;
-      const uint64_t t0 = globaltimer_ns();
-      for (uint32_t i = 0;; ++i) {
-        int v;
-        asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-        if (v >= e) break;
-        // bounded: ~2 s, or 2^26 polls if the timer does not advance
-        if (((i & 1023) == 1023 && globaltimer_ns() - t0 > kP2PWaitNs) ||
-            i == (1u << 26)) {
-          ok = false;
-          break;
-        }
-      }
-    }
-    if (!ok) atomicOr(err, DEV_ERR_WAIT_TIMEOUT);
-    s_epoch = e;
-  }
+  const unsigned e = (unsigned)P->state[0] + 1u;
+  const int par = e & 1;
+  if (threadIdx.x == 0)   // after one wait has run out, stop waiting
+    s_broken = *reinterpret_cast<volatile int *>(err) & DEV_ERR_WAIT_TIMEOUT;
   __syncthreads();
-  const int par = s_epoch & 1;
+  bool ok = !s_broken;
+  const uint64_t t0 = globaltimer_ns();
   float *hr = h + (size_t)m * N;
   float ss = 0.f;
   for (int i = threadIdx.x; i < N; i += blockDim.x) {
     float v = hr[i];
-    for (int q = 0; q < P->size; ++q)   // rank order: identical on every rank
-      v += __ldcg(&P->recv_local[(((size_t)par * P->size + q) * P->mmax + m) *
-                                     P->ncols + i]);
+    for (int q = 0; q < P->size; ++q) {   // rank order: identical on every rank
+      const unsigned long long *src =
+          P->recv_local + (((size_t)par * P->size + q) * P->mmax + m) * P->ncols + i;
+      unsigned long long word;
+      for (uint32_t it = 0;; ++it) {
+        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(word) : "l"(src) : "memory");
+        if ((unsigned)(word >> 32) == e || !ok) break;
+        // bounded: ~2 s, or 2^26 polls if the timer does not advance
+        if (((it & 255) == 255 && globaltimer_ns() - t0 > kP2PWaitNs) || it == (1u << 26)) {
+          ok = false;
+          atomicOr(err, DEV_ERR_WAIT_TIMEOUT);
+        }
+      }
+      v += __uint_as_float((unsigned)(word & 0xffffffffu));
+    }
     hr[i] = v;
     ss = fmaf(v, v, ss);
   }
@@ -129,6 +135,14 @@ __global__ void rmsnorm_p2p_kernel(float *h, const P2PDev *P, const float *w,
     else
       yf[o + i] = y;
   }
+  // the last block to finish records the call as done (read by the next
+  // scatter and reader, which run after this kernel)
+  if (threadIdx.x == 0) {
+    if (atomicAdd(&P->state[1], 1) == (int)gridDim.x - 1) {
+      P->state[1] = 0;
+      P->state[0] = (int)e;
+    }
+  }
 }
 
 }  // namespace
@@ -143,8 +157,7 @@ int tllm_p2p_create(int size, int mmax, int ncols, void **ctx,
   TLLM_CHECK_ARG(mmax > 0 && ncols > 0 && ncols % 4 == 0, "bad slot shape");
   P2PHost *h = new P2PHost();
   memset(h, 0, sizeof(*h));
-  const size_t recv_bytes = (size_t)2 * size * mmax * ncols * sizeof(float);
-  const size_t bytes = recv_bytes + 256;   // + flags
+  const size_t bytes = p2p_recv_bytes(size, mmax, ncols);
   void *base = nullptr;
   cudaError_t e = cudaMalloc(&base, bytes);
   if (e != cudaSuccess) {
@@ -171,8 +184,7 @@ int tllm_p2p_create(int size, int mmax, int ncols, void **ctx,
   h->table.size = size;
   h->table.mmax = mmax;
   h->table.ncols = ncols;
-  h->table.recv_local = static_cast<float *>(base);
-  h->table.flags_local = reinterpret_cast<int *>(static_cast<char *>(base) + recv_bytes);
+  h->table.recv_local = static_cast<unsigned long long *>(base);
   h->table.state = state;
   memcpy(ipc_handle, &h->handle, sizeof(cudaIpcMemHandle_t));
   *ctx = h;
@@ -189,7 +201,6 @@ int tllm_p2p_open(void *ctx, int rank, const void *handles) {
   P2PDev &t = h->table;
   TLLM_CHECK_ARG(rank >= 0 && rank < t.size, "rank %d not in [0, %d)", rank, t.size);
   t.rank = rank;
-  const size_t recv_bytes = (size_t)2 * t.size * t.mmax * t.ncols * sizeof(float);
   for (int q = 0; q < t.size; ++q) {
     void *p = nullptr;
     if (q == rank) {
@@ -205,8 +216,7 @@ int tllm_p2p_open(void *ctx, int rank, const void *handles) {
       }
       h->peer_base[q] = p;
     }
-    t.peer_recv[q] = static_cast<float *>(p);
-    t.peer_flags[q] = reinterpret_cast<int *>(static_cast<char *>(p) + recv_bytes);
+    t.peer_recv[q] = static_cast<unsigned long long *>(p);
   }
   TLLM_CUDA(cudaMemcpy(h->dev, &t, sizeof(P2PDev), cudaMemcpyHostToDevice));
   h->opened = true;
@@ -241,11 +251,13 @@ int tllm_rmsnorm_p2p(float *h, const void *p2p, const float *w, void *y,
   TLLM_CHECK_ARG(err, "device error word unavailable");
   const bool act = y_dtype != TLLM_F32;
   TLLM_CHECK_ARG(!act || y_plane_rows >= M, "y_plane_rows < M");
-  rmsnorm_p2p_kernel<<<M, 256, 0, resolve(stream)>>>(
-      h, P, w,
-      act ? static_cast<uint16_t *>(y) : nullptr, act ? nullptr : static_cast<float *>(y),
-      act ? (size_t)y_plane_rows * N : 0, y_dtype == TLLM_SPLIT ? 2 : 1, N, eps, err);
-  TLLM_LAUNCH_CHECK();
+  // resident before the projection that scatters has finished
+  // (programmatic serialization); the kernel waits for it first
+  TLLM_CUDA(launch_pdl(rmsnorm_p2p_kernel, dim3(M), dim3(256), 0, resolve(stream), h, P,
+                       w, act ? static_cast<uint16_t *>(y) : nullptr,
+                       act ? nullptr : static_cast<float *>(y),
+                       act ? (size_t)y_plane_rows * N : 0, y_dtype == TLLM_SPLIT ? 2 : 1,
+                       N, eps, err));
   return TLLM_OK;
 }
 
