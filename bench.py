@@ -324,18 +324,13 @@ class LlamaDecodeWorkload:
             for i in range(w.L):
                 L = w.layers[i]
                 k, v = s.kv[i]
-                nxt = w.layers[i + 1]["qkv"] if i + 1 < w.L else w.lm_head
                 linear(s.x, L["qkv"], op=_lib.EPI_QKV, ws=s.lin_ws, M=B, qkv=dict(
                     cos=w.cos, sin=w.sin, row_seq=s.row_seq, row_pos=s.pos, q_out=s.q,
                     k_cache=k, v_cache=v, n_head=w.H, n_kv_head=w.Hkv, head_dim=w.D))
-                linear(s.attn, L["o"], out_dev=s.x, op=_lib.EPI_STORE, ws=s.lin_ws, M=B,
-                       prefetch=s._pf(L["gu"]))
-                linear(s.x, L["gu"], out_dev=s.act, op=_lib.EPI_SWIGLU, ws=s.lin_ws, M=B,
-                       prefetch=s._pf(L["down"]))
-                linear(s.act, L["down"], out_dev=s.x, op=_lib.EPI_STORE, ws=s.lin_ws, M=B,
-                       prefetch=s._pf(nxt))
-            linear(s.x, w.lm_head, out_dev=s.logits, ws=s.lin_ws, M=B,
-                   prefetch=s._pf(w.layers[0]["qkv"]))
+                linear(s.attn, L["o"], out_dev=s.x, op=_lib.EPI_STORE, ws=s.lin_ws, M=B)
+                linear(s.x, L["gu"], out_dev=s.act, op=_lib.EPI_SWIGLU, ws=s.lin_ws, M=B)
+                linear(s.act, L["down"], out_dev=s.x, op=_lib.EPI_STORE, ws=s.lin_ws, M=B)
+            linear(s.x, w.lm_head, out_dev=s.logits, ws=s.lin_ws, M=B)
         for (M, N, K) in w.linear_shapes(B)[:4]:
             alg += w.L * (N * K * 2 + M * K * 4 + M * N * 4)
         M, N, K = w.linear_shapes(B)[4]

@@ -227,12 +227,6 @@ int tllm_gqa_rows(const float *q, long q_row_stride, long q_head_stride,
  *              tllm_rmsnorm_p2p completes the all-reduce. No counterpart in
  *              the reference (single-GPU); it replaces the all-reduce of a
  *              row-parallel o_proj / down_proj.
- * next_w (optional, TLLM_BF16_TILED, next_N x next_K): the weights of the
- *   projection that runs next on these rows (same M and activation format).
- *   Once a CTA has requested its own weights it prefetches into L2 up to
- *   next_bytes of the chunks that projection's CTAs read first, so HBM keeps
- *   streaming through this kernel's drain and epilogue. Only a hint: results
- *   do not depend on it. No counterpart in the reference.
  * Scratch for split-K: tllm_linear_workspace; counters zero-filled once
  * (the kernel leaves them at zero).
  */
@@ -250,9 +244,8 @@ int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
                 const int32_t *row_seq, const int32_t *row_pos, float *q_out,
                 void *k_cache, void *v_cache, int kv_dtype, int max_seq,
                 int n_head, int n_kv_head, int head_dim, int32_t *lens_out,
-                const void *p2p, const void *next_w, int next_w_dtype,
-                int next_N, int next_K, size_t next_bytes, void *partial,
-                size_t partial_bytes, int32_t *counters, tllm_stream_t stream);
+                const void *p2p, void *partial, size_t partial_bytes,
+                int32_t *counters, tllm_stream_t stream);
 
 /* C = A @ B, fp32, A (M, K), B (K, N) row-major: the reference's weight
  * layout (triton_llm/kernels/gemm.py:53-109). */

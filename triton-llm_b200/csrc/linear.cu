@@ -267,12 +267,6 @@ struct TcParams {
   int M, N, K, S, k_chunks, n_tiles, wstages, xstages;
   int nacc;      // independent TMEM accumulators (a multiple of issuers)
   int issuers;   // MMA-issuing threads (2 or 4; divides both ring depths)
-  // L2 prefetch of the next projection's first weight chunks (tiled
-  // weights; pf == nullptr: none): its CTAs (tile, split) start at chunk
-  // split * pf_per of pf_k_chunks; the first pf_chunks of each of pf_units
-  // = tiles x splits CTAs are fetched
-  const uint8_t *pf;
-  int pf_units, pf_splits, pf_per, pf_k_chunks, pf_chunks;
   uint32_t tcols;  // TMEM columns allocated (power of two >= 32)
   int w_tiled;   // TLLM_BF16_TILED weights: tile (nt, kc) = rows
                  // (nt * k_chunks + kc) * 128 .. +127 of a (., 64) view
@@ -384,27 +378,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                            nt * kTcBN, pol);
       }
       s_wissued = c;
-      if (p.pf) {
-        // this CTA's weights are all requested: spend the rest of its life
-        // (the MMA drain and the epilogue, when HBM would idle) pulling the
-        // next projection's first chunks into L2, spread over the grid
-        const int G = gridDim.x * gridDim.y * gridDim.z;
-        const int me = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
-        const int total = p.pf_units * p.pf_chunks;
-        for (int t = me; t < total; t += G) {
-          const int j = t / p.pf_units;
-          const int u = t - j * p.pf_units;
-          const int tile = u / p.pf_splits;
-          const int sp = u - tile * p.pf_splits;
-          const int kc = sp * p.pf_per + j;
-          const int kend = (sp + 1) * p.pf_per < p.pf_k_chunks ? (sp + 1) * p.pf_per
-                                                              : p.pf_k_chunks;
-          if (kc >= kend) continue;
-          const uint8_t *a = p.pf + ((size_t)tile * p.pf_k_chunks + kc) * kTcW;
-          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"(kTcW)
-                       : "memory");
-        }
-      }
     }
     __syncwarp();
   } else if (warp == 2) {
@@ -1163,9 +1136,8 @@ int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
                 const int32_t *row_seq, const int32_t *row_pos, float *q_out,
                 void *k_cache, void *v_cache, int kv_dtype, int max_seq,
                 int n_head, int n_kv_head, int head_dim, int32_t *lens_out,
-                const void *p2p, const void *next_w, int next_w_dtype,
-                int next_N, int next_K, size_t next_bytes, void *partial,
-                size_t partial_bytes, int32_t *counters, tllm_stream_t stream) {
+                const void *p2p, void *partial, size_t partial_bytes,
+                int32_t *counters, tllm_stream_t stream) {
   TLLM_INJECT("launch");
   TLLM_CHECK_ARG(M >= 0 && N >= 0 && K >= 0, "negative shape");
   if (M == 0 || N == 0) return TLLM_OK;
@@ -1283,25 +1255,6 @@ int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
     p.tcols = cols;
   }
   p.w_tiled = tiled ? 1 : 0;
-  p.pf = nullptr;
-  p.pf_units = p.pf_splits = p.pf_per = p.pf_k_chunks = p.pf_chunks = 0;
-  if (next_w && next_w_dtype == TLLM_BF16_TILED && next_bytes >= (size_t)kTcW &&
-      next_N > 0 && next_K > 0 && next_K % kTcBK == 0) {
-    // the next projection's plan for the same rows and activation format
-    const TcPlan nx = tc_plan(M, next_N, next_K, PL);
-    const int per = (nx.k_chunks + nx.S - 1) / nx.S;
-    const long units = (long)nx.n_tiles * nx.S;
-    long chunks = (long)(next_bytes / kTcW) / units;
-    if (chunks > per) chunks = per;
-    if (chunks > 0) {
-      p.pf = static_cast<const uint8_t *>(next_w);
-      p.pf_units = (int)units;
-      p.pf_splits = nx.S;
-      p.pf_per = per;
-      p.pf_k_chunks = nx.k_chunks;
-      p.pf_chunks = (int)chunks;
-    }
-  }
   dim3 grid(pl.n_tiles, S, pl.m_tiles);
   if (PL == 2) return launch_tc_mt<2>(p, pl.MT, tw, tx, grid, pl.smem, st);
   return launch_tc_mt<1>(p, pl.MT, tw, tx, grid, pl.smem, st);

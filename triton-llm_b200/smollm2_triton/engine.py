@@ -216,8 +216,6 @@ class LlamaSession:
         self.ids = gpu.zeros((B,), np.int32)     # tokens fed to the next step
         self.row_seq = gpu.to_device(np.arange(B, dtype=np.int32))
         self._p2p = bool(p2p)
-        # L2 prefetch of the next projection's weights (MB; 0 turns it off)
-        self.prefetch_bytes = int(float(os.environ.get("TLLM_PREFETCH_MB", "0")) * (1 << 20))
         self._buffers(B)
         self.attn_ws = DecodeWorkspace(B, wts.H, Hkv, D, S,
                                        _lib.BF16 if self.kv_bf16 else _lib.F32)
@@ -288,38 +286,26 @@ class LlamaSession:
         gqa_rows(q, k, v, row_seq, lens if decode else row_len, attn, M, w.H,
                  w.H * w.D, w.D, w.H * w.D, w.D, self.S if decode else (max_len or self.S),
                  workspace=attn_ws)
-        # each projection pulls the first chunks of the next one's weights
-        # into L2 while it drains (not across attention, which streams the
-        # cache through L2)
-        nxt = w.layers[i + 1]["qkv"] if i + 1 < w.L else w.lm_head
         if part is None:
-            linear(attn, L["o"], out_dev=h, op=_lib.EPI_RESID, resid_dev=h, ws=ws, M=M,
-                   prefetch=self._pf(L["gu"]))
+            linear(attn, L["o"], out_dev=h, op=_lib.EPI_RESID, resid_dev=h, ws=ws, M=M)
             rms_norm_rows(h, L["ln2"], x, M, w.eps)
         else:
-            self._reduce(attn, L["o"], part, M, ws, self._pf(L["gu"]))
+            self._reduce(attn, L["o"], part, M, ws)
             self._norm_add(h, part, L["ln2"], x, M)
-        linear(x, L["gu"], out_dev=act, op=_lib.EPI_SWIGLU, ws=ws, M=M,
-               prefetch=self._pf(L["down"]))
+        linear(x, L["gu"], out_dev=act, op=_lib.EPI_SWIGLU, ws=ws, M=M)
         if part is None:
-            linear(act, L["down"], out_dev=h, op=_lib.EPI_RESID, resid_dev=h, ws=ws, M=M,
-                   prefetch=self._pf(nxt))
+            linear(act, L["down"], out_dev=h, op=_lib.EPI_RESID, resid_dev=h, ws=ws, M=M)
         else:
-            self._reduce(act, L["down"], part, M, ws, self._pf(nxt))
+            self._reduce(act, L["down"], part, M, ws)
 
-    def _pf(self, lin):
-        """L2 prefetch hint for the projection that runs next."""
-        return (lin, self.prefetch_bytes) if self.prefetch_bytes > 0 else None
-
-    def _reduce(self, src, lin, part, M, ws, prefetch=None):
+    def _reduce(self, src, lin, part, M, ws):
         """A row-parallel projection whose partial sums the group adds:
         ``part`` is a PeerGroup (fused: the epilogue scatters to every rank)
         or an fp32 buffer (stored, then NCCL all-reduce)."""
         if isinstance(part, PeerGroup):
-            linear(src, lin, op=_lib.EPI_SCATTER, ws=ws, M=M, p2p=part, prefetch=prefetch)
+            linear(src, lin, op=_lib.EPI_SCATTER, ws=ws, M=M, p2p=part)
         else:
-            linear(src, lin, out_dev=part, op=_lib.EPI_STORE, ws=ws, M=M,
-                   prefetch=prefetch)
+            linear(src, lin, out_dev=part, op=_lib.EPI_STORE, ws=ws, M=M)
             self.tp.all_reduce(self._rows_view(part, M))
 
     def _norm_add(self, h, part, wn, x, M):
@@ -434,8 +420,7 @@ class LlamaSession:
                         self.row_seq, self.pos, self.lens, self.lin_ws, True,
                         self.attn_ws, part=self._decode_part())
         self._final_norm(self.h, self.x, B, self._decode_part())
-        linear(self.x, w.lm_head, out_dev=self.logits, ws=self.lin_ws, M=B,
-               prefetch=self._pf(w.layers[0]["qkv"]))
+        linear(self.x, w.lm_head, out_dev=self.logits, ws=self.lin_ws, M=B)
         n = 1 + 7 * w.L + 2
         if sample:
             _lib.call("tllm_argmax", self.logits.ptr, B, w.V, w.V, self.ids.ptr,

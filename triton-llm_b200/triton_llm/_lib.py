@@ -95,7 +95,7 @@ SIGNATURES: dict[str, list] = {
     "tllm_linear_plan": [_i, _i, _i, _i, _pi],
     "tllm_linear": [_vp, _i, _i, _vp, _i, _i, _i, _i, _i, _vp, _vp, _i, _i, _i,
                     _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i,
-                    _vp, _vp, _vp, _i, _i, _i, _sz, _vp, _sz, _vp, _vp],
+                    _vp, _vp, _vp, _sz, _vp, _vp],
     "tllm_gemm_f32": [_vp, _vp, _vp, _i, _i, _i, _vp],
     # rows / elementwise
     "tllm_rmsnorm": [_vp, _vp, _vp, _i, _i, _i, _i, _f, _vp],

@@ -172,7 +172,7 @@ def to_split(x_dev, M=None, out=None, planes=2):
 
 def linear(x_dev, lin: Linear, out_dev=None, op=_lib.EPI_STORE, resid_dev=None,
            ws: LinearWorkspace | None = None, M=None, ld_out=0, qkv=None,
-           p2p=None, prefetch=None, stream=None):
+           p2p=None, stream=None):
     """Run one projection on the first M rows of ``x_dev``.
 
     ``x_dev``: fp32 (rows, K) or TLLM_SPLIT (2, rows, K) (``gpu.split_empty``);
@@ -180,9 +180,6 @@ def linear(x_dev, lin: Linear, out_dev=None, op=_lib.EPI_STORE, resid_dev=None,
     ``out_dev``: fp32 or TLLM_SPLIT. ``qkv`` = dict(cos, sin, row_seq,
     row_pos, q_out, k_cache, v_cache, n_head, n_kv_head, head_dim, lens_out)
     for op QKV. ``p2p``: a ``triton_llm.tp.PeerGroup`` for op SCATTER.
-    ``prefetch`` = (Linear, bytes): the projection that runs next on these
-    rows; up to ``bytes`` of its first weight chunks are pulled into L2 by
-    this one's CTAs after they have requested their own weights.
     """
     split_in = getattr(x_dev, "is_split", False)
     rows = int(x_dev.shape[1] if split_in else x_dev.shape[0])
@@ -197,9 +194,6 @@ def linear(x_dev, lin: Linear, out_dev=None, op=_lib.EPI_STORE, resid_dev=None,
                          else (None, _lib.F32, 0))
     q = qkv or {}
     kc = q.get("k_cache")
-    nxt, nbytes = prefetch if prefetch is not None else (None, 0)
-    if nxt is not None and not nxt.bf16:
-        nxt, nbytes = None, 0
     _lib.call(
         "tllm_linear", xptr, xdt, xplane, lin.w.ptr, lin.dtype, M, lin.N, lin.K,
         int(op), _lib.ptr(lin.b), optr, odt, oplane, int(ld_out), _lib.ptr(resid_dev),
@@ -210,8 +204,6 @@ def linear(x_dev, lin: Linear, out_dev=None, op=_lib.EPI_STORE, resid_dev=None,
         int(kc.shape[2]) if kc is not None else 0, int(q.get("n_head", 0)),
         int(q.get("n_kv_head", 0)), int(q.get("head_dim", 0)),
         _lib.ptr(q.get("lens_out")), p2p.ctx if p2p is not None else None,
-        nxt.w.ptr if nxt is not None else None, nxt.dtype if nxt is not None else 0,
-        nxt.N if nxt is not None else 0, nxt.K if nxt is not None else 0, int(nbytes),
         ws.partial.ptr if ws else None, ws.partial_bytes if ws else 0,
         ws.counters.ptr if ws else None, stream)
     return out_dev
