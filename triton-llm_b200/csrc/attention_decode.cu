@@ -83,9 +83,10 @@ struct DecodeParams {
   long q_sb, q_sh, o_sb, o_sh;
   float *part_acc;       // (B, n_head, max_splits, D)
   float *part_ml;        // (B, n_head, max_splits, 2)
-  int *counters;         // (B, gridDim.y)
+  int *counters;         // (B, n_y)
   int *err;              // device error word
   int n_head, n_kv, group, n_gsub;
+  int n_y;               // kv heads x query-head groups (gridDim.y)
   int max_seq, max_len, chunk, max_splits;
   float qscale;          // sm_scale * log2(e)
 };
@@ -400,7 +401,7 @@ __global__ void __launch_bounds__(kThreads)
   __threadfence();
   __syncthreads();
   if (tid == 0) {
-    int *ctr = p.counters + (size_t)b * gridDim.y + y;
+    int *ctr = p.counters + (size_t)b * p.n_y + y;
     const int ticket = atomicAdd(ctr, 1);
     s_flag = (ticket == n_splits - 1) ? 2 : 0;
     if (s_flag) *ctr = 0;  // every other CTA has taken its ticket already
@@ -448,13 +449,15 @@ __global__ void __launch_bounds__(kThreads)
 // Tensor-core variant for bf16 caches (head_dim 64 / 128).
 //
 // Same decomposition, ring and split merge as above, but the products run on
-// the tensor cores with mma.sync m16n8k16 (bf16 in, fp32 accumulate):
-//   S (16 heads x 16 keys) = Q (16 x D) . K_w^T      per consumer warp
-//   O (16 heads x D)      += P (16 x 16 keys) . V_w
-// where warp w owns keys [16w, 16w + 16) of every 64-key tile. The query
-// heads of the CTA are the 16 M rows (rows >= G are zero). q and p are each
-// split into a bf16 head and a bf16 residual (x = hi + lo) and both halves
-// are multiplied, so scores and weights keep ~16 mantissa bits: the result
+// the tensor cores with mma.sync m16n8k16 (bf16 in, fp32 accumulate), with
+// the keys as the M rows and the CTA's query heads as the N columns:
+//   S^T (16 keys x 8 heads)  = K_w (16 x D) . Q^T      per consumer warp
+//   O^T (D x 8 heads)       += V_w^T (D x 16 keys) . P^T
+// where warp w owns keys [16w, 16w + 16) of every 64-key tile; a decode
+// group of G <= 8 heads (16 with two n8 blocks) fills the narrow side, so
+// half the MMAs of the heads-as-rows form are spent. q and p are each split
+// into a bf16 head and a bf16 residual (x = hi + lo) and both halves are
+// multiplied, so scores and weights keep ~16 mantissa bits: the result
 // matches fp32 arithmetic on the bf16 cache to ~1e-6 relative. K/V tiles
 // arrive through TMA with 128-byte swizzle (64-dim sub-tiles of 128 B rows),
 // which makes the ldmatrix reads bank-conflict free.
@@ -495,6 +498,13 @@ __device__ __forceinline__ void split_bf16x2(float x0, float x1, uint32_t &hi,
   hi = pack_bf16x2(x0, x1);
   lo = pack_bf16x2(x0 - bf16lo(hi), x1 - bf16hi(hi));
 }
+// transpose of the 8 x 8 bf16 matrix held in the C / A fragment layout
+// (lane l: row l / 4, columns 2 (l % 4), + 1)
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+  uint32_t r;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(r) : "r"(x));
+  return r;
+}
 
 
 template <int D>
@@ -510,7 +520,7 @@ struct MmaShape {
       2 * (size_t)STAGES * TILE_BYTES + 2 * STAGES * sizeof(uint64_t);
 };
 
-template <int D>
+template <int D, int QB>
 __global__ void __launch_bounds__(kThreads)
     gqa_decode_mma_kernel(const DecodeParams p, const int G,
                           const __grid_constant__ CUtensorMap tmk,
@@ -590,40 +600,56 @@ __global__ void __launch_bounds__(kThreads)
     }
   }
 
-  const int r0 = lane >> 2;          // fragment rows r0 and r0 + 8
-  const int cq = (lane & 3) * 2;     // fragment column pair
-  float o[S::NT][4];
-  float m_r[2] = {-INFINITY, -INFINITY};
-  float l_r[2] = {0.f, 0.f};
+  // Swapped operands: the keys are the MMA's M rows and the (few) query
+  // heads its N columns, so a decode group of G <= 8 heads fills an n8
+  // block instead of 3 of the 16 rows of an m16 block:
+  //   S^T (16 keys x 8 heads)  = K_w (16 x D) . Q^T        per consumer warp
+  //   O^T (D x 8 heads)       += V_w^T (D x 16 keys) . P^T
+  // C fragments hold rows r0, r0 + 8 (keys, resp. dims) and columns
+  // cq, cq + 1 (heads); P^T reaches the B-operand layout by transposing its
+  // two 8 x 8 blocks in registers (movmatrix).
+  const int r0 = lane >> 2;
+  const int cq = (lane & 3) * 2;
+  float o[QB][D / 16][4];
+  float m_r[QB][2], l_r[QB][2];
+#pragma unroll
+  for (int qb = 0; qb < QB; ++qb) {
+    m_r[qb][0] = m_r[qb][1] = -INFINITY;
+    l_r[qb][0] = l_r[qb][1] = 0.f;
+  }
   if (warp < kConsumerWarps) {
-    // ---- q fragments (A operand), scaled and split into hi / lo
-    uint32_t qh[S::KSTEPS][4], ql[S::KSTEPS][4];
+    // ---- Q^T fragments (B operand: k = dims, n = heads), scaled, hi / lo
+    uint32_t qh[QB][S::KSTEPS][2], ql[QB][S::KSTEPS][2];
 #pragma unroll
-    for (int kk = 0; kk < S::KSTEPS; ++kk) {
+    for (int qb = 0; qb < QB; ++qb) {
+      const int g = qb * 8 + r0;
 #pragma unroll
-      for (int f = 0; f < 4; ++f) {
-        const int row = r0 + ((f & 1) ? 8 : 0);
-        const int col = kk * 16 + cq + ((f & 2) ? 8 : 0);
-        float x0 = 0.f, x1 = 0.f;
-        if (row < G) {
-          const float2 v = *reinterpret_cast<const float2 *>(
-              p.q + b * p.q_sb + (long)(head0 + row) * p.q_sh + col);
-          x0 = v.x * p.qscale;
-          x1 = v.y * p.qscale;
+      for (int kk = 0; kk < S::KSTEPS; ++kk) {
+#pragma unroll
+        for (int f = 0; f < 2; ++f) {
+          const int col = kk * 16 + cq + 8 * f;
+          float x0 = 0.f, x1 = 0.f;
+          if (g < G) {
+            const float2 v = *reinterpret_cast<const float2 *>(
+                p.q + b * p.q_sb + (long)(head0 + g) * p.q_sh + col);
+            x0 = v.x * p.qscale;
+            x1 = v.y * p.qscale;
+          }
+          split_bf16x2(x0, x1, qh[qb][kk][f], ql[qb][kk][f]);
         }
-        split_bf16x2(x0, x1, qh[kk][f], ql[kk][f]);
       }
+#pragma unroll
+      for (int mb = 0; mb < D / 16; ++mb)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[qb][mb][e] = 0.f;
     }
-#pragma unroll
-    for (int n = 0; n < S::NT; ++n)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) o[n][e] = 0.f;
 
-    // ldmatrix lane addressing (row = key within the warp's 16, 16-B chunk)
-    const int k_key = warp * 16 + ((lane >> 4) & 1) * 8 + (lane & 7);
-    const int k_dof = ((lane >> 3) & 1) * 8;
-    const int v_key = warp * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
-    const int v_dof = ((lane >> 4) & 1) * 8;
+    // ldmatrix lane addressing: K as the A operand (rows = keys), V^T as
+    // the A operand via .trans (source rows = keys)
+    const int a_key = warp * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
+    const int a_dof = ((lane >> 4) & 1) * 8;
+    const int t_key = warp * 16 + ((lane >> 4) & 1) * 8 + (lane & 7);
+    const int t_dof = ((lane >> 3) & 1) * 8;
 
     for (int t = 0; t < ntiles; ++t) {
       const int s = t % S::STAGES;
@@ -637,68 +663,73 @@ __global__ void __launch_bounds__(kThreads)
       uint8_t *vt = v_st + s * S::TILE_BYTES;
       const int valid = min(S::KT, nrows - t * S::KT);
 
-      // ---- S = Q K^T over this warp's 16 keys
-      float sc[2][4];
+      // ---- S^T = K Q^T over this warp's 16 keys
+      float sc[QB][4];
 #pragma unroll
-      for (int n = 0; n < 2; ++n)
+      for (int qb = 0; qb < QB; ++qb)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) sc[n][e] = 0.f;
+        for (int e = 0; e < 4; ++e) sc[qb][e] = 0.f;
 #pragma unroll
       for (int kk = 0; kk < S::KSTEPS; ++kk) {
-        const int dim = kk * 16 + k_dof;
+        const int dim = kk * 16 + a_dof;
         const int sub = dim >> 6;
         const int chunk = (dim & 63) >> 3;
-        const uint32_t addr = smem_u32(kt + sub * S::SUB_BYTES + k_key * 128 +
-                                       ((chunk ^ (k_key & 7)) << 4));
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(addr, b0, b1, b2, b3);
-        mma_bf16(sc[0], qh[kk], b0, b1);
-        mma_bf16(sc[0], ql[kk], b0, b1);
-        mma_bf16(sc[1], qh[kk], b2, b3);
-        mma_bf16(sc[1], ql[kk], b2, b3);
+        const uint32_t addr = smem_u32(kt + sub * S::SUB_BYTES + a_key * 128 +
+                                       ((chunk ^ (a_key & 7)) << 4));
+        uint32_t ka[4];
+        ldsm_x4(addr, ka[0], ka[1], ka[2], ka[3]);
+#pragma unroll
+        for (int qb = 0; qb < QB; ++qb) {
+          mma_bf16(sc[qb], ka, qh[qb][kk][0], qh[qb][kk][1]);
+          mma_bf16(sc[qb], ka, ql[qb][kk][0], ql[qb][kk][1]);
+        }
       }
       const bool partial = valid < S::KT;
       if (partial) {
 #pragma unroll
-        for (int n = 0; n < 2; ++n)
+        for (int qb = 0; qb < QB; ++qb)
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const int key = warp * 16 + n * 8 + cq + (e & 1);
-            if (key >= valid) sc[n][e] = -INFINITY;
+            const int key = warp * 16 + r0 + 8 * (e >> 1);
+            if (key >= valid) sc[qb][e] = -INFINITY;
           }
       }
 
-      // ---- online softmax on rows r0 (e = 0,1) and r0 + 8 (e = 2,3)
+      // ---- online softmax per head (columns cq + c; keys r0, r0 + 8 here,
+      //      the other 14 keys in the lanes of the same lane % 4)
+      uint32_t pb[QB][4];   // P^T B fragments: hi b0, hi b1, lo b0, lo b1
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        float mx = fmaxf(fmaxf(sc[0][2 * h], sc[0][2 * h + 1]),
-                         fmaxf(sc[1][2 * h], sc[1][2 * h + 1]));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        const float mn = fmaxf(m_r[h], mx);
-        const float msafe = (mn == -INFINITY) ? 0.f : mn;
-        if (mn != m_r[h]) {
-          const float alpha = fast_exp2(m_r[h] - msafe);  // 0 when m was -inf
-          l_r[h] *= alpha;
+      for (int qb = 0; qb < QB; ++qb) {
 #pragma unroll
-          for (int n = 0; n < S::NT; ++n) {
-            o[n][2 * h] *= alpha;
-            o[n][2 * h + 1] *= alpha;
+        for (int c = 0; c < 2; ++c) {
+          float mx = fmaxf(sc[qb][c], sc[qb][c + 2]);
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+          const float mn = fmaxf(m_r[qb][c], mx);
+          const float msafe = (mn == -INFINITY) ? 0.f : mn;
+          if (mn != m_r[qb][c]) {
+            const float alpha = fast_exp2(m_r[qb][c] - msafe);  // 0 when m was -inf
+            l_r[qb][c] *= alpha;
+#pragma unroll
+            for (int mb = 0; mb < D / 16; ++mb) {
+              o[qb][mb][c] *= alpha;
+              o[qb][mb][c + 2] *= alpha;
+            }
+            m_r[qb][c] = mn;
           }
-          m_r[h] = mn;
+          sc[qb][c] = fast_exp2(sc[qb][c] - msafe);
+          sc[qb][c + 2] = fast_exp2(sc[qb][c + 2] - msafe);
+          l_r[qb][c] += sc[qb][c] + sc[qb][c + 2];
         }
-#pragma unroll
-        for (int n = 0; n < 2; ++n) {
-          sc[n][2 * h] = fast_exp2(sc[n][2 * h] - msafe);
-          sc[n][2 * h + 1] = fast_exp2(sc[n][2 * h + 1] - msafe);
-          l_r[h] += sc[n][2 * h] + sc[n][2 * h + 1];
-        }
+        uint32_t h01, l01, h23, l23;
+        split_bf16x2(sc[qb][0], sc[qb][1], h01, l01);   // keys r0
+        split_bf16x2(sc[qb][2], sc[qb][3], h23, l23);   // keys r0 + 8
+        pb[qb][0] = movmatrix_t(h01);
+        pb[qb][1] = movmatrix_t(h23);
+        pb[qb][2] = movmatrix_t(l01);
+        pb[qb][3] = movmatrix_t(l23);
       }
-      uint32_t ph[4], pl[4];
-      split_bf16x2(sc[0][0], sc[0][1], ph[0], pl[0]);
-      split_bf16x2(sc[0][2], sc[0][3], ph[1], pl[1]);
-      split_bf16x2(sc[1][0], sc[1][1], ph[2], pl[2]);
-      split_bf16x2(sc[1][2], sc[1][3], ph[3], pl[3]);
 
       if (partial && warp * 16 + 16 > valid) {
         // rows past the end may hold anything (even NaN): zero this warp's
@@ -714,31 +745,35 @@ __global__ void __launch_bounds__(kThreads)
         __syncwarp();
       }
 
-      // ---- O += P V
+      // ---- O^T += V^T P^T
 #pragma unroll
-      for (int jj = 0; jj < D / 16; ++jj) {
-        const int dim = jj * 16 + v_dof;
+      for (int mb = 0; mb < D / 16; ++mb) {
+        const int dim = mb * 16 + t_dof;
         const int sub = dim >> 6;
         const int chunk = (dim & 63) >> 3;
-        const uint32_t addr = smem_u32(vt + sub * S::SUB_BYTES + v_key * 128 +
-                                       ((chunk ^ (v_key & 7)) << 4));
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(addr, b0, b1, b2, b3);
-        mma_bf16(o[2 * jj], ph, b0, b1);
-        mma_bf16(o[2 * jj], pl, b0, b1);
-        mma_bf16(o[2 * jj + 1], ph, b2, b3);
-        mma_bf16(o[2 * jj + 1], pl, b2, b3);
+        const uint32_t addr = smem_u32(vt + sub * S::SUB_BYTES + t_key * 128 +
+                                       ((chunk ^ (t_key & 7)) << 4));
+        uint32_t va[4];
+        ldsm_x4_t(addr, va[0], va[1], va[2], va[3]);
+#pragma unroll
+        for (int qb = 0; qb < QB; ++qb) {
+          mma_bf16(o[qb][mb], va, pb[qb][0], pb[qb][1]);
+          mma_bf16(o[qb][mb], va, pb[qb][2], pb[qb][3]);
+        }
       }
       if (partial) fence_proxy_async();  // generic writes before the next TMA
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
     }
-    // quad-reduce the row sums (each lane holds 4 of the warp's 16 keys)
+    // sum the head weights over the 8 lanes of each lane % 4 (keys)
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      l_r[h] += __shfl_xor_sync(0xffffffffu, l_r[h], 1);
-      l_r[h] += __shfl_xor_sync(0xffffffffu, l_r[h], 2);
-    }
+    for (int qb = 0; qb < QB; ++qb)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        l_r[qb][c] += __shfl_xor_sync(0xffffffffu, l_r[qb][c], 4);
+        l_r[qb][c] += __shfl_xor_sync(0xffffffffu, l_r[qb][c], 8);
+        l_r[qb][c] += __shfl_xor_sync(0xffffffffu, l_r[qb][c], 16);
+      }
   }
   if (failed) {
     atomicOr(p.err, DEV_ERR_WAIT_TIMEOUT);
@@ -752,23 +787,26 @@ __global__ void __launch_bounds__(kThreads)
     return;
   }
 
-  // ---- merge the 4 consumer warps (rows < G)
+  // ---- merge the 4 consumer warps (heads < G)
   float *w_acc = reinterpret_cast<float *>(smem);   // [4][G][D]
   float *w_m = w_acc + kConsumerWarps * G * D;      // [4][G]
   float *w_l = w_m + kConsumerWarps * G;            // [4][G]
   if (warp < kConsumerWarps) {
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int row = r0 + 8 * h;
-      if (row < G) {
+    for (int qb = 0; qb < QB; ++qb) {
 #pragma unroll
-        for (int n = 0; n < S::NT; ++n) {
-          *reinterpret_cast<float2 *>(&w_acc[(warp * G + row) * D + n * 8 + cq]) =
-              make_float2(o[n][2 * h], o[n][2 * h + 1]);
-        }
-        if ((lane & 3) == 0) {
-          w_m[warp * G + row] = m_r[h];
-          w_l[warp * G + row] = l_r[h];
+      for (int c = 0; c < 2; ++c) {
+        const int g = qb * 8 + cq + c;
+        if (g < G) {
+#pragma unroll
+          for (int mb = 0; mb < D / 16; ++mb) {
+            w_acc[(warp * G + g) * D + mb * 16 + r0] = o[qb][mb][c];
+            w_acc[(warp * G + g) * D + mb * 16 + r0 + 8] = o[qb][mb][c + 2];
+          }
+          if (r0 == 0) {
+            w_m[warp * G + g] = m_r[qb][c];
+            w_l[warp * G + g] = l_r[qb][c];
+          }
         }
       }
     }
@@ -811,7 +849,7 @@ __global__ void __launch_bounds__(kThreads)
   __threadfence();
   __syncthreads();
   if (tid == 0) {
-    int *ctr = p.counters + (size_t)b * gridDim.y + y;
+    int *ctr = p.counters + (size_t)b * p.n_y + y;
     const int ticket = atomicAdd(ctr, 1);
     s_flag = (ticket == n_splits - 1) ? 2 : 0;
     if (s_flag) *ctr = 0;
@@ -964,14 +1002,16 @@ int launch_mma(const DecodeParams &p, int G, const CUtensorMap &mk,
   size_t smem = S::RING;
   if (merge > smem) smem = merge;
   if (sweights > smem) smem = sweights;
-  auto kern = gqa_decode_mma_kernel<D>;
-  static bool configured[64] = {};
+  // query heads per CTA as n8 blocks of the swapped MMA
+  auto kern = G <= 8 ? gqa_decode_mma_kernel<D, 1> : gqa_decode_mma_kernel<D, 2>;
+  static bool configured[64][2] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !configured[dev]) {
+  const int qi = G <= 8 ? 0 : 1;
+  if (dev < 0 || dev >= 64 || !configured[dev][qi]) {
     TLLM_CUDA(cudaFuncSetAttribute(
         kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    if (dev >= 0 && dev < 64) configured[dev] = true;
+    if (dev >= 0 && dev < 64) configured[dev][qi] = true;
   }
   TLLM_CUDA(launch_pdl(kern, grid, dim3(kThreads), smem, st, p, G, mk, mv));
   return TLLM_OK;
@@ -1125,6 +1165,7 @@ static int rows_impl(const float *q, long q_sb, long q_sh, const void *k_cache,
   p.max_splits = max_splits;
   p.qscale = sm_scale * kLog2e;
 
+  p.n_y = ygrid;
   dim3 grid(max_splits, ygrid, batch);
   cudaStream_t st = resolve(stream);
   if (mma)

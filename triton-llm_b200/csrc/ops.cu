@@ -80,6 +80,85 @@ __global__ void rmsnorm_add_kernel(float *h, const float *add, const float *w,
   for (int i = threadIdx.x; i < N; i += blockDim.x) y.put(o + i, (hr[i] / rms) * w[i]);
 }
 
+// RMSNorm of rows whose length is a multiple of 4 and at most 4 * 4 *
+// blockDim.x: every thread holds its float4s in registers, so the row is
+// read once (twice for the fused residual add: h and the addend) and the
+// output leaves as one 8- or 16-byte store per plane and float4.
+// ADD: h += add in place first (the residual add of a row-sharded
+// projection). Same formula as rmsnorm_kernel; the sum of squares runs in
+// another order.
+__device__ __forceinline__ void put4(const RowOut &y, size_t i, float4 v) {
+  if (y.s) {
+    const uint16_t h0 = f32_to_bf16_bits(v.x), h1 = f32_to_bf16_bits(v.y);
+    const uint16_t h2 = f32_to_bf16_bits(v.z), h3 = f32_to_bf16_bits(v.w);
+    *reinterpret_cast<uint2 *>(y.s + i) =
+        make_uint2((uint32_t)h0 | ((uint32_t)h1 << 16), (uint32_t)h2 | ((uint32_t)h3 << 16));
+    if (y.planes == 2) {
+      const uint16_t l0 = f32_to_bf16_bits(v.x - bf16_bits_to_f32(h0));
+      const uint16_t l1 = f32_to_bf16_bits(v.y - bf16_bits_to_f32(h1));
+      const uint16_t l2 = f32_to_bf16_bits(v.z - bf16_bits_to_f32(h2));
+      const uint16_t l3 = f32_to_bf16_bits(v.w - bf16_bits_to_f32(h3));
+      *reinterpret_cast<uint2 *>(y.s + y.plane + i) =
+          make_uint2((uint32_t)l0 | ((uint32_t)l1 << 16), (uint32_t)l2 | ((uint32_t)l3 << 16));
+    }
+  } else {
+    *reinterpret_cast<float4 *>(y.f + i) = v;
+  }
+}
+
+constexpr int kVecPer = 4;   // float4s per thread
+
+template <bool ADD>
+__global__ void rmsnorm_vec_kernel(float *x, const float *add, const float *w,
+                                   RowOut y, int N, float eps) {
+  griddep_launch();
+  griddep_wait();
+  __shared__ float red[32];
+  const int n4 = N >> 2;
+  float4 *xr = reinterpret_cast<float4 *>(x + (size_t)blockIdx.x * N);
+  const float4 *ar = reinterpret_cast<const float4 *>(add + (ADD ? (size_t)blockIdx.x * N : 0));
+  const float4 *w4 = reinterpret_cast<const float4 *>(w);
+  float4 v[kVecPer];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kVecPer; ++k) {
+    const int i = threadIdx.x + k * blockDim.x;
+    v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i < n4) {
+      float4 t = xr[i];
+      if constexpr (ADD) {
+        const float4 a = ar[i];
+        t.x += a.x;
+        t.y += a.y;
+        t.z += a.z;
+        t.w += a.w;
+        xr[i] = t;
+      }
+      v[k] = t;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kVecPer; ++k) {
+    ss = fmaf(v[k].x, v[k].x, ss);
+    ss = fmaf(v[k].y, v[k].y, ss);
+    ss = fmaf(v[k].z, v[k].z, ss);
+    ss = fmaf(v[k].w, v[k].w, ss);
+  }
+  ss = block_sum(ss, red);
+  const float rms = sqrtf(ss / (float)N + eps);
+  const size_t o = (size_t)blockIdx.x * N;
+#pragma unroll
+  for (int k = 0; k < kVecPer; ++k) {
+    const int i = threadIdx.x + k * blockDim.x;
+    if (i < n4) {
+      const float4 g = w4[i];
+      put4(y, o + 4 * (size_t)i,
+           make_float4((v[k].x / rms) * g.x, (v[k].y / rms) * g.y, (v[k].z / rms) * g.z,
+                       (v[k].w / rms) * g.w));
+    }
+  }
+}
+
 // two-pass LayerNorm (triton_llm/kernels/layernorm.py:56-66)
 __global__ void layernorm_kernel(const float *x, const float *g, const float *b,
                                  RowOut y, int N, float eps) {
@@ -361,6 +440,27 @@ using namespace tllm;
 
 extern "C" {
 
+// threads of the vector RMSNorm: a multiple of 32 with <= kVecPer float4s
+// each
+static int rms_vec_threads(int N) {
+  const int n4 = N / 4;
+  int t = (n4 + kVecPer - 1) / kVecPer;
+  t = (t + 31) & ~31;
+  return t < 32 ? 32 : t;
+}
+
+static bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// rows of N % 4 == 0 (<= 4096 floats), 16-byte aligned operands, and an
+// output whose planes keep 8-byte alignment
+static bool rms_vec_ok(const float *x, const float *add, const float *w,
+                       const RowOut &o, int N) {
+  if (N % 4 != 0 || N > 4 * kVecPer * 256) return false;
+  if (!aligned16(x) || (add && !aligned16(add)) || !aligned16(w)) return false;
+  if (o.s) return (reinterpret_cast<uintptr_t>(o.s) & 7) == 0 && o.plane % 4 == 0;
+  return aligned16(o.f);
+}
+
 static int row_out(RowOut *o, void *y, int y_dtype, int y_plane_rows, int M,
                    int N) {
   TLLM_CHECK_ARG(y_dtype == TLLM_F32 || y_dtype == TLLM_SPLIT ||
@@ -392,6 +492,11 @@ int tllm_rmsnorm(const float *x, const float *w, void *y, int y_dtype,
   RowOut o;
   int rc = row_out(&o, y, y_dtype, y_plane_rows, M, N);
   if (rc) return rc;
+  if (rms_vec_ok(x, nullptr, w, o, N)) {
+    TLLM_CUDA(launch_pdl(rmsnorm_vec_kernel<false>, dim3(M), dim3(rms_vec_threads(N)), 0,
+                         resolve(stream), const_cast<float *>(x), nullptr, w, o, N, eps));
+    return TLLM_OK;
+  }
   TLLM_CUDA(launch_pdl(rmsnorm_kernel, dim3(M),
                        dim3(row_threads(N) > 256 ? 256 : row_threads(N)), 0,
                        resolve(stream), x, w, o, N, eps));
@@ -409,6 +514,11 @@ int tllm_rmsnorm_add(float *h, const float *add, const float *w, void *y,
   RowOut o;
   int rc = row_out(&o, y, y_dtype, y_plane_rows, M, N);
   if (rc) return rc;
+  if (rms_vec_ok(h, add, w, o, N)) {
+    TLLM_CUDA(launch_pdl(rmsnorm_vec_kernel<true>, dim3(M), dim3(rms_vec_threads(N)), 0,
+                         resolve(stream), h, add, w, o, N, eps));
+    return TLLM_OK;
+  }
   TLLM_CUDA(launch_pdl(rmsnorm_add_kernel, dim3(M),
                        dim3(row_threads(N) > 256 ? 256 : row_threads(N)), 0,
                        resolve(stream), h, add, w, o, N, eps));

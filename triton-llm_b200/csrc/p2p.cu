@@ -77,6 +77,35 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
+constexpr int kP2PVecPer = 4;   // float4s per thread (as the vector RMSNorm)
+
+// The four words of columns 4i .. 4i + 3 from rank q's slot once all of
+// them carry call number e (bounded wait).
+__device__ __forceinline__ float4 p2p_take4(const unsigned long long *src,
+                                            unsigned e, bool &ok, uint64_t t0,
+                                            int *err) {
+  unsigned long long a0, a1, a2, a3;
+  for (uint32_t it = 0;; ++it) {
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];"
+                 : "=l"(a0), "=l"(a1) : "l"(src) : "memory");
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];"
+                 : "=l"(a2), "=l"(a3) : "l"(src + 2) : "memory");
+    const bool here = (unsigned)(a0 >> 32) == e && (unsigned)(a1 >> 32) == e &&
+                      (unsigned)(a2 >> 32) == e && (unsigned)(a3 >> 32) == e;
+    if (here || !ok) break;
+    // bounded: ~2 s, or 2^26 polls if the timer does not advance
+    if (((it & 255) == 255 && globaltimer_ns() - t0 > kP2PWaitNs) || it == (1u << 26)) {
+      ok = false;
+      atomicOr(err, DEV_ERR_WAIT_TIMEOUT);
+    }
+  }
+  return make_float4(__uint_as_float((unsigned)a0), __uint_as_float((unsigned)a1),
+                     __uint_as_float((unsigned)a2), __uint_as_float((unsigned)a3));
+}
+
+// One row per block, the float4 layout and reduction order of the vector
+// RMSNorm in ops.cu (blockDim.x threads, kP2PVecPer float4s each), so the
+// peer path and a one-rank group give the same bits as tllm_rmsnorm_add.
 __global__ void rmsnorm_p2p_kernel(float *h, const P2PDev *P, const float *w,
                                    uint16_t *ys, float *yf, size_t yplane,
                                    int planes, int N, float eps, int *err) {
@@ -94,46 +123,64 @@ __global__ void rmsnorm_p2p_kernel(float *h, const P2PDev *P, const float *w,
   __syncthreads();
   bool ok = !s_broken;
   const uint64_t t0 = globaltimer_ns();
-  float *hr = h + (size_t)m * N;
-  float ss = 0.f;
-  for (int i = threadIdx.x; i < N; i += blockDim.x) {
-    float v = hr[i];
-    for (int q = 0; q < P->size; ++q) {   // rank order: identical on every rank
-      const unsigned long long *src =
-          P->recv_local + (((size_t)par * P->size + q) * P->mmax + m) * P->ncols + i;
-      unsigned long long word;
-      for (uint32_t it = 0;; ++it) {
-        asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(word) : "l"(src) : "memory");
-        if ((unsigned)(word >> 32) == e || !ok) break;
-        // bounded: ~2 s, or 2^26 polls if the timer does not advance
-        if (((it & 255) == 255 && globaltimer_ns() - t0 > kP2PWaitNs) || it == (1u << 26)) {
-          ok = false;
-          atomicOr(err, DEV_ERR_WAIT_TIMEOUT);
-        }
+  const int n4 = N >> 2;
+  float4 *h4 = reinterpret_cast<float4 *>(h + (size_t)m * N);
+  float4 v[kP2PVecPer];
+#pragma unroll
+  for (int k = 0; k < kP2PVecPer; ++k) {
+    const int i = threadIdx.x + k * blockDim.x;
+    v[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i < n4) {
+      float4 t = h4[i];
+      for (int q = 0; q < P->size; ++q) {   // rank order: identical on every rank
+        const unsigned long long *src =
+            P->recv_local + (((size_t)par * P->size + q) * P->mmax + m) * P->ncols + 4 * i;
+        const float4 a = p2p_take4(src, e, ok, t0, err);
+        t.x += a.x;
+        t.y += a.y;
+        t.z += a.z;
+        t.w += a.w;
       }
-      v += __uint_as_float((unsigned)(word & 0xffffffffu));
+      h4[i] = t;
+      v[k] = t;
     }
-    hr[i] = v;
-    ss = fmaf(v, v, ss);
   }
-  // block sum of squares
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kP2PVecPer; ++k) {
+    ss = fmaf(v[k].x, v[k].x, ss);
+    ss = fmaf(v[k].y, v[k].y, ss);
+    ss = fmaf(v[k].z, v[k].z, ss);
+    ss = fmaf(v[k].w, v[k].w, ss);
+  }
+  // block sum of squares (xor butterflies: every lane holds the same sum)
   for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  __syncthreads();
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
-  if (threadIdx.x < 32) {
-    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+  {
+    const int nw = (blockDim.x + 31) >> 5;
+    float t = (threadIdx.x & 31) < nw ? red[threadIdx.x & 31] : 0.f;
     for (int off = 16; off > 0; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
-    if (threadIdx.x == 0) red[0] = t;
+    ss = t;
   }
-  __syncthreads();
-  const float rms = sqrtf(red[0] / (float)N + eps);
+  const float rms = sqrtf(ss / (float)N + eps);
   const size_t o = (size_t)m * N;
-  for (int i = threadIdx.x; i < N; i += blockDim.x) {
-    const float y = (hr[i] / rms) * w[i];
-    if (ys)
-      store_act(ys, yplane, o + i, y, planes);
-    else
-      yf[o + i] = y;
+  const float4 *w4 = reinterpret_cast<const float4 *>(w);
+#pragma unroll
+  for (int k = 0; k < kP2PVecPer; ++k) {
+    const int i = threadIdx.x + k * blockDim.x;
+    if (i >= n4) continue;
+    const float4 g = w4[i];
+    const float y[4] = {(v[k].x / rms) * g.x, (v[k].y / rms) * g.y, (v[k].z / rms) * g.z,
+                        (v[k].w / rms) * g.w};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      if (ys)
+        store_act(ys, yplane, o + 4 * (size_t)i + c, y[c], planes);
+      else
+        yf[o + 4 * (size_t)i + c] = y[c];
+    }
   }
   // the last block to finish records the call as done (read by the next
   // scatter and reader, which run after this kernel)
@@ -253,7 +300,14 @@ int tllm_rmsnorm_p2p(float *h, const void *p2p, const float *w, void *y,
   TLLM_CHECK_ARG(!act || y_plane_rows >= M, "y_plane_rows < M");
   // resident before the projection that scatters has finished
   // (programmatic serialization); the kernel waits for it first
-  TLLM_CUDA(launch_pdl(rmsnorm_p2p_kernel, dim3(M), dim3(256), 0, resolve(stream), h, P,
+  TLLM_CHECK_ARG(N % 4 == 0 && N <= 4 * kP2PVecPer * 1024, "N must be a multiple of 4, <= %d",
+                 4 * kP2PVecPer * 1024);
+  TLLM_CHECK_ARG((reinterpret_cast<uintptr_t>(h) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(w) & 15) == 0,
+                 "h and w must be 16-byte aligned");
+  int threads = ((N / 4 + kP2PVecPer - 1) / kP2PVecPer + 31) & ~31;
+  if (threads < 32) threads = 32;
+  TLLM_CUDA(launch_pdl(rmsnorm_p2p_kernel, dim3(M), dim3(threads), 0, resolve(stream), h, P,
                        w, act ? static_cast<uint16_t *>(y) : nullptr,
                        act ? nullptr : static_cast<float *>(y),
                        act ? (size_t)y_plane_rows * N : 0, y_dtype == TLLM_SPLIT ? 2 : 1,
