@@ -316,6 +316,7 @@ class LlamaDecodeWorkload:
         """All projection GEMMs of one step replayed alone (weights stream)."""
         from triton_llm import _lib
         from triton_llm.kernels.linear import linear
+        from triton_llm.kernels.mlp import mlp_block
         s, w = self.sess, self.wts
         B = s.B
         g = gpu.Graph()
@@ -327,19 +328,27 @@ class LlamaDecodeWorkload:
                 linear(s.x, L["qkv"], op=_lib.EPI_QKV, ws=s.lin_ws, M=B, qkv=dict(
                     cos=w.cos, sin=w.sin, row_seq=s.row_seq, row_pos=s.pos, q_out=s.q,
                     k_cache=k, v_cache=v, n_head=w.H, n_kv_head=w.Hkv, head_dim=w.D))
-                linear(s.attn, L["o"], out_dev=s.x, op=_lib.EPI_STORE, ws=s.lin_ws, M=B)
-                linear(s.x, L["gu"], out_dev=s.act, op=_lib.EPI_SWIGLU, ws=s.lin_ws, M=B)
-                linear(s.act, L["down"], out_dev=s.x, op=_lib.EPI_STORE, ws=s.lin_ws, M=B)
+                if s.mlp_ws is not None:
+                    # the step's own form: o, norm, gate/up, down in one launch
+                    mlp_block(s.attn, L["o"], s.h, L["ln2"], s.x, L["gu"], s.act, L["down"],
+                              B, w.eps, s.mlp_ws)
+                else:
+                    linear(s.attn, L["o"], out_dev=s.x, op=_lib.EPI_STORE, ws=s.lin_ws, M=B)
+                    linear(s.x, L["gu"], out_dev=s.act, op=_lib.EPI_SWIGLU, ws=s.lin_ws, M=B)
+                    linear(s.act, L["down"], out_dev=s.x, op=_lib.EPI_STORE, ws=s.lin_ws, M=B)
             linear(s.x, w.lm_head, out_dev=s.logits, ws=s.lin_ws, M=B)
         for (M, N, K) in w.linear_shapes(B)[:4]:
             alg += w.L * (N * K * 2 + M * K * 4 + M * N * 4)
         M, N, K = w.linear_shapes(B)[4]
         alg += N * K * 2 + M * K * 4 + M * N * 4
-        n_launch = 4 * w.L + 1
+        n_launch = (2 if s.mlp_ws is not None else 4) * w.L + 1
         ms = _time_graph(gpu, g, 5)
         achieved = alg / (ms / 1e3) / 1e9
-        return {"kernels": "linear_tc_kernel (qkv+rope+append, o, gate/up+swiglu, "
-                           "down, lm_head)",
+        return {"kernels": ("linear_tc_kernel (qkv+rope+append, lm_head) + mlp_kernel "
+                            "(o, norm, gate/up+swiglu, down in one launch)"
+                            if s.mlp_ws is not None else
+                            "linear_tc_kernel (qkv+rope+append, o, gate/up+swiglu, "
+                            "down, lm_head)"),
                 "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "bound": "hbm",
                 "algorithmic_bytes_per_step": alg, "ms_per_step": round(ms, 4),

@@ -247,6 +247,34 @@ int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
                 const void *p2p, void *partial, size_t partial_bytes,
                 int32_t *counters, tllm_stream_t stream);
 
+/*
+ * The decode MLP half of a Llama-style layer in one persistent launch (no
+ * counterpart in the reference, which runs it as o GEMM, add, rms_norm,
+ * gate/up GEMMs, swiglu, down GEMM and add: smollm2_triton/model.py:344-357):
+ *   h   += attn . Wo^T
+ *   x    = RMSNorm(h) * ln_w            (eps; the norm before the MLP)
+ *   act  = silu(x . Wg^T) * (x . Wu^T)
+ *   h   += act . Wd^T
+ * attn, x and act are TLLM_BF16 operand buffers (one plane of
+ * *_plane_rows >= M rows of attn_dim, hidden and ffn values); x and act are
+ * overwritten with the norm and SwiGLU outputs. Weights TLLM_BF16_TILED: Wo
+ * (hidden, attn_dim), Wgu (2 ffn, hidden) with gate/up rows interleaved in
+ * blocks of 8 as for op SWIGLU of tllm_linear, Wd (hidden, ffn). h fp32
+ * (M, hidden), in place. M <= 64, hidden % 128 == 0, attn_dim % 64 == 0,
+ * ffn % 64 == 0. One CTA per SM, launched cooperatively; the three GEMMs
+ * share one weight stream split evenly over the SMs, and the phases meet at
+ * grid barriers. workspace: tllm_mlp_workspace bytes, 256-byte aligned,
+ * zero-filled before the first call; the kernel keeps its counters valid
+ * across calls, and calls that overlap on the GPU must not share one.
+ */
+int tllm_mlp_workspace(int M, int attn_dim, int hidden, int ffn,
+                       size_t *bytes);
+int tllm_mlp(const void *attn, int attn_plane_rows, const void *w_o, float *h,
+             const float *ln_w, float eps, void *x, int x_plane_rows,
+             const void *w_gu, void *act, int act_plane_rows,
+             const void *w_down, int M, int attn_dim, int hidden, int ffn,
+             void *workspace, size_t workspace_bytes, tllm_stream_t stream);
+
 /* C = A @ B, fp32, A (M, K), B (K, N) row-major: the reference's weight
  * layout (triton_llm/kernels/gemm.py:53-109). */
 int tllm_gemm_f32(const float *a, const float *b, float *c, int M, int N,

@@ -597,3 +597,82 @@ def test_scatter_rejects_bad_arguments(gpu):
                           gpu.allocate((2 * N,), np.float32),
                           gpu.allocate((4, 2 * N), np.float32), 4)
     peer.close()
+
+
+# ----------------------------------------------------- fused decode MLP block --
+def _close_mlp(got, want, msg):
+    # both paths sum in fp32 but in different orders (split-K pieces, the
+    # norm's sum of squares) and round x and act to bf16 afterwards, so a
+    # few elements land one bf16 step apart before the down projection;
+    # every element stays within 5e-3 and the mean difference near zero
+    np.testing.assert_allclose(got, want, rtol=5e-3, atol=5e-3, err_msg=msg)
+    assert float(np.abs(got - want).mean()) < 2e-5, msg
+
+@pytest.mark.parametrize("M", [1, 8, 33, 64])
+def test_mlp_block_matches_the_four_launches(gpu, M):
+    """tllm_mlp (o + residual, RMSNorm, gate/up + SwiGLU, down + residual in
+    one launch) against the same layer as four launches, on two calls in a
+    row and in a replayed CUDA graph (its counters survive between calls)."""
+    from triton_llm import _lib
+    from triton_llm.kernels.linear import Linear, LinearWorkspace, linear, swiglu_rows
+    from triton_llm.kernels.mlp import MlpWorkspace, mlp_block
+    from triton_llm.kernels.rms_norm import rms_norm_rows
+    hidden, attn_dim, ffn, eps = 1024, 1024, 2816, 1e-5
+    rng = np.random.default_rng(40 + M)
+    w = lambda n, k: (rng.standard_normal((n, k), dtype=F32) * 0.03).astype(F32)  # noqa: E731
+    wo = Linear(w(hidden, attn_dim), "bfloat16")
+    wgu = Linear(swiglu_rows(w(ffn, hidden), w(ffn, hidden)), "bfloat16")
+    wd = Linear(w(hidden, ffn), "bfloat16")
+    ln = gpu.to_device((1.0 + 0.1 * rng.standard_normal(hidden)).astype(F32))
+    attn = gpu.to_device_split(rng.standard_normal((M, attn_dim), dtype=F32), planes=1)
+    h0 = rng.standard_normal((M, hidden), dtype=F32)
+    lws = LinearWorkspace([(M, hidden, attn_dim), (M, 2 * ffn, hidden), (M, hidden, ffn)])
+    mws = MlpWorkspace(M, attn_dim, hidden, ffn)
+
+    def four(h):
+        x = gpu.act_empty(M, hidden, 1)
+        act = gpu.act_empty(M, ffn, 1)
+        linear(attn, wo, out_dev=h, op=_lib.EPI_RESID, resid_dev=h, ws=lws, M=M)
+        rms_norm_rows(h, wo_ln, x, M, eps)
+        linear(x, wgu, out_dev=act, op=_lib.EPI_SWIGLU, ws=lws, M=M)
+        linear(act, wd, out_dev=h, op=_lib.EPI_RESID, resid_dev=h, ws=lws, M=M)
+        return x, act
+
+    wo_ln = ln
+    h_ref = gpu.to_device(h0)
+    x_ref, act_ref = four(h_ref)
+    href = h_ref.to_numpy()
+    x = gpu.act_empty(M, hidden, 1)
+    act = gpu.act_empty(M, ffn, 1)
+    for call in range(2):
+        h = gpu.to_device(h0)
+        mlp_block(attn, wo, h, ln, x, wgu, act, wd, M, eps, mws)
+        gpu.device_synchronize()
+        np.testing.assert_allclose(gpu.split_to_host(x, M), gpu.split_to_host(x_ref, M),
+                                   rtol=1e-2, atol=1e-2, err_msg=f"x, call {call}")
+        _close_mlp(h.to_numpy(), href, f"h, call {call}")
+    h = gpu.to_device(h0)
+    g = gpu.Graph()
+    with g:
+        mlp_block(attn, wo, h, ln, x, wgu, act, wd, M, eps, mws)
+    for rep in range(3):
+        gpu.copy_d2d(h, gpu.to_device(h0))
+        g.launch()
+        gpu.device_synchronize()
+        _close_mlp(h.to_numpy(), href, f"h, replay {rep}")
+    del g
+
+
+def test_mlp_block_rejects_bad_shapes(gpu):
+    from triton_llm.kernels.linear import Linear
+    from triton_llm.kernels.mlp import MlpWorkspace, mlp_block
+    with pytest.raises(ValueError):
+        MlpWorkspace(65, 1024, 1024, 2048)        # more rows than a tile
+    with pytest.raises(ValueError):
+        MlpWorkspace(8, 1024, 1000, 2048)         # hidden not a multiple of 128
+    ws = MlpWorkspace(8, 128, 128, 128)
+    lin = Linear(np.zeros((128, 128), F32), "float32")
+    a = gpu.act_empty(8, 128, 1)
+    with pytest.raises(ValueError):               # fp32 weights
+        mlp_block(a, lin, gpu.allocate((8, 128), np.float32), gpu.allocate((128,), np.float32),
+                  a, lin, a, lin, 8, 1e-5, ws)

@@ -148,9 +148,12 @@ def test_smol135m_bf16_32_steps_vs_oracle(gpu):
     np.testing.assert_allclose(logits[:steps], wl[:steps], atol=2e-2)
 
 
-@pytest.mark.parametrize("mode", ["float32", "bf16w-split", "bf16w"])
-def test_llama3b_slice_matches_reference(gpu, golden, mode):
-    """Llama-3.2-3B geometry (24/8/128, 2 layers, 128256 vocab)."""
+@pytest.mark.parametrize("mode", ["float32", "bf16w-split", "bf16w", "bf16w-fused-mlp"])
+def test_llama3b_slice_matches_reference(gpu, golden, mode, monkeypatch):
+    """Llama-3.2-3B geometry (24/8/128, 2 layers, 128256 vocab); the last
+    mode runs the decode MLP half as one launch (tllm_mlp)."""
+    if mode == "bf16w-fused-mlp":
+        monkeypatch.setenv("TLLM_FUSED_MLP", "1")
     g = golden("llama3b_2l_slice")
     w = inputs.round_linear_weights_bf16(inputs.llama_weights(inputs.LLAMA3B_2L, 0))
     if mode == "float32":

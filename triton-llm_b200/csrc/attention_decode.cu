@@ -515,7 +515,6 @@ struct MmaShape {
   static constexpr int TILE_BYTES = SUB * SUB_BYTES;
   static constexpr int STAGES = D <= 64 ? 4 : 3;
   static constexpr int KSTEPS = D / 16;
-  static constexpr int NT = D / 8;
   static constexpr size_t RING =
       2 * (size_t)STAGES * TILE_BYTES + 2 * STAGES * sizeof(uint64_t);
 };

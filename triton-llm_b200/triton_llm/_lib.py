@@ -97,6 +97,9 @@ SIGNATURES: dict[str, list] = {
                     _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i,
                     _vp, _vp, _vp, _sz, _vp, _vp],
     "tllm_gemm_f32": [_vp, _vp, _vp, _i, _i, _i, _vp],
+    "tllm_mlp_workspace": [_i, _i, _i, _i, _psz],
+    "tllm_mlp": [_vp, _i, _vp, _vp, _vp, _f, _vp, _i, _vp, _vp, _i, _vp, _i, _i, _i, _i,
+                 _vp, _sz, _vp],
     # rows / elementwise
     "tllm_rmsnorm": [_vp, _vp, _vp, _i, _i, _i, _i, _f, _vp],
     "tllm_rmsnorm_add": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp],
