@@ -30,6 +30,27 @@ from .config import GPT2Config
 class GPT2Model:
     """GPT-2 inference model (batch 1 API of the reference)."""
 
+    @classmethod
+    def from_safetensors(cls, path, config: GPT2Config | None = None, dtype: str = "float32"):
+        """Build from a safetensors checkpoint (file, shards or directory);
+        names may carry HuggingFace's ``transformer.`` prefix."""
+        from collections.abc import Mapping
+        from triton_llm.safetensors import load_state_dict
+        sd = load_state_dict(path)
+        pre = "transformer."
+
+        class _Names(Mapping):   # lazy view without the prefix
+            def __getitem__(self, k):
+                return sd[k] if k in sd else sd[pre + k]
+
+            def __iter__(self):
+                return (k[len(pre):] if k.startswith(pre) else k for k in sd)
+
+            def __len__(self):
+                return len(sd)
+
+        return cls(config or GPT2Config(), _Names(), dtype=dtype)
+
     def __init__(self, config: GPT2Config, weights: dict, dtype: str = "float32"):
         self.config = c = config
         self.H = c.n_head

@@ -54,6 +54,13 @@ class SmolLM2Config:
             raise ValueError(f"Unknown variant: {name!r}. Available: {list(variants.keys())}")
         return SmolLM2Config(**variants[name])
 
+    @classmethod
+    def from_dict(cls, d: dict) -> "SmolLM2Config":
+        """From a HuggingFace ``config.json`` dict (unknown keys ignored)."""
+        import dataclasses
+        names = {f.name for f in dataclasses.fields(cls)}
+        return cls(**{k: v for k, v in d.items() if k in names})
+
     # GPT-2 style aliases used by shared code (reference config.py:114-126)
     @property
     def n_embd(self):

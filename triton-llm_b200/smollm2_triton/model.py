@@ -42,6 +42,23 @@ class SmolLM2ForCausalLM:
         (~16 mantissa bits, twice the tensor-core work).
     """
 
+    @classmethod
+    def from_safetensors(cls, path, config: SmolLM2Config | None = None, **kw):
+        """Build from a safetensors checkpoint (a file, a list of shards, or a
+        directory with ``model.safetensors`` or an index and its shards; the
+        directory's ``config.json`` gives the config when none is passed).
+        Tensors are read from the memory-mapped files one at a time."""
+        import json
+        import os
+        from triton_llm.safetensors import load_state_dict
+        if config is None:
+            cj = os.path.join(path, "config.json") if os.path.isdir(str(path)) else None
+            if not cj or not os.path.exists(cj):
+                raise ValueError("pass a config, or a directory holding config.json")
+            with open(cj) as f:
+                config = SmolLM2Config.from_dict(json.load(f))
+        return cls(config, load_state_dict(path), **kw)
+
     def __init__(self, config: SmolLM2Config, weights: dict, dtype: str | None = None,
                  kv_dtype: str | None = None, act_dtype: str = "bfloat16"):
         self.config = config
