@@ -350,20 +350,30 @@ class LlamaSession:
         else:
             self._norm_add(h, part, w.norm, x, M)
 
-    def prefill(self, prompts, all_logits=False):
-        """Run the prompts of sequences 0..len(prompts)-1 through the model.
+    def prefill(self, prompts, all_logits=False, slots=None):
+        """Run the prompts through the model into cache sequences ``slots``
+        (default 0..len(prompts)-1).
 
-        Every sequence restarts at position 0. Returns the logits of the last
-        prompt token of each sequence (host, (n, V)), or of every prompt
-        token when ``all_logits`` (host, (sum(len), V)). Afterwards
-        ``ids`` holds the greedy next token of each sequence and ``pos``
-        the prompt lengths, ready for ``decode_step``.
+        Every such sequence restarts at position 0. Returns the logits of the
+        last prompt token of each prompt (host, (n, V)), or of every prompt
+        token when ``all_logits`` (host, (sum(len), V)). Afterwards ``ids``
+        holds the greedy next token of each prompt's sequence and ``pos`` the
+        prompt lengths, ready for ``decode_step``. Without ``slots`` the other
+        sequences are reset to position 0; with ``slots`` they keep their
+        state (a serving loop admitting requests into free slots).
         """
         w = self.w
         prompts = [np.asarray(p, np.int32).reshape(-1) for p in prompts]
         nseq = len(prompts)
         if nseq > self.B:
             raise ValueError(f"{nseq} prompts for a batch of {self.B}")
+        keep = slots is not None
+        slots = np.arange(nseq, dtype=np.int32) if slots is None else \
+            np.asarray(slots, np.int32).reshape(-1)
+        if len(slots) != nseq or (slots < 0).any() or (slots >= self.B).any() or \
+                len(set(slots.tolist())) != nseq:
+            raise ValueError(f"slots {slots.tolist()} do not name {nseq} distinct "
+                             f"sequences of the batch of {self.B}")
         lens = np.array([len(p) for p in prompts], np.int64)
         if (lens <= 0).any():
             raise ValueError("every prompt needs at least one token")
@@ -373,7 +383,7 @@ class LlamaSession:
         if M > self._prefill_rows:
             self._prefill_buffers(M, 256 << 20)
         ids = np.concatenate(prompts)
-        seq = np.repeat(np.arange(nseq, dtype=np.int32), lens)
+        seq = np.repeat(slots, lens)
         pos = np.concatenate([np.arange(n, dtype=np.int32) for n in lens])
         self.p_ids.from_numpy(np.pad(ids, (0, self._prefill_rows - M)))
         self.p_seq.from_numpy(np.pad(seq, (0, self._prefill_rows - M)))
@@ -406,10 +416,14 @@ class LlamaSession:
             linear(self.x, w.lm_head, out_dev=self.logits, ws=self.lin_ws, M=nseq)
             host = self.logits.to_numpy()[:nseq]
             next_ids = np.argmax(host, axis=-1).astype(np.int32)
-        ids_full = np.zeros(self.B, np.int32)
-        ids_full[:nseq] = next_ids
-        pos_full = np.zeros(self.B, np.int32)
-        pos_full[:nseq] = lens
+        if keep:
+            ids_full = self.ids.to_numpy()
+            pos_full = self.pos.to_numpy()
+        else:
+            ids_full = np.zeros(self.B, np.int32)
+            pos_full = np.zeros(self.B, np.int32)
+        ids_full[slots] = next_ids
+        pos_full[slots] = lens
         self.ids.from_numpy(ids_full)
         self.pos.from_numpy(pos_full)
         self.lens.from_numpy(pos_full)

@@ -173,6 +173,27 @@ class SmolLM2ForCausalLM:
                 f"+ {max_new_tokens} new) exceeds max_position_embeddings "
                 f"({self.config.max_position_embeddings})")
 
+    def enable_batching(self, max_batch: int = 8, max_seq: int | None = None):
+        """Serve greedy generate_gpu / generate_stream_gpu calls from any
+        thread through one batched session (``BatchScheduler``): concurrent
+        requests share each decode step instead of queueing behind each
+        other. Sampling with temperature keeps the single-request path."""
+        from .engine import LlamaSession
+        from .scheduler import BatchScheduler
+        self.disable_batching()
+        self._init_gpu_weights()
+        S = int(max_seq or self.config.max_position_embeddings)
+        self._sched = BatchScheduler(
+            lambda B, S: LlamaSession(self.dev, B, S, kv_dtype=self._kv_dtype,
+                                      act_dtype=self._act_dtype),
+            max_batch, S)
+        return self._sched
+
+    def disable_batching(self):
+        if getattr(self, "_sched", None) is not None:
+            self._sched.close()
+            self._sched = None
+
     def generate_gpu(self, token_ids: np.ndarray, max_new_tokens: int = 20,
                      temperature: float = 1.0, top_k: int = 0,
                      eos_token_id: int | None = None) -> np.ndarray:
@@ -184,6 +205,9 @@ class SmolLM2ForCausalLM:
         """
         token_ids = np.asarray(token_ids)
         self._validate(token_ids, max_new_tokens, temperature, top_k)
+        if getattr(self, "_sched", None) is not None and temperature <= 1e-6:
+            out = self._sched.generate(token_ids[0], max_new_tokens, eos_token_id)
+            return out.reshape(1, -1).astype(np.int32)
         out = [int(t) for t in token_ids[0]]
         for tok, _ in self._stream(token_ids, max_new_tokens, temperature, top_k,
                                    eos_token_id):
@@ -197,6 +221,9 @@ class SmolLM2ForCausalLM:
         (smollm2_triton/model.py:471-541)."""
         token_ids = np.asarray(token_ids)
         self._validate(token_ids, max_new_tokens, temperature, top_k)
+        if getattr(self, "_sched", None) is not None and temperature <= 1e-6:
+            yield from self._sched.submit(token_ids[0], max_new_tokens, eos_token_id).stream()
+            return
         yield from self._stream(token_ids, max_new_tokens, temperature, top_k,
                                 eos_token_id)
 
