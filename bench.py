@@ -495,6 +495,141 @@ class SmolDecodeWorkload(LlamaDecodeWorkload):
         return r
 
 
+class GPT2Workload:
+    """GPT-2 small (12 x 768, 12 heads, GELU, LayerNorm,
+    vocab 50257), fp32 weights N(0, 0.02) from seed 0 in HF order, batch 1:
+    a 32-token prompt (uniform ids, seed 0) prefilled, then greedy decode
+    steps through the model's own cached forward (``GPT2Model._forward_cached``
+    + argmax), the reference's generate loop. Each step brings the (1, V)
+    logits to the host like the reference API does."""
+
+    name = "gpt2"
+    scaling = "weak"
+    dtype = "f32"
+    model = "gpt2"
+
+    def __init__(self, ranks, steps, warmup):
+        self.ranks = ranks
+        self.steps, self.warmup = steps, warmup
+        self.prompt_len = 32
+        # every phase (2 warm-ups, timed, e2e warm-up, e2e, check) restarts
+        # at the prompt; the cache holds the longest of them
+        self.S = self.prompt_len + max(steps, warmup) + 8
+
+    def config(self):
+        return {"workload": "cfg1 GPT-2 small fp32 greedy decode, batch 1",
+                "model": "GPT-2 small (124M)", "layers": 12, "hidden": 768,
+                "heads": 12, "ffn": 3072, "vocab": 50257, "batch": 1,
+                "prompt": "32 uniform ids (seed 0), prefilled before timing",
+                "weights": "N(0,0.02) fp32, seed 0, HF state-dict order",
+                "timed": "K decode steps: cached forward of one token (87 kernels), "
+                         "logits to the host, argmax on the host",
+                "l2": "inputs larger than L2: 495 MB of fp32 weights per step"}
+
+    def setup(self):
+        import inputs
+        from triton_llm import gpu
+        from gpt2_triton import GPT2Config, GPT2Model
+        self.gpu = gpu
+        self.cfg = GPT2Config()
+        self.w = inputs.gpt2_weights(inputs.GPT2_SMALL, 0)
+        self.m = GPT2Model(self.cfg, self.w, dtype="float32")
+        self.prompt = np.random.default_rng(0).integers(0, 50257, self.prompt_len).astype(np.int32)
+        self.m._init_cache(self.S)
+        self.prefill_logits = self.m.forward(self.prompt[None], use_cache=True)[0]
+        self.first = int(np.argmax(self.prefill_logits[-1]))
+        self.launches_per_step = 87
+        self.h2d = 3 * 4 * max(self.m._rows, 1)
+        self.d2h = 50257 * 4
+        self.reset()
+
+    def reset(self):
+        self.m._cache_len = self.prompt_len
+        self.tok = self.first
+
+    def capture(self):
+        pass   # the reference's step returns logits to the host: no graph
+
+    def step(self):
+        logits = self.m._forward_cached(np.array([[self.tok]], np.int32))
+        self.tok = int(np.argmax(logits[0, -1]))
+
+    def units_per_step(self):
+        return 1
+
+    def e2e_begin(self):
+        self.reset()
+
+    def step_e2e(self):
+        self.step()
+
+    def kernel_roofline(self, gpu, peak):
+        """The step's fp32 projections (CUDA-core GEMV) replayed alone."""
+        from triton_llm import _lib
+        from triton_llm.kernels.linear import linear
+        m = self.m
+        g = gpu.Graph()
+        alg = 0
+        with g:
+            for L in m.layers:
+                for name, op in (("proj", _lib.EPI_STORE), ("fc", _lib.EPI_GELU),
+                                 ("mproj", _lib.EPI_STORE)):
+                    lin = L[name]
+                    src = m.act if name == "mproj" else m.x
+                    dst = m.act if name == "fc" else m.h
+                    linear(src, lin, out_dev=dst, op=op, ws=m.lin_ws, M=1)
+                linear(m.x, L["qkv"], out_dev=m.act, ws=m.lin_ws, M=1)   # 3n <= 4n wide
+            linear(m.x, m.lm_head, out_dev=m.logits, ws=m.lin_ws, M=1)
+        for L in m.layers:
+            for name in ("qkv", "proj", "fc", "mproj"):
+                alg += L[name].N * L[name].K * 4
+        alg += m.lm_head.N * m.lm_head.K * 4
+        ms = _time_graph(gpu, g, 10)
+        achieved = alg / (ms / 1e3) / 1e9
+        return {"kernel": "linear_f32_kernel (fp32 weights, CUDA cores; 49 launches)",
+                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "bound": "hbm",
+                "algorithmic_bytes_per_launch": alg, "launch_ms": round(ms, 5),
+                "timing": "projection-only CUDA graph of one decode step, 10 replays",
+                "traffic": None}
+
+    def projection_roofline(self, gpu, peak):
+        return None
+
+    def check(self):
+        """Prefill logits of the prompt vs the oracle (fp32 reference math)."""
+        from oracle.models import GPT2Oracle
+        o = GPT2Oracle(self.cfg, self.w)
+        o.init_cache(self.prompt_len + 1)
+        want = o.forward_cached(self.prompt[None])[0]
+        return float(np.abs(self.prefill_logits - want).max())
+
+
+def gpt2_cpu_sample(steps: int):
+    """The oracle's GPT-2 decode step (numpy, BLAS threads = host cores)
+    after the 32-token prompt, median over ``steps``. Returns (tokens/s,
+    text)."""
+    import inputs
+    from oracle.models import GPT2Oracle
+    from gpt2_triton import GPT2Config
+    cfg = GPT2Config()
+    o = GPT2Oracle(cfg, inputs.gpt2_weights(inputs.GPT2_SMALL, 0))
+    prompt = np.random.default_rng(0).integers(0, 50257, 32).astype(np.int32)
+    o.init_cache(32 + steps + 2)
+    logits = o.forward_cached(prompt[None])
+    tok = int(np.argmax(logits[0, -1]))
+    ts = []
+    for _ in range(steps):
+        t = time.perf_counter()
+        logits = o.forward_cached(np.array([[tok]], np.int32))
+        tok = int(np.argmax(logits[0, -1]))
+        ts.append(time.perf_counter() - t)
+    per = statistics.median(ts)
+    return 1.0 / per, (f"oracle GPT-2 small decode step after a 32-token prompt, "
+                       f"median of {steps} steps ({per * 1e3:.1f} ms), numpy restatement "
+                       "(oracle/), batch 1 like the reference")
+
+
 def llama_cpu_sample(ctx: int, steps: int, model="Llama-3.2-3B-Instruct", log=None):
     """The oracle's decode step for ONE sequence at context ``ctx`` through
     2 of the model's layers and the lm_head, timed with numpy using every
@@ -930,7 +1065,7 @@ class ProjLlamaLayerWorkload(_IsolatedWorkload):
 
 
 WORKLOADS = {"llama3b": LlamaDecodeWorkload, "llama3b_tp": LlamaTPWorkload,
-             "smol135m": SmolDecodeWorkload,
+             "smol135m": SmolDecodeWorkload, "gpt2": GPT2Workload,
              "gqa": GQAWorkload,
              "gqa_llama3b": GQALlamaLayerWorkload, "proj_llama3b": ProjLlamaLayerWorkload}
 
@@ -970,6 +1105,8 @@ def cpu_baseline(name, cores, steps, pool=None, ctx=None):
         return llama_cpu_sample(int(ctx), steps)
     if name == "smol135m":
         return llama_cpu_sample(int(ctx), steps, model=SmolDecodeWorkload.model)
+    if name == "gpt2":
+        return gpt2_cpu_sample(max(steps, 3))
     return None
 
 
@@ -1094,6 +1231,11 @@ def reference_arm(args, ranks, cores):
         cfg = {"workload": "cfg5 Llama-3.2-3B long-context greedy decode, KV-head TP",
                "model": LlamaTPWorkload.model, "batch": 8, "ctx": LlamaTPWorkload.ctx}
         scaling = "strong"
+    elif args.workload == "gpt2":
+        value, sample = gpt2_cpu_sample(max(args.steps, 3))
+        cfg = {"workload": "cfg1 GPT-2 small fp32 greedy decode, batch 1",
+               "model": "GPT-2 small (124M)", "batch": 1, "prompt": 32}
+        scaling = "weak"
     elif args.workload == "smol135m":
         value, sample = llama_cpu_sample(640, max(args.steps, 3),
                                          model=SmolDecodeWorkload.model)
