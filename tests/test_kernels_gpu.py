@@ -608,16 +608,19 @@ def _close_mlp(got, want, msg):
     np.testing.assert_allclose(got, want, rtol=5e-3, atol=5e-3, err_msg=msg)
     assert float(np.abs(got - want).mean()) < 2e-5, msg
 
-@pytest.mark.parametrize("M", [1, 8, 33, 64])
-def test_mlp_block_matches_the_four_launches(gpu, M):
+@pytest.mark.parametrize("M,hidden,ffn", [(1, 1024, 2816), (8, 1024, 2816),
+                                          (33, 1024, 2816), (64, 1024, 2816),
+                                          (8, 256, 9600)])
+def test_mlp_block_matches_the_four_launches(gpu, M, hidden, ffn):
     """tllm_mlp (o + residual, RMSNorm, gate/up + SwiGLU, down + residual in
     one launch) against the same layer as four launches, on two calls in a
-    row and in a replayed CUDA graph (its counters survive between calls)."""
+    row and in a replayed CUDA graph (its counters survive between calls).
+    The last shape has more gate/up tiles than SMs (whole tiles in turn)."""
     from triton_llm import _lib
     from triton_llm.kernels.linear import Linear, LinearWorkspace, linear, swiglu_rows
     from triton_llm.kernels.mlp import MlpWorkspace, mlp_block
     from triton_llm.kernels.rms_norm import rms_norm_rows
-    hidden, attn_dim, ffn, eps = 1024, 1024, 2816, 1e-5
+    attn_dim, eps = hidden, 1e-5
     rng = np.random.default_rng(40 + M)
     w = lambda n, k: (rng.standard_normal((n, k), dtype=F32) * 0.03).astype(F32)  # noqa: E731
     wo = Linear(w(hidden, attn_dim), "bfloat16")

@@ -13,13 +13,15 @@
 // per SM streams the weights of all three GEMMs through one ring without a
 // break, and the phases meet at grid barriers.
 //
-// Work split (stream-K): the (tile, k-chunk) pairs of a GEMM are cut into
-// gridDim.x equal ranges, one per CTA, so every SM streams the same number
-// of weight bytes whatever the tile count. A CTA's range crosses tile
-// boundaries; each piece of a tile (a segment) is accumulated in TMEM. A
-// tile cut into several segments is finished by the CTA that completes it
-// last (atomic ticket): it adds the segments' fp32 partials in k order
-// (fixed, so results do not depend on timing) and runs the epilogue.
+// Work split: each GEMM's 128-row weight tiles are split along k into S
+// equal pieces, S the most that keeps tiles x S within the grid, one piece
+// per CTA (with more tiles than CTAs, S = 1 and a CTA takes whole tiles
+// c, c + grid, ...). The S CTAs of a tile write their fp32 partials to
+// global memory, wait for one another (all CTAs are resident: a
+// cooperative launch), and each finishes rows m = split, split + S, ... of
+// the tile, adding the S partials in split order (fixed, so results do not
+// depend on timing) -- the distributed reduction that a cluster does in
+// shared memory.
 //
 // Roles (12 warps): warp 0 lane 0 streams weight tiles (TMA, evict-first),
 // warp 2 lane 0 streams activation tiles (after the grid barrier that makes
@@ -60,11 +62,13 @@ constexpr uint64_t kMlWaitNs = 2000000000ull;
 
 struct MlPhase {
   int n_tiles, k_chunks;
-  long total;          // n_tiles * k_chunks
-  int active;          // CTAs with work: min(grid, total), so none is empty
-  int max_seg;         // partial slots per tile
-  float *partial;      // [n_tiles][max_seg][MT][128]
-  int *tickets;        // [n_tiles], zero between launches
+  int splits;          // S: k pieces per tile (every piece non-empty)
+  int per;             // chunks per piece (the last may have fewer)
+  int active;          // n_tiles * S CTAs have a piece (S > 1)
+  float *partial;      // [n_tiles][S][MT][128] (S > 1)
+  // [n_tiles] pieces written, monotonic over launches (each adds S); zero
+  // when the workspace is made
+  unsigned long long *arrive;
 };
 
 struct MlParams {
@@ -76,7 +80,7 @@ struct MlParams {
   uint16_t *x;         // (., hidden) bf16 operand rows
   uint16_t *act;       // (., ffn) bf16 operand rows
   float *rss;          // [o tiles][64] row sums of squares per o tile
-  unsigned *bar;       // {arrivals, generation}
+  unsigned long long *bar;   // grid barrier arrivals, monotonic (3 G a launch)
   int *err;
 };
 
@@ -88,13 +92,15 @@ __device__ __forceinline__ uint64_t ml_now() {
 __device__ __forceinline__ void ml_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
-__device__ __forceinline__ unsigned ml_ld_acquire(const unsigned *p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ unsigned long long ml_ld_acquire64(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void ml_st_release(unsigned *p, unsigned v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ unsigned long long ml_add_release64(unsigned long long *p) {
+  unsigned long long old;
+  asm volatile("atom.release.gpu.global.add.u64 %0, [%1], 1;" : "=l"(old) : "l"(p) : "memory");
+  return old;
 }
 // generic-proxy writes before later TMA (async-proxy) reads of them
 __device__ __forceinline__ void ml_fence_proxy_global() {
@@ -107,23 +113,21 @@ __device__ __forceinline__ bool ml_broken(const int *err) {
   return (*reinterpret_cast<const volatile int *>(err) & DEV_ERR_WAIT_TIMEOUT) != 0;
 }
 
-// One arrival of this CTA at the grid barrier (caller: one thread, after
-// its CTA's writes of the phase).
-__device__ void ml_grid_arrive(unsigned *bar, int G) {
-  __threadfence();
-  const unsigned gen = ml_ld_acquire(bar + 1);
-  if (atomicAdd(bar, 1u) == (unsigned)G - 1) {
-    bar[0] = 0;
-    __threadfence();
-    ml_st_release(bar + 1, gen + 1);
-  }
+// Grid barriers: one monotonic 64-bit arrival counter. A launch starts with
+// it at a multiple of 3 G (every launch adds exactly 3 G arrivals), and its
+// barrier k (1..3) is complete once the counter reaches base + k G. An
+// arrival is one release add by a CTA's leader after its CTA's writes of
+// the phase; a CTA arrives at barrier k + 1 only after it has seen barrier
+// k complete.
+__device__ __forceinline__ void ml_grid_arrive(unsigned long long *bar) {
+  asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(bar) : "memory");
 }
-// Bounded wait until the barrier generation reaches `target`.
-__device__ bool ml_grid_wait(const unsigned *bar, unsigned target, int *err) {
+// Bounded wait until the arrival counter reaches `target`.
+__device__ bool ml_grid_wait(const unsigned long long *bar, unsigned long long target, int *err) {
   if (ml_broken(err)) return false;
   const uint64_t t0 = ml_now();
   for (uint32_t it = 0;; ++it) {
-    if ((int)(ml_ld_acquire(bar + 1) - target) >= 0) return true;
+    if (ml_ld_acquire64(bar) >= target) return true;
     if (((it & 63) == 63 && ml_now() - t0 > kMlWaitNs) || it == (1u << 26)) {
       atomicOr(err, DEV_ERR_WAIT_TIMEOUT);
       return false;
@@ -131,39 +135,38 @@ __device__ bool ml_grid_wait(const unsigned *bar, unsigned target, int *err) {
   }
 }
 
-// chunks [c T / G, (c + 1) T / G) belong to CTA c
-__device__ __forceinline__ long ml_start(long T, int G, int c) { return (long)c * T / G; }
-__device__ int ml_owner(long chunk, long T, int G) {
-  int c = (int)((chunk * G) / T);
-  while (c + 1 < G && ml_start(T, G, c + 1) <= chunk) ++c;
-  while (c > 0 && ml_start(T, G, c) > chunk) --c;
-  return c;
-}
-
-// The segments of this CTA's range in one phase, in order.
+// This CTA's pieces of one phase: with S > 1 at most one (tile c / S,
+// split c % S); with S == 1 the whole tiles c, c + G, c + 2G, ...
 struct MlSegs {
-  long g, e;
-  int kc;
-  __device__ MlSegs(const MlPhase &ph, int c)
-      : g(c < ph.active ? ml_start(ph.total, ph.active, c) : 0),
-        e(c < ph.active ? ml_start(ph.total, ph.active, c + 1) : 0),
-        kc(ph.k_chunks) {}
-  __device__ bool next(int &tile, int &k0, int &n) {
-    if (g >= e) return false;
-    tile = (int)(g / kc);
-    const long tend = (long)(tile + 1) * kc;
-    const long se = e < tend ? e : tend;
-    k0 = (int)(g - (long)tile * kc);
-    n = (int)(se - g);
-    g = se;
+  int tile, split_, S, G, n_tiles, per, kc;
+  bool one;
+  __device__ MlSegs(const MlPhase &ph, int c, int grid)
+      : S(ph.splits), G(grid), n_tiles(ph.n_tiles), per(ph.per), kc(ph.k_chunks) {
+    one = S > 1;
+    tile = one ? (c < ph.active ? c / S : n_tiles) : c;
+    split_ = one && c < ph.active ? c - (c / S) * S : 0;
+  }
+  __device__ bool next(int &t, int &k0, int &n) {
+    if (tile >= n_tiles) return false;
+    t = tile;
+    k0 = split_ * per;
+    n = min(per, kc - k0);
+    tile = one ? n_tiles : tile + G;
     return true;
   }
 };
 
+// 1 / d for d in [1, 2]: the hardware approximation refined by one
+// Newton-Raphson step, r' = r + r (1 - d r); no special cases to branch on
+__device__ __forceinline__ float ml_rcp(float d) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(d));
+  return fmaf(r, fmaf(-d, r, 1.f), r);
+}
 __device__ __forceinline__ float ml_silu(float x) {
   // x * sigmoid(x), sigmoid from exp(-|x|) (triton_llm/kernels/swiglu.py:51-54)
   const float e = expf(-fabsf(x));
-  const float r = __frcp_rn(1.f + e);
+  const float r = ml_rcp(1.f + e);
   return x * (x >= 0.f ? r : e * r);
 }
 
@@ -182,8 +185,8 @@ __global__ void __launch_bounds__(kMlThreads, 1)
   __shared__ uint64_t wfull[kMlWS], wempty[kMlWS], xfull[kMlXS], xempty[kMlXS];
   __shared__ uint64_t accf[2], acce[2];
   __shared__ uint32_t s_tmem;
-  __shared__ unsigned s_gen0;
-  __shared__ int s_fail, s_last;
+  __shared__ unsigned long long s_base;
+  __shared__ int s_fail;
   __shared__ float s_red[4][kMlMaxM];
   __shared__ float s_rms[kMlMaxM];
   uint8_t *wring = smem;
@@ -213,9 +216,10 @@ __global__ void __launch_bounds__(kMlThreads, 1)
       mbar_init(&acce[b], 1);       // the epilogue leader
     }
     s_fail = 0;
-    // no CTA can have passed the first barrier yet: its generation now is
-    // this launch's base
-    s_gen0 = ml_ld_acquire(p.bar + 1);
+    // barrier 1 cannot complete before this CTA arrives, so the counter is
+    // below base + G: rounding down to a multiple of 3 G gives the base
+    const unsigned long long c = ml_ld_acquire64(p.bar);
+    s_base = c - c % (3ull * (unsigned)G);
     fence_mbar_init();
   }
   if (warp == 1) tmem_alloc(&s_tmem, TCOLS);
@@ -223,7 +227,8 @@ __global__ void __launch_bounds__(kMlThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s_tmem;
-  const unsigned gen0 = s_gen0;
+  const unsigned long long base = s_base;
+  const unsigned long long G64 = (unsigned)G;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -236,7 +241,7 @@ __global__ void __launch_bounds__(kMlThreads, 1)
       bool ok = true;
       for (int ph = 0; ph < 3 && ok; ++ph) {
         const CUtensorMap *tw = ph == 0 ? &tw0 : (ph == 1 ? &tw1 : &tw2);
-        MlSegs segs(p.ph[ph], me);
+        MlSegs segs(p.ph[ph], me, G);
         int tile, k0, n;
         while (ok && segs.next(tile, k0, n)) {
           for (int j = 0; j < n; ++j, ++g) {
@@ -266,14 +271,14 @@ __global__ void __launch_bounds__(kMlThreads, 1)
       for (int ph = 0; ph < 3 && ok; ++ph) {
         if (ph > 0) {
           // gate/up reads x (ready at barrier 2), down reads act (barrier 3)
-          if (!ml_grid_wait(p.bar, gen0 + (ph == 1 ? 2u : 3u), p.err)) {
+          if (!ml_grid_wait(p.bar, base + (ph == 1 ? 2 : 3) * G64, p.err)) {
             ok = false;
             break;
           }
           ml_fence_proxy_global();
         }
         const CUtensorMap *tx = ph == 0 ? &tx0 : (ph == 1 ? &tx1 : &tx2);
-        MlSegs segs(p.ph[ph], me);
+        MlSegs segs(p.ph[ph], me, G);
         int tile, k0, n;
         while (ok && segs.next(tile, k0, n)) {
           for (int j = 0; j < n; ++j, ++g) {
@@ -298,7 +303,7 @@ __global__ void __launch_bounds__(kMlThreads, 1)
       int seg = 0;
       bool ok = true;
       for (int ph = 0; ph < 3; ++ph) {
-        MlSegs segs(p.ph[ph], me);
+        MlSegs segs(p.ph[ph], me, G);
         int tile, k0, n;
         while (segs.next(tile, k0, n)) {
           const int buf = seg & 1;
@@ -351,7 +356,7 @@ __global__ void __launch_bounds__(kMlThreads, 1)
     int seg = 0;
     for (int ph = 0; ph < 3; ++ph) {
       const MlPhase &P = p.ph[ph];
-      MlSegs segs(P, me);
+      MlSegs segs(P, me, G);
       int tile, k0, n;
       while (segs.next(tile, k0, n)) {
         const int buf = seg & 1;
@@ -390,86 +395,107 @@ __global__ void __launch_bounds__(kMlThreads, 1)
         g += n;
         ++seg;
 
-        // this segment's place among the tile's pieces
-        const long c_first = (long)tile * P.k_chunks;
-        const int o_first = ml_owner(c_first, P.total, P.active);
-        const int o_last = ml_owner(c_first + P.k_chunks - 1, P.total, P.active);
-        const int nseg = o_last - o_first + 1;
-        const int sidx = me - o_first;
-        bool finish = true;
-        if (nseg > 1) {
-          float *part = P.partial + (((size_t)tile * P.max_seg + sidx) * MT) * kMlBN;
+        const int S = P.splits;
+        const int split = S > 1 ? me - tile * S : 0;   // this CTA's piece
+        // rows this CTA finishes: m_i = split + S i for i < nr (every row
+        // below M when S == 1); from here on v[i] holds row m_i. The row
+        // loops run over every i with clamped load addresses and only the
+        // stores predicated, so the loads of a batch are in flight together
+        // (a branch per row would wait out one L2 round trip per row).
+        const int lim = min(MT, p.M);
+        const int nr = split < lim ? (lim - split + S - 1) / S : 0;
+        constexpr int H = MT / 2;   // rows per batch; S >= 2 leaves at most H
+        if (S > 1) {
+          float *part = P.partial + (((size_t)tile * S + split) * MT) * kMlBN + r;
 #pragma unroll
-          for (int m = 0; m < MT; ++m) part[(size_t)m * kMlBN + r] = v[m];
-          __threadfence();
+          for (int m = 0; m < MT; ++m) part[(size_t)m * kMlBN] = v[m];
           ml_named_sync(1, 128);
-          if (leader) s_last = atomicAdd(&P.tickets[tile], 1) == nseg - 1;
-          ml_named_sync(1, 128);
-          finish = s_last;
-          if (finish) {
-            __threadfence();
-            // k order: segments 0 .. nseg - 1, all read back from the
-            // partial buffer (this one too); each group of loads goes out
-            // together
-            constexpr int HB = MT >= 32 ? 32 : MT;
-            const float *src0 = P.partial + ((size_t)tile * P.max_seg * MT) * kMlBN + r;
-            for (int q = 0; q < nseg; ++q) {
-              const float *src = src0 + (size_t)q * MT * kMlBN;
-#pragma unroll
-              for (int m0 = 0; m0 < MT; m0 += HB) {
-                float t[HB];
-#pragma unroll
-                for (int m = 0; m < HB; ++m) t[m] = __ldcg(src + (size_t)(m0 + m) * kMlBN);
-#pragma unroll
-                for (int m = 0; m < HB; ++m) v[m0 + m] = q == 0 ? t[m] : v[m0 + m] + t[m];
+          if (leader) {
+            // the tile's counter holds a multiple of S before this launch
+            // and S more after it: wait for the next multiple (bounded)
+            const unsigned long long old = ml_add_release64(&P.arrive[tile]);
+            const unsigned long long want = old - old % (unsigned)S + (unsigned)S;
+            const uint64_t t0 = ml_now();
+            for (uint32_t it = 0;; ++it) {
+              if (ml_ld_acquire64(&P.arrive[tile]) >= want) break;
+              if (ml_broken(p.err) ||
+                  ((it & 63) == 63 && ml_now() - t0 > kMlWaitNs) || it == (1u << 26)) {
+                atomicOr(p.err, DEV_ERR_WAIT_TIMEOUT);
+                break;
               }
             }
-            if (leader) P.tickets[tile] = 0;   // every piece has arrived
+          }
+          ml_named_sync(1, 128);
+          // the rows of this slice, summed over the pieces in split order
+          const float *src = P.partial + ((size_t)tile * S * MT) * kMlBN + r;
+#pragma unroll
+          for (int i = 0; i < MT; ++i) v[i] = 0.f;
+#pragma unroll 1
+          for (int q = 0; q < S; ++q) {
+            const float *pq = src + (size_t)q * MT * kMlBN;
+#pragma unroll
+            for (int i = 0; i < H; ++i)
+              v[i] += __ldcg(pq + (size_t)min(split + S * i, MT - 1) * kMlBN);
           }
         }
-        if (!finish) continue;
-        // ---- epilogue of a complete tile
+        // ---- epilogue of this CTA's rows of the tile
         const int n0 = tile * kMlBN;
         if (ph == 1) {
           // SwiGLU: rows R (first 8 of a 16-block) and R + 8 pair up
           const int R = n0 + r;
           const bool head = (lane & 8) == 0;
           const int j = (R >> 4) * 8 + (R & 7);
+          // rows i and i + 1 go together: lane L (gate) finishes row i and
+          // lane L + 8 (up) row i + 1, one exchange and one silu each
 #pragma unroll
-          for (int m = 0; m < MT; ++m) {
-            const float up = __shfl_down_sync(0xffffffffu, v[m], 8);
-            if (head && m < p.M)
-              p.act[(size_t)m * p.ffn + j] = f32_to_bf16_bits(ml_silu(v[m]) * up);
+          for (int hb = 0; hb < 2; ++hb) {
+            if (hb * H >= nr) break;
+#pragma unroll
+            for (int k = 0; k < H; k += 2) {
+              const int i0 = hb * H + k;
+              const float t = __shfl_xor_sync(0xffffffffu, head ? v[i0 + 1] : v[i0], 8);
+              const float gate = head ? v[i0] : t;
+              const float up = head ? t : v[i0 + 1];
+              const int i = head ? i0 : i0 + 1;
+              const float a = ml_silu(gate) * up;
+              if (i < nr) p.act[(size_t)(split + S * i) * p.ffn + j] = f32_to_bf16_bits(a);
+            }
           }
         } else {
-          // residual: h[m][n0 + r] += acc (o, down); all loads first (other
-          // CTAs wrote h: L2, not L1), then the stores
+          // residual: h[m][n0 + r] += acc (o, down); loads first (other CTAs
+          // wrote h: L2, not L1), then the stores
           float *hcol = p.h + n0 + r;
-          constexpr int RB = MT >= 32 ? 32 : MT;
 #pragma unroll
-          for (int m0 = 0; m0 < MT; m0 += RB) {
-            float hv[RB];
+          for (int hb = 0; hb < 2; ++hb) {
+            if (hb * H >= nr) break;
+            float hv[H];
 #pragma unroll
-            for (int m = 0; m < RB; ++m)
-              hv[m] = m0 + m < p.M ? __ldcg(hcol + (size_t)(m0 + m) * p.hidden) : 0.f;
+            for (int k = 0; k < H; ++k)
+              hv[k] = __ldcg(hcol + (size_t)min(split + S * (hb * H + k), lim - 1) * p.hidden);
 #pragma unroll
-            for (int m = 0; m < RB; ++m) {
-              v[m0 + m] = hv[m] + v[m0 + m];
-              if (m0 + m < p.M) hcol[(size_t)(m0 + m) * p.hidden] = v[m0 + m];
+            for (int k = 0; k < H; ++k) {
+              const int i = hb * H + k;
+              v[i] += hv[k];
+              if (i < nr) hcol[(size_t)(split + S * i) * p.hidden] = v[i];
             }
           }
           if (ph == 0) {
             // row sums of squares of the new h over this tile's columns
 #pragma unroll
-            for (int m = 0; m < MT; ++m) {
-              float sq = m < p.M ? v[m] * v[m] : 0.f;
+            for (int hb = 0; hb < 2; ++hb) {
+              if (hb * H >= nr) break;
 #pragma unroll
-              for (int off = 16; off > 0; off >>= 1)
-                sq += __shfl_xor_sync(0xffffffffu, sq, off);
-              if (lane == 0) s_red[ew][m] = sq;
+              for (int k = 0; k < H; ++k) {
+                const int i = hb * H + k;
+                float sq = v[i] * v[i];
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1)
+                  sq += __shfl_xor_sync(0xffffffffu, sq, off);
+                if (lane == 0 && i < nr) s_red[ew][split + S * i] = sq;
+              }
             }
             ml_named_sync(1, 128);
-            if (et < p.M)
+            if (et < lim && et >= split && (et - split) % S == 0)
               p.rss[(size_t)tile * kMlMaxM + et] =
                   ((s_red[0][et] + s_red[1][et]) + s_red[2][et]) + s_red[3][et];
             ml_named_sync(1, 128);
@@ -480,10 +506,15 @@ __global__ void __launch_bounds__(kMlThreads, 1)
       if (ph == 2) break;
       if (ph == 1) ml_fence_proxy_global();   // act is read by TMA after barrier 3
       ml_named_sync(1, 128);
-      if (leader) ml_grid_arrive(p.bar, G);   // barrier 1 (after o) / 3 (after gate/up)
+      if (leader) {
+        // a CTA without a gate/up piece gets here before barrier 2 is
+        // complete; its arrival must not count toward barrier 2
+        if (ph == 1) ml_grid_wait(p.bar, base + 2 * G64, p.err);
+        ml_grid_arrive(p.bar);   // barrier 1 (after o) / 3 (after gate/up)
+      }
       if (ph == 0) {
         // ---- RMSNorm of the complete h rows: x = (h / rms) * w (bf16)
-        if (leader) ml_grid_wait(p.bar, gen0 + 1, p.err);
+        if (leader) ml_grid_wait(p.bar, base + G64, p.err);
         ml_named_sync(1, 128);
         if (et < p.M) {
           float ss = 0.f;
@@ -507,7 +538,7 @@ __global__ void __launch_bounds__(kMlThreads, 1)
         }
         ml_fence_proxy_global();   // x is read by TMA after barrier 2
         ml_named_sync(1, 128);
-        if (leader) ml_grid_arrive(p.bar, G);   // barrier 2
+        if (leader) ml_grid_arrive(p.bar);   // barrier 2
       }
     }
   }
@@ -519,29 +550,12 @@ __global__ void __launch_bounds__(kMlThreads, 1)
   if (warp == 1) tmem_free(tmem, TCOLS);
 }
 
-// segment slots per tile: the most CTAs a tile's chunks spread over
-int ml_max_seg(long total, int k_chunks, int n_tiles, int G) {
-  int mx = 1;
-  auto owner = [&](long chunk) {
-    int c = (int)((chunk * G) / total);
-    while (c + 1 < G && (long)(c + 1) * total / G <= chunk) ++c;
-    while (c > 0 && (long)c * total / G > chunk) --c;
-    return c;
-  };
-  for (int t = 0; t < n_tiles; ++t) {
-    const long c0 = (long)t * k_chunks;
-    const int s = owner(c0 + k_chunks - 1) - owner(c0) + 1;
-    if (s > mx) mx = s;
-  }
-  return mx;
-}
-
 int ml_mt_for(int M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
 
 struct MlLayout {
   int G, MT;
-  int tiles[3], kc[3], max_seg[3], active[3];
-  size_t off_bar, off_rss, off_tickets[3], off_part[3], bytes;
+  int tiles[3], kc[3], splits[3], per[3];
+  size_t off_bar, off_rss, off_count[3], off_part[3], bytes;
 };
 
 int ml_grid() {
@@ -571,13 +585,24 @@ MlLayout ml_layout(int M, int attn_dim, int hidden, int ffn) {
   for (int i = 0; i < 3; ++i) {
     L.tiles[i] = N[i] / kMlBN;
     L.kc[i] = K[i] / kMlBK;
-    const long T = (long)L.tiles[i] * L.kc[i];
-    L.active[i] = (int)(T < L.G ? T : L.G);
-    L.max_seg[i] = ml_max_seg(T, L.kc[i], L.tiles[i], L.active[i]);
-    L.off_tickets[i] = take((size_t)L.tiles[i] * sizeof(int));
+    // the most k pieces per tile that keep tiles x pieces within the grid,
+    // none of them empty
+    int S = L.G / L.tiles[i];
+    if (S < 1) S = 1;
+    if (S > L.kc[i]) S = L.kc[i];
+    int per = (L.kc[i] + S - 1) / S;
+    while (S > 1 && (S - 1) * per >= L.kc[i]) {
+      --S;
+      per = (L.kc[i] + S - 1) / S;
+    }
+    L.splits[i] = S;
+    L.per[i] = per;
+    L.off_count[i] = take((size_t)L.tiles[i] * sizeof(unsigned long long));
   }
   for (int i = 0; i < 3; ++i)
-    L.off_part[i] = take((size_t)L.tiles[i] * L.max_seg[i] * L.MT * kMlBN * sizeof(float));
+    L.off_part[i] = L.splits[i] > 1
+                        ? take((size_t)L.tiles[i] * L.splits[i] * L.MT * kMlBN * sizeof(float))
+                        : 0;
   L.bytes = off;
   return L;
 }
@@ -664,11 +689,11 @@ int tllm_mlp(const void *attn, int attn_plane_rows, const void *w_o, float *h,
   for (int i = 0; i < 3; ++i) {
     p.ph[i].n_tiles = L.tiles[i];
     p.ph[i].k_chunks = L.kc[i];
-    p.ph[i].total = (long)L.tiles[i] * L.kc[i];
-    p.ph[i].max_seg = L.max_seg[i];
-    p.ph[i].active = L.active[i];
-    p.ph[i].partial = reinterpret_cast<float *>(ws + L.off_part[i]);
-    p.ph[i].tickets = reinterpret_cast<int *>(ws + L.off_tickets[i]);
+    p.ph[i].splits = L.splits[i];
+    p.ph[i].per = L.per[i];
+    p.ph[i].active = L.tiles[i] * L.splits[i];
+    p.ph[i].partial = L.splits[i] > 1 ? reinterpret_cast<float *>(ws + L.off_part[i]) : nullptr;
+    p.ph[i].arrive = reinterpret_cast<unsigned long long *>(ws + L.off_count[i]);
   }
   p.M = M;
   p.hidden = hidden;
@@ -679,7 +704,7 @@ int tllm_mlp(const void *attn, int attn_plane_rows, const void *w_o, float *h,
   p.x = static_cast<uint16_t *>(x);
   p.act = static_cast<uint16_t *>(act);
   p.rss = reinterpret_cast<float *>(ws + L.off_rss);
-  p.bar = reinterpret_cast<unsigned *>(ws + L.off_bar);
+  p.bar = reinterpret_cast<unsigned long long *>(ws + L.off_bar);
   p.err = err;
   // weights: tiled bf16, (tiles * k_chunks * 128, 64) rows of 128 bytes
   CUtensorMap tw[3], tx[3];
