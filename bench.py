@@ -522,7 +522,8 @@ class GPT2Workload:
                 "heads": 12, "ffn": 3072, "vocab": 50257, "batch": 1,
                 "prompt": "32 uniform ids (seed 0), prefilled before timing",
                 "weights": "N(0,0.02) fp32, seed 0, HF state-dict order",
-                "timed": "K decode steps: cached forward of one token (87 kernels), "
+                "timed": "K decode steps: cached forward of one token (ids, position and "
+                         "length to the device, one CUDA-graph replay of its 87 kernels), "
                          "logits to the host, argmax on the host",
                 "l2": "inputs larger than L2: 495 MB of fp32 weights per step"}
 
@@ -548,7 +549,7 @@ class GPT2Workload:
         self.tok = self.first
 
     def capture(self):
-        pass   # the reference's step returns logits to the host: no graph
+        pass   # the model captures its own decode-step graph on first use
 
     def step(self):
         logits = self.m._forward_cached(np.array([[self.tok]], np.int32))

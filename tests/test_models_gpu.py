@@ -269,6 +269,23 @@ def test_gpt2_tiny_generate_and_full_forward(gpu, golden):
     np.testing.assert_array_equal(np.argmax(full[0, 4:], axis=-1), g["tokens"][5:])
 
 
+def test_gpt2_decode_graph_matches_launches(gpu, golden):
+    """The one-token cached forward replays a captured CUDA graph; it gives
+    the tokens and (within fp32 summation-order noise) the logits of the
+    launch-by-launch path, and a new cache makes it capture again."""
+    g = golden("gpt2_tiny")
+    w = inputs.gpt2_weights_legacy(inputs.GPT2_TINY, 42)
+    m_graph, m_eager = _gpt2(inputs.GPT2_TINY, w), _gpt2(inputs.GPT2_TINY, w)
+    m_eager.use_graph = False
+    for rep in range(2):   # the second _init_cache forces a new capture
+        tg, lg = _gpt2_run(m_graph, [5, 12, 7, 0, 3], 10)
+        te, le = _gpt2_run(m_eager, [5, 12, 7, 0, 3], 10)
+        np.testing.assert_array_equal(tg, g["tokens"])
+        np.testing.assert_array_equal(tg, te)
+        np.testing.assert_allclose(lg, le, atol=1e-5 * np.abs(le).max(), rtol=1e-5)
+        assert m_graph._graph is not None and m_eager._graph is None
+
+
 def test_gpt2_small_slice_matches_reference(gpu, golden):
     """BASELINE config 1 geometry (GPT-2 small, fp32)."""
     g = golden("gpt2_small_slice")

@@ -24,7 +24,8 @@
 //    memory (ranks summed in fixed order, so results do not depend on
 //    scheduling) and runs the epilogue for that slice.
 //  * linear_f32_kernel (fp32 weights, GPT-2 and the fp32 drop-in): one warp
-//    per weight-row pair, 16-byte loads along K, fp32 FMA, same epilogues.
+//    per (weight-row pair, K slice), 16-byte streaming loads along K with
+//    two batches in flight per lane, fp32 FMA, same epilogues.
 //
 // Epilogue row pairing: rows r and r + 8 of a 16-row block are handled by
 // one thread. SwiGLU weights are stored with gate and up rows interleaved in
@@ -748,45 +749,91 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 }
 
 // ------------------------------------------------------------------------
-// fp32 weights, CUDA cores: one warp per weight-row pair (r, r + 8)
+// fp32 weights, CUDA cores: a warp per (weight-row pair (r, r + 8), K slice)
 // ------------------------------------------------------------------------
 constexpr int kF32Warps = 8;
+constexpr int kF32U = 4;   // float4 loads of each row in flight per lane and batch
 
-template <int MB>
+__device__ __forceinline__ float4 f32_ld4(const float *p) {
+  const uint4 u = ld_stream(p);
+  return make_float4(__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z),
+                     __uint_as_float(u.w));
+}
+
+// A CTA takes kF32Warps / KS row pairs; the KS warps of a pair stream KS
+// consecutive K slices (multiples of 128 floats), each lane keeping two
+// batches of kF32U float4 loads per row in flight (the batch being summed
+// and the next one). The first batch is issued before the wait for the
+// previous kernel (weights do not depend on it). The KS partial sums of a
+// pair are added in slice order through shared memory.
+template <int MB, int KS>
 __global__ void __launch_bounds__(kF32Warps * 32)
     linear_f32_kernel(const float *x, const float *w, Epilogue e, int M,
                       int N, int K, int m0) {
+  constexpr int PPC = kF32Warps / KS;
+  __shared__ float s_part[kF32Warps][2][MB];
   griddep_launch();
-  const int warp = (blockIdx.x * kF32Warps) + (threadIdx.x >> 5);
+  const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const int slice = warp % KS;
+  const int pair = blockIdx.x * PPC + warp / KS;
   // pair index -> rows r (first 8 of a 16-block) and r + 8
-  const int r = (warp >> 3) * 16 + (warp & 7);
-  if (r >= ((N + 15) / 16) * 16) return;
+  const int r = (pair >> 3) * 16 + (pair & 7);
+  const bool live = r < ((N + 15) / 16) * 16;
   const int r1 = r + 8;
+  const bool ok0 = live && r < N, ok1 = live && r1 < N;
+  const int steps = (K + 127) / 128;            // warp-wide float4 rows
+  const int per = (steps + KS - 1) / KS;
+  const int kb = slice * per * 128;
+  const int ke = min(K, kb + per * 128);
+  const float *w0 = w + (size_t)(ok0 ? r : 0) * K;
+  const float *w1 = w + (size_t)(ok1 ? r1 : 0) * K;
   float acc0[MB], acc1[MB];
 #pragma unroll
   for (int i = 0; i < MB; ++i) acc0[i] = acc1[i] = 0.f;
-  const float *w0 = w + (size_t)r * K;
-  const float *w1 = w + (size_t)r1 * K;
-  const bool ok0 = r < N, ok1 = r1 < N;
-  for (int k = lane * 4; k < K; k += 128) {
-    float4 a = ok0 ? __ldg(reinterpret_cast<const float4 *>(w0 + k))
-                   : make_float4(0, 0, 0, 0);
-    float4 b = ok1 ? __ldg(reinterpret_cast<const float4 *>(w1 + k))
-                   : make_float4(0, 0, 0, 0);
+  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 a[kF32U], b[kF32U];
+  int k0 = kb + lane * 4;
 #pragma unroll
-    for (int i = 0; i < MB; ++i) {
-      if (m0 + i < M) {
-        const float4 xv =
-            __ldg(reinterpret_cast<const float4 *>(x + (size_t)(m0 + i) * K + k));
-        acc0[i] = fmaf(a.x, xv.x, acc0[i]);
-        acc0[i] = fmaf(a.y, xv.y, acc0[i]);
-        acc0[i] = fmaf(a.z, xv.z, acc0[i]);
-        acc0[i] = fmaf(a.w, xv.w, acc0[i]);
-        acc1[i] = fmaf(b.x, xv.x, acc1[i]);
-        acc1[i] = fmaf(b.y, xv.y, acc1[i]);
-        acc1[i] = fmaf(b.z, xv.z, acc1[i]);
-        acc1[i] = fmaf(b.w, xv.w, acc1[i]);
+  for (int u = 0; u < kF32U; ++u) {
+    const int k = k0 + u * 128;
+    a[u] = ok0 && k < ke ? f32_ld4(w0 + k) : z;
+    b[u] = ok1 && k < ke ? f32_ld4(w1 + k) : z;
+  }
+  griddep_wait();   // x and the epilogue's inputs come from earlier kernels
+  for (; k0 < ke; k0 += 128 * kF32U) {
+    float4 ca[kF32U], cb[kF32U];
+#pragma unroll
+    for (int u = 0; u < kF32U; ++u) {
+      ca[u] = a[u];
+      cb[u] = b[u];
+    }
+    const int kn = k0 + 128 * kF32U;
+#pragma unroll
+    for (int u = 0; u < kF32U; ++u) {
+      const int k = kn + u * 128;
+      a[u] = ok0 && k < ke ? f32_ld4(w0 + k) : z;
+      b[u] = ok1 && k < ke ? f32_ld4(w1 + k) : z;
+    }
+#pragma unroll
+    for (int u = 0; u < kF32U; ++u) {
+      const int k = k0 + u * 128;
+      if (k < ke) {
+#pragma unroll
+        for (int i = 0; i < MB; ++i) {
+          if (m0 + i < M) {
+            const float4 xv =
+                __ldg(reinterpret_cast<const float4 *>(x + (size_t)(m0 + i) * K + k));
+            acc0[i] = fmaf(ca[u].x, xv.x, acc0[i]);
+            acc0[i] = fmaf(ca[u].y, xv.y, acc0[i]);
+            acc0[i] = fmaf(ca[u].z, xv.z, acc0[i]);
+            acc0[i] = fmaf(ca[u].w, xv.w, acc0[i]);
+            acc1[i] = fmaf(cb[u].x, xv.x, acc1[i]);
+            acc1[i] = fmaf(cb[u].y, xv.y, acc1[i]);
+            acc1[i] = fmaf(cb[u].z, xv.z, acc1[i]);
+            acc1[i] = fmaf(cb[u].w, xv.w, acc1[i]);
+          }
+        }
       }
     }
   }
@@ -798,15 +845,49 @@ __global__ void __launch_bounds__(kF32Warps * 32)
       acc1[i] += __shfl_xor_sync(0xffffffffu, acc1[i], off);
     }
   }
-  if (lane < MB) {
-    float v0 = 0.f, v1 = 0.f;
+  if constexpr (KS > 1) {
+    if (lane == 0) {
 #pragma unroll
-    for (int i = 0; i < MB; ++i)
-      if (i == lane) {
-        v0 = acc0[i];
-        v1 = acc1[i];
+      for (int i = 0; i < MB; ++i) {
+        s_part[warp][0][i] = acc0[i];
+        s_part[warp][1][i] = acc1[i];
       }
-    epi_pair_rt(e, N, M, r, m0 + lane, v0, v1);
+    }
+    __syncthreads();
+    if (slice != 0 || !live) return;
+    if (lane < MB) {
+      float v0 = 0.f, v1 = 0.f;
+#pragma unroll
+      for (int s = 0; s < KS; ++s) {
+        v0 += s_part[warp + s][0][lane];
+        v1 += s_part[warp + s][1][lane];
+      }
+      epi_pair_rt(e, N, M, r, m0 + lane, v0, v1);
+    }
+  } else {
+    if (!live) return;
+    if (lane < MB) {
+      float v0 = 0.f, v1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < MB; ++i)
+        if (i == lane) {
+          v0 = acc0[i];
+          v1 = acc1[i];
+        }
+      epi_pair_rt(e, N, M, r, m0 + lane, v0, v1);
+    }
+  }
+}
+
+template <int MB>
+cudaError_t f32_launch(int KS, int blocks, cudaStream_t st, const float *x, const float *w,
+               const Epilogue &e, int M, int N, int K, int m0) {
+  const dim3 grid(blocks), block(kF32Warps * 32);
+  switch (KS) {
+    case 1: return launch_pdl(linear_f32_kernel<MB, 1>, grid, block, 0, st, x, w, e, M, N, K, m0);
+    case 2: return launch_pdl(linear_f32_kernel<MB, 2>, grid, block, 0, st, x, w, e, M, N, K, m0);
+    case 4: return launch_pdl(linear_f32_kernel<MB, 4>, grid, block, 0, st, x, w, e, M, N, K, m0);
+    default: return launch_pdl(linear_f32_kernel<MB, 8>, grid, block, 0, st, x, w, e, M, N, K, m0);
   }
 }
 
@@ -1192,12 +1273,18 @@ int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
     TLLM_CHECK_ARG(x_dtype == TLLM_F32, "fp32 weights take fp32 activations");
     TLLM_CHECK_ARG(K % 4 == 0, "K must be a multiple of 4");
     const int pairs = ((N + 15) / 16) * 8;
-    const int blocks = (pairs + kF32Warps - 1) / kF32Warps;
+    // K slices per pair: enough warps for two CTAs of 8 on every SM, each
+    // slice at least one warp-wide row of 128 floats
+    int KS = 1;
+    while (KS < kF32Warps && (long)pairs * KS < 2L * kF32Warps * sm_count() &&
+           2 * KS * 128 <= K)
+      KS *= 2;
+    const int blocks = (pairs * KS + kF32Warps - 1) / kF32Warps;
+    const float *xf = static_cast<const float *>(x);
+    const float *wf = static_cast<const float *>(w);
     for (int m0 = 0; m0 < M; m0 += 8) {
-      linear_f32_kernel<8><<<blocks, kF32Warps * 32, 0, st>>>(
-          static_cast<const float *>(x), static_cast<const float *>(w), e, M,
-          N, K, m0);
-      TLLM_LAUNCH_CHECK();
+      TLLM_CUDA(M - m0 == 1 ? f32_launch<1>(KS, blocks, st, xf, wf, e, M, N, K, m0)
+                            : f32_launch<8>(KS, blocks, st, xf, wf, e, M, N, K, m0));
     }
     return TLLM_OK;
   }

@@ -11,6 +11,13 @@ tanh-GELU in the epilogue), mlp c_proj (+ bias + residual). Weights stay fp32
 weights, stored (in, out), are transposed once to the kernels' (out, in)
 layout. The cache replaces the reference's per-head np.concatenate lists
 (model.py:267-273, :340-341) with a (n_head, max_seq, d) buffer per layer.
+
+A one-token cached forward (the decode step) replays a CUDA graph of the
+whole step -- embedding to lm_head -- captured on first use: the token,
+its position and the cache length reach the kernels through device
+buffers, the attention's grid is sized for the full cache, so one graph
+serves every position. It is captured again whenever a buffer it uses is
+reallocated. ``use_graph = False`` runs the same launches one by one.
 """
 
 from __future__ import annotations
@@ -82,6 +89,10 @@ class GPT2Model:
         self.lm_head = Linear(self.wte, dt)              # tied (model.py:60-65)
         self.wte_dev = self.lm_head                      # embedding reads the same copy
         self.wpe_dev = f32(self.wpe)
+        self.use_graph = True
+        self._graph = None
+        self._graph_key = None
+        self._alloc_gen = 0   # bumped when a buffer a graph may hold is replaced
         self.kv_cache = None
         self._cache_len = 0
         self._max_seq = 0
@@ -98,15 +109,18 @@ class GPT2Model:
         self.h, self.x = f(M, n), a(M, n)
         self.q, self.attn = f(M, self.H, self.D), a(M, n)
         self.act, self.logits = a(M, 4 * n), f(M, c.vocab_size)
-        self.ids_d = gpu.allocate((M,), np.int32)
-        self.pos_d = gpu.allocate((M,), np.int32)
-        self.len_d = gpu.allocate((M,), np.int32)
+        # token ids, positions and cache lengths: one buffer, one copy a step
+        self.meta_d = gpu.allocate((3 * M,), np.int32)
+        self.ids_d = gpu.sub_view(self.meta_d, 0, (M,))
+        self.pos_d = gpu.sub_view(self.meta_d, 4 * M, (M,))
+        self.len_d = gpu.sub_view(self.meta_d, 8 * M, (M,))
         self.seq_d = gpu.zeros((M,), np.int32)
         shapes = [(M, 3 * n, n), (M, n, n), (M, 4 * n, n), (M, n, 4 * n),
                   (M, c.vocab_size, n)]
         self.lin_ws = LinearWorkspace(shapes)
         self.attn_ws = None
         self._rows = M
+        self._alloc_gen += 1
 
     def _init_cache(self, max_seq: int | None = None):
         """Empty preallocated cache (the reference starts empty lists)."""
@@ -120,23 +134,43 @@ class GPT2Model:
             for _ in range(c.n_layer)]
         self._max_seq = S
         self._cache_len = 0
+        self._alloc_gen += 1
 
     def _run(self, ids: np.ndarray, prev: int):
         """ids (M,) at positions prev..prev+M-1 of sequence 0 -> logits (M, V)."""
-        c, n, H, D = self.config, self.n, self.H, self.D
+        c = self.config
         M = len(ids)
         self._ensure_rows(M)
-        pos = np.arange(prev, prev + M, dtype=np.int32)
-        self.ids_d.from_numpy(np.pad(ids.astype(np.int32), (0, self._rows - M)))
-        self.pos_d.from_numpy(np.pad(pos, (0, self._rows - M)))
-        self.len_d.from_numpy(np.pad(pos + 1, (0, self._rows - M)))
-        h, x = self.h, self.x
-        embedding_dev(gpu.sub_view(self.ids_d, 0, (M,)), self.wte_dev, h, self.wpe_dev,
-                      gpu.sub_view(self.pos_d, 0, (M,)))
         if (self.attn_ws is None or self.attn_ws.shape[0] < M
                 or self.attn_ws.shape[4] != self._max_seq):
             kvd = _lib.BF16 if self.bf16 else _lib.F32
-            self.attn_ws = DecodeWorkspace(max(M, 1), H, H, D, self._max_seq, kvd)
+            self.attn_ws = DecodeWorkspace(max(M, 1), self.H, self.H, self.D,
+                                           self._max_seq, kvd)
+            self._alloc_gen += 1
+        pos = np.arange(prev, prev + M, dtype=np.int32)
+        pad = lambda a: np.pad(a, (0, self._rows - M))  # noqa: E731
+        self.meta_d.from_numpy(np.concatenate([pad(ids.astype(np.int32)), pad(pos),
+                                               pad(pos + 1)]))
+        if M == 1 and self.use_graph:
+            key = (self._rows, self._max_seq, self._alloc_gen)
+            if self._graph_key != key:
+                self._graph = None
+                g = gpu.Graph()
+                with g:
+                    self._device_step(1, self._max_seq)
+                self._graph, self._graph_key = g, key
+            self._graph.launch()
+        else:
+            self._device_step(M, prev + M)
+        return gpu.sub_view(self.logits, 0, (M, c.vocab_size)).to_numpy()
+
+    def _device_step(self, M: int, max_len: int):
+        """The launches of one forward over M rows (device buffers only);
+        ``max_len`` bounds the cache lengths the attention grid covers."""
+        c, n, H, D = self.config, self.n, self.H, self.D
+        h, x = self.h, self.x
+        embedding_dev(gpu.sub_view(self.ids_d, 0, (M,)), self.wte_dev, h, self.wpe_dev,
+                      gpu.sub_view(self.pos_d, 0, (M,)))
         for i, L in enumerate(self.layers):
             kv = self.kv_cache[i]
             layer_norm_dev(h, L["ln1"][0], L["ln1"][1], x, c.layer_norm_epsilon, M=M)
@@ -144,7 +178,7 @@ class GPT2Model:
                 row_seq=self.seq_d, row_pos=self.pos_d, q_out=self.q,
                 k_cache=kv["k"], v_cache=kv["v"], n_head=H, n_kv_head=H, head_dim=D))
             gqa_rows(self.q, kv["k"], kv["v"], self.seq_d, self.len_d, self.attn, M, H,
-                     H * D, D, H * D, D, prev + M, workspace=self.attn_ws)
+                     H * D, D, H * D, D, max_len, workspace=self.attn_ws)
             linear(self.attn, L["proj"], out_dev=h, op=_lib.EPI_RESID, resid_dev=h,
                    ws=self.lin_ws, M=M)
             layer_norm_dev(h, L["ln2"][0], L["ln2"][1], x, c.layer_norm_epsilon, M=M)
@@ -153,7 +187,6 @@ class GPT2Model:
                    ws=self.lin_ws, M=M)
         layer_norm_dev(h, self.ln_f[0], self.ln_f[1], x, c.layer_norm_epsilon, M=M)
         linear(x, self.lm_head, out_dev=self.logits, ws=self.lin_ws, M=M)
-        return gpu.sub_view(self.logits, 0, (M, c.vocab_size)).to_numpy()
 
     # ------------------------------------------------------------------
     def forward(self, token_ids: np.ndarray, use_cache: bool = False) -> np.ndarray:
@@ -168,6 +201,7 @@ class GPT2Model:
         self._init_cache(max(token_ids.shape[1], 1))
         logits = self._run(token_ids[0], 0)
         self.kv_cache, self._cache_len, self._max_seq = saved
+        self._alloc_gen += 1
         return logits.reshape(1, -1, self.config.vocab_size)
 
     def _forward_cached(self, token_ids: np.ndarray) -> np.ndarray:
