@@ -181,6 +181,39 @@ def test_linear_store_bias(gpu, M, bf16):
     _close(out.to_numpy(), ref + b, bound, msg=f"M={M}")
 
 
+@pytest.mark.parametrize("planes", [1, 2])
+@pytest.mark.parametrize("M", [1, 7, 16, 32])
+@pytest.mark.parametrize("op", ["store", "resid", "gelu", "swiglu"])
+def test_linear_skinny_matches_tensor_core_kernel(gpu, monkeypatch, op, M, planes):
+    """Batches up to 32 rows take the mma.sync skinny kernel; it gives what
+    the tcgen05 kernel gives on the same operands (both sum in fp32, in a
+    different order)."""
+    from triton_llm import _lib
+    from triton_llm.kernels.linear import Linear, LinearWorkspace, linear, swiglu_rows
+    rng = np.random.default_rng(60 + M)
+    N, K = (1536, 576) if op == "swiglu" else (576, 1536)
+    w = rng.standard_normal((N, K), dtype=F32) * 0.05
+    if op == "swiglu":
+        w = swiglu_rows(w[:N // 2], w[N // 2:])
+    lin = Linear(w.astype(F32), "bfloat16", np.linspace(-1, 1, N).astype(F32)
+                 if op in ("store", "gelu") else None)
+    x = gpu.to_device_split(rng.standard_normal((M, K), dtype=F32), planes=planes)
+    h0 = rng.standard_normal((M, N), dtype=F32)
+    code = {"store": _lib.EPI_STORE, "resid": _lib.EPI_RESID, "gelu": _lib.EPI_GELU,
+            "swiglu": _lib.EPI_SWIGLU}[op]
+    ws = LinearWorkspace([(M, N, K)])
+    outs = []
+    for max_m in ("32", "0"):   # skinny kernel, then the tcgen05 kernel
+        monkeypatch.setenv("TLLM_SKINNY_MAX_M", max_m)
+        out = gpu.to_device(h0) if op == "resid" else gpu.allocate(
+            (M, N // 2 if op == "swiglu" else N), np.float32)
+        linear(x, lin, out_dev=out, op=code, resid_dev=out if op == "resid" else None,
+               ws=ws, M=M)
+        outs.append(out.to_numpy())
+    scale = np.abs(outs[1]).max()
+    np.testing.assert_allclose(outs[0], outs[1], rtol=1e-4, atol=1e-5 * scale)
+
+
 @pytest.mark.parametrize("bf16", [True, False])
 def test_linear_split_k_deterministic(gpu, bf16):
     """Few weight tiles and long K: the kernel splits K across CTAs and the

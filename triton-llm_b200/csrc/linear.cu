@@ -892,6 +892,166 @@ cudaError_t f32_launch(int KS, int blocks, cudaStream_t st, const float *x, cons
 }
 
 // ------------------------------------------------------------------------
+// bf16 weights, small batches: mma.sync skinny GEMM
+// ------------------------------------------------------------------------
+// At decode batch sizes a projection is a weight stream with a few
+// activation rows: this kernel has none of the tcgen05 kernel's set-up
+// (tensor maps, TMEM, rings, clusters). A warp owns one 16-row weight block
+// over one K slice; per 32-k step each lane loads 16 bytes of rows r and
+// r + 8 (r = lane / 4) straight from HBM into registers and 16 bytes of each
+// of its activation rows (L1 hits), and issues two m16n8k16 MMAs per 8
+// activation rows. The k order inside a step is permuted the same way for
+// both operands (lane q = lane % 4 supplies logical k {2q, 2q+1, 2q+8,
+// 2q+9} of MMA j from physical k 8q + 4j .. 8q + 4j + 3), so every operand
+// fragment is one contiguous 16-byte load and the dot products are
+// unchanged. The accumulator gives each lane rows r and r + 8 at
+// activation rows 2q and 2q + 1 of each 8-row block -- the row pairing of
+// the shared epilogue. The KS slices of a block are added in slice order
+// through shared memory.
+constexpr int kSkWarps = 8;
+constexpr int kSkU = 4;   // 32-k steps per load batch (two batches in flight)
+
+__device__ __forceinline__ void sk_mma(float (&c)[4], uint32_t a0, uint32_t a1,
+                                       uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, "
+      "{%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// 16 bytes of weight row n at k (k % 8 == 0, inside one 64-wide chunk)
+__device__ __forceinline__ const uint16_t *sk_w(const uint16_t *w, bool tiled, int kc,
+                                                int K, int n, int k) {
+  return tiled ? w + ((((size_t)(n >> 7) * kc + (k >> 6)) << 7) + (n & 127)) * kTcBK +
+                     (k & 63)
+               : w + (size_t)n * K + k;
+}
+
+template <int MT, int PL, int KS>
+__global__ void __launch_bounds__(kSkWarps * 32)
+    linear_mma_kernel(const uint16_t *x, int x_plane_rows, const uint16_t *w, int tiled,
+                      Epilogue e, int M, int N, int K) {
+  constexpr int NB = MT / 8;                // 8-row activation blocks
+  constexpr int RB = kSkWarps / KS;         // weight blocks per CTA
+  __shared__ float s_part[KS > 1 ? kSkWarps : 1][NB * 4][32];
+  griddep_launch();
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int slice = warp % KS;
+  const int row0 = (blockIdx.x * RB + warp / KS) * 16;
+  const bool live = row0 < N;
+  const int g = lane >> 2, q = lane & 3;
+  const int ra = row0 + g;
+  // tiled weights are padded with zero rows to a multiple of 128; rows of
+  // plain weights past N are clamped (their sums are never stored)
+  const int na = tiled ? ra : min(ra, N - 1);
+  const int nb8 = tiled ? ra + 8 : min(ra + 8, N - 1);
+  const int kc = K >> 6;
+  const int steps = K >> 5;
+  const int per = (steps + KS - 1) / KS;
+  const int s0 = live ? slice * per : 0;
+  const int s1 = live ? min(steps, s0 + per) : 0;
+  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+  uint4 wa[kSkU], wb[kSkU];
+#pragma unroll
+  for (int u = 0; u < kSkU; ++u) {
+    const int k = (s0 + u) * 32 + q * 8;
+    const bool in = s0 + u < s1;
+    wa[u] = in ? ld_stream(sk_w(w, tiled, kc, K, na, k)) : z;
+    wb[u] = in ? ld_stream(sk_w(w, tiled, kc, K, nb8, k)) : z;
+  }
+  griddep_wait();   // the activations and the epilogue's inputs
+  float acc[NB][4];
+#pragma unroll
+  for (int b = 0; b < NB; ++b)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[b][i] = 0.f;
+  const uint16_t *xr[NB];
+#pragma unroll
+  for (int b = 0; b < NB; ++b) xr[b] = x + (size_t)min(b * 8 + g, M - 1) * K + q * 8;
+  const size_t xplane = (size_t)x_plane_rows * K;
+  for (int s = s0; s < s1; s += kSkU) {
+    uint4 ca[kSkU], cb[kSkU];
+#pragma unroll
+    for (int u = 0; u < kSkU; ++u) {
+      ca[u] = wa[u];
+      cb[u] = wb[u];
+    }
+#pragma unroll
+    for (int u = 0; u < kSkU; ++u) {
+      const int sn = s + kSkU + u;
+      const int k = sn * 32 + q * 8;
+      const bool in = sn < s1;
+      wa[u] = in ? ld_stream(sk_w(w, tiled, kc, K, na, k)) : z;
+      wb[u] = in ? ld_stream(sk_w(w, tiled, kc, K, nb8, k)) : z;
+    }
+#pragma unroll
+    for (int u = 0; u < kSkU; ++u) {
+      if (s + u < s1) {
+        const int k = (s + u) * 32;
+#pragma unroll
+        for (int pl = 0; pl < PL; ++pl) {
+#pragma unroll
+          for (int b = 0; b < NB; ++b) {
+            const uint4 xv = __ldg(reinterpret_cast<const uint4 *>(xr[b] + pl * xplane + k));
+            sk_mma(acc[b], ca[u].x, cb[u].x, ca[u].y, cb[u].y, xv.x, xv.y);
+            sk_mma(acc[b], ca[u].z, cb[u].z, ca[u].w, cb[u].w, xv.z, xv.w);
+          }
+        }
+      }
+    }
+  }
+  if constexpr (KS > 1) {
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) s_part[warp][b * 4 + i][lane] = acc[b][i];
+    __syncthreads();
+    if (slice != 0 || !live) return;
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float t = 0.f;
+#pragma unroll
+        for (int sl = 0; sl < KS; ++sl) t += s_part[warp + sl][b * 4 + i][lane];
+        acc[b][i] = t;
+      }
+  } else {
+    if (!live) return;
+  }
+  // c0 (r, 2q), c1 (r, 2q + 1), c2 (r + 8, 2q), c3 (r + 8, 2q + 1)
+#pragma unroll
+  for (int b = 0; b < NB; ++b) {
+    const int m = b * 8 + 2 * q;
+    epi_pair_rt(e, N, M, ra, m, acc[b][0], acc[b][2]);
+    epi_pair_rt(e, N, M, ra, m + 1, acc[b][1], acc[b][3]);
+  }
+}
+
+template <int MT, int PL>
+cudaError_t sk_launch(int KS, dim3 grid, cudaStream_t st, const uint16_t *x, int xr,
+                      const uint16_t *w, int tiled, const Epilogue &e, int M, int N, int K) {
+  const dim3 block(kSkWarps * 32);
+  switch (KS) {
+    case 1: return launch_pdl(linear_mma_kernel<MT, PL, 1>, grid, block, 0, st, x, xr, w, tiled, e, M, N, K);
+    case 2: return launch_pdl(linear_mma_kernel<MT, PL, 2>, grid, block, 0, st, x, xr, w, tiled, e, M, N, K);
+    case 4: return launch_pdl(linear_mma_kernel<MT, PL, 4>, grid, block, 0, st, x, xr, w, tiled, e, M, N, K);
+    default: return launch_pdl(linear_mma_kernel<MT, PL, 8>, grid, block, 0, st, x, xr, w, tiled, e, M, N, K);
+  }
+}
+
+// Largest batch the skinny kernel takes (TLLM_SKINNY_MAX_M overrides: 0
+// sends every bf16 projection to the tcgen05 kernel, at most 32).
+int sk_max_m() {
+  const char *sv = getenv("TLLM_SKINNY_MAX_M");
+  const int v = sv && sv[0] ? atoi(sv) : 32;
+  return v < 0 ? 0 : (v > 32 ? 32 : v);
+}
+
+// ------------------------------------------------------------------------
 // host side
 // ------------------------------------------------------------------------
 struct TcPlan {
@@ -1300,6 +1460,32 @@ int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
   (void)partial;
   (void)partial_bytes;
   (void)counters;
+  if (op != EPI_SCATTER && M <= sk_max_m()) {
+    // K slices per 16-row block: enough warps for two CTAs of 8 on every
+    // SM, at least one 32-k step each
+    const int blocks16 = (N + 15) / 16;
+    int KS = 1;
+    while (KS < kSkWarps && (long)blocks16 * KS < 2L * kSkWarps * sm_count() &&
+           2 * KS <= K / 32)
+      KS *= 2;
+    const int RB = kSkWarps / KS;
+    const dim3 grid((blocks16 + RB - 1) / RB);
+    const uint16_t *xb = static_cast<const uint16_t *>(x);
+    const uint16_t *wb = static_cast<const uint16_t *>(w);
+    const int tl = w_dtype == TLLM_BF16_TILED;
+    cudaError_t ce;
+    if (M <= 8)
+      ce = PL == 1 ? sk_launch<8, 1>(KS, grid, st, xb, x_plane_rows, wb, tl, e, M, N, K)
+                   : sk_launch<8, 2>(KS, grid, st, xb, x_plane_rows, wb, tl, e, M, N, K);
+    else if (M <= 16)
+      ce = PL == 1 ? sk_launch<16, 1>(KS, grid, st, xb, x_plane_rows, wb, tl, e, M, N, K)
+                   : sk_launch<16, 2>(KS, grid, st, xb, x_plane_rows, wb, tl, e, M, N, K);
+    else
+      ce = PL == 1 ? sk_launch<32, 1>(KS, grid, st, xb, x_plane_rows, wb, tl, e, M, N, K)
+                   : sk_launch<32, 2>(KS, grid, st, xb, x_plane_rows, wb, tl, e, M, N, K);
+    TLLM_CUDA(ce);
+    return TLLM_OK;
+  }
   const TcPlan pl = tc_plan(M, N, K, PL);
   const int S = pl.S;
   CUtensorMap tw, tx;
