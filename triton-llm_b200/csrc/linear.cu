@@ -929,6 +929,105 @@ __device__ __forceinline__ const uint16_t *sk_w(const uint16_t *w, bool tiled, i
                : w + (size_t)n * K + k;
 }
 
+// Epilogue of one lane's accumulators: weight rows r and r + 8, activation
+// rows b * 8 + 2q + t (t = 0, 1) for the blocks b in `bmask`; v[b] holds
+// {c0, c1, c2, c3} = {(r, t=0), (r, t=1), (r+8, t=0), (r+8, t=1)}. Same
+// arithmetic as epi_pair, but every load an op needs (residual rows,
+// positions, RoPE tables) is issued before the first store: the stores may
+// alias the loads (in-place residual), so per-row code would wait out one
+// memory round trip per row.
+template <int NB>
+__device__ __forceinline__ void sk_epilogue(const Epilogue &e, int N, int M, int r, int q,
+                                            const float (&v)[NB][4], unsigned bmask) {
+  const int r1 = r + 8;
+  const bool ok0 = r < N, ok1 = r1 < N;
+  bool okm[NB][2];
+  int mm[NB][2];
+#pragma unroll
+  for (int b = 0; b < NB; ++b)
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      mm[b][t] = b * 8 + 2 * q + t;
+      okm[b][t] = ((bmask >> b) & 1) && mm[b][t] < M;
+    }
+  const int op = e.op;
+  if (op == EPI_STORE || op == EPI_RESID || op == EPI_GELU) {
+    const float b0 = e.bias && ok0 ? e.bias[r] : 0.f;
+    const float b1 = e.bias && ok1 ? e.bias[r1] : 0.f;
+    float rv[NB][2][2];
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const size_t o = (size_t)mm[b][t] * e.ld_out;
+        const bool ld = op == EPI_RESID && okm[b][t];
+        rv[b][t][0] = ld && ok0 ? e.resid[o + r] : 0.f;
+        rv[b][t][1] = ld && ok1 ? e.resid[o + r1] : 0.f;
+      }
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        if (!okm[b][t]) continue;
+        const size_t o = (size_t)mm[b][t] * e.ld_out;
+        float a0 = v[b][t] + b0, a1 = v[b][2 + t] + b1;
+        if (op == EPI_RESID) {
+          a0 = rv[b][t][0] + a0;
+          a1 = rv[b][t][1] + a1;
+        } else if (op == EPI_GELU) {
+          a0 = gelu_tanh(a0);
+          a1 = gelu_tanh(a1);
+        }
+        if (ok0) store_out(e, o + r, a0);
+        if (ok1) store_out(e, o + r1, a1);
+      }
+  } else if (op == EPI_SWIGLU) {
+    if (!ok1) return;
+    const int j = (r >> 4) * 8 + (r & 7);
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+#pragma unroll
+      for (int t = 0; t < 2; ++t)
+        if (okm[b][t])
+          store_out(e, (size_t)mm[b][t] * e.ld_out + j, silu_ref(v[b][t]) * v[b][2 + t]);
+  } else {  // EPI_QKV
+    if (!ok1) return;
+    const QkvGeom g = qkv_geom(e, r);
+    const float b0 = e.bias ? e.bias[r] : 0.f;
+    const float b1 = e.bias ? e.bias[r1] : 0.f;
+    int pos[NB][2], seq[NB][2];
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        pos[b][t] = okm[b][t] ? e.row_pos[mm[b][t]] : -1;
+        seq[b][t] = okm[b][t] ? e.row_seq[mm[b][t]] : -1;
+      }
+    const bool rot = e.cos && !g.is_v;
+    float cs[NB][2], sn[NB][2];
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int ps = pos[b][t];
+        const bool in = rot && okm[b][t] && ps >= 0 && ps < e.max_seq;
+        const size_t ti = (size_t)(in ? ps : 0) * (e.D / 2) + g.d0;
+        cs[b][t] = in ? e.cos[ti] : 1.f;
+        sn[b][t] = in ? e.sin[ti] : 0.f;
+      }
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        if (!okm[b][t]) continue;
+        float x0 = v[b][t] + b0, x1 = v[b][2 + t] + b1;
+        const int ps = pos[b][t];
+        if (rot && ps >= 0 && ps < e.max_seq) rope_pair(cs[b][t], sn[b][t], x0, x1);
+        qkv_store(e, g, mm[b][t], ps, seq[b][t], x0, x1);
+      }
+  }
+}
+
 template <int MT, int PL, int KS>
 __global__ void __launch_bounds__(kSkWarps * 32)
     linear_mma_kernel(const uint16_t *x, int x_plane_rows, const uint16_t *w, int tiled,
@@ -1003,32 +1102,35 @@ __global__ void __launch_bounds__(kSkWarps * 32)
       }
     }
   }
+  unsigned bmask = (1u << NB) - 1;
   if constexpr (KS > 1) {
 #pragma unroll
     for (int b = 0; b < NB; ++b)
 #pragma unroll
       for (int i = 0; i < 4; ++i) s_part[warp][b * 4 + i][lane] = acc[b][i];
     __syncthreads();
-    if (slice != 0 || !live) return;
+    if (!live) return;
+    // the KS warps of a block share its epilogue: slice s finishes the
+    // activation blocks b = s (mod KS), each summed over the slices in order
+    const int w0 = warp - slice;
+    bmask = 0;
 #pragma unroll
-    for (int b = 0; b < NB; ++b)
+    for (int b = 0; b < NB; ++b) {
+      if (b % KS != slice) continue;
+      bmask |= 1u << b;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         float t = 0.f;
 #pragma unroll
-        for (int sl = 0; sl < KS; ++sl) t += s_part[warp + sl][b * 4 + i][lane];
+        for (int sl = 0; sl < KS; ++sl) t += s_part[w0 + sl][b * 4 + i][lane];
         acc[b][i] = t;
       }
+    }
+    if (!bmask) return;
   } else {
     if (!live) return;
   }
-  // c0 (r, 2q), c1 (r, 2q + 1), c2 (r + 8, 2q), c3 (r + 8, 2q + 1)
-#pragma unroll
-  for (int b = 0; b < NB; ++b) {
-    const int m = b * 8 + 2 * q;
-    epi_pair_rt(e, N, M, ra, m, acc[b][0], acc[b][2]);
-    epi_pair_rt(e, N, M, ra, m + 1, acc[b][1], acc[b][3]);
-  }
+  sk_epilogue<NB>(e, N, M, ra, q, acc, bmask);
 }
 
 template <int MT, int PL>
@@ -1041,6 +1143,16 @@ cudaError_t sk_launch(int KS, dim3 grid, cudaStream_t st, const uint16_t *x, int
     case 4: return launch_pdl(linear_mma_kernel<MT, PL, 4>, grid, block, 0, st, x, xr, w, tiled, e, M, N, K);
     default: return launch_pdl(linear_mma_kernel<MT, PL, 8>, grid, block, 0, st, x, xr, w, tiled, e, M, N, K);
   }
+}
+
+// Largest weight matrix the skinny kernel takes (TLLM_SKINNY_MAX_MB, in
+// MiB, overrides): below it a projection is bound by latency, where the
+// tcgen05 kernel's set-up costs most; above it the tcgen05 kernel's deep
+// TMA ring streams HBM better.
+size_t sk_max_bytes() {
+  const char *sv = getenv("TLLM_SKINNY_MAX_MB");
+  const long v = sv && sv[0] ? atol(sv) : 8;
+  return (size_t)(v < 0 ? 0 : v) << 20;
 }
 
 // Largest batch the skinny kernel takes (TLLM_SKINNY_MAX_M overrides: 0
@@ -1460,7 +1572,7 @@ int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
   (void)partial;
   (void)partial_bytes;
   (void)counters;
-  if (op != EPI_SCATTER && M <= sk_max_m()) {
+  if (op != EPI_SCATTER && M <= sk_max_m() && (size_t)N * K * 2 <= sk_max_bytes()) {
     // K slices per 16-row block: enough warps for two CTAs of 8 on every
     // SM, at least one 32-k step each
     const int blocks16 = (N + 15) / 16;
