@@ -112,12 +112,19 @@ template <bool ADD>
 __global__ void rmsnorm_vec_kernel(float *x, const float *add, const float *w,
                                    RowOut y, int N, float eps) {
   griddep_launch();
+  const int n4 = N >> 2;
+  // the weights do not come from the previous kernel: load them while it
+  // finishes
+  float4 g[kVecPer];
+#pragma unroll
+  for (int k = 0; k < kVecPer; ++k) {
+    const int i = threadIdx.x + k * blockDim.x;
+    g[k] = i < n4 ? reinterpret_cast<const float4 *>(w)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   griddep_wait();
   __shared__ float red[32];
-  const int n4 = N >> 2;
   float4 *xr = reinterpret_cast<float4 *>(x + (size_t)blockIdx.x * N);
   const float4 *ar = reinterpret_cast<const float4 *>(add + (ADD ? (size_t)blockIdx.x * N : 0));
-  const float4 *w4 = reinterpret_cast<const float4 *>(w);
   float4 v[kVecPer];
   float ss = 0.f;
 #pragma unroll
@@ -150,12 +157,10 @@ __global__ void rmsnorm_vec_kernel(float *x, const float *add, const float *w,
 #pragma unroll
   for (int k = 0; k < kVecPer; ++k) {
     const int i = threadIdx.x + k * blockDim.x;
-    if (i < n4) {
-      const float4 g = w4[i];
+    if (i < n4)
       put4(y, o + 4 * (size_t)i,
-           make_float4((v[k].x / rms) * g.x, (v[k].y / rms) * g.y, (v[k].z / rms) * g.z,
-                       (v[k].w / rms) * g.w));
-    }
+           make_float4((v[k].x / rms) * g[k].x, (v[k].y / rms) * g[k].y,
+                       (v[k].z / rms) * g[k].z, (v[k].w / rms) * g[k].w));
   }
 }
 
@@ -179,6 +184,61 @@ __global__ void layernorm_kernel(const float *x, const float *g, const float *b,
   const float rstd = 1.f / sqrtf(var + eps);
   for (int i = threadIdx.x; i < N; i += blockDim.x)
     y.put(o + i, (xr[i] - mean) * rstd * g[i] + b[i]);
+}
+
+// The same two passes with the row held in registers (float4 loads, one
+// read of x); gain and bias are loaded before the wait for the previous
+// kernel.
+__global__ void layernorm_vec_kernel(const float *x, const float *g, const float *b,
+                                     RowOut y, int N, float eps) {
+  griddep_launch();
+  const int n4 = N >> 2;
+  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 gv[kVecPer], bv[kVecPer];
+#pragma unroll
+  for (int k = 0; k < kVecPer; ++k) {
+    const int i = threadIdx.x + k * blockDim.x;
+    gv[k] = i < n4 ? reinterpret_cast<const float4 *>(g)[i] : z;
+    bv[k] = i < n4 ? reinterpret_cast<const float4 *>(b)[i] : z;
+  }
+  griddep_wait();
+  __shared__ float red[32];
+  const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)blockIdx.x * N);
+  float4 v[kVecPer];
+  float s = 0.f;
+#pragma unroll
+  for (int k = 0; k < kVecPer; ++k) {
+    const int i = threadIdx.x + k * blockDim.x;
+    v[k] = i < n4 ? xr[i] : z;
+    s += ((v[k].x + v[k].y) + v[k].z) + v[k].w;
+  }
+  const float mean = block_sum(s, red) / (float)N;
+  float q = 0.f;
+#pragma unroll
+  for (int k = 0; k < kVecPer; ++k) {
+    const int i = threadIdx.x + k * blockDim.x;
+    if (i < n4) {
+      const float c0 = v[k].x - mean, c1 = v[k].y - mean, c2 = v[k].z - mean,
+                  c3 = v[k].w - mean;
+      q = fmaf(c0, c0, q);
+      q = fmaf(c1, c1, q);
+      q = fmaf(c2, c2, q);
+      q = fmaf(c3, c3, q);
+    }
+  }
+  const float var = block_sum(q, red) / (float)N;
+  const float rstd = 1.f / sqrtf(var + eps);
+  const size_t o = (size_t)blockIdx.x * N;
+#pragma unroll
+  for (int k = 0; k < kVecPer; ++k) {
+    const int i = threadIdx.x + k * blockDim.x;
+    if (i < n4)
+      put4(y, o + 4 * (size_t)i,
+           make_float4((v[k].x - mean) * rstd * gv[k].x + bv[k].x,
+                       (v[k].y - mean) * rstd * gv[k].y + bv[k].y,
+                       (v[k].z - mean) * rstd * gv[k].z + bv[k].z,
+                       (v[k].w - mean) * rstd * gv[k].w + bv[k].w));
+  }
 }
 
 // fp32 (rows, cols) -> operand-format planes of plane_rows rows
@@ -536,6 +596,11 @@ int tllm_layernorm(const float *x, const float *g, const float *b, void *y,
   RowOut o;
   int rc = row_out(&o, y, y_dtype, y_plane_rows, M, N);
   if (rc) return rc;
+  if (rms_vec_ok(x, nullptr, g, o, N) && aligned16(b)) {
+    TLLM_CUDA(launch_pdl(layernorm_vec_kernel, dim3(M), dim3(rms_vec_threads(N)), 0,
+                         resolve(stream), x, g, b, o, N, eps));
+    return TLLM_OK;
+  }
   TLLM_CUDA(launch_pdl(layernorm_kernel, dim3(M), dim3(256), 0, resolve(stream), x,
                        g, b, o, N, eps));
   return TLLM_OK;
