@@ -914,8 +914,9 @@ constexpr int kSkU = 4;   // 32-k steps per load batch (two batches in flight)
 __device__ __forceinline__ void sk_mma(float (&c)[4], uint32_t a0, uint32_t a1,
                                        uint32_t a2, uint32_t a3, uint32_t b0,
                                        uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, "
+  // no side effects besides c: not volatile, so loads may be scheduled
+  // across it
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, "
       "{%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
@@ -1086,17 +1087,27 @@ __global__ void __launch_bounds__(kSkWarps * 32)
       wa[u] = in ? ld_stream(sk_w(w, tiled, kc, K, na, k)) : z;
       wb[u] = in ? ld_stream(sk_w(w, tiled, kc, K, nb8, k)) : z;
     }
+    // the activation fragments of the whole batch first (L1/L2 hits, one
+    // round trip), then the MMAs
+    uint4 xv[kSkU][PL][NB];
+#pragma unroll
+    for (int u = 0; u < kSkU; ++u) {
+      const int k = min(s + u, s1 - 1) * 32;
+#pragma unroll
+      for (int pl = 0; pl < PL; ++pl)
+#pragma unroll
+        for (int b = 0; b < NB; ++b)
+          xv[u][pl][b] = __ldg(reinterpret_cast<const uint4 *>(xr[b] + pl * xplane + k));
+    }
 #pragma unroll
     for (int u = 0; u < kSkU; ++u) {
       if (s + u < s1) {
-        const int k = (s + u) * 32;
 #pragma unroll
         for (int pl = 0; pl < PL; ++pl) {
 #pragma unroll
           for (int b = 0; b < NB; ++b) {
-            const uint4 xv = __ldg(reinterpret_cast<const uint4 *>(xr[b] + pl * xplane + k));
-            sk_mma(acc[b], ca[u].x, cb[u].x, ca[u].y, cb[u].y, xv.x, xv.y);
-            sk_mma(acc[b], ca[u].z, cb[u].z, ca[u].w, cb[u].w, xv.z, xv.w);
+            sk_mma(acc[b], ca[u].x, cb[u].x, ca[u].y, cb[u].y, xv[u][pl][b].x, xv[u][pl][b].y);
+            sk_mma(acc[b], ca[u].z, cb[u].z, ca[u].w, cb[u].w, xv[u][pl][b].z, xv[u][pl][b].w);
           }
         }
       }
