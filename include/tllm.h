@@ -264,8 +264,11 @@ int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
  * ffn % 64 == 0. One CTA per SM, launched cooperatively; the three GEMMs
  * share one weight stream split evenly over the SMs, and the phases meet at
  * grid barriers. workspace: tllm_mlp_workspace bytes, 256-byte aligned,
- * zero-filled before the first call; the kernel keeps its counters valid
- * across calls, and calls that overlap on the GPU must not share one.
+ * zero-filled before the first call; its barrier and per-tile counters
+ * only grow (each call adds a fixed amount), so they stay valid across
+ * calls and graph replays without a reset. Calls that overlap on the GPU
+ * must not share one, and after a call that set the device error word
+ * (a bounded wait gave up) it must be zero-filled again.
  */
 int tllm_mlp_workspace(int M, int attn_dim, int hidden, int ffn,
                        size_t *bytes);

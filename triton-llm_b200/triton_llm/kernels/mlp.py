@@ -29,6 +29,11 @@ class MlpWorkspace:
         self.nbytes = n.value
         self.buf = gpu.zeros((max(self.nbytes, 1),), np.uint8)
 
+    def reset(self):
+        """Zero the counters again (needed after a call that set the device
+        error word: a bounded wait that gave up leaves them mid-count)."""
+        gpu.memset(self.buf, 0)
+
 
 def supported(rows: int, attn_dim: int, hidden: int, ffn: int) -> bool:
     return (0 < rows <= MAX_ROWS and hidden % 128 == 0 and attn_dim % 64 == 0
