@@ -77,6 +77,21 @@ def test_argument_errors_before_any_device_work():
     assert st == _lib.OK and pb.value > 0 and cb.value == 4 * 9 * 4
 
 
+def test_mlp_workspace_rejects_unsupported_shapes():
+    """tllm_mlp_workspace checks the block's shape rules on the host."""
+    lib = _lib.load()
+    n = ctypes.c_size_t()
+    for args, msg in [((0, 1024, 1024, 2816), "M must be in"),
+                      ((65, 1024, 1024, 2816), "M must be in"),
+                      ((8, 1024, 1000, 2816), "hidden must be a multiple of 128"),
+                      ((8, 1000, 1024, 2816), "attn_dim must be a multiple of 64"),
+                      ((8, 1024, 1024, 2800), "ffn must be a multiple of 64")]:
+        assert lib.tllm_mlp_workspace(*args, ctypes.byref(n)) == _lib.ERR_INVALID_ARG
+        assert msg in _lib.last_error()
+    assert lib.tllm_mlp_workspace(8, 1024, 1024, 2816, ctypes.byref(n)) == _lib.OK
+    assert n.value > 0 and n.value % 256 == 0
+
+
 def _has_device():
     n = ctypes.c_int(0)
     return _lib.load().tllm_device_count(ctypes.byref(n)) == 0 and n.value > 0
