@@ -344,11 +344,7 @@ class LlamaDecodeWorkload:
         n_launch = (2 if s.mlp_ws is not None else 4) * w.L + 1
         ms = _time_graph(gpu, g, 5)
         achieved = alg / (ms / 1e3) / 1e9
-        return {"kernels": ("linear_tc_kernel (qkv+rope+append, lm_head) + mlp_kernel "
-                            "(o, norm, gate/up+swiglu, down in one launch)"
-                            if s.mlp_ws is not None else
-                            "linear_tc_kernel (qkv+rope+append, o, gate/up+swiglu, "
-                            "down, lm_head)"),
+        return {"kernels": projection_kernels(w.linear_shapes(B), s.mlp_ws is not None),
                 "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "bound": "hbm",
                 "algorithmic_bytes_per_step": alg, "ms_per_step": round(ms, 4),
@@ -629,6 +625,22 @@ def gpt2_cpu_sample(steps: int):
     return 1.0 / per, (f"oracle GPT-2 small decode step after a 32-token prompt, "
                        f"median of {steps} steps ({per * 1e3:.1f} ms), numpy restatement "
                        "(oracle/), batch 1 like the reference")
+
+
+def projection_kernels(shapes, fused_mlp: bool) -> str:
+    """Which kernel runs each projection of a step (qkv, o, gate/up, down,
+    lm_head shapes), grouped by kernel, for the roofline line."""
+    from triton_llm.kernels.linear import kernel_name
+    names = ["qkv+rope+append", "o", "gate/up+swiglu", "down", "lm_head"]
+    groups = {}
+    for (M, N, K), nm in zip(shapes, names):
+        if fused_mlp and nm in ("o", "gate/up+swiglu", "down"):
+            continue
+        groups.setdefault(kernel_name(M, N, K), []).append(nm)
+    text = " + ".join(f"{k} ({', '.join(v)})" for k, v in groups.items())
+    if fused_mlp:
+        text += " + mlp_kernel (o, norm, gate/up+swiglu, down in one launch)"
+    return text
 
 
 def llama_cpu_sample(ctx: int, steps: int, model="Llama-3.2-3B-Instruct", log=None):

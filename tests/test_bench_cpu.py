@@ -67,3 +67,36 @@ def test_reference_arm_two_ranks_rank0_only():
     assert len(rank0) == 1
     _check_line(json.loads(rank0[0]))
     assert not outs[1][1].strip()   # rank 1 prints nothing
+
+
+def test_projection_kernel_labels(monkeypatch):
+    """The roofline line names the kernel tllm_linear picks for each
+    projection (the skinny kernel for small decode batches on small
+    matrices, tcgen05 otherwise, fp32 CUDA cores for fp32 weights)."""
+    for p in (REPO / "triton-llm_b200", REPO):
+        if str(p) not in sys.path:
+            sys.path.insert(0, str(p))
+    import bench
+    from triton_llm.kernels.linear import kernel_name
+    monkeypatch.delenv("TLLM_SKINNY_MAX_M", raising=False)
+    monkeypatch.delenv("TLLM_SKINNY_MAX_MB", raising=False)
+    smol = [(32, 960, 576), (32, 576, 576), (32, 3072, 576), (32, 576, 1536), (32, 49152, 576)]
+    llama = [(64, 5120, 3072), (64, 3072, 3072), (64, 16384, 3072), (64, 3072, 8192),
+             (64, 128256, 3072)]
+    assert bench.projection_kernels(smol, False) == (
+        "linear_mma_kernel (qkv+rope+append, o, gate/up+swiglu, down) + "
+        "linear_tc_kernel (lm_head)")
+    assert bench.projection_kernels(llama, False) == (
+        "linear_tc_kernel (qkv+rope+append, o, gate/up+swiglu, down, lm_head)")
+    assert "mlp_kernel" in bench.projection_kernels(llama, True)
+    assert kernel_name(8, 4096, 1024) == "linear_mma_kernel"        # exactly 8 MiB
+    assert kernel_name(8, 4096, 1088) == "linear_tc_kernel"         # above it
+    assert kernel_name(33, 576, 576) == "linear_tc_kernel"
+    assert kernel_name(8, 576, 576, scatter=True) == "linear_tc_kernel"
+    assert kernel_name(1, 768, 768, bf16=False) == "linear_f32_kernel"
+    monkeypatch.setenv("TLLM_SKINNY_MAX_M", "0")
+    assert kernel_name(1, 576, 576) == "linear_tc_kernel"
+    monkeypatch.setenv("TLLM_SKINNY_MAX_M", "32")
+    monkeypatch.setenv("TLLM_SKINNY_MAX_MB", "1")
+    assert kernel_name(32, 576, 576) == "linear_mma_kernel"         # 0.63 MiB
+    assert kernel_name(32, 3072, 576) == "linear_tc_kernel"         # 3.4 MiB

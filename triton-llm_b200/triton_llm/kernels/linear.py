@@ -147,6 +147,29 @@ class LinearWorkspace:
         self.counters = gpu.zeros((max(cb_max // 4, 1),), np.int32)
 
 
+def _env_int(name: str, default: int) -> int:
+    v = os.environ.get(name, "")
+    try:
+        return int(v) if v else default
+    except ValueError:
+        return 0   # like atoi on the C side
+
+
+def kernel_name(M: int, N: int, K: int, bf16: bool = True, scatter: bool = False) -> str:
+    """The kernel ``tllm_linear`` runs for an (M, N, K) projection, by the
+    C side's rule: fp32 weights -> linear_f32_kernel; bf16 weights with at
+    most TLLM_SKINNY_MAX_M (32) rows on a matrix of at most
+    TLLM_SKINNY_MAX_MB (8) MiB, and not SCATTER -> linear_mma_kernel;
+    otherwise linear_tc_kernel."""
+    if not bf16:
+        return "linear_f32_kernel"
+    max_m = min(max(_env_int("TLLM_SKINNY_MAX_M", 32), 0), 32)
+    max_bytes = max(_env_int("TLLM_SKINNY_MAX_MB", 8), 0) << 20
+    if not scatter and M <= max_m and N * K * 2 <= max_bytes:
+        return "linear_mma_kernel"
+    return "linear_tc_kernel"
+
+
 def plan(M: int, N: int, K: int, planes: int = 1) -> dict:
     """Launch plan of the bf16 tensor-core path (tllm_linear_plan) for
     activations with 1 (TLLM_BF16) or 2 (TLLM_SPLIT) planes."""
