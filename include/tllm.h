@@ -202,7 +202,12 @@ int tllm_gqa_rows(const float *q, long q_row_stride, long q_head_stride,
  * w_dtype BF16 or BF16_TILED: tensor-core path; x is TLLM_BF16 (one
  *   bf16 plane) or TLLM_SPLIT (hi and lo planes, ~16 mantissa bits), planes
  *   of x_plane_rows >= M rows (see tllm_split_bf16), K % 64 == 0.
- *   BF16_TILED streams each weight tile as one 16 KB block.
+ *   BF16_TILED streams each weight tile as one 16 KB block. M <= 32 on a
+ *   matrix of at most 8 MiB (environment TLLM_SKINNY_MAX_M,
+ *   TLLM_SKINNY_MAX_MB; every op but SCATTER) runs the decode kernel
+ *   (mma.sync, weights streamed straight into registers, no set-up); other
+ *   shapes run the tcgen05 kernel (TMA ring, TMEM accumulators, split-K
+ *   over a cluster). The two agree to fp32 summation order.
  * w_dtype F32 : CUDA-core fp32 path; x must be F32 (M, K), K % 4 == 0.
  * out_dtype F32, TLLM_SPLIT or TLLM_BF16 (planes of out_plane_rows rows of
  *   ld_out); op RESID needs F32.
