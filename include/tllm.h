@@ -381,7 +381,7 @@ int tllm_fill_random(void *ptr, int dtype, long n, uint64_t seed, float std,
  * All calls on a device share the array and it keeps the last call's data:
  * calls that overlap on the GPU race and must not be issued. Device-side
  * error codes of these calls are kept in the same array, not in the word
- * read by tllm_device_error.
+ * read by tllm_device_error: read them with tllm_gqa_decode_noalloc_error.
  */
 int tllm_gqa_decode_noalloc(const float *q, const void *k_cache,
                             const void *v_cache, int kv_dtype,
@@ -389,6 +389,15 @@ int tllm_gqa_decode_noalloc(const float *q, const void *k_cache,
                             int n_head, int n_kv_head, int head_dim,
                             int max_seq, int max_len, float sm_scale,
                             tllm_stream_t stream);
+
+/* Device-side error bits raised by tllm_gqa_decode_noalloc calls on the
+ * current device since the last reset, with the bit values of
+ * tllm_device_error: 1 = a bounded wait ran out (the output is then
+ * incomplete), 2 = a sequence length above max_len (it was clamped). Waits
+ * for the whole device, copies the word out (allocating nothing) and clears
+ * it when reset != 0. No counterpart in the reference (it belongs to
+ * tllm_gqa_decode_noalloc). */
+int tllm_gqa_decode_noalloc_error(int *code, int reset);
 
 #ifdef __cplusplus
 }

@@ -21,6 +21,9 @@ Fixtures written next to this script (small .npz files, committed):
                      rounded to bf16, 4-token prompt + 2 greedy steps
   gpt2_small_slice.npz (--slow) GPT-2 small N(0,0.02) seed 0, 8-token
                      prompt + 2 greedy steps
+  gpt2_cfg1.npz      (--slow) BASELINE config 1: GPT-2 small N(0,0.02) seed
+                     0, 32-token prompt + 32 greedy steps; tokens and a
+                     digest of the per-step logits (inputs.logits_digest)
 """
 
 from __future__ import annotations
@@ -253,6 +256,17 @@ def main():
         _log(f"  tokens {toks.tolist()}")
         np.savez_compressed(HERE / "gpt2_small_slice.npz", tokens=toks,
                             logits=logits)
+    if a.slow and want("gpt2_cfg1"):
+        # BASELINE config 1 as stated: GPT-2 small, N(0,0.02) seed-0 weights,
+        # 32-token prompt (default_rng(0)), 32 greedy steps. About an hour of
+        # CPU under the interpreter.
+        _log("gpt2_cfg1")
+        w = inputs.gpt2_weights(inputs.GPT2_SMALL, 0)
+        prompt = np.random.default_rng(0).integers(0, 50257, 32).tolist()
+        toks, logits = gpt2_run(inputs.GPT2_SMALL, w, prompt, 32)
+        _log(f"  tokens {toks.tolist()}")
+        np.savez_compressed(HERE / "gpt2_cfg1.npz", tokens=toks,
+                            **inputs.logits_digest(logits))
     _log("done")
 
 

@@ -111,6 +111,31 @@ def llama_weights(shape: LlamaShape, seed=0, std=0.02):
     return w
 
 
+DIGEST_COLS = 4096   # logit columns kept per step by logits_digest
+DIGEST_TOPK = 32
+
+
+def digest_columns(vocab, seed=12345):
+    """The fixed, sorted logit columns a digest keeps (seeded, no repeats)."""
+    rng = np.random.default_rng(seed)
+    return np.sort(rng.choice(vocab, size=min(DIGEST_COLS, vocab), replace=False))
+
+
+def logits_digest(logits):
+    """Compact record of per-step logits (steps, V) of a long greedy run:
+    the full rows of the first and last step, every step's values at
+    ``digest_columns`` and its top-``DIGEST_TOPK`` (index, value) pairs in
+    descending order, and each step's gap between its two largest logits
+    (the margin its greedy token has)."""
+    lg = np.asarray(logits, F32)
+    cols = digest_columns(lg.shape[1])
+    top = np.argsort(-lg, axis=1, kind="stable")[:, :DIGEST_TOPK]
+    topv = np.take_along_axis(lg, top, axis=1)
+    return {"first": lg[0].copy(), "last": lg[-1].copy(), "cols": cols,
+            "at_cols": lg[:, cols].copy(), "top_idx": top.astype(np.int32),
+            "top_val": topv, "gap": (topv[:, 0] - topv[:, 1]).astype(F32)}
+
+
 def bf16_round(x):
     a = np.ascontiguousarray(x, dtype=F32)
     u = a.view(np.uint32).astype(np.uint64)

@@ -1321,3 +1321,22 @@ extern "C" int tllm_gqa_decode_noalloc(
                    n_kv_head, head_dim, batch, max_seq, max_len, sm_scale, base,
                    kNoAllocPartialBytes, counters, err_word, st);
 }
+
+// The device error word of tllm_gqa_decode_noalloc sits at the end of the
+// static scratch array, so reading it allocates nothing either: the whole
+// device is synchronised (the calls may have used any stream), the word is
+// copied out and optionally cleared.
+extern "C" int tllm_gqa_decode_noalloc_error(int *code, int reset) {
+  TLLM_CHECK_ARG(code, "code is NULL");
+  unsigned char *base = nullptr;
+  int rc = noalloc_scratch(&base);
+  if (rc) return rc;
+  int *err_word = reinterpret_cast<int *>(base + kNoAllocErrOffset);
+  TLLM_CUDA(cudaDeviceSynchronize());
+  TLLM_CUDA(cudaMemcpy(code, err_word, sizeof(int), cudaMemcpyDeviceToHost));
+  if (reset) {
+    TLLM_CUDA(cudaMemset(err_word, 0, sizeof(int)));
+    TLLM_CUDA(cudaDeviceSynchronize());
+  }
+  return TLLM_OK;
+}
