@@ -10,12 +10,13 @@ maximum over ranks.
 
 Workloads:
   llama3b  (default) config 4: Llama-3.2-3B architecture, bf16 weights and
-           KV cache, random-init weights N(0, 0.02); per rank a ragged batch
-           of 64 sequences whose cached contexts are uniform in
-           [1024, 8192] (K/V filled N(0, 1)); K greedy decode steps. The
-           64*N lengths come from one seeded stream and are partitioned
-           across ranks balancing total context (triton_llm.shard), so the
-           per-GPU work is fixed as N grows (weak scaling).
+           KV cache, random-init weights N(0, 0.02); one ragged batch of 64
+           sequences whose cached contexts are uniform in [1024, 8192] (K/V
+           filled N(0, 1)); K greedy decode steps. The 64 lengths come from
+           one seeded stream and are partitioned across the N ranks (64 / N
+           each) balancing total context (triton_llm.shard), so the total
+           work is fixed as N grows (strong scaling).
+  llama3b_weak  the same with 64 sequences on every rank (weak scaling).
   gqa      config 2: the isolated split-KV GQA decode-attention kernel, 64
            ragged sequences (U[128, 2048], seed 1), 9 q / 3 kv heads,
            head_dim 64, bf16 cache; one step = one launch over the batch.
@@ -172,14 +173,23 @@ def measured_peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def profiled_traffic(key: str):
+def profiled_traffic(key: str, alg_bytes: int | None = None):
     """Per-launch DRAM bytes of a kernel from a committed ncu summary
-    (profiles/traffic.json), or None."""
+    (profiles/traffic.json), or None. When the summary records the ratio of
+    DRAM traffic to algorithmic bytes and ``alg_bytes`` is given, the
+    traffic of this launch is that ratio times its algorithmic bytes (the
+    capture's case and this launch differ only in the contexts read, which
+    traffic follows in proportion); else the captured launch's bytes."""
     p = REPO / "profiles" / "traffic.json"
     if p.exists():
         try:
             d = json.loads(p.read_text()).get(key)
-            return d.get("bytes_per_launch") if d else None
+            if not d:
+                return None
+            r = d.get("traffic_over_algorithmic")
+            if r and alg_bytes:
+                return int(round(r * alg_bytes))
+            return d.get("bytes_per_launch")
         except Exception:
             return None
     return None
@@ -201,14 +211,16 @@ def _time_graph(gpu, graph, reps):
 
 # -------------------------------------------------------- config 4: Llama ----
 class LlamaDecodeWorkload:
-    """Llama-3.2-3B ragged-batch decode (bf16)."""
+    """Llama-3.2-3B ragged-batch decode (bf16), one batch
+    of 64 sequences split over the N ranks (64 / N each, strong scaling)."""
 
     name = "llama3b"
-    scaling = "weak"
+    scaling = "strong"
     dtype = "bf16"
     act = "bfloat16"
     model = "Llama-3.2-3B-Instruct"
-    per_rank = 64
+    global_batch = 64        # per_rank = global_batch / N
+    per_rank = None          # fixed per-rank batch instead (weak scaling)
     lo, hi = 1024, 8192
     len_seed = 4
 
@@ -217,9 +229,14 @@ class LlamaDecodeWorkload:
         self.ranks = ranks
         self.steps, self.warmup = steps, warmup
         n = ranks.world
-        self.all_lens = shard.ragged_lengths(self.per_rank * n, self.lo, self.hi,
-                                             self.len_seed)
-        self.parts = shard.partition(self.all_lens, n, self.per_rank)
+        if self.per_rank is None:
+            if self.global_batch % n:
+                raise SystemExit(f"{self.global_batch} sequences do not split over {n} GPUs")
+            per = self.global_batch // n
+        else:
+            per = self.per_rank
+        self.all_lens = shard.ragged_lengths(per * n, self.lo, self.hi, self.len_seed)
+        self.parts = shard.partition(self.all_lens, n, per)
         self.idx = self.parts[ranks.rank]
         self.lens = self.all_lens[self.idx].astype(np.int32)
         self.B = len(self.lens)
@@ -227,10 +244,14 @@ class LlamaDecodeWorkload:
         self.S = ((self.hi + steps + warmup + 2 + 63) // 64) * 64
 
     def config(self):
+        n = self.ranks.world
+        split = ("one batch split over the GPUs" if self.per_rank is None
+                 else f"{self.per_rank} sequences per GPU")
         return {"workload": "cfg4 Llama-3.2-3B ragged-batch greedy decode",
                 "model": self.model, "layers": 28, "hidden": 3072,
                 "heads": "24 q / 8 kv, head_dim 128", "ffn": 8192, "vocab": 128256,
-                "batch_per_gpu": self.B, "global_batch": self.B * self.ranks.world,
+                "batch_per_gpu": self.B, "global_batch": self.B * n,
+                "batching": split,
                 "ctx": f"U[{self.lo},{self.hi}] seed {self.len_seed}, "
                        "partitioned by total context",
                 "sum_ctx_this_rank": int(self.lens.sum()),
@@ -256,8 +277,9 @@ class LlamaDecodeWorkload:
         s = self.sess
         _lib.call("tllm_fill_random", s.kv_arena.ptr, _lib.BF16,
                   int(np.prod(s.kv_arena.shape)), 1000 + self.ranks.rank, 1.0, None)
-        rng = np.random.default_rng(100 + self.ranks.rank)
-        self.ids0 = rng.integers(0, cfg.vocab_size, self.B).astype(np.int32)
+        rng = np.random.default_rng(100)
+        all_ids = rng.integers(0, cfg.vocab_size, len(self.all_lens)).astype(np.int32)
+        self.ids0 = all_ids[self.idx]
         self.reset()
         self.launches_per_step = s.decode_step(True)
         gpu.device_synchronize()
@@ -310,7 +332,10 @@ class LlamaDecodeWorkload:
                 "launch_ms": round(ms, 5),
                 "timing": f"attention-only CUDA graph of the {w.L} layer launches of "
                           "one step on the same cache, 5 replays, CUDA events",
-                "traffic": profiled_traffic("llama3b_attention")}
+                "traffic": profiled_traffic("llama3b_attention", alg),
+                "traffic_source": "ncu DRAM read+write / algorithmic bytes of one "
+                                  "config-4 layer launch (profiles/traffic.json), "
+                                  "times this launch's algorithmic bytes"}
 
     def projection_roofline(self, gpu, peak):
         """All projection GEMMs of one step replayed alone (weights stream)."""
@@ -366,6 +391,15 @@ class LlamaDecodeWorkload:
         out = gpu.split_to_host(s.attn, n).reshape(n, w.H, w.D)
         ref = ops.gqa_decode(q, kc, vc, lens)
         return float(np.abs(out - ref).max())
+
+
+class LlamaWeakWorkload(LlamaDecodeWorkload):
+    """Config 4's model and contexts with 64 sequences on EVERY GPU (the
+    per-GPU work fixed as N grows: weak scaling)."""
+
+    name = "llama3b_weak"
+    scaling = "weak"
+    per_rank = 64
 
 
 class LlamaTPWorkload(LlamaDecodeWorkload):
@@ -450,6 +484,7 @@ class LlamaTPWorkload(LlamaDecodeWorkload):
     def kernel_roofline(self, gpu, peak):
         r = super().kernel_roofline(gpu, peak)
         r["traffic"] = None   # the committed capture is of the config-4 cache
+        r.pop("traffic_source", None)
         return r
 
     def units_per_step(self):
@@ -464,6 +499,7 @@ class SmolDecodeWorkload(LlamaDecodeWorkload):
     with its K/V filled N(0, 1), and the K timed steps continue from there."""
 
     name = "smol135m"
+    scaling = "weak"
     model = "SmolLM2-135M"
     per_rank = 32
     lo, hi = 640, 640
@@ -488,6 +524,7 @@ class SmolDecodeWorkload(LlamaDecodeWorkload):
         r = super().kernel_roofline(gpu, peak)
         r["kernel"] = "gqa_decode_mma_kernel<64> (+ split merge)"
         r["traffic"] = None
+        r.pop("traffic_source", None)
         return r
 
 
@@ -665,29 +702,38 @@ def llama_cpu_sample(ctx: int, steps: int, model="Llama-3.2-3B-Instruct", log=No
         c["k"][:, :ctx] = inputs.bf16_round(rng.standard_normal(c["k"][:, :ctx].shape, dtype=np.float32))
         c["v"][:, :ctx] = inputs.bf16_round(rng.standard_normal(c["v"][:, :ctx].shape, dtype=np.float32))
 
-    def timed(n):
-        o.cache_len = ctx
-        o.forward_cached(np.array([[1]], np.int32))       # warm
+    from oracle import ops
+    n = max(steps, 5)
+
+    def med(fn):
+        fn()                                              # warm
         ts = []
         for i in range(n):
-            o.cache_len = ctx
             t = time.perf_counter()
-            o.forward_cached(np.array([[i % 1000]], np.int32))
+            fn(i)
             ts.append(time.perf_counter() - t)
         return statistics.median(ts)
 
-    t2 = timed(steps)
-    layers = o.layers
-    o.layers = layers[:1]
-    t1 = timed(max(2, min(steps, 6)))
-    o.layers = layers
-    t_layer = max(t2 - t1, 1e-6)
-    t_head = max(t1 - t_layer, 0.0)
+    def step(i=0):
+        o.cache_len = ctx
+        o.forward_cached(np.array([[i % 1000]], np.int32))
+
+    x = rng.standard_normal((1, cfg.hidden_size), dtype=np.float32)
+
+    def head(i=0):
+        ops.gemm(ops.rms_norm(x, o.ln_f, o.eps), o.lm_head_w)
+
+    # the lm_head (final norm + GEMV over the vocabulary) timed alone, then
+    # whole 2-layer steps; a layer is the step minus the head, halved
+    t_head = med(head)
+    t_step = med(step)
+    t_layer = max(t_step - t_head, 1e-6) / len(o.layers)
     per_token = t_head + full.num_hidden_layers * t_layer
-    text = (f"oracle decode step, 1 sequence at ctx {ctx}, 2 of {full.num_hidden_layers} "
-            f"layers + lm_head timed ({steps} steps; layer {t_layer * 1e3:.1f} ms, "
-            f"head {t_head * 1e3:.1f} ms), extrapolated to {full.num_hidden_layers} layers; "
-            "batch 1 like the reference, numpy restatement (oracle/)")
+    text = (f"oracle decode step, 1 sequence at ctx {ctx}: lm_head timed alone "
+            f"({t_head * 1e3:.1f} ms) and {len(o.layers)}-layer steps "
+            f"({t_step * 1e3:.1f} ms), medians of {n}; per layer {t_layer * 1e3:.1f} ms, "
+            f"extrapolated to {full.num_hidden_layers} layers; batch 1 like the "
+            "reference, numpy restatement (oracle/)")
     return 1.0 / per_token, text
 
 
@@ -1077,7 +1123,8 @@ class ProjLlamaLayerWorkload(_IsolatedWorkload):
         return float(np.abs(gpu.split_to_host(self.act)[:, :32] - ref).max())
 
 
-WORKLOADS = {"llama3b": LlamaDecodeWorkload, "llama3b_tp": LlamaTPWorkload,
+WORKLOADS = {"llama3b": LlamaDecodeWorkload, "llama3b_weak": LlamaWeakWorkload,
+             "llama3b_tp": LlamaTPWorkload,
              "smol135m": SmolDecodeWorkload, "gpt2": GPT2Workload,
              "gqa": GQAWorkload,
              "gqa_llama3b": GQALlamaLayerWorkload, "proj_llama3b": ProjLlamaLayerWorkload}
@@ -1114,7 +1161,7 @@ def gqa_cpu_baseline(cores, pool, budget_s=15.0):
 def cpu_baseline(name, cores, steps, pool=None, ctx=None):
     if name == "gqa":
         return gqa_cpu_baseline(cores, pool)
-    if name in ("llama3b", "llama3b_tp"):
+    if name in ("llama3b", "llama3b_weak", "llama3b_tp"):
         return llama_cpu_sample(int(ctx), steps)
     if name == "smol135m":
         return llama_cpu_sample(int(ctx), steps, model=SmolDecodeWorkload.model)
@@ -1260,10 +1307,12 @@ def reference_arm(args, ranks, cores):
         lens = shard.ragged_lengths(64, LlamaDecodeWorkload.lo, LlamaDecodeWorkload.hi,
                                     LlamaDecodeWorkload.len_seed)
         value, sample = llama_cpu_sample(int(lens.mean()), max(args.steps, 3))
+        weak = args.workload == "llama3b_weak"
         cfg = {"workload": "cfg4 Llama-3.2-3B ragged-batch greedy decode",
-               "model": LlamaDecodeWorkload.model, "batch": 64,
+               "model": LlamaDecodeWorkload.model,
+               "global_batch": 64 * ranks.world if weak else 64,
                "ctx": "U[1024,8192] seed 4"}
-        scaling = "weak"
+        scaling = "weak" if weak else "strong"
     return {"impl": "reference", "metric": METRIC, "value": round(value, 4),
             "unit": "tokens/s", "n_gpus": ranks.world, "steps": args.steps,
             "warmup": args.warmup, "higher_is_better": True, "scaling": scaling,

@@ -14,6 +14,11 @@ of the B200 path:
   are appended to the cache, and attention reads the rounded values (both
   for decode and prefill). Activations, norms, attention outputs and logits
   stay fp32 -- the storage points of the B200 bf16 path.
+* ``act_dtype="bfloat16"`` (SmolLM2 only) additionally rounds every
+  projection input to bf16 where the B200 path stores it as a one-plane
+  bf16 operand: the RMSNorm outputs (both norms of a layer and the final
+  norm), the attention output and the SwiGLU output. The residual stream,
+  q and the logits stay fp32.
 """
 
 from __future__ import annotations
@@ -33,11 +38,12 @@ class SmolLM2Oracle:
     """One sequence of a SmolLM2 / Llama model (batch 1, like the reference)."""
 
     def __init__(self, config, weights, weight_dtype="float32",
-                 kv_dtype=None):
+                 kv_dtype=None, act_dtype="float32"):
         self.config = c = config
         self.wbf16 = weight_dtype in ("bfloat16", "bf16")
         kvd = kv_dtype or weight_dtype
         self.kvbf16 = kvd in ("bfloat16", "bf16")
+        self.actbf16 = act_dtype in ("bfloat16", "bf16")
         wb = self.wbf16
         self.n_layer = c.num_hidden_layers
         self.H = c.num_attention_heads
@@ -92,7 +98,7 @@ class SmolLM2Oracle:
         for i, Lw in enumerate(self.layers):
             cache = self.cache[i]
             residual = h
-            x = ops.rms_norm(h, Lw["ln1"], self.eps)
+            x = _store(ops.rms_norm(h, Lw["ln1"], self.eps), self.actbf16)
             q = ops.gemm(x, Lw["wq"])
             k = ops.gemm(x, Lw["wk"])
             v = ops.gemm(x, Lw["wv"])
@@ -115,14 +121,16 @@ class SmolLM2Oracle:
                     kf, vf = kh, vh
                 o = ops.gqa_attention(qh, kf, vf, H, Hkv, causal=True)
             o = o.reshape(H, seq, d).transpose(1, 0, 2).reshape(seq, H * d)
+            o = _store(o, self.actbf16)
             h = ops.add(ops.gemm(o, Lw["wo"]), residual)
             residual = h
-            x = ops.rms_norm(h, Lw["ln2"], self.eps)
+            x = _store(ops.rms_norm(h, Lw["ln2"], self.eps), self.actbf16)
             g = ops.gemm(x, Lw["wg"])
             u = ops.gemm(x, Lw["wu"])
-            h = ops.add(ops.gemm(ops.swiglu(g, u), Lw["wd"]), residual)
+            act = _store(ops.swiglu(g, u), self.actbf16)
+            h = ops.add(ops.gemm(act, Lw["wd"]), residual)
         self.cache_len = total
-        x = ops.rms_norm(h, self.ln_f, self.eps)
+        x = _store(ops.rms_norm(h, self.ln_f, self.eps), self.actbf16)
         return ops.gemm(x, self.lm_head_w).reshape(1, seq, -1)
 
     def generate(self, token_ids, max_new_tokens, max_seq=None):

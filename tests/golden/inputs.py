@@ -111,6 +111,72 @@ def llama_weights(shape: LlamaShape, seed=0, std=0.02):
     return w
 
 
+# Llama-3.2-3B (BASELINE configs 4/5), full depth
+LLAMA3B = LlamaShape(128256, 3072, 28, 24, 8, 8192, 8192, 1e-5, 500000.0)
+
+
+def llama_keys(shape: LlamaShape):
+    """HF state-dict keys of a Llama model, in ``llama_weights`` order, with
+    their shapes."""
+    n, v = shape.hidden_size, shape.vocab_size
+    nh, nkv = shape.num_attention_heads, shape.num_key_value_heads
+    dk, ffn = n // nh, shape.intermediate_size
+    out = [("model.embed_tokens.weight", (v, n))]
+    for i in range(shape.num_hidden_layers):
+        p = f"model.layers.{i}."
+        out += [(p + "self_attn.q_proj.weight", (nh * dk, n)),
+                (p + "self_attn.k_proj.weight", (nkv * dk, n)),
+                (p + "self_attn.v_proj.weight", (nkv * dk, n)),
+                (p + "self_attn.o_proj.weight", (n, nh * dk)),
+                (p + "mlp.gate_proj.weight", (ffn, n)),
+                (p + "mlp.up_proj.weight", (ffn, n)),
+                (p + "mlp.down_proj.weight", (n, ffn)),
+                (p + "input_layernorm.weight", (n,)),
+                (p + "post_attention_layernorm.weight", (n,))]
+    out.append(("model.norm.weight", (n,)))
+    return out
+
+
+class LazyLlamaWeights:
+    """Random-init N(0, std) weights of a Llama model, generated when a key
+    is read (so a 3B-parameter model never has to sit in host memory twice).
+
+    Tensor ``i`` of ``llama_keys`` is ``default_rng([seed, i])
+    .standard_normal`` times std; with ``bf16`` the matrices are rounded to
+    bf16 (the weights the bf16 path stores exactly). Every read of a key
+    gives the same values. Mapping-like: keys(), items(), [], in, len.
+    """
+
+    def __init__(self, shape: LlamaShape, seed=0, std=0.02, bf16=True):
+        self.shape, self.seed, self.std, self.bf16 = shape, seed, std, bf16
+        self._keys = llama_keys(shape)
+        self._index = {k: (i, s) for i, (k, s) in enumerate(self._keys)}
+
+    def __getitem__(self, key):
+        i, shp = self._index[key]
+        rng = np.random.default_rng([self.seed, i])
+        a = (rng.standard_normal(shp, dtype=F32) * F32(self.std)).astype(F32)
+        return bf16_round(a) if (self.bf16 and a.ndim == 2) else a
+
+    def __contains__(self, key):
+        return key in self._index
+
+    def __len__(self):
+        return len(self._keys)
+
+    def __iter__(self):
+        return iter(k for k, _ in self._keys)
+
+    def keys(self):
+        return [k for k, _ in self._keys]
+
+    def items(self):
+        return ((k, self[k]) for k, _ in self._keys)
+
+    def get(self, key, default=None):
+        return self[key] if key in self else default
+
+
 DIGEST_COLS = 4096   # logit columns kept per step by logits_digest
 DIGEST_TOPK = 32
 
