@@ -4,9 +4,10 @@
                     [--impl b200|reference] [--no-cpu-baseline]
 
 Prints ONE JSON line on rank 0. Under torchrun (N > 1) every rank drives
-its own GPU as an independent data-parallel replica; ranks meet only at host
-barriers (gloo) around the timed regions, and every time reported is the
-maximum over ranks.
+its own GPU (a data-parallel replica, or a tensor-parallel shard for
+llama3b_tp); ranks meet at host barriers around the timed regions over the
+package's TCP rendezvous (triton_llm.rendezvous, MASTER_PORT + 1), and every
+time reported is the maximum over ranks.
 
 Workloads:
   llama3b  (default) config 4: Llama-3.2-3B architecture, bf16 weights and
@@ -67,39 +68,33 @@ FALLBACK_HBM_GBS = 6650.0
 
 # ------------------------------------------------------------------ ranks ----
 class Ranks:
+    """This process's rank; ranks meet over the package's TCP rendezvous
+    (triton_llm.rendezvous: host barriers and max / sum of host numbers, no
+    torch.distributed)."""
+
     def __init__(self):
         self.rank = int(os.environ.get("RANK", "0"))
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
         self.local = int(os.environ.get("LOCAL_RANK", "0"))
-        self.pg = None
+        self.rdzv = None
         if self.world > 1:
-            import datetime
-            import torch.distributed as dist
-            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
-            self.pg = dist
+            from triton_llm.rendezvous import Rendezvous
+            self.rdzv = Rendezvous.from_env(timeout=600.0)
 
     def barrier(self):
-        if self.pg:
-            self.pg.barrier()
-
-    def _reduce(self, x: float, op) -> float:
-        if not self.pg:
-            return x
-        import torch
-        t = torch.tensor([x], dtype=torch.float64)
-        self.pg.all_reduce(t, op=op)
-        return float(t.item())
+        if self.rdzv:
+            self.rdzv.barrier()
 
     def max(self, x: float) -> float:
-        return self._reduce(x, self.pg.ReduceOp.MAX) if self.pg else x
+        return self.rdzv.reduce_max(x) if self.rdzv else x
 
     def sum(self, x: float) -> float:
-        return self._reduce(x, self.pg.ReduceOp.SUM) if self.pg else x
+        return self.rdzv.reduce_sum(x) if self.rdzv else x
 
     def close(self):
-        if self.pg:
-            self.pg.barrier()
-            self.pg.destroy_process_group()
+        if self.rdzv:
+            self.rdzv.barrier()
+            self.rdzv.close()
 
 
 # ----------------------------------------------------------------- clocks ----
@@ -449,7 +444,7 @@ class LlamaTPWorkload(LlamaDecodeWorkload):
         from smollm2_triton.engine import LlamaSession, LlamaWeights
         self.gpu = gpu
         r = self.ranks
-        self.tp = TPGroup(r.rank, r.world, r.local)
+        self.tp = TPGroup(r.rank, r.world, r.local, rdzv=r.rdzv)
         cfg = SmolLM2Config.from_pretrained(self.model)
         self.cfg = cfg
         self.wts = LlamaWeights(cfg, None, "bfloat16", seed=0, std=0.02, max_pos=self.S,
@@ -1264,6 +1259,8 @@ def run_b200(args, ranks):
             gpu.device_synchronize()
             ranks.barrier()   # no peer still writes into the slots
             wl.sess.close()
+    if getattr(wl, "tp", None) is not None:
+        wl.tp.close()         # NCCL communicator, on every rank
     import gc
     gc.collect()
     gpu.device_synchronize()

@@ -327,6 +327,35 @@ int tllm_p2p_destroy(void *ctx);
 int tllm_rmsnorm_p2p(float *h, const void *p2p, const float *w, void *y,
                      int y_dtype, int y_plane_rows, int M, int N, float eps,
                      tllm_stream_t stream);
+
+/*
+ * NCCL all-reduce of a tensor-parallel group (no counterpart in the
+ * reference, which runs on one device; its roadmap defers tensor
+ * parallelism, ROADMAP.md:121). NCCL is loaded on first use (libnccl.so.2,
+ * or TLLM_NCCL_LIB); TLLM_ERR_NCCL when it is missing. Rank 0 makes a
+ * unique id (tllm_nccl_unique_id_bytes bytes) and the caller hands it to
+ * every rank over its own host channel; each rank then calls
+ * tllm_nccl_init with its device current. Communicators are non-blocking:
+ * init, an all-reduce that cannot be enqueued at once, and destroy are
+ * polled for at most timeout_ms (<= 0: 120 s), after which the
+ * communicator is aborted and TLLM_ERR_TIMEOUT returned -- a rank that
+ * never joins or has died ends its peers' waits with an error, not a hang.
+ * tllm_nccl_all_reduce sums `count` F32 or BF16 elements of `buf` in place
+ * over the group, ordered on `stream` (NULL = library stream); it may be
+ * captured in a CUDA graph. tllm_nccl_check reports the communicator's
+ * asynchronous state (0 = healthy, 7 = in progress, other = an ncclResult_t
+ * error) for a host-side health check between steps.
+ */
+int tllm_nccl_version(int *version);
+int tllm_nccl_unique_id_bytes(void);
+int tllm_nccl_unique_id(void *id);
+int tllm_nccl_init(void **comm, int size, int rank, const void *id,
+                   int timeout_ms);
+int tllm_nccl_all_reduce(void *comm, void *buf, size_t count, int dtype,
+                         tllm_stream_t stream, int timeout_ms);
+int tllm_nccl_check(void *comm, int *state);
+int tllm_nccl_destroy(void *comm, int timeout_ms);
+int tllm_nccl_abort(void *comm);
 /* triton_llm/kernels/layernorm.py:79-152 (two-pass mean / variance);
  * output as for tllm_rmsnorm. */
 int tllm_layernorm(const float *x, const float *gamma, const float *beta,

@@ -199,44 +199,45 @@ def _session_greedy(wts, prompts, n_new, max_seq, act):
             for b, p in enumerate(prompts)]
 
 
-def _batched_vs_oracle(shape, w, prompts, n_new, max_seq, label):
-    """Both projection-input modes of the bf16 path against the oracle with
-    the same storage points: one bf16 plane vs bf16-rounded activations,
-    hi + lo planes vs fp32 activations. One set of device weights and one
-    oracle (its activation rounding switched between the runs)."""
+def _batched_vs_oracle(shape, w, prompts, n_new, max_seq, label, act):
+    """One projection-input mode of the bf16 path against the oracle with the
+    same storage points: one bf16 plane vs bf16-rounded activations, hi + lo
+    planes vs fp32 activations."""
     from smollm2_triton import SmolLM2Config
     from smollm2_triton.engine import LlamaWeights
     cfg = SmolLM2Config(**shape.config_kwargs())
     wts = LlamaWeights(cfg, w, "bfloat16", max_pos=max_seq)
-    o = omodels.SmolLM2Oracle(cfg, w, weight_dtype="bfloat16")
-    for act in ("bfloat16", "split"):
-        got = _session_greedy(wts, prompts, n_new, max_seq, act)
-        o.actbf16 = _oracle_act(act) == "bfloat16"
-        for b, ((gt, gl), p) in enumerate(zip(got, prompts)):
-            wt, wl = o.generate(np.array([p], np.int32), n_new)
-            upto = _assert_tokens(gt, wt[0], wl, f"{label} act={act} batch row {b}")
-            steps = max(upto - len(p), 1)
-            np.testing.assert_allclose(gl[:steps], wl[:steps], atol=2e-2)
+    got = _session_greedy(wts, prompts, n_new, max_seq, act)
+    del wts
+    o = omodels.SmolLM2Oracle(cfg, w, weight_dtype="bfloat16", act_dtype=_oracle_act(act))
+    for b, ((gt, gl), p) in enumerate(zip(got, prompts)):
+        wt, wl = o.generate(np.array([p], np.int32), n_new)
+        upto = _assert_tokens(gt, wt[0], wl, f"{label} act={act} batch row {b}")
+        steps = max(upto - len(p), 1)
+        np.testing.assert_allclose(gl[:steps], wl[:steps], atol=2e-2)
 
 
-def test_smol135m_batched_graph_32_steps_vs_oracle(gpu):
+@pytest.mark.parametrize("act", ["split", "bfloat16"])
+def test_smol135m_batched_graph_32_steps_vs_oracle(gpu, act):
     """Config 3 geometry on the benchmark's path (ragged batch of 4, graph
     replay): 32 greedy tokens per sequence identical to the oracle."""
     w = inputs.round_linear_weights_bf16(inputs.llama_weights(inputs.SMOL_135M, 0))
     rng = np.random.default_rng(6)
     prompts = [rng.integers(0, 49152, n).tolist() for n in (1, 9, 40, 17)]
-    _batched_vs_oracle(inputs.SMOL_135M, w, prompts, 32, 128, "SmolLM2-135M")
+    _batched_vs_oracle(inputs.SMOL_135M, w, prompts, 32, 128, "SmolLM2-135M", act)
 
 
-def test_llama3b_full_depth_32_steps_vs_oracle(gpu):
+@pytest.mark.parametrize("act", ["split", "bfloat16"])
+def test_llama3b_full_depth_32_steps_vs_oracle(gpu, act):
     """Config 4 geometry at full depth (Llama-3.2-3B: 28 layers, 24/8 heads,
-    head_dim 128, vocab 128256), bf16, on the benchmark's path (ragged
-    batch of 2, graph replay): 32 greedy tokens per sequence identical to
-    the oracle with the same storage points, logits within 2e-2."""
+    head_dim 128, vocab 128256), bf16 weights and cache, on the benchmark's
+    path (ragged batch of 2, graph replay): 32 greedy tokens per sequence
+    identical to the oracle with the same storage points, logits within
+    2e-2."""
     w = inputs.LazyLlamaWeights(inputs.LLAMA3B, seed=0)
     rng = np.random.default_rng(4)
     prompts = [rng.integers(0, 128256, n).tolist() for n in (5, 11)]
-    _batched_vs_oracle(inputs.LLAMA3B, w, prompts, 32, 64, "Llama-3.2-3B")
+    _batched_vs_oracle(inputs.LLAMA3B, w, prompts, 32, 64, "Llama-3.2-3B", act)
 
 
 @pytest.mark.parametrize("mode", ["float32", "bf16w-split", "bf16w", "bf16w-fused-mlp"])

@@ -4,7 +4,9 @@
   plus an all-reduce of the o / down partial sums reproduces the oracle's
   full forward pass -- the TP math, independent of the GPU.
 * GPU, 2 ranks (skipped with fewer than 2 GPUs): the TP engine on the
-  Llama-3.2-3B 2-layer slice against the reference's own logits and tokens.
+  Llama-3.2-3B 2-layer slice against the reference's own logits and tokens,
+  run as two plain processes over the package's rendezvous and NCCL binding
+  (no torch in them).
 """
 
 from __future__ import annotations
@@ -109,15 +111,16 @@ _GPU_TP = r"""
 import os, sys, json
 import numpy as np
 sys.path[:0] = [os.path.join(os.getcwd(), p) for p in ("triton-llm_b200", ".", "tests/golden")]
-import torch, torch.distributed as dist
 import inputs
 rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
-dist.init_process_group("nccl", device_id=torch.device("cuda", rank))
 from triton_llm import gpu
+from triton_llm.rendezvous import Rendezvous
 from triton_llm.tp import TPGroup
 from smollm2_triton import SmolLM2Config
 from smollm2_triton.engine import LlamaSession, LlamaWeights
-tp = TPGroup(rank, world, rank)
+assert "torch" not in sys.modules
+rdzv = Rendezvous.from_env(timeout=300)
+tp = TPGroup(rank, world, rank, rdzv=rdzv, timeout_ms=60000)
 g = np.load("tests/golden/llama3b_2l_slice.npz")
 w = inputs.round_linear_weights_bf16(inputs.llama_weights(inputs.LLAMA3B_2L, 0))
 cfg = SmolLM2Config(**inputs.LLAMA3B_2L.config_kwargs())
@@ -149,14 +152,16 @@ for p2p in (True, False):
     s2.close()
 same = runs[0][0] == runs[1][0]
 p2p_err = float(np.abs(runs[0][1] - runs[1][1]).max())
+healthy = tp.healthy()
 if rank == 0:
     print(json.dumps({"tokens": toks, "want": g["tokens"].tolist(), "err": err,
-                      "p2p_same_tokens": same, "p2p_err": p2p_err,
-                      "dev_err": gpu.device_error()}))
+                      "p2p_same_tokens": same, "p2p_err": p2p_err, "healthy": healthy,
+                      "dev_err": gpu.device_error(), "torch": "torch" in sys.modules}))
 tp.barrier()
 sess.close()
 del sess
-dist.destroy_process_group()
+tp.close()
+rdzv.close()
 """
 
 
@@ -168,6 +173,25 @@ def _gpu_count():
         return 0
 
 
+def _launch_ranks(script, world, timeout_s=600):
+    """One process per GPU (rank r on device r), meeting over the package's
+    TCP rendezvous; no torchrun and no torch.distributed. NVLS is off (the
+    peer path uses plain peer loads and stores; NCCL must not bind NVLink
+    multicast objects in a test)."""
+    port = _free_port()
+    procs = []
+    for r in range(world):
+        env = dict(os.environ, RANK=str(r), WORLD_SIZE=str(world), LOCAL_RANK=str(r),
+                   MASTER_ADDR="127.0.0.1", TLLM_RDZV_PORT=str(port),
+                   NCCL_NVLS_ENABLE="0")
+        procs.append(subprocess.Popen(
+            ["timeout", "-k", "30", str(timeout_s), sys.executable, str(script)],
+            cwd=str(REPO), env=env, stdout=subprocess.PIPE, stderr=subprocess.PIPE,
+            text=True))
+    outs = [p.communicate() for p in procs]
+    return [p.returncode for p in procs], outs
+
+
 @pytest.mark.gpu
 def test_tp2_engine_matches_reference(tmp_path):
     if _gpu_count() < 2:
@@ -175,15 +199,12 @@ def test_tp2_engine_matches_reference(tmp_path):
     import json
     script = tmp_path / "tp2.py"
     script.write_text(_GPU_TP)
-    cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run",
-           "--nnodes=1", "--nproc-per-node=2", "--master-addr", "127.0.0.1",
-           "--master-port", str(_free_port()), str(script)]
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
-    r = subprocess.run(cmd, cwd=str(REPO), capture_output=True, text=True, env=env)
-    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
-    line = [ln for ln in r.stdout.splitlines() if ln.startswith("{")][-1]
+    rcs, outs = _launch_ranks(script, 2)
+    assert rcs == [0, 0], "\n".join(o[0][-2000:] + o[1][-4000:] for o in outs)
+    line = [ln for ln in outs[0][0].splitlines() if ln.startswith("{")][-1]
     d = json.loads(line)
     assert d["tokens"] == d["want"], d
     assert d["err"] < 1e-3, d
     assert d["p2p_same_tokens"] and d["p2p_err"] < 1e-3, d
-    assert d["dev_err"] == 0, d
+    assert d["dev_err"] == 0 and d["healthy"], d
+    assert not d["torch"], "the tensor-parallel path imported torch"

@@ -20,7 +20,8 @@ void clear_error();
 
 // Fault injection for host-side failure tests: TLLM_FAULT_INJECT="malloc:N"
 // makes the N-th tllm_malloc of the process fail (N counts from 1);
-// "launch:N" makes the N-th kernel entry point fail before it launches.
+// "launch:N" makes the N-th kernel entry point fail before it launches;
+// "nccl:N" makes the N-th NCCL call (unique id, init, all-reduce) fail.
 bool inject_fault(const char *site);
 
 // The library stream of the current device (created lazily).
@@ -388,6 +389,13 @@ __device__ __forceinline__ void griddep_wait() {
 }
 __device__ __forceinline__ void griddep_launch() {
   asm volatile("griddepcontrol.launch_dependents;" :::);
+}
+
+// Bulk prefetch of `bytes` (a multiple of 16) at global address `src`
+// (16-byte aligned) into L2; no completion to wait for.
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes)
+               : "memory");
 }
 
 // Launch `kern` with programmatic stream serialization (unless disabled):

@@ -28,8 +28,8 @@ void set_error(const char *fmt, ...) {
 void clear_error() { g_err.clear(); }
 
 // ---- fault injection -------------------------------------------------------
-static std::atomic<long> g_site_count[2];
-static long g_fault_at[2] = {-1, -1};
+static std::atomic<long> g_site_count[3];
+static long g_fault_at[3] = {-1, -1, -1};
 static std::once_flag g_fault_once;
 
 static void parse_fault_env() {
@@ -48,6 +48,7 @@ static void parse_fault_env() {
       long n = atol(item.c_str() + colon + 1);
       if (site == "malloc") g_fault_at[0] = n;
       if (site == "launch") g_fault_at[1] = n;
+      if (site == "nccl") g_fault_at[2] = n;
     }
     if (comma == std::string::npos) break;
     pos = comma + 1;
@@ -56,7 +57,7 @@ static void parse_fault_env() {
 
 bool inject_fault(const char *site) {
   std::call_once(g_fault_once, parse_fault_env);
-  int idx = (site[0] == 'm') ? 0 : 1;
+  int idx = (site[0] == 'm') ? 0 : (site[0] == 'n' ? 2 : 1);
   if (g_fault_at[idx] < 0) return false;
   long n = ++g_site_count[idx];
   return n == g_fault_at[idx];

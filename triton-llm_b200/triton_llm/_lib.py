@@ -110,6 +110,15 @@ SIGNATURES: dict[str, list] = {
     "tllm_p2p_create": [_i, _i, _i, ctypes.POINTER(_vp), _vp],
     "tllm_p2p_open": [_vp, _i, _vp],
     "tllm_p2p_destroy": [_vp],
+    # NCCL (tensor-parallel all-reduce)
+    "tllm_nccl_version": [_pi],
+    "tllm_nccl_unique_id_bytes": [],
+    "tllm_nccl_unique_id": [_vp],
+    "tllm_nccl_init": [ctypes.POINTER(ctypes.c_void_p), _i, _i, _vp, _i],
+    "tllm_nccl_all_reduce": [_vp, _vp, _sz, _i, _vp, _i],
+    "tllm_nccl_check": [_vp, _pi],
+    "tllm_nccl_destroy": [_vp, _i],
+    "tllm_nccl_abort": [_vp],
     "tllm_layernorm": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp],
     "tllm_split_bf16": [_vp, _vp, _i, _i, _i, _i, _vp],
     "tllm_embedding": [_vp, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _vp],
