@@ -212,7 +212,7 @@ class LlamaDecodeWorkload:
     name = "llama3b"
     scaling = "strong"
     dtype = "bf16"
-    act = "bfloat16"
+    act = "split"
     model = "Llama-3.2-3B-Instruct"
     global_batch = 64        # per_rank = global_batch / N
     per_rank = None          # fixed per-rank batch instead (weak scaling)
@@ -1329,8 +1329,9 @@ def main():
     ap.add_argument("--workload", default="llama3b", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--act", default="bfloat16", choices=["bfloat16", "split"],
-                    help="projection input format of the bf16 path")
+    ap.add_argument("--act", default="split", choices=["bfloat16", "split"],
+                    help="projection input format of the bf16 path (hi + lo planes, "
+                         "the default, or one bf16 plane)")
     args = ap.parse_args()
     LlamaDecodeWorkload.act = args.act
     LlamaTPWorkload.act = args.act

@@ -391,13 +391,6 @@ __device__ __forceinline__ void griddep_launch() {
   asm volatile("griddepcontrol.launch_dependents;" :::);
 }
 
-// Bulk prefetch of `bytes` (a multiple of 16) at global address `src`
-// (16-byte aligned) into L2; no completion to wait for.
-__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes)
-               : "memory");
-}
-
 // Launch `kern` with programmatic stream serialization (unless disabled):
 // its CTAs may become resident while the previous kernel on the stream is
 // still running, so the kernel must call griddep_wait() before it reads or

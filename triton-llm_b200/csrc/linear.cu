@@ -271,9 +271,6 @@ struct TcParams {
   uint32_t tcols;  // TMEM columns allocated (power of two >= 32)
   int w_tiled;   // TLLM_BF16_TILED weights: tile (nt, kc) = rows
                  // (nt * k_chunks + kc) * 128 .. +127 of a (., 64) view
-  int l2pf;      // tiled weights: chunks after the first ring-full that the
-                 // producer prefetches into L2 at start (0 = none)
-  const uint8_t *wbase;   // the tiled weights (for the L2 prefetch)
 };
 
 // one activation stage: the bf16 planes (1 or 2) of an MT x 64 tile
@@ -366,14 +363,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // previous kernel
       asm volatile("prefetch.tensormap [%0];" ::"l"(&tw) : "memory");
       const uint64_t pol = l2_policy_evict_first();
-      if (p.l2pf > 0 && p.w_tiled && nch > WS) {
-        // this CTA's chunks after the first ring-full are contiguous (one
-        // weight tile row, consecutive k): one bulk L2 prefetch keeps HBM
-        // busy while the MMAs still wait for the previous kernel
-        const int n = min(nch - WS, p.l2pf);
-        bulk_prefetch_l2(p.wbase + ((size_t)(nt * p.k_chunks + kc0 + WS) * kTcW),
-                         (uint32_t)n * kTcW);
-      }
       int c = 0;
       for (; c < nch; ++c) {
         const int s = c % WS;
@@ -1662,11 +1651,6 @@ int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
     p.tcols = cols;
   }
   p.w_tiled = tiled ? 1 : 0;
-  {
-    static const int l2pf = env_int("TLLM_LINEAR_L2PF", 0);
-    p.l2pf = tiled ? l2pf : 0;
-    p.wbase = static_cast<const uint8_t *>(w);
-  }
   dim3 grid(pl.n_tiles, S, pl.m_tiles);
   if (PL == 2) return launch_tc_mt<2>(p, pl.MT, tw, tx, grid, pl.smem, st);
   return launch_tc_mt<1>(p, pl.MT, tw, tx, grid, pl.smem, st);

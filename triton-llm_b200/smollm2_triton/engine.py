@@ -25,8 +25,9 @@ reference's (n_kv_head, max_seq, d_k) (model.py:219-225) with a batch axis.
 
 Activation buffers that only feed projections (the normed x, the attention
 output, the SwiGLU output) are kept in the tensor-core operand format when
-the weights are bf16 -- bf16 (default) or hi + lo bf16 planes
-(act_dtype="split", ~16 mantissa bits) -- and the kernels that produce them
+the weights are bf16 -- hi + lo bf16 planes (act_dtype="split", the
+default: ~16 mantissa bits, close to the reference's fp32 activations) or
+one bf16 plane (act_dtype="bfloat16") -- and the kernels that produce them
 write that format directly. The residual stream h, q and the logits stay
 fp32.
 """
@@ -173,7 +174,7 @@ class LlamaSession:
 
     def __init__(self, wts: LlamaWeights, batch: int, max_seq: int,
                  max_prefill_rows: int = 0, attn_budget_bytes: int = 256 << 20,
-                 kv_dtype: str | None = None, act_dtype: str = "bfloat16",
+                 kv_dtype: str | None = None, act_dtype: str = "split",
                  tp=None, p2p: bool | None = None):
         self.w = wts
         # tensor parallelism: o / down produce partial sums that ``tp``

@@ -37,9 +37,12 @@ class SmolLM2ForCausalLM:
         ``config.torch_dtype``). Activations and accumulation are fp32.
     kv_dtype : "float32" | "bfloat16" | None
         KV cache precision when it should differ from ``dtype``.
-    act_dtype : "bfloat16" | "split"
-        Projection inputs of the bf16 path: bf16, or hi + lo bf16 planes
-        (~16 mantissa bits, twice the tensor-core work).
+    act_dtype : "split" | "bfloat16"
+        Projection inputs of the bf16 path: hi + lo bf16 planes (default:
+        ~16 mantissa bits, close to the reference's fp32 activations, twice
+        the tensor-core work), or one bf16 plane (faster; its rounding can
+        flip a greedy token where the reference's top two logits are within
+        ~1e-5).
     """
 
     @classmethod
@@ -60,7 +63,7 @@ class SmolLM2ForCausalLM:
         return cls(config, load_state_dict(path), **kw)
 
     def __init__(self, config: SmolLM2Config, weights: dict, dtype: str | None = None,
-                 kv_dtype: str | None = None, act_dtype: str = "bfloat16"):
+                 kv_dtype: str | None = None, act_dtype: str = "split"):
         self.config = config
         if config.n_head % config.n_kv_head != 0:
             raise ValueError(
