@@ -55,6 +55,10 @@ if "reference" in sys.argv:
     for _v in ("OMP_NUM_THREADS", "OPENBLAS_NUM_THREADS", "MKL_NUM_THREADS"):
         os.environ[_v] = _n
 
+# NCCL prints its version line on stdout at init; the bench's stdout is one
+# JSON line (NCCL_DEBUG set explicitly is kept).
+os.environ.setdefault("NCCL_DEBUG", "NONE")
+
 import numpy as np  # noqa: E402
 
 REPO = Path(__file__).resolve().parent
