@@ -390,3 +390,30 @@ def test_gpt2_small_slice_matches_reference(gpu, golden):
     toks, logits = _gpt2_run(m, prompt, 2)
     np.testing.assert_array_equal(toks, g["tokens"])
     np.testing.assert_allclose(logits, g["logits"], atol=1e-4)
+
+
+def _digest_compare(logits, g, atol):
+    """Per-step logits (steps, V) against a reference digest
+    (inputs.logits_digest): full first and last rows, every step at the
+    digest's columns and at the reference's top-32 indices."""
+    np.testing.assert_allclose(logits[0], g["first"], atol=atol)
+    np.testing.assert_allclose(logits[-1], g["last"], atol=atol)
+    np.testing.assert_allclose(logits[:, g["cols"]], g["at_cols"], atol=atol)
+    np.testing.assert_allclose(np.take_along_axis(logits, g["top_idx"], axis=1),
+                               g["top_val"], atol=atol)
+
+
+def test_gpt2_cfg1_32_steps_match_reference(gpu, golden):
+    """BASELINE config 1 as stated (GPT-2 small, fp32, N(0,0.02) seed-0
+    weights, 32-token prompt, 32 greedy steps) against the reference's own
+    run of the same inputs (its Triton kernels under the interpreter): the
+    64 tokens identical and the logits of every step within 1e-4."""
+    g = golden("gpt2_cfg1")
+    m = _gpt2(inputs.GPT2_SMALL, inputs.gpt2_weights(inputs.GPT2_SMALL, 0))
+    prompt = g["tokens"][:32].tolist()
+    toks, logits = _gpt2_run(m, prompt, 32)
+    same = int(np.sum(np.cumprod(toks[32:] == g["tokens"][32:])))
+    print(f"GPT-2 small config 1: tokens identical for {same}/32 steps "
+          f"(smallest reference top-2 gap {float(g['gap'].min()):.2e})")
+    np.testing.assert_array_equal(toks, g["tokens"])
+    _digest_compare(logits, g, 1e-4)
