@@ -201,3 +201,19 @@ def test_gpt2_small_slice(golden):
     toks, logits = orc.generate(prompt, 2)
     np.testing.assert_array_equal(toks[0], g["tokens"])
     np.testing.assert_allclose(logits, g["logits"], atol=1e-4)
+
+
+def test_gpt2_cfg1_32_steps(golden):
+    """BASELINE config 1 (32-token prompt, 32 greedy steps): the oracle
+    reproduces the reference's own tokens and, at the digest's columns and
+    top-32 indices, its logits."""
+    g = golden("gpt2_cfg1")
+    shape = inputs.GPT2_SMALL
+    orc = models.GPT2Oracle(_Cfg(**shape.config_kwargs()), inputs.gpt2_weights(shape, 0))
+    toks, logits = orc.generate(g["tokens"][:32].tolist(), 32)
+    np.testing.assert_array_equal(toks[0], g["tokens"])
+    np.testing.assert_allclose(logits[0], g["first"], atol=1e-4)
+    np.testing.assert_allclose(logits[-1], g["last"], atol=1e-4)
+    np.testing.assert_allclose(logits[:, g["cols"]], g["at_cols"], atol=1e-4)
+    np.testing.assert_allclose(np.take_along_axis(logits, g["top_idx"], axis=1),
+                               g["top_val"], atol=1e-4)
