@@ -274,11 +274,7 @@ class LlamaDecodeWorkload:
         self.wts = LlamaWeights(cfg, None, "bfloat16", seed=0, std=0.02, max_pos=self.S)
         self.sess = LlamaSession(self.wts, self.B, self.S, act_dtype=self.act)
         s = self.sess
-        _lib.call("tllm_fill_random", s.kv_arena.ptr, _lib.BF16,
-                  int(np.prod(s.kv_arena.shape)), 1000 + self.ranks.rank, 1.0, None)
-        rng = np.random.default_rng(100)
-        all_ids = rng.integers(0, cfg.vocab_size, len(self.all_lens)).astype(np.int32)
-        self.ids0 = all_ids[self.idx]
+        self.fill_context()
         self.reset()
         self.launches_per_step = s.decode_step(True)
         gpu.device_synchronize()
@@ -288,6 +284,17 @@ class LlamaDecodeWorkload:
         self.out_host = gpu.pinned_empty((self.B,), np.int32)
         self.h2d = self.B * 4
         self.d2h = self.B * 4
+
+    def fill_context(self):
+        """The cached contexts: K/V filled N(0, 1) on the device (a
+        counter-based generator) and random next tokens."""
+        from triton_llm import _lib
+        s = self.sess
+        _lib.call("tllm_fill_random", s.kv_arena.ptr, _lib.BF16,
+                  int(np.prod(s.kv_arena.shape)), 1000 + self.ranks.rank, 1.0, None)
+        rng = np.random.default_rng(100)
+        all_ids = rng.integers(0, self.cfg.vocab_size, len(self.all_lens)).astype(np.int32)
+        self.ids0 = all_ids[self.idx]
 
     def reset(self):
         self.sess.set_state(self.lens, self.ids0)
@@ -492,32 +499,64 @@ class LlamaTPWorkload(LlamaDecodeWorkload):
 
 
 class SmolDecodeWorkload(LlamaDecodeWorkload):
-    """SmolLM2-135M decode, 32 sequences per GPU (bf16).
-    The configuration's run is a 512-token prompt and 256 greedy steps per
-    sequence (mean context 640); here every sequence starts at context 640
-    with its K/V filled N(0, 1), and the K timed steps continue from there."""
+    """SmolLM2-135M, 32 sequences per GPU (bf16): every
+    sequence's 512-token prompt (uniform ids, seed 3) runs through the
+    model's own prefill (timed apart and reported as ``prefill``), then K
+    greedy decode steps continue from position 512 (the configuration's 256
+    steps: --steps 256)."""
 
     name = "smol135m"
     scaling = "weak"
     model = "SmolLM2-135M"
     per_rank = 32
-    lo, hi = 640, 640
+    lo, hi = 512, 512
+    prompt_seed = 3
+
+    def fill_context(self):
+        from triton_llm import gpu
+        s = self.sess
+        rng = np.random.default_rng(self.prompt_seed + self.ranks.rank)
+        prompts = rng.integers(0, self.cfg.vocab_size, (self.B, self.lo)).astype(np.int32)
+        s.prefill(prompts)                      # warm: buffers, kernels
+        gpu.device_synchronize()
+        e0, e1 = gpu.Event(), gpu.Event()
+        t = time.perf_counter()
+        e0.record()
+        s.prefill(prompts)
+        e1.record()
+        gpu.device_synchronize()
+        wall = time.perf_counter() - t
+        ms = e0.elapsed_ms(e1)
+        toks = self.B * self.lo
+        self.prefill_info = {
+            "tokens": toks, "device_ms": round(ms, 3), "wall_ms": round(wall * 1e3, 3),
+            "tokens_per_s": round(toks / (ms / 1e3), 1),
+            "what": f"{self.B} prompts x {self.lo} tokens through the model's prefill "
+                    "(embedding, 30 layers with the causal prefill attention kernel, "
+                    "final norm, lm_head of the last rows), host argmax; not part of "
+                    "the decode tokens/s"}
+        self.ids0 = s.ids.to_numpy().astype(np.int32)
 
     def config(self):
         w = self.ranks.world
-        return {"workload": "cfg3 SmolLM2-135M batched greedy decode",
-                "model": self.model, "layers": 30, "hidden": 576,
-                "heads": "9 q / 3 kv, head_dim 64", "ffn": 1536, "vocab": 49152,
-                "batch_per_gpu": self.B, "global_batch": self.B * w,
-                "ctx": "640 for every sequence (the mean of a 512-token prompt + 256 steps)",
-                "weights": "random N(0,0.02) bf16 (seed 0), tied embeddings",
-                "projection_inputs": ("bf16 hi/lo planes" if self.act == "split" else "bf16"),
-                "kv_cache": f"bf16 (B, 3, {self.S}, 64) per layer, filled N(0,1)",
-                "parallelism": f"dp{w} (independent replicas, no collective)",
-                "timed": "K steps, each one CUDA-graph replay of the full decode step "
-                         "(embedding, 30 layers, norm, lm_head, argmax)",
-                "l2": "inputs smaller than L2 (269 MB weights + ~0.5 GB KV per step "
-                      "exceed it together; no flush)"}
+        c = {"workload": "cfg3 SmolLM2-135M batched greedy decode",
+             "model": self.model, "layers": 30, "hidden": 576,
+             "heads": "9 q / 3 kv, head_dim 64", "ffn": 1536, "vocab": 49152,
+             "batch_per_gpu": self.B, "global_batch": self.B * w,
+             "prompt": f"{self.lo} uniform ids per sequence (seed {self.prompt_seed}), "
+                       "prefilled through the model",
+             "ctx": f"{self.lo} .. {self.lo} + K during the timed steps",
+             "weights": "random N(0,0.02) bf16 (seed 0), tied embeddings",
+             "projection_inputs": ("bf16 hi/lo planes" if self.act == "split" else "bf16"),
+             "kv_cache": f"bf16 (B, 3, {self.S}, 64) per layer",
+             "parallelism": f"dp{w} (independent replicas, no collective)",
+             "timed": "K steps, each one CUDA-graph replay of the full decode step "
+                      "(embedding, 30 layers, norm, lm_head, argmax)",
+             "l2": "inputs smaller than L2 (269 MB weights + ~0.4 GB KV per step "
+                   "exceed it together; no flush)"}
+        if getattr(self, "prefill_info", None):
+            c["prefill"] = self.prefill_info
+        return c
 
     def kernel_roofline(self, gpu, peak):
         r = super().kernel_roofline(gpu, peak)

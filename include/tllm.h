@@ -167,6 +167,30 @@ int tllm_gqa_decode(const float *q, const void *k_cache, const void *v_cache,
                     tllm_stream_t stream);
 
 /*
+ * Causal GQA prefill attention over the preallocated cache. Replaces the
+ * prefill attention of smollm2_triton/model.py:318-348 (attention_gqa with
+ * causal=True at :341-343; mask of triton_llm/kernels/attention_gqa.py:
+ * 97-119) for every prompt of a batch in one launch. blocks holds n_blocks
+ * rows of four int32 (16-byte aligned): first row, rows (1..64), cache
+ * sequence, first position; row first_row + i is the query at position
+ * first_position + i and attends cache rows [0, first_position + i] of that
+ * sequence (its K/V must already be in the cache: the QKV epilogue writes
+ * them). Rows of a block are consecutive positions of one sequence; a
+ * prompt of L rows takes ceil(L / 64) blocks. q / out as for tllm_gqa_rows.
+ * bf16 caches with head_dim 64 or 128 (else TLLM_ERR_UNSUPPORTED: use
+ * tllm_gqa_rows). A block that is out of range (rows, positions past
+ * max_seq, sequence past cache_batch) is skipped and sets bit 2 of the
+ * device error word. No scratch.
+ */
+int tllm_gqa_prefill(const float *q, long q_row_stride, long q_head_stride,
+                     const void *k_cache, const void *v_cache, int kv_dtype,
+                     const int32_t *blocks, int n_blocks, void *out,
+                     int out_dtype, long out_plane_rows, long out_row_stride,
+                     long out_head_stride, int n_head, int n_kv_head,
+                     int head_dim, int cache_batch, int max_seq,
+                     float sm_scale, tllm_stream_t stream);
+
+/*
  * GQA attention for query rows that each read a prefix of one cached
  * sequence: row r attends to the first row_len[r] cache rows of sequence
  * row_seq[r] (row_seq NULL: sequence r). q and out of (row r, head h) are at

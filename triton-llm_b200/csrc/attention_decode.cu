@@ -24,6 +24,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "mma_sync.cuh"
 
 namespace tllm {
 
@@ -64,13 +65,6 @@ struct Vec<__nv_bfloat16> {
     f[7] = bf16hi(v.w);
   }
 };
-
-// 2^x with the MUFU instruction (relative error ~2^-22; -inf -> +0).
-__device__ __forceinline__ float fast_exp2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
 
 struct DecodeParams {
   const float *q;        // row b, head h at q + b * q_sb + h * q_sh
@@ -462,42 +456,6 @@ __global__ void __launch_bounds__(kThreads)
 // arrive through TMA with 128-byte swizzle (64-dim sub-tiles of 128 B rows),
 // which makes the ldmatrix reads bank-conflict free.
 // --------------------------------------------------------------------------
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0,
-                                        uint32_t &r1, uint32_t &r2,
-                                        uint32_t &r3) {
-  asm volatile(
-      "ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-      : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-      : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0,
-                                          uint32_t &r1, uint32_t &r2,
-                                          uint32_t &r3) {
-  asm volatile(
-      "ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-      : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-      : "r"(addr));
-}
-__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4],
-                                         uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
-      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-// (x0, x1) -> bf16x2 with x0 in the low half (round to nearest even)
-__device__ __forceinline__ uint32_t pack_bf16x2(float x0, float x1) {
-  uint32_t r;
-  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(x1), "f"(x0));
-  return r;
-}
-// x = hi + lo with hi, lo bf16 pairs
-__device__ __forceinline__ void split_bf16x2(float x0, float x1, uint32_t &hi,
-                                             uint32_t &lo) {
-  hi = pack_bf16x2(x0, x1);
-  lo = pack_bf16x2(x0 - bf16lo(hi), x1 - bf16hi(hi));
-}
 // transpose of the 8 x 8 bf16 matrix held in the C / A fragment layout
 // (lane l: row l / 4, columns 2 (l % 4), + 1)
 __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
@@ -898,11 +856,13 @@ __global__ void __launch_bounds__(kThreads)
 // --------------------------------------------------------------------------
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() { return tensor_map_encoder(); }
 
+}  // namespace
+
 // Tensor map over a KV cache viewed as (planes, max_seq, D) with a box of
 // (rows x box_inner) elements; swizzle128 selects the 128-byte swizzle.
 int make_kv_map(CUtensorMap *m, const void *base, int dtype, int D,
-                int max_seq, long planes, int rows, int box_inner = 0,
-                bool swizzle128 = false) {
+                int max_seq, long planes, int rows, int box_inner,
+                bool swizzle128) {
   auto fn = encode_fn();
   if (!fn) {
     set_error("cuTensorMapEncodeTiled is not available from the driver");
@@ -930,6 +890,8 @@ int make_kv_map(CUtensorMap *m, const void *base, int dtype, int D,
   }
   return TLLM_OK;
 }
+
+namespace {
 
 int pick_group_tile(int group) {
   for (int g = 8; g >= 1; --g)

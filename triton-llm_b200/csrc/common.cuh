@@ -61,6 +61,16 @@ int *device_error_ptr();
 
 }  // namespace tllm
 
+struct CUtensorMap_st;
+namespace tllm {
+// Tensor map over a KV cache viewed as (planes, max_seq, D) with a box of
+// (rows x box_inner) elements (box_inner 0 = D); swizzle128 selects the
+// 128-byte swizzle (attention_decode.cu).
+int make_kv_map(CUtensorMap_st *m, const void *base, int dtype, int D,
+                int max_seq, long planes, int rows, int box_inner = 0,
+                bool swizzle128 = false);
+}  // namespace tllm
+
 #define TLLM_CHECK_ARG(cond, ...)                 \
   do {                                            \
     if (!(cond)) {                                \

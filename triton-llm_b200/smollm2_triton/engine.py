@@ -39,7 +39,8 @@ import os
 import numpy as np
 
 from triton_llm import gpu, _lib, shard
-from triton_llm.kernels import gqa_rows, DecodeWorkspace
+from triton_llm.kernels import gqa_rows, gqa_prefill, prefill_blocks, DecodeWorkspace
+from triton_llm.kernels.attention_prefill import prefill_supported
 from triton_llm.kernels.linear import (Linear, LinearWorkspace, linear, qkv_rows,
                                        swiglu_rows)
 from triton_llm.kernels.rms_norm import (rms_norm_add_rows, rms_norm_p2p_rows,
@@ -223,6 +224,7 @@ class LlamaSession:
                                        _lib.BF16 if self.kv_bf16 else _lib.F32)
         self.lin_ws = LinearWorkspace(wts.linear_shapes(B))
         self._prefill_rows = 0
+        self._p_blocks, self._p_nblocks = None, 0
         if max_prefill_rows:
             self._prefill_buffers(max_prefill_rows, attn_budget_bytes)
         self.graph = None
@@ -295,10 +297,15 @@ class LlamaSession:
             k_cache=k, v_cache=v, n_head=w.H, n_kv_head=w.Hkv, head_dim=w.D,
             lens_out=lens if decode else None))
         # decode: row b reads its own sequence for lens[b] keys (set by the
-        # QKV epilogue); prefill: row r reads its sequence's causal prefix
-        gqa_rows(q, k, v, row_seq, lens if decode else row_len, attn, M, w.H,
-                 w.H * w.D, w.D, w.H * w.D, w.D, self.S if decode else (max_len or self.S),
-                 workspace=attn_ws)
+        # QKV epilogue); prefill: row r reads its sequence's causal prefix,
+        # in blocks of 64 rows (tllm_gqa_prefill) where the cache allows
+        if not decode and self._p_blocks is not None:
+            gqa_prefill(q, k, v, self._p_blocks, self._p_nblocks, attn, w.H,
+                        w.H * w.D, w.D, w.H * w.D, w.D)
+        else:
+            gqa_rows(q, k, v, row_seq, lens if decode else row_len, attn, M, w.H,
+                     w.H * w.D, w.D, w.H * w.D, w.D,
+                     self.S if decode else (max_len or self.S), workspace=attn_ws)
         if part is None and decode and self.mlp_ws is not None:
             _mlp.mlp_block(attn, L["o"], h, L["ln2"], x, L["gu"], act, L["down"], M,
                            w.eps, self.mlp_ws)
@@ -390,6 +397,11 @@ class LlamaSession:
         self.p_seq.from_numpy(np.pad(seq, (0, self._prefill_rows - M)))
         self.p_pos.from_numpy(np.pad(pos, (0, self._prefill_rows - M)))
         self.p_len.from_numpy(np.pad(pos + 1, (0, self._prefill_rows - M)))
+        self._p_blocks, self._p_nblocks = None, 0
+        if prefill_supported(self.kv[0][0]):
+            blocks = prefill_blocks(lens, slots)
+            self._p_blocks = gpu.to_device(blocks)
+            self._p_nblocks = len(blocks)
         h, x = self.p_h, self.p_x
         embedding_dev(gpu.sub_view(self.p_ids, 0, (M,)), w.embed, h)
         for i in range(w.L):

@@ -89,6 +89,8 @@ SIGNATURES: dict[str, list] = {
     "tllm_gqa_decode_noalloc": [_vp, _vp, _vp, _i, _vp, _vp, _i, _i, _i, _i,
                                 _i, _i, _f, _vp],
     "tllm_gqa_decode_noalloc_error": [_pi, _i],
+    "tllm_gqa_prefill": [_vp, _l, _l, _vp, _vp, _i, _vp, _i, _vp, _i, _l, _l, _l,
+                         _i, _i, _i, _i, _i, _f, _vp],
     "tllm_gqa_rows": [_vp, _l, _l, _vp, _vp, _i, _vp, _vp, _vp, _i, _l, _l, _l,
                       _i, _i, _i, _i, _i, _i, _i, _f, _vp, _sz, _vp, _vp],
     # projections

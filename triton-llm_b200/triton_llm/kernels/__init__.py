@@ -8,7 +8,7 @@ points used by the models are exported next to them.
 from .add import add
 from .attention import attention
 from .attention_gqa import attention_gqa, gqa_decode, DecodeWorkspace
-from .attention_prefill import gqa_rows
+from .attention_prefill import gqa_rows, gqa_prefill, prefill_blocks
 from .embedding import embedding, embedding_dev
 from .gelu import gelu
 from .gemm import gemm
@@ -35,6 +35,8 @@ __all__ = [
     # batched / fused entry points of the B200 path
     "gqa_decode",
     "gqa_rows",
+    "gqa_prefill",
+    "prefill_blocks",
     "DecodeWorkspace",
     "embedding_dev",
     "layer_norm_dev",
