@@ -555,9 +555,9 @@ def test_first_call_inside_graph_capture(gpu):
 # ------------------------------------------------- fused peer all-reduce --
 def _peer_group_1(rows, cols):
     """A one-rank peer group (the scatter writes this GPU's own slots)."""
-    from types import SimpleNamespace
-    from triton_llm.tp import PeerGroup
-    return PeerGroup(SimpleNamespace(rank=0, size=1, group=None, _dist=None), rows, cols)
+    from triton_llm import gpu
+    from triton_llm.tp import PeerGroup, TPGroup
+    return PeerGroup(TPGroup(0, 1, gpu.current_device()), rows, cols)
 
 
 @pytest.mark.parametrize("planes", [2, 1])
