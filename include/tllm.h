@@ -259,6 +259,37 @@ int tllm_gqa_rows(const float *q, long q_row_stride, long q_head_stride,
  * Scratch for split-K: tllm_linear_workspace; counters zero-filled once
  * (the kernel leaves them at zero).
  */
+/*
+ * RMSNorm folded into the projections on either side of it
+ * (kernels/rms_norm.py:50-55: y = x / sqrt(sum(x^2) / N + eps) * w, then
+ * y @ W). Since sum_k W[n, k] (x_k / r) w_k = (sum_k W[n, k] x_k w_k) / r
+ * for a per-row r, the norm weight goes on the operand and the row scale
+ * after the product:
+ *   producer (op RESID, the projection that writes x): also stores
+ *     fx[m, n] = out[m, n] * next_norm_w[n] in operand format (fx_dtype
+ *     TLLM_SPLIT or TLLM_BF16, planes fx_plane_rows rows apart, rows of N)
+ *     and ss_out[(n / 16) * ss_ld + m] = sum of out[m, n]^2 over each
+ *     16-column block (ceil(N / 16) partials per row);
+ *   consumer (op STORE, SWIGLU or QKV, the projection that reads fx):
+ *     divides row m of the product by
+ *     sqrt(sum_{p < ss_parts} ss_in[p * ss_ld + m] / ss_cols + eps)
+ *     before bias, SwiGLU or RoPE.
+ * The norm's own launch disappears. bf16 weights only. No counterpart in the
+ * reference (it launches rms_norm between the GEMMs).
+ */
+typedef struct {
+  const float *next_norm_w;  /* producer */
+  void *fx;
+  int fx_dtype;
+  int fx_plane_rows;
+  float *ss_out;
+  const float *ss_in;        /* consumer */
+  int ss_parts;
+  int ss_cols;
+  float eps;
+  int ss_ld;                 /* both: row stride of the partials (>= M) */
+} tllm_norm_fold;
+
 int tllm_linear_workspace(int M, int N, int K, size_t *partial_bytes,
                           size_t *counter_bytes);
 /* Launch plan of the bf16 path for (M, N, K) and activation format x_dtype
@@ -275,6 +306,17 @@ int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
                 int n_head, int n_kv_head, int head_dim, int32_t *lens_out,
                 const void *p2p, void *partial, size_t partial_bytes,
                 int32_t *counters, tllm_stream_t stream);
+/* tllm_linear with a folded RMSNorm (tllm_norm_fold above; NULL = none). */
+int tllm_linear_folded(const void *x, int x_dtype, int x_plane_rows, const void *w,
+                int w_dtype, int M, int N, int K, int op, const float *bias,
+                void *out, int out_dtype, int out_plane_rows, int ld_out,
+                const float *resid, const float *cos_t, const float *sin_t,
+                const int32_t *row_seq, const int32_t *row_pos, float *q_out,
+                void *k_cache, void *v_cache, int kv_dtype, int max_seq,
+                int n_head, int n_kv_head, int head_dim, int32_t *lens_out,
+                const void *p2p, void *partial, size_t partial_bytes,
+                int32_t *counters, const tllm_norm_fold *fold,
+                tllm_stream_t stream);
 
 /*
  * The decode MLP half of a Llama-style layer in one persistent launch (no

@@ -16,9 +16,14 @@ of the B200 path:
   stay fp32 -- the storage points of the B200 bf16 path.
 * ``act_dtype="bfloat16"`` (SmolLM2 only) additionally rounds every
   projection input to bf16 where the B200 path stores it as a one-plane
-  bf16 operand: the RMSNorm outputs (both norms of a layer and the final
-  norm), the attention output and the SwiGLU output. The residual stream,
-  q and the logits stay fp32.
+  bf16 operand: the attention output, the SwiGLU output and the inputs of
+  the projections after each RMSNorm. The B200 path folds most RMSNorms
+  into the projections around them (the norm weight on the operand, the
+  row's 1/rms after the product): there the stored operand is h * w and
+  the product is divided by the rms afterwards -- ln2 of every layer, ln1
+  of every layer but the first, and the final norm of single-token steps.
+  The first layer's ln1 and a prefill's final norm round the normalised
+  rows themselves. The residual stream, q and the logits stay fp32.
 """
 
 from __future__ import annotations
@@ -32,6 +37,13 @@ F32 = np.float32
 
 def _store(x, bf16):
     return ops.bf16_round(x) if bf16 else np.asarray(x, F32)
+
+
+def _rms(h, eps):
+    """The rms of each row as ops.rms_norm computes it."""
+    h = np.asarray(h, F32)
+    ss = np.sum(h * h, axis=-1, dtype=F32, keepdims=True)
+    return np.sqrt(ss / F32(h.shape[-1]) + F32(eps)).astype(F32)
 
 
 class SmolLM2Oracle:
@@ -98,10 +110,8 @@ class SmolLM2Oracle:
         for i, Lw in enumerate(self.layers):
             cache = self.cache[i]
             residual = h
-            x = _store(ops.rms_norm(h, Lw["ln1"], self.eps), self.actbf16)
-            q = ops.gemm(x, Lw["wq"])
-            k = ops.gemm(x, Lw["wk"])
-            v = ops.gemm(x, Lw["wv"])
+            q, k, v = self._normed_gemms(h, Lw["ln1"], (Lw["wq"], Lw["wk"], Lw["wv"]),
+                                         folded=i > 0)
             qh = q.reshape(seq, H, d).transpose(1, 0, 2).reshape(-1, d)
             kh = k.reshape(seq, Hkv, d).transpose(1, 0, 2).reshape(-1, d)
             vh = v.reshape(seq, Hkv, d).transpose(1, 0, 2).reshape(-1, d)
@@ -124,14 +134,23 @@ class SmolLM2Oracle:
             o = _store(o, self.actbf16)
             h = ops.add(ops.gemm(o, Lw["wo"]), residual)
             residual = h
-            x = _store(ops.rms_norm(h, Lw["ln2"], self.eps), self.actbf16)
-            g = ops.gemm(x, Lw["wg"])
-            u = ops.gemm(x, Lw["wu"])
+            g, u = self._normed_gemms(h, Lw["ln2"], (Lw["wg"], Lw["wu"]), folded=True)
             act = _store(ops.swiglu(g, u), self.actbf16)
             h = ops.add(ops.gemm(act, Lw["wd"]), residual)
         self.cache_len = total
-        x = _store(ops.rms_norm(h, self.ln_f, self.eps), self.actbf16)
-        return ops.gemm(x, self.lm_head_w).reshape(1, seq, -1)
+        (logits,) = self._normed_gemms(h, self.ln_f, (self.lm_head_w,), folded=seq == 1)
+        return logits.reshape(1, seq, -1)
+
+    def _normed_gemms(self, h, w_norm, mats, folded):
+        """rms_norm(h) @ each matrix (smollm2_triton/model.py:281-287, :357-365,
+        :371-375). With bf16 projection inputs, a norm the B200 path folds
+        stores h * w (rounded) and divides the products by the rms."""
+        if self.actbf16 and folded:
+            xw = _store(np.asarray(h, F32) * np.asarray(w_norm, F32), True)
+            rms = _rms(h, self.eps)
+            return [(ops.gemm(xw, m) / rms).astype(F32) for m in mats]
+        x = _store(ops.rms_norm(h, w_norm, self.eps), self.actbf16)
+        return [ops.gemm(x, m) for m in mats]
 
     def generate(self, token_ids, max_new_tokens, max_seq=None):
         """Greedy generation (smollm2_triton/model.py:452-469), returns ids

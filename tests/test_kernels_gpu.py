@@ -714,3 +714,121 @@ def test_mlp_block_rejects_bad_shapes(gpu):
     with pytest.raises(ValueError):               # fp32 weights
         mlp_block(a, lin, gpu.allocate((8, 128), np.float32), gpu.allocate((128,), np.float32),
                   a, lin, a, lin, 8, 1e-5, ws)
+
+
+# ---------------------------------------------------------- folded RMSNorm --
+@pytest.mark.parametrize("planes", [1, 2])
+@pytest.mark.parametrize("M,N,K", [(64, 3072, 3072), (8, 576, 576), (33, 1000, 1536)])
+def test_folded_norm_producer(gpu, M, N, K, planes):
+    """op RESID with a folded norm: h is what the plain RESID call writes
+    (bit for bit), fx = the operand format of h * w, and the partial sums
+    are the sums of squares of h over each 16-column block."""
+    from triton_llm import _lib
+    from triton_llm.kernels.linear import FoldedNorm, Linear, LinearWorkspace, linear
+    rng = np.random.default_rng(M + N)
+    lin = Linear((rng.standard_normal((N, K), dtype=F32) * 0.05).astype(F32), "bfloat16")
+    x = gpu.to_device_split(rng.standard_normal((M, K), dtype=F32), planes=planes)
+    h0 = rng.standard_normal((M, N), dtype=F32)
+    wn = rng.standard_normal(N, dtype=F32)
+    ws = LinearWorkspace([(M, N, K)])
+    ha = gpu.to_device(h0)
+    linear(x, lin, out_dev=ha, op=_lib.EPI_RESID, resid_dev=ha, ws=ws, M=M)
+    hb = gpu.to_device(h0)
+    fx = gpu.act_empty(M + 3, N, planes)
+    ss = gpu.allocate((-(-N // 16), M + 5), np.float32)
+    fold = FoldedNorm(gpu.to_device(wn), fx, ss, N, 1e-5)
+    linear(x, lin, out_dev=hb, op=_lib.EPI_RESID, resid_dev=hb, ws=ws, M=M, fold_out=fold)
+    h = hb.to_numpy()
+    np.testing.assert_array_equal(h, ha.to_numpy())
+    got_fx = gpu.split_to_host(fx, M)
+    want_fx = (h * wn).astype(F32)
+    if planes == 1:
+        np.testing.assert_array_equal(got_fx, ops.bf16_round(want_fx))
+    else:
+        hi = ops.bf16_round(want_fx)
+        np.testing.assert_array_equal(got_fx, hi + ops.bf16_round(want_fx - hi))
+    parts = -(-N // 16)
+    pad = np.zeros((M, parts * 16), np.float64)
+    pad[:, :N] = h.astype(np.float64) ** 2
+    want_ss = pad.reshape(M, parts, 16).sum(axis=2).T
+    np.testing.assert_allclose(ss.to_numpy()[:, :M], want_ss, rtol=2e-6)
+
+
+@pytest.mark.parametrize("planes", [1, 2])
+@pytest.mark.parametrize("op", ["store", "swiglu", "qkv"])
+@pytest.mark.parametrize("M", [8, 64])
+def test_folded_norm_consumer(gpu, op, M, planes):
+    """A projection reading h * w with the rows divided by their rms gives
+    what RMSNorm followed by the plain projection gives (to the fp32 sums
+    and the operand rounding of the two forms)."""
+    from triton_llm import _lib
+    from triton_llm.kernels.linear import (FoldedNorm, Linear, LinearWorkspace, linear,
+                                           qkv_rows, swiglu_rows)
+    from triton_llm.kernels.rms_norm import rms_norm_rows
+    from triton_llm.kernels.rope import precompute_cos_sin
+    rng = np.random.default_rng(7 * M + planes)
+    n = 576
+    h = (rng.standard_normal((M, n), dtype=F32) * 3).astype(F32)
+    wn = (rng.standard_normal(n, dtype=F32) * 0.5 + 1).astype(F32)
+    H, Hkv, D = 9, 3, 64
+    if op == "swiglu":
+        w = rng.standard_normal((2 * 1536, n), dtype=F32) * 0.05
+        w = swiglu_rows(w[:1536], w[1536:])
+    elif op == "qkv":
+        w, _ = qkv_rows(rng.standard_normal((H * D, n), dtype=F32) * 0.05,
+                        rng.standard_normal((Hkv * D, n), dtype=F32) * 0.05,
+                        rng.standard_normal((Hkv * D, n), dtype=F32) * 0.05, D)
+    else:
+        w = rng.standard_normal((4096, n), dtype=F32) * 0.05
+    lin = Linear(np.ascontiguousarray(w, F32), "bfloat16")
+    code = {"store": _lib.EPI_STORE, "swiglu": _lib.EPI_SWIGLU, "qkv": _lib.EPI_QKV}[op]
+    ws = LinearWorkspace([(M, lin.N, n)])
+    hd, wd = gpu.to_device(h), gpu.to_device(wn)
+    S = 16
+    cos, sin = precompute_cos_sin(S, D, 1e5)
+    cd, sd = gpu.to_device(cos), gpu.to_device(sin)
+    seq = gpu.to_device(np.arange(M, dtype=np.int32))
+    pos = gpu.to_device((np.arange(M) % S).astype(np.int32))
+
+    def run(x, fold):
+        if op == "qkv":
+            q = gpu.allocate((M, H, D), np.float32)
+            kc = gpu.zeros((M, Hkv, S, D), np.float32)
+            vc = gpu.zeros((M, Hkv, S, D), np.float32)
+            linear(x, lin, op=code, ws=ws, M=M, fold_in=fold, qkv=dict(
+                cos=cd, sin=sd, row_seq=seq, row_pos=pos, q_out=q, k_cache=kc,
+                v_cache=vc, n_head=H, n_kv_head=Hkv, head_dim=D))
+            return np.concatenate([q.to_numpy().ravel(), kc.to_numpy().ravel(),
+                                   vc.to_numpy().ravel()])
+        out = gpu.allocate((M, lin.N // 2 if op == "swiglu" else lin.N), np.float32)
+        linear(x, lin, out_dev=out, op=code, ws=ws, M=M, fold_in=fold)
+        return out.to_numpy()
+
+    # reference: RMSNorm kernel, then the plain projection
+    xa = gpu.act_empty(M, n, planes)
+    rms_norm_rows(hd, wd, xa, M, 1e-5)
+    want = run(xa, None)
+    # folded: the operand h * w and the partial sums a producer would write
+    fx = gpu.to_device_split((h * wn).astype(F32), planes=planes)
+    parts = n // 16
+    ssh = (h.astype(F32) ** 2).reshape(M, parts, 16).sum(axis=2, dtype=F32).T.copy()
+    ss = gpu.to_device(np.ascontiguousarray(ssh, F32))
+    got = run(fx, FoldedNorm(wd, fx, ss, n, 1e-5))
+    scale = np.abs(want).max()
+    tol = 2e-5 if planes == 2 else 2e-2
+    np.testing.assert_allclose(got, want, atol=tol * scale)
+
+
+def test_folded_norm_rejects_bad_use(gpu):
+    from triton_llm import _lib
+    from triton_llm.kernels.linear import FoldedNorm, Linear, LinearWorkspace, linear
+    M, N = 4, 128
+    lin = Linear(np.zeros((N, N), F32), "bfloat16")
+    fx = gpu.act_empty(M, N, 2)
+    fold = FoldedNorm(gpu.to_device(np.ones(N, F32)), fx, gpu.allocate((8, M), np.float32),
+                      N, 1e-5)
+    out = gpu.allocate((M, N), np.float32)
+    with pytest.raises(ValueError):   # a producer must be op RESID
+        linear(fx, lin, out_dev=out, op=_lib.EPI_STORE, M=M, fold_out=fold)
+    with pytest.raises(ValueError):   # a consumer cannot be op RESID
+        linear(fx, lin, out_dev=out, op=_lib.EPI_RESID, resid_dev=out, M=M, fold_in=fold)

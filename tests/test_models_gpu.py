@@ -417,3 +417,24 @@ def test_gpt2_cfg1_32_steps_match_reference(gpu, golden):
           f"(smallest reference top-2 gap {float(g['gap'].min()):.2e})")
     np.testing.assert_array_equal(toks, g["tokens"])
     _digest_compare(logits, g, 1e-4)
+
+
+@pytest.mark.parametrize("act", ["split", "bfloat16"])
+def test_folded_norms_equal_explicit_norms(gpu, monkeypatch, act):
+    """The engine with its RMSNorms folded into the projections (default)
+    and with every norm launched on its own (TLLM_NORM_FOLD=0) give the same
+    greedy tokens, and logits within the activation format's rounding."""
+    from smollm2_triton import SmolLM2Config
+    from smollm2_triton.engine import LlamaWeights
+    w = inputs.round_linear_weights_bf16(inputs.llama_weights(inputs.SMOL_135M, 0))
+    cfg = SmolLM2Config(**inputs.SMOL_135M.config_kwargs())
+    wts = LlamaWeights(cfg, w, "bfloat16", max_pos=64)
+    rng = np.random.default_rng(12)
+    prompts = [rng.integers(0, 49152, n).tolist() for n in (3, 20)]
+    runs = []
+    for fold in ("1", "0"):
+        monkeypatch.setenv("TLLM_NORM_FOLD", fold)
+        runs.append(_session_greedy(wts, prompts, 16, 64, act))
+    for (ta, la), (tb, lb) in zip(*runs):
+        np.testing.assert_array_equal(ta, tb)
+        np.testing.assert_allclose(la, lb, atol=1e-4 if act == "split" else 2e-3)

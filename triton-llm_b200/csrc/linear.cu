@@ -84,7 +84,32 @@ struct Epilogue {
   int *err;
   // EPI_SCATTER
   const P2PDev *p2p;
+  // RMSNorm folded into the neighbouring projections. Producer (EPI_RESID):
+  // besides out, fx[m, n] = out[m, n] * fx_w[n] in operand format and
+  // ss_out[(n / 16) * ss_ld + m] = sum of out[m, n]^2 over each 16-column
+  // block. Consumer (EPI_STORE / EPI_SWIGLU / EPI_QKV): row m of the product
+  // divided by sqrt(sum_{p < ss_parts} ss_in[p * ss_ld + m] / ss_cols + eps).
+  const float *fx_w;
+  uint16_t *fx;
+  size_t fx_plane;
+  int fx_planes;
+  float *ss_out;
+  const float *ss_in;
+  int ss_parts, ss_cols, ss_ld;
+  float ss_eps;
 };
+
+// sqrt(mean of squares + eps) of activation row m from the producer's
+// per-block partial sums, summed by one warp (lane-strided, then a fixed
+// butterfly: deterministic). Every lane returns the value.
+__device__ __forceinline__ float fold_rms_warp(const Epilogue &e, int m) {
+  float t = 0.f;
+  for (int p = threadIdx.x & 31; p < e.ss_parts; p += 32)
+    t += e.ss_in[(size_t)p * e.ss_ld + m];
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  return sqrtf(t / (float)e.ss_cols + e.ss_eps);
+}
 
 __device__ __forceinline__ float gelu_tanh(float x) {
   // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))) with tanh built from
@@ -308,6 +333,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __shared__ int s_wissued, s_xissued, s_fail;
   __shared__ int s_empty_acc[kTcMaxIssuers];   // an issuer whose accumulators were never written
   __shared__ unsigned s_epoch;     // EPI_SCATTER: this call's number
+  __shared__ float s_rms[MT];      // folded RMSNorm: rms of each activation row
   const int WS = p.wstages;
   uint8_t *wring = smem;
   uint8_t *xring = smem + WS * kTcW;
@@ -448,6 +474,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       umma_commit(accb);            // this issuer's MMAs complete
     }
     __syncwarp();
+  } else if ((warp == 4 || warp == 6) && p.e.ss_in) {
+    // folded RMSNorm consumer: warps 4 and 6 (idle in the main loop) sum
+    // the producer's partials of this tile's activation rows
+    griddep_wait();
+    for (int ml = (warp == 4 ? 0 : 1); ml < MT; ml += 2) {
+      const int m = mt * MT + ml;
+      const float r = m < p.M ? fold_rms_warp(p.e, m) : 1.f;
+      if (lane == 0) s_rms[ml] = r;
+    }
   }
 
   // ---- epilogue ----
@@ -568,6 +603,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       } else {
         const Epilogue &e = p.e;
         const bool full = n + 3 < p.N;
+        float fw[4] = {0.f, 0.f, 0.f, 0.f};   // folded producer: next norm weight
+        if (OP == EPI_RESID && e.ss_out) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            if (n + k < p.N) fw[k] = e.fx_w[n + k];
+        }
         float bias[4] = {0.f, 0.f, 0.f, 0.f};
         if (e.bias) {
 #pragma unroll
@@ -598,9 +639,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
 #pragma unroll
         for (int i = 0; i < kTcRB; ++i) {
-          if (!ok[i]) continue;
+          if (!ok[i]) continue;   // uniform over the warp (one row per i)
           const size_t o = (size_t)mrow[i] * e.ld_out + n;
           float a[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+          if (OP == EPI_STORE && e.ss_in) {
+            const float rms = s_rms[mrow[i] - mt * MT];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) a[k] = a[k] / rms;
+          }
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             if (e.bias) a[k] += bias[k];
@@ -613,6 +659,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
             for (int k = 0; k < 4; ++k)
               if (n + k < p.N) store_out(e, o + k, a[k]);
+          }
+          if (OP == EPI_RESID && e.ss_out) {
+            // the next RMSNorm, folded: h * w as its projection's operand and
+            // the sums of squares of h over each 16-column block (lanes
+            // 4j .. 4j + 3 hold block j of this tile's 128 columns)
+            float sq = 0.f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              if (n + k < p.N) {
+                store_act(e.fx, e.fx_plane, o + k, a[k] * fw[k], e.fx_planes);
+                sq = fmaf(a[k], a[k], sq);
+              }
+            }
+            sq += __shfl_xor_sync(0xffffffffu, sq, 1);
+            sq += __shfl_xor_sync(0xffffffffu, sq, 2);
+            if ((lane & 3) == 0 && n < p.N)
+              e.ss_out[(size_t)(n >> 4) * e.ss_ld + mrow[i]] = sq;
           }
         }
       }
@@ -649,6 +712,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 v1[i][h] += ld_dsmem_f32(tile_s + (ml * kTcBN + r + 8) * 4, q);
               }
             }
+          }
+        }
+      }
+      if (p.e.ss_in) {
+#pragma unroll
+        for (int i = 0; i < kTcRB; ++i) {
+          if (!in_tile[i]) continue;
+          const float rms = s_rms[mlb + i * kTcWarps * S];
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            v0[i][h] = v0[i][h] / rms;
+            v1[i][h] = v1[i][h] / rms;
           }
         }
       }
@@ -939,7 +1014,8 @@ __device__ __forceinline__ const uint16_t *sk_w(const uint16_t *w, bool tiled, i
 // memory round trip per row.
 template <int NB>
 __device__ __forceinline__ void sk_epilogue(const Epilogue &e, int N, int M, int r, int q,
-                                            const float (&v)[NB][4], unsigned bmask) {
+                                            float (&v)[NB][4], unsigned bmask,
+                                            const float *s_rms) {
   const int r1 = r + 8;
   const bool ok0 = r < N, ok1 = r1 < N;
   bool okm[NB][2];
@@ -952,6 +1028,17 @@ __device__ __forceinline__ void sk_epilogue(const Epilogue &e, int N, int M, int
       okm[b][t] = ((bmask >> b) & 1) && mm[b][t] < M;
     }
   const int op = e.op;
+  if (e.ss_in && op != EPI_RESID) {
+    // folded RMSNorm consumer: row m of the product divided by its rms
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const float rms = okm[b][t] ? s_rms[mm[b][t]] : 1.f;
+        v[b][t] = v[b][t] / rms;
+        v[b][2 + t] = v[b][2 + t] / rms;
+      }
+  }
   if (op == EPI_STORE || op == EPI_RESID || op == EPI_GELU) {
     const float b0 = e.bias && ok0 ? e.bias[r] : 0.f;
     const float b1 = e.bias && ok1 ? e.bias[r1] : 0.f;
@@ -982,6 +1069,36 @@ __device__ __forceinline__ void sk_epilogue(const Epilogue &e, int N, int M, int
         if (ok0) store_out(e, o + r, a0);
         if (ok1) store_out(e, o + r1, a1);
       }
+    if (op == EPI_RESID && e.ss_out) {
+      // the next RMSNorm, folded: h * w as its projection's operand and the
+      // sums of squares of h over this 16-row weight block (the 8 lanes of
+      // one q hold its rows r, r + 8 for the same activation rows)
+      const float w0 = ok0 ? e.fx_w[r] : 0.f, w1 = ok1 ? e.fx_w[r1] : 0.f;
+#pragma unroll
+      for (int b = 0; b < NB; ++b)
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          const size_t o = (size_t)mm[b][t] * e.ld_out;
+          const float a0 = v[b][t] + b0 + rv[b][t][0];
+          const float a1 = v[b][2 + t] + b1 + rv[b][t][1];
+          float sq = 0.f;
+          if (okm[b][t]) {
+            if (ok0) {
+              store_act(e.fx, e.fx_plane, o + r, a0 * w0, e.fx_planes);
+              sq = fmaf(a0, a0, sq);
+            }
+            if (ok1) {
+              store_act(e.fx, e.fx_plane, o + r1, a1 * w1, e.fx_planes);
+              sq = fmaf(a1, a1, sq);
+            }
+          }
+          sq += __shfl_xor_sync(0xffffffffu, sq, 4);
+          sq += __shfl_xor_sync(0xffffffffu, sq, 8);
+          sq += __shfl_xor_sync(0xffffffffu, sq, 16);
+          if (okm[b][t] && (threadIdx.x & 31) < 4)
+            e.ss_out[(size_t)(r >> 4) * e.ss_ld + mm[b][t]] = sq;
+        }
+    }
   } else if (op == EPI_SWIGLU) {
     if (!ok1) return;
     const int j = (r >> 4) * 8 + (r & 7);
@@ -1063,6 +1180,16 @@ __global__ void __launch_bounds__(kSkWarps * 32)
     wb[u] = in ? ld_stream(sk_w(w, tiled, kc, K, nb8, k)) : z;
   }
   griddep_wait();   // the activations and the epilogue's inputs
+  __shared__ float s_rms[MT];
+  if (e.ss_in) {
+    // folded RMSNorm consumer: every warp takes rows w, w + 8, ... (the
+    // weight loads above are in flight meanwhile)
+    for (int m = warp; m < MT; m += kSkWarps) {
+      const float r = m < M ? fold_rms_warp(e, m) : 1.f;
+      if (lane == 0) s_rms[m] = r;
+    }
+    __syncthreads();
+  }
   float acc[NB][4];
 #pragma unroll
   for (int b = 0; b < NB; ++b)
@@ -1141,7 +1268,7 @@ __global__ void __launch_bounds__(kSkWarps * 32)
   } else {
     if (!live) return;
   }
-  sk_epilogue<NB>(e, N, M, ra, q, acc, bmask);
+  sk_epilogue<NB>(e, N, M, ra, q, acc, bmask, s_rms);
 }
 
 template <int MT, int PL>
@@ -1492,6 +1619,17 @@ int tllm_linear_plan(int M, int N, int K, int x_dtype, int *plan) {
   return TLLM_OK;
 }
 
+int tllm_linear_folded(const void *x, int x_dtype, int x_plane_rows, const void *w,
+                       int w_dtype, int M, int N, int K, int op, const float *bias,
+                       void *out, int out_dtype, int out_plane_rows, int ld_out,
+                       const float *resid, const float *cos_t, const float *sin_t,
+                       const int32_t *row_seq, const int32_t *row_pos, float *q_out,
+                       void *k_cache, void *v_cache, int kv_dtype, int max_seq,
+                       int n_head, int n_kv_head, int head_dim, int32_t *lens_out,
+                       const void *p2p, void *partial, size_t partial_bytes,
+                       int32_t *counters, const tllm_norm_fold *fold,
+                       tllm_stream_t stream);
+
 // y = epilogue(x @ W^T); see tllm.h for the argument encoding.
 int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
                 int w_dtype, int M, int N, int K, int op, const float *bias,
@@ -1502,6 +1640,25 @@ int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
                 int n_head, int n_kv_head, int head_dim, int32_t *lens_out,
                 const void *p2p, void *partial, size_t partial_bytes,
                 int32_t *counters, tllm_stream_t stream) {
+  return tllm_linear_folded(x, x_dtype, x_plane_rows, w, w_dtype, M, N, K, op, bias,
+                            out, out_dtype, out_plane_rows, ld_out, resid, cos_t,
+                            sin_t, row_seq, row_pos, q_out, k_cache, v_cache,
+                            kv_dtype, max_seq, n_head, n_kv_head, head_dim,
+                            lens_out, p2p, partial, partial_bytes, counters,
+                            nullptr, stream);
+}
+
+// tllm_linear with a folded RMSNorm on either side (fold may be NULL).
+int tllm_linear_folded(const void *x, int x_dtype, int x_plane_rows, const void *w,
+                       int w_dtype, int M, int N, int K, int op, const float *bias,
+                       void *out, int out_dtype, int out_plane_rows, int ld_out,
+                       const float *resid, const float *cos_t, const float *sin_t,
+                       const int32_t *row_seq, const int32_t *row_pos, float *q_out,
+                       void *k_cache, void *v_cache, int kv_dtype, int max_seq,
+                       int n_head, int n_kv_head, int head_dim, int32_t *lens_out,
+                       const void *p2p, void *partial, size_t partial_bytes,
+                       int32_t *counters, const tllm_norm_fold *fold,
+                       tllm_stream_t stream) {
   TLLM_INJECT("launch");
   TLLM_CHECK_ARG(M >= 0 && N >= 0 && K >= 0, "negative shape");
   if (M == 0 || N == 0) return TLLM_OK;
@@ -1547,6 +1704,35 @@ int tllm_linear(const void *x, int x_dtype, int x_plane_rows, const void *w,
   }
   e.err = device_error_ptr();
   TLLM_CHECK_ARG(e.err, "device error word unavailable");
+  if (fold && fold->ss_out) {   // producer of the next norm's operand
+    TLLM_CHECK_ARG(op == EPI_RESID, "a folded-norm producer must use op RESID");
+    TLLM_CHECK_ARG(fold->next_norm_w && fold->fx, "folded norm: NULL weight or operand");
+    TLLM_CHECK_ARG(fold->fx_dtype == TLLM_SPLIT || fold->fx_dtype == TLLM_BF16,
+                   "folded norm: operand dtype SPLIT or BF16");
+    TLLM_CHECK_ARG(fold->fx_plane_rows >= M && fold->ss_ld >= M,
+                   "folded norm: fx_plane_rows / ss_ld < M");
+    TLLM_CHECK_ARG(e.ld_out == N, "folded norm: the residual rows must be dense");
+    e.fx_w = fold->next_norm_w;
+    e.fx = static_cast<uint16_t *>(fold->fx);
+    e.fx_plane = (size_t)fold->fx_plane_rows * N;
+    e.fx_planes = fold->fx_dtype == TLLM_SPLIT ? 2 : 1;
+    e.ss_out = fold->ss_out;
+    e.ss_ld = fold->ss_ld;
+  }
+  if (fold && fold->ss_in) {    // consumer: rows scaled by 1 / rms
+    TLLM_CHECK_ARG(op == EPI_STORE || op == EPI_SWIGLU || op == EPI_QKV,
+                   "a folded-norm consumer must use op STORE, SWIGLU or QKV");
+    TLLM_CHECK_ARG(fold->ss_parts > 0 && fold->ss_cols > 0 && fold->ss_ld >= M,
+                   "folded norm: ss_parts, ss_cols > 0 and ss_ld >= M");
+    TLLM_CHECK_ARG(w_dtype != TLLM_F32, "folded norm needs bf16 weights");
+    e.ss_in = fold->ss_in;
+    e.ss_parts = fold->ss_parts;
+    e.ss_cols = fold->ss_cols;
+    e.ss_ld = fold->ss_ld;
+    e.ss_eps = fold->eps;
+  }
+  if (fold && (fold->ss_out || fold->ss_in))
+    TLLM_CHECK_ARG(w_dtype != TLLM_F32, "folded norm needs bf16 weights");
   int rc = check_epilogue(e, N);
   if (rc) return rc;
   cudaStream_t st = resolve(stream);

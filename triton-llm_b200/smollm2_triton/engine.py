@@ -41,8 +41,8 @@ import numpy as np
 from triton_llm import gpu, _lib, shard
 from triton_llm.kernels import gqa_rows, gqa_prefill, prefill_blocks, DecodeWorkspace
 from triton_llm.kernels.attention_prefill import prefill_supported
-from triton_llm.kernels.linear import (Linear, LinearWorkspace, linear, qkv_rows,
-                                       swiglu_rows)
+from triton_llm.kernels.linear import (FoldedNorm, Linear, LinearWorkspace, linear,
+                                       qkv_rows, swiglu_rows)
 from triton_llm.kernels.rms_norm import (rms_norm_add_rows, rms_norm_p2p_rows,
                                          rms_norm_rows)
 from triton_llm.kernels.rope import precompute_cos_sin
@@ -243,6 +243,11 @@ class LlamaSession:
         self.q, self.attn = f(M, w.H, w.D), self._act(M, w.H * w.D)
         self.act, self.logits = self._act(M, w.F), f(M, w.V)
         self.part = f(M, w.n) if self.tp is not None and self.tp.size > 1 else None
+        # RMSNorms folded into the projections around them (bf16 weights,
+        # unsharded layers): per-16-column partial sums of squares of h
+        self.fold = (w.bf16 and self.part is None
+                     and os.environ.get("TLLM_NORM_FOLD", "1") != "0")
+        self.ss = f(-(-w.n // 16), M) if self.fold else None
         self.peer = None
         if self.part is not None and self._p2p:
             self.peer = self.tp.peer_group(M, w.n)
@@ -265,6 +270,7 @@ class LlamaSession:
         self.p_q, self.p_attn = f(M, w.H, w.D), self._act(M, w.H * w.D)
         self.p_act = self._act(M, w.F)
         self.p_part = f(M, w.n) if self.part is not None else None
+        self.p_ss = f(-(-w.n // 16), M) if self.fold else None
         self.p_ids = gpu.allocate((M,), np.int32)
         self.p_seq = gpu.allocate((M,), np.int32)
         self.p_pos = gpu.allocate((M,), np.int32)
@@ -288,11 +294,17 @@ class LlamaSession:
         w = self.w
         L = w.layers[i]
         k, v = self.kv[i]
+        ss = self.ss if decode else self.p_ss
+        fold_ln1 = None
         if part is not None and i > 0:
             self._norm_add(h, part, L["ln1"], x, M)
+        elif ss is not None and part is None and i > 0 and self.mlp_ws is None:
+            # ln1 folded: the previous layer's down projection wrote h * ln1
+            # and the partial sums; the QKV epilogue divides by the rms
+            fold_ln1 = FoldedNorm(L["ln1"], x, ss, w.n, w.eps)
         else:
             rms_norm_rows(h, L["ln1"], x, M, w.eps)
-        linear(x, L["qkv"], op=_lib.EPI_QKV, ws=ws, M=M, qkv=dict(
+        linear(x, L["qkv"], op=_lib.EPI_QKV, ws=ws, M=M, fold_in=fold_ln1, qkv=dict(
             cos=w.cos, sin=w.sin, row_seq=row_seq, row_pos=row_pos, q_out=q,
             k_cache=k, v_cache=v, n_head=w.H, n_kv_head=w.Hkv, head_dim=w.D,
             lens_out=lens if decode else None))
@@ -310,6 +322,19 @@ class LlamaSession:
             _mlp.mlp_block(attn, L["o"], h, L["ln2"], x, L["gu"], act, L["down"], M,
                            w.eps, self.mlp_ws)
             return
+        ss = self.ss if decode else self.p_ss
+        if part is None and ss is not None:
+            # ln2 folded: o writes h * ln2 and the partial sums, gate/up
+            # divides its rows by the rms; down does the same for the next
+            # norm (the next layer's ln1, or the final norm of a decode step)
+            ln2 = FoldedNorm(L["ln2"], x, ss, w.n, w.eps)
+            linear(attn, L["o"], out_dev=h, op=_lib.EPI_RESID, resid_dev=h, ws=ws, M=M,
+                   fold_out=ln2)
+            linear(x, L["gu"], out_dev=act, op=_lib.EPI_SWIGLU, ws=ws, M=M, fold_in=ln2)
+            nxt = self._next_norm(i, x, ss, decode)
+            linear(act, L["down"], out_dev=h, op=_lib.EPI_RESID, resid_dev=h, ws=ws, M=M,
+                   fold_out=nxt)
+            return
         if part is None:
             linear(attn, L["o"], out_dev=h, op=_lib.EPI_RESID, resid_dev=h, ws=ws, M=M)
             rms_norm_rows(h, L["ln2"], x, M, w.eps)
@@ -321,6 +346,15 @@ class LlamaSession:
             linear(act, L["down"], out_dev=h, op=_lib.EPI_RESID, resid_dev=h, ws=ws, M=M)
         else:
             self._reduce(act, L["down"], part, M, ws)
+
+    def _next_norm(self, i, x, ss, decode):
+        """The folded norm after layer i's down projection: the next layer's
+        ln1, or (decode) the final norm; None after a prefill's last layer
+        (the prefill normalises the rows it keeps on its own)."""
+        w = self.w
+        if i + 1 < w.L:
+            return FoldedNorm(w.layers[i + 1]["ln1"], x, ss, w.n, w.eps)
+        return FoldedNorm(w.norm, x, ss, w.n, w.eps) if decode else None
 
     def _reduce(self, src, lin, part, M, ws):
         """A row-parallel projection whose partial sums the group adds:
@@ -462,9 +496,16 @@ class LlamaSession:
             self._layer(i, B, self.h, self.x, self.q, self.attn, self.act,
                         self.row_seq, self.pos, self.lens, self.lin_ws, True,
                         self.attn_ws, part=self._decode_part())
-        self._final_norm(self.h, self.x, B, self._decode_part())
-        linear(self.x, w.lm_head, out_dev=self.logits, ws=self.lin_ws, M=B)
-        n = 1 + (4 if self.mlp_ws is not None else 7) * w.L + 2
+        if self.ss is not None and self.mlp_ws is None:
+            # the final norm folded into the lm_head (the last down projection
+            # wrote h * norm and the partial sums)
+            linear(self.x, w.lm_head, out_dev=self.logits, ws=self.lin_ws, M=B,
+                   fold_in=FoldedNorm(w.norm, self.x, self.ss, w.n, w.eps))
+            n = 1 + 1 + 5 * w.L + 1
+        else:
+            self._final_norm(self.h, self.x, B, self._decode_part())
+            linear(self.x, w.lm_head, out_dev=self.logits, ws=self.lin_ws, M=B)
+            n = 1 + (4 if self.mlp_ws is not None else 7) * w.L + 2
         if sample:
             _lib.call("tllm_argmax", self.logits.ptr, B, w.V, w.V, self.ids.ptr,
                       self.pos.ptr, None)

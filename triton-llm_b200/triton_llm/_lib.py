@@ -99,6 +99,9 @@ SIGNATURES: dict[str, list] = {
     "tllm_linear": [_vp, _i, _i, _vp, _i, _i, _i, _i, _i, _vp, _vp, _i, _i, _i,
                     _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i,
                     _vp, _vp, _vp, _sz, _vp, _vp],
+    "tllm_linear_folded": [_vp, _i, _i, _vp, _i, _i, _i, _i, _i, _vp, _vp, _i, _i, _i,
+                           _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i,
+                           _vp, _vp, _vp, _sz, _vp, _vp, _vp],
     "tllm_gemm_f32": [_vp, _vp, _vp, _i, _i, _i, _vp],
     "tllm_mlp_workspace": [_i, _i, _i, _i, _psz],
     "tllm_mlp": [_vp, _i, _vp, _vp, _vp, _f, _vp, _i, _vp, _vp, _i, _vp, _i, _i, _i, _i,
@@ -132,6 +135,14 @@ SIGNATURES: dict[str, list] = {
 }
 
 EPI_STORE, EPI_RESID, EPI_GELU, EPI_SWIGLU, EPI_QKV, EPI_SCATTER = 0, 1, 2, 3, 4, 5
+
+
+class NormFold(ctypes.Structure):
+    """tllm_norm_fold (include/tllm.h): an RMSNorm folded into the
+    projections on either side of it."""
+    _fields_ = [("next_norm_w", _vp), ("fx", _vp), ("fx_dtype", _i),
+                ("fx_plane_rows", _i), ("ss_out", _vp), ("ss_in", _vp),
+                ("ss_parts", _i), ("ss_cols", _i), ("eps", _f), ("ss_ld", _i)]
 EL_SWIGLU, EL_ADD, EL_GELU = 0, 1, 2
 
 _lib = None

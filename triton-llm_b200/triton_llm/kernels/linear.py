@@ -193,9 +193,34 @@ def to_split(x_dev, M=None, out=None, planes=2):
     return out
 
 
+class FoldedNorm:
+    """An RMSNorm folded into the projections around it (tllm_norm_fold):
+    the projection that writes its input (op RESID) also writes ``fx`` =
+    h * ``weight`` in operand format and per-16-column sums of squares into
+    ``ss``; the projection that reads ``fx`` divides each output row by the
+    row's rms. ``fx`` is an operand buffer of at least ``rows`` rows; ``ss``
+    fp32 (ceil(hidden / 16), rows)."""
+
+    def __init__(self, weight, fx, ss, hidden: int, eps: float):
+        self.weight, self.fx, self.ss = weight, fx, ss
+        self.hidden, self.eps = int(hidden), float(eps)
+        self.parts = -(-self.hidden // 16)
+        self.ld = int(ss.shape[1])
+
+    def producer(self):
+        _, dt, plane = gpu.act_args(self.fx)
+        return _lib.NormFold(self.weight.data_ptr(), self.fx.data_ptr(), dt, plane,
+                             self.ss.data_ptr(), None, 0, self.hidden, self.eps, self.ld)
+
+    def consumer(self):
+        return _lib.NormFold(None, None, 0, 0, None, self.ss.data_ptr(), self.parts,
+                             self.hidden, self.eps, self.ld)
+
+
 def linear(x_dev, lin: Linear, out_dev=None, op=_lib.EPI_STORE, resid_dev=None,
            ws: LinearWorkspace | None = None, M=None, ld_out=0, qkv=None,
-           p2p=None, stream=None):
+           p2p=None, stream=None, fold_in: FoldedNorm | None = None,
+           fold_out: FoldedNorm | None = None):
     """Run one projection on the first M rows of ``x_dev``.
 
     ``x_dev``: fp32 (rows, K) or TLLM_SPLIT (2, rows, K) (``gpu.split_empty``);
@@ -203,6 +228,9 @@ def linear(x_dev, lin: Linear, out_dev=None, op=_lib.EPI_STORE, resid_dev=None,
     ``out_dev``: fp32 or TLLM_SPLIT. ``qkv`` = dict(cos, sin, row_seq,
     row_pos, q_out, k_cache, v_cache, n_head, n_kv_head, head_dim, lens_out)
     for op QKV. ``p2p``: a ``triton_llm.tp.PeerGroup`` for op SCATTER.
+    ``fold_in``: ``x_dev`` is ``fold_in.fx`` (h * norm weight) and the rows
+    are divided by their rms; ``fold_out`` (op RESID): also write the next
+    norm's ``fx`` and partial sums (``FoldedNorm``).
     """
     split_in = getattr(x_dev, "is_split", False)
     rows = int(x_dev.shape[1] if split_in else x_dev.shape[0])
@@ -217,8 +245,18 @@ def linear(x_dev, lin: Linear, out_dev=None, op=_lib.EPI_STORE, resid_dev=None,
                          else (None, _lib.F32, 0))
     q = qkv or {}
     kc = q.get("k_cache")
+    fold = None
+    if fold_in is not None or fold_out is not None:
+        fold = fold_out.producer() if fold_out is not None else _lib.NormFold()
+        if fold_in is not None:
+            c = fold_in.consumer()
+            fold.ss_in, fold.ss_parts, fold.ss_cols = c.ss_in, c.ss_parts, c.ss_cols
+            fold.eps = c.eps
+            if fold_out is not None and fold_out.ld != fold_in.ld:
+                raise ValueError("folded norms on both sides need the same ss row stride")
+            fold.ss_ld = c.ss_ld
     _lib.call(
-        "tllm_linear", xptr, xdt, xplane, lin.w.ptr, lin.dtype, M, lin.N, lin.K,
+        "tllm_linear_folded", xptr, xdt, xplane, lin.w.ptr, lin.dtype, M, lin.N, lin.K,
         int(op), _lib.ptr(lin.b), optr, odt, oplane, int(ld_out), _lib.ptr(resid_dev),
         _lib.ptr(q.get("cos")), _lib.ptr(q.get("sin")), _lib.ptr(q.get("row_seq")),
         _lib.ptr(q.get("row_pos")), _lib.ptr(q.get("q_out")), _lib.ptr(kc),
@@ -228,5 +266,6 @@ def linear(x_dev, lin: Linear, out_dev=None, op=_lib.EPI_STORE, resid_dev=None,
         int(q.get("n_kv_head", 0)), int(q.get("head_dim", 0)),
         _lib.ptr(q.get("lens_out")), p2p.ctx if p2p is not None else None,
         ws.partial.ptr if ws else None, ws.partial_bytes if ws else 0,
-        ws.counters.ptr if ws else None, stream)
+        ws.counters.ptr if ws else None,
+        ctypes.byref(fold) if fold is not None else None, stream)
     return out_dev
