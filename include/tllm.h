@@ -268,8 +268,9 @@ int tllm_gqa_rows(const float *q, long q_row_stride, long q_head_stride,
  *   producer (op RESID, the projection that writes x): also stores
  *     fx[m, n] = out[m, n] * next_norm_w[n] in operand format (fx_dtype
  *     TLLM_SPLIT or TLLM_BF16, planes fx_plane_rows rows apart, rows of N)
- *     and ss_out[(n / 16) * ss_ld + m] = sum of out[m, n]^2 over each
- *     16-column block (ceil(N / 16) partials per row);
+ *     and ss_out[p * ss_ld + m] = sum of out[m, n]^2 over column part p
+ *     (tllm_linear_fold_parts gives the number of parts per row: the
+ *     128-column tiles or the 16-column blocks of the kernel that runs);
  *   consumer (op STORE, SWIGLU or QKV, the projection that reads fx):
  *     divides row m of the product by
  *     sqrt(sum_{p < ss_parts} ss_in[p * ss_ld + m] / ss_cols + eps)
@@ -289,6 +290,10 @@ typedef struct {
   float eps;
   int ss_ld;                 /* both: row stride of the partials (>= M) */
 } tllm_norm_fold;
+
+/* Partial sums per row that a folded-norm producer tllm_linear(M, N, K,
+ * bf16 weights, op RESID) writes: its consumers' ss_parts. */
+int tllm_linear_fold_parts(int M, int N, int K, int *parts);
 
 int tllm_linear_workspace(int M, int N, int K, size_t *partial_bytes,
                           size_t *counter_bytes);

@@ -736,7 +736,7 @@ def test_folded_norm_producer(gpu, M, N, K, planes):
     hb = gpu.to_device(h0)
     fx = gpu.act_empty(M + 3, N, planes)
     ss = gpu.allocate((-(-N // 16), M + 5), np.float32)
-    fold = FoldedNorm(gpu.to_device(wn), fx, ss, N, 1e-5)
+    fold = FoldedNorm(gpu.to_device(wn), fx, ss, N, 1e-5, M, K)
     linear(x, lin, out_dev=hb, op=_lib.EPI_RESID, resid_dev=hb, ws=ws, M=M, fold_out=fold)
     h = hb.to_numpy()
     np.testing.assert_array_equal(h, ha.to_numpy())
@@ -747,11 +747,14 @@ def test_folded_norm_producer(gpu, M, N, K, planes):
     else:
         hi = ops.bf16_round(want_fx)
         np.testing.assert_array_equal(got_fx, hi + ops.bf16_round(want_fx - hi))
-    parts = -(-N // 16)
-    pad = np.zeros((M, parts * 16), np.float64)
+    from triton_llm.kernels.linear import fold_parts, kernel_name
+    parts = fold_parts(M, N, K)
+    width = 16 if kernel_name(M, N, K) == "linear_mma_kernel" else 128
+    assert parts == -(-N // width)
+    pad = np.zeros((M, parts * width), np.float64)
     pad[:, :N] = h.astype(np.float64) ** 2
-    want_ss = pad.reshape(M, parts, 16).sum(axis=2).T
-    np.testing.assert_allclose(ss.to_numpy()[:, :M], want_ss, rtol=2e-6)
+    want_ss = pad.reshape(M, parts, width).sum(axis=2).T
+    np.testing.assert_allclose(ss.to_numpy()[:parts, :M], want_ss, rtol=2e-6)
 
 
 @pytest.mark.parametrize("planes", [1, 2])
@@ -808,12 +811,15 @@ def test_folded_norm_consumer(gpu, op, M, planes):
     xa = gpu.act_empty(M, n, planes)
     rms_norm_rows(hd, wd, xa, M, 1e-5)
     want = run(xa, None)
-    # folded: the operand h * w and the partial sums a producer would write
+    # folded: the operand h * w and the partial sums a skinny producer
+    # (M rows, K = 576: 16-column parts) would write
     fx = gpu.to_device_split((h * wn).astype(F32), planes=planes)
     parts = n // 16
     ssh = (h.astype(F32) ** 2).reshape(M, parts, 16).sum(axis=2, dtype=F32).T.copy()
     ss = gpu.to_device(np.ascontiguousarray(ssh, F32))
-    got = run(fx, FoldedNorm(wd, fx, ss, n, 1e-5))
+    fold = FoldedNorm(wd, fx, ss, n, 1e-5, M, 576)
+    fold.parts = parts
+    got = run(fx, fold)
     scale = np.abs(want).max()
     tol = 2e-5 if planes == 2 else 2e-2
     np.testing.assert_allclose(got, want, atol=tol * scale)
@@ -826,7 +832,7 @@ def test_folded_norm_rejects_bad_use(gpu):
     lin = Linear(np.zeros((N, N), F32), "bfloat16")
     fx = gpu.act_empty(M, N, 2)
     fold = FoldedNorm(gpu.to_device(np.ones(N, F32)), fx, gpu.allocate((8, M), np.float32),
-                      N, 1e-5)
+                      N, 1e-5, M, N)
     out = gpu.allocate((M, N), np.float32)
     with pytest.raises(ValueError):   # a producer must be op RESID
         linear(fx, lin, out_dev=out, op=_lib.EPI_STORE, M=M, fold_out=fold)

@@ -271,9 +271,11 @@ def test_llama3b_slice_matches_reference(gpu, golden, mode, monkeypatch):
 
 def test_generate_batch_equals_single(gpu):
     """Ragged batched greedy generation (one CUDA graph per step) gives each
-    prompt the tokens it gets alone."""
+    prompt the tokens it gets alone (default hi + lo projection inputs: the
+    batch changes the kernels' tiling and so the fp32 summation order, which
+    one-plane bf16 rounding can turn into a flipped near-tie)."""
     w = inputs.round_linear_weights_bf16(inputs.llama_weights(inputs.SMOL_135M, 0))
-    m = _smol(inputs.SMOL_135M, w, dtype="bfloat16")
+    m = _smol(inputs.SMOL_135M, w, dtype="bfloat16", act_dtype="split")
     rng = np.random.default_rng(2)
     prompts = [rng.integers(0, 49152, n).tolist() for n in (1, 7, 30, 12)]
     batch = m.generate_batch(prompts, max_new_tokens=10)

@@ -86,9 +86,10 @@ struct Epilogue {
   const P2PDev *p2p;
   // RMSNorm folded into the neighbouring projections. Producer (EPI_RESID):
   // besides out, fx[m, n] = out[m, n] * fx_w[n] in operand format and
-  // ss_out[(n / 16) * ss_ld + m] = sum of out[m, n]^2 over each 16-column
-  // block. Consumer (EPI_STORE / EPI_SWIGLU / EPI_QKV): row m of the product
-  // divided by sqrt(sum_{p < ss_parts} ss_in[p * ss_ld + m] / ss_cols + eps).
+  // ss_out[part * ss_ld + m] = sum of out[m, n]^2 over each column part (the
+  // 128 columns of a tcgen05 tile, the 16 of a skinny weight block).
+  // Consumer (EPI_STORE / EPI_SWIGLU / EPI_QKV): row m of the product divided
+  // by sqrt(sum_{p < ss_parts} ss_in[p * ss_ld + m] / ss_cols + eps).
   const float *fx_w;
   uint16_t *fx;
   size_t fx_plane;
@@ -99,16 +100,30 @@ struct Epilogue {
   float ss_eps;
 };
 
-// sqrt(mean of squares + eps) of activation row m from the producer's
-// per-block partial sums, summed by one warp (lane-strided, then a fixed
-// butterfly: deterministic). Every lane returns the value.
-__device__ __forceinline__ float fold_rms_warp(const Epilogue &e, int m) {
-  float t = 0.f;
-  for (int p = threadIdx.x & 31; p < e.ss_parts; p += 32)
-    t += e.ss_in[(size_t)p * e.ss_ld + m];
-#pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-  return sqrtf(t / (float)e.ss_cols + e.ss_eps);
+// sqrt(mean of squares + eps) of activation rows m0 .. m0 + rows - 1 from
+// the producer's partial sums, into s_rms[0 .. rows), computed by the nthr
+// threads t = 0 .. nthr - 1 (whole warps): T threads per row (a power of two
+// <= 32, as many as the threads allow) each add the parts j, j + T, ... in
+// order, then a fixed butterfly -- deterministic, and every row's loads are
+// in flight at once.
+__device__ __forceinline__ void fold_rms_rows(const Epilogue &e, int m0, int rows,
+                                              int M, float *s_rms, int t, int nthr) {
+  int T = 1;
+  while (T < 32 && T * 2 * rows <= nthr) T *= 2;
+  const int per_pass = nthr / T;
+  for (int base = 0; base < rows; base += per_pass) {
+    const int rl = base + t / T;
+    const int j = t % T;
+    const int m = m0 + rl;
+    float acc = 0.f;
+    if (rl < rows && m < M) {
+#pragma unroll 4
+      for (int p = j; p < e.ss_parts; p += T) acc += e.ss_in[(size_t)p * e.ss_ld + m];
+    }
+    for (int o = T / 2; o >= 1; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (j == 0 && rl < rows)
+      s_rms[rl] = m < M ? sqrtf(acc / (float)e.ss_cols + e.ss_eps) : 1.f;
+  }
 }
 
 __device__ __forceinline__ float gelu_tanh(float x) {
@@ -478,11 +493,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // folded RMSNorm consumer: warps 4 and 6 (idle in the main loop) sum
     // the producer's partials of this tile's activation rows
     griddep_wait();
-    for (int ml = (warp == 4 ? 0 : 1); ml < MT; ml += 2) {
-      const int m = mt * MT + ml;
-      const float r = m < p.M ? fold_rms_warp(p.e, m) : 1.f;
-      if (lane == 0) s_rms[ml] = r;
-    }
+    fold_rms_rows(p.e, mt * MT, MT, p.M, s_rms, (warp == 4 ? 0 : 32) + lane, 64);
   }
 
   // ---- epilogue ----
@@ -662,8 +673,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
           if (OP == EPI_RESID && e.ss_out) {
             // the next RMSNorm, folded: h * w as its projection's operand and
-            // the sums of squares of h over each 16-column block (lanes
-            // 4j .. 4j + 3 hold block j of this tile's 128 columns)
+            // the sum of squares of h over this tile's 128 columns (the warp
+            // holds the whole row of the tile)
             float sq = 0.f;
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
@@ -672,10 +683,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 sq = fmaf(a[k], a[k], sq);
               }
             }
-            sq += __shfl_xor_sync(0xffffffffu, sq, 1);
-            sq += __shfl_xor_sync(0xffffffffu, sq, 2);
-            if ((lane & 3) == 0 && n < p.N)
-              e.ss_out[(size_t)(n >> 4) * e.ss_ld + mrow[i]] = sq;
+#pragma unroll
+            for (int sh = 1; sh < 32; sh <<= 1) sq += __shfl_xor_sync(0xffffffffu, sq, sh);
+            if (lane == 0) e.ss_out[(size_t)nt * e.ss_ld + mrow[i]] = sq;
           }
         }
       }
@@ -1182,12 +1192,9 @@ __global__ void __launch_bounds__(kSkWarps * 32)
   griddep_wait();   // the activations and the epilogue's inputs
   __shared__ float s_rms[MT];
   if (e.ss_in) {
-    // folded RMSNorm consumer: every warp takes rows w, w + 8, ... (the
-    // weight loads above are in flight meanwhile)
-    for (int m = warp; m < MT; m += kSkWarps) {
-      const float r = m < M ? fold_rms_warp(e, m) : 1.f;
-      if (lane == 0) s_rms[m] = r;
-    }
+    // folded RMSNorm consumer: the whole CTA sums the partials of its rows
+    // (the weight loads above are in flight meanwhile)
+    fold_rms_rows(e, 0, MT, M, s_rms, threadIdx.x, kSkWarps * 32);
     __syncthreads();
   }
   float acc[NB][4];
@@ -1384,7 +1391,7 @@ int configure_tc() {
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !configured[dev]) {
     TLLM_CUDA(cudaFuncSetAttribute(
-        kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 226 * 1024));
+        kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 225 * 1024));
     TLLM_CUDA(cudaFuncSetAttribute(
         kern, cudaFuncAttributePreferredSharedMemoryCarveout,
         cudaSharedmemCarveoutMaxShared));
@@ -1597,6 +1604,14 @@ int tllm_linear_workspace(int M, int N, int K, size_t *partial_bytes,
   TLLM_CHECK_ARG(M >= 0 && N >= 0 && K >= 0, "negative shape");
   *partial_bytes = 0;
   *counter_bytes = 0;
+  return TLLM_OK;
+}
+
+int tllm_linear_fold_parts(int M, int N, int K, int *parts) {
+  TLLM_CHECK_ARG(parts, "NULL output");
+  TLLM_CHECK_ARG(M > 0 && N > 0 && K > 0, "M, N, K must be > 0");
+  const bool skinny = M <= sk_max_m() && (size_t)N * K * 2 <= sk_max_bytes();
+  *parts = skinny ? (N + 15) / 16 : (N + kTcBN - 1) / kTcBN;
   return TLLM_OK;
 }
 

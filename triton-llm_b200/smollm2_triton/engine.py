@@ -301,7 +301,7 @@ class LlamaSession:
         elif ss is not None and part is None and i > 0 and self.mlp_ws is None:
             # ln1 folded: the previous layer's down projection wrote h * ln1
             # and the partial sums; the QKV epilogue divides by the rms
-            fold_ln1 = FoldedNorm(L["ln1"], x, ss, w.n, w.eps)
+            fold_ln1 = FoldedNorm(L["ln1"], x, ss, w.n, w.eps, M, w.F)
         else:
             rms_norm_rows(h, L["ln1"], x, M, w.eps)
         linear(x, L["qkv"], op=_lib.EPI_QKV, ws=ws, M=M, fold_in=fold_ln1, qkv=dict(
@@ -327,11 +327,11 @@ class LlamaSession:
             # ln2 folded: o writes h * ln2 and the partial sums, gate/up
             # divides its rows by the rms; down does the same for the next
             # norm (the next layer's ln1, or the final norm of a decode step)
-            ln2 = FoldedNorm(L["ln2"], x, ss, w.n, w.eps)
+            ln2 = FoldedNorm(L["ln2"], x, ss, w.n, w.eps, M, w.H * w.D)
             linear(attn, L["o"], out_dev=h, op=_lib.EPI_RESID, resid_dev=h, ws=ws, M=M,
                    fold_out=ln2)
             linear(x, L["gu"], out_dev=act, op=_lib.EPI_SWIGLU, ws=ws, M=M, fold_in=ln2)
-            nxt = self._next_norm(i, x, ss, decode)
+            nxt = self._next_norm(i, x, ss, decode, M)
             linear(act, L["down"], out_dev=h, op=_lib.EPI_RESID, resid_dev=h, ws=ws, M=M,
                    fold_out=nxt)
             return
@@ -347,14 +347,14 @@ class LlamaSession:
         else:
             self._reduce(act, L["down"], part, M, ws)
 
-    def _next_norm(self, i, x, ss, decode):
+    def _next_norm(self, i, x, ss, decode, M):
         """The folded norm after layer i's down projection: the next layer's
         ln1, or (decode) the final norm; None after a prefill's last layer
         (the prefill normalises the rows it keeps on its own)."""
         w = self.w
         if i + 1 < w.L:
-            return FoldedNorm(w.layers[i + 1]["ln1"], x, ss, w.n, w.eps)
-        return FoldedNorm(w.norm, x, ss, w.n, w.eps) if decode else None
+            return FoldedNorm(w.layers[i + 1]["ln1"], x, ss, w.n, w.eps, M, w.F)
+        return FoldedNorm(w.norm, x, ss, w.n, w.eps, M, w.F) if decode else None
 
     def _reduce(self, src, lin, part, M, ws):
         """A row-parallel projection whose partial sums the group adds:
@@ -500,7 +500,7 @@ class LlamaSession:
             # the final norm folded into the lm_head (the last down projection
             # wrote h * norm and the partial sums)
             linear(self.x, w.lm_head, out_dev=self.logits, ws=self.lin_ws, M=B,
-                   fold_in=FoldedNorm(w.norm, self.x, self.ss, w.n, w.eps))
+                   fold_in=FoldedNorm(w.norm, self.x, self.ss, w.n, w.eps, B, w.F))
             n = 1 + 1 + 5 * w.L + 1
         else:
             self._final_norm(self.h, self.x, B, self._decode_part())

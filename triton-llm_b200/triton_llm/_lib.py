@@ -96,6 +96,7 @@ SIGNATURES: dict[str, list] = {
     # projections
     "tllm_linear_workspace": [_i, _i, _i, _psz, _psz],
     "tllm_linear_plan": [_i, _i, _i, _i, _pi],
+    "tllm_linear_fold_parts": [_i, _i, _i, _pi],
     "tllm_linear": [_vp, _i, _i, _vp, _i, _i, _i, _i, _i, _vp, _vp, _i, _i, _i,
                     _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i,
                     _vp, _vp, _vp, _sz, _vp, _vp],

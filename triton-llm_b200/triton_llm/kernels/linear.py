@@ -193,18 +193,30 @@ def to_split(x_dev, M=None, out=None, planes=2):
     return out
 
 
+def fold_parts(M: int, N: int, K: int) -> int:
+    """Partial sums per row a folded-norm producer (M, N, K) writes."""
+    out = ctypes.c_int(0)
+    _lib.call("tllm_linear_fold_parts", int(M), int(N), int(K), ctypes.byref(out))
+    return out.value
+
+
 class FoldedNorm:
     """An RMSNorm folded into the projections around it (tllm_norm_fold):
-    the projection that writes its input (op RESID) also writes ``fx`` =
-    h * ``weight`` in operand format and per-16-column sums of squares into
-    ``ss``; the projection that reads ``fx`` divides each output row by the
-    row's rms. ``fx`` is an operand buffer of at least ``rows`` rows; ``ss``
-    fp32 (ceil(hidden / 16), rows)."""
+    the projection that writes its input (op RESID; ``rows`` rows, K =
+    ``producer_k``) also writes ``fx`` = h * ``weight`` in operand format
+    and per-column-part sums of squares into ``ss``; the projection that
+    reads ``fx`` divides each output row by the row's rms. ``fx`` is an
+    operand buffer of at least ``rows`` rows; ``ss`` fp32
+    (>= ceil(hidden / 16), >= rows)."""
 
-    def __init__(self, weight, fx, ss, hidden: int, eps: float):
+    def __init__(self, weight, fx, ss, hidden: int, eps: float, rows: int,
+                 producer_k: int):
         self.weight, self.fx, self.ss = weight, fx, ss
         self.hidden, self.eps = int(hidden), float(eps)
-        self.parts = -(-self.hidden // 16)
+        self.parts = fold_parts(rows, self.hidden, producer_k)
+        if self.parts > int(ss.shape[0]) or rows > int(ss.shape[1]):
+            raise ValueError(f"partial-sum buffer {tuple(ss.shape)} too small for "
+                             f"{self.parts} parts x {rows} rows")
         self.ld = int(ss.shape[1])
 
     def producer(self):
