@@ -676,11 +676,29 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             // the sum of squares of h over this tile's 128 columns (the warp
             // holds the whole row of the tile)
             float sq = 0.f;
+            if (full && (o & 3) == 0 && (e.fx_plane & 3) == 0) {
+              // four adjacent operand values: one 8-byte store per plane
+              uint32_t hi[2], lo[2];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              if (n + k < p.N) {
-                store_act(e.fx, e.fx_plane, o + k, a[k] * fw[k], e.fx_planes);
+              for (int k = 0; k < 4; k += 2) {
+                const float f0 = a[k] * fw[k], f1 = a[k + 1] * fw[k + 1];
+                const uint16_t h0 = f32_to_bf16_bits(f0), h1 = f32_to_bf16_bits(f1);
+                hi[k / 2] = (uint32_t)h0 | ((uint32_t)h1 << 16);
+                lo[k / 2] = (uint32_t)f32_to_bf16_bits(f0 - bf16_bits_to_f32(h0)) |
+                            ((uint32_t)f32_to_bf16_bits(f1 - bf16_bits_to_f32(h1)) << 16);
                 sq = fmaf(a[k], a[k], sq);
+                sq = fmaf(a[k + 1], a[k + 1], sq);
+              }
+              *reinterpret_cast<uint2 *>(e.fx + o) = make_uint2(hi[0], hi[1]);
+              if (e.fx_planes == 2)
+                *reinterpret_cast<uint2 *>(e.fx + e.fx_plane + o) = make_uint2(lo[0], lo[1]);
+            } else {
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                if (n + k < p.N) {
+                  store_act(e.fx, e.fx_plane, o + k, a[k] * fw[k], e.fx_planes);
+                  sq = fmaf(a[k], a[k], sq);
+                }
               }
             }
 #pragma unroll
@@ -1025,7 +1043,7 @@ __device__ __forceinline__ const uint16_t *sk_w(const uint16_t *w, bool tiled, i
 template <int NB>
 __device__ __forceinline__ void sk_epilogue(const Epilogue &e, int N, int M, int r, int q,
                                             float (&v)[NB][4], unsigned bmask,
-                                            const float *s_rms) {
+                                            const float (&rrow)[NB][2]) {
   const int r1 = r + 8;
   const bool ok0 = r < N, ok1 = r1 < N;
   bool okm[NB][2];
@@ -1044,7 +1062,7 @@ __device__ __forceinline__ void sk_epilogue(const Epilogue &e, int N, int M, int
     for (int b = 0; b < NB; ++b)
 #pragma unroll
       for (int t = 0; t < 2; ++t) {
-        const float rms = okm[b][t] ? s_rms[mm[b][t]] : 1.f;
+        const float rms = okm[b][t] ? rrow[b][t] : 1.f;
         v[b][t] = v[b][t] / rms;
         v[b][2 + t] = v[b][2 + t] / rms;
       }
@@ -1190,12 +1208,34 @@ __global__ void __launch_bounds__(kSkWarps * 32)
     wb[u] = in ? ld_stream(sk_w(w, tiled, kc, K, nb8, k)) : z;
   }
   griddep_wait();   // the activations and the epilogue's inputs
-  __shared__ float s_rms[MT];
+  // folded RMSNorm consumer: the rms of this lane's activation rows
+  // b * 8 + 2q + t; the 8 lanes of one q split the partials (lane g adds
+  // parts g, g + 8, ...) and meet in a fixed butterfly. No block barrier:
+  // these loads overlap the activation loads below.
+  float rrow[NB][2];
+#pragma unroll
+  for (int b = 0; b < NB; ++b) rrow[b][0] = rrow[b][1] = 1.f;
   if (e.ss_in) {
-    // folded RMSNorm consumer: the whole CTA sums the partials of its rows
-    // (the weight loads above are in flight meanwhile)
-    fold_rms_rows(e, 0, MT, M, s_rms, threadIdx.x, kSkWarps * 32);
-    __syncthreads();
+    float acc_r[NB][2];
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int m = min(b * 8 + 2 * q + t, M - 1);
+        float a = 0.f;
+        for (int p = g; p < e.ss_parts; p += 8) a += e.ss_in[(size_t)p * e.ss_ld + m];
+        acc_r[b][t] = a;
+      }
+#pragma unroll
+    for (int b = 0; b < NB; ++b)
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        float a = acc_r[b][t];
+        a += __shfl_xor_sync(0xffffffffu, a, 4);
+        a += __shfl_xor_sync(0xffffffffu, a, 8);
+        a += __shfl_xor_sync(0xffffffffu, a, 16);
+        rrow[b][t] = sqrtf(a / (float)e.ss_cols + e.ss_eps);
+      }
   }
   float acc[NB][4];
 #pragma unroll
@@ -1275,7 +1315,7 @@ __global__ void __launch_bounds__(kSkWarps * 32)
   } else {
     if (!live) return;
   }
-  sk_epilogue<NB>(e, N, M, ra, q, acc, bmask, s_rms);
+  sk_epilogue<NB>(e, N, M, ra, q, acc, bmask, rrow);
 }
 
 template <int MT, int PL>
