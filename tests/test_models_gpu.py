@@ -423,21 +423,26 @@ def test_gpt2_cfg1_32_steps_match_reference(gpu, golden):
 
 @pytest.mark.parametrize("act", ["split", "bfloat16"])
 def test_folded_norms_equal_explicit_norms(gpu, monkeypatch, act):
-    """The engine with its RMSNorms folded into the projections (default)
-    and with every norm launched on its own (TLLM_NORM_FOLD=0): with hi + lo
-    projection inputs the same greedy tokens and logits to 1e-4; with one
-    bf16 plane the two round different values (h * w against the normalised
-    row), so only the first step's logits are compared, to bf16 rounding."""
+    """The engine with its RMSNorms folded into the projections (the default
+    where every projection runs on the tensor-core kernel: Llama-3.2-3B
+    widths) and with every norm launched on its own (TLLM_NORM_FOLD=0): with
+    hi + lo projection inputs the same greedy tokens and logits to 1e-4;
+    with one bf16 plane the two round different values (h * w against the
+    normalised row), so only the first step's logits are compared, to bf16
+    rounding."""
     from smollm2_triton import SmolLM2Config
-    from smollm2_triton.engine import LlamaWeights
-    w = inputs.round_linear_weights_bf16(inputs.llama_weights(inputs.SMOL_135M, 0))
-    cfg = SmolLM2Config(**inputs.SMOL_135M.config_kwargs())
+    from smollm2_triton.engine import LlamaSession, LlamaWeights
+    w = inputs.round_linear_weights_bf16(inputs.llama_weights(inputs.LLAMA3B_2L, 0))
+    cfg = SmolLM2Config(**inputs.LLAMA3B_2L.config_kwargs())
     wts = LlamaWeights(cfg, w, "bfloat16", max_pos=64)
     rng = np.random.default_rng(12)
-    prompts = [rng.integers(0, 49152, n).tolist() for n in (3, 20)]
+    prompts = [rng.integers(0, 128256, n).tolist() for n in (3, 20)]
     runs = []
     for fold in ("1", "0"):
         monkeypatch.setenv("TLLM_NORM_FOLD", fold)
+        probe = LlamaSession(wts, len(prompts), 64, act_dtype=act)
+        assert (probe.ss is not None) == (fold == "1")
+        del probe
         runs.append(_session_greedy(wts, prompts, 16, 64, act))
     for (ta, la), (tb, lb) in zip(*runs):
         if act == "split":

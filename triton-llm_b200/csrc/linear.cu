@@ -117,8 +117,17 @@ __device__ __forceinline__ void fold_rms_rows(const Epilogue &e, int m0, int row
     const int m = m0 + rl;
     float acc = 0.f;
     if (rl < rows && m < M) {
-#pragma unroll 4
-      for (int p = j; p < e.ss_parts; p += T) acc += e.ss_in[(size_t)p * e.ss_ld + m];
+      // eight loads in flight per round, added in part order
+      for (int p0 = j; p0 < e.ss_parts; p0 += 8 * T) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int pp = p0 + u * T;
+          v[u] = pp < e.ss_parts ? e.ss_in[(size_t)pp * e.ss_ld + m] : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) acc += v[u];
+      }
     }
     for (int o = T / 2; o >= 1; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
     if (j == 0 && rl < rows)

@@ -41,8 +41,8 @@ import numpy as np
 from triton_llm import gpu, _lib, shard
 from triton_llm.kernels import gqa_rows, gqa_prefill, prefill_blocks, DecodeWorkspace
 from triton_llm.kernels.attention_prefill import prefill_supported
-from triton_llm.kernels.linear import (FoldedNorm, Linear, LinearWorkspace, linear,
-                                       qkv_rows, swiglu_rows)
+from triton_llm.kernels.linear import (FoldedNorm, Linear, LinearWorkspace, kernel_name,
+                                       linear, qkv_rows, swiglu_rows)
 from triton_llm.kernels.rms_norm import (rms_norm_add_rows, rms_norm_p2p_rows,
                                          rms_norm_rows)
 from triton_llm.kernels.rope import precompute_cos_sin
@@ -244,10 +244,14 @@ class LlamaSession:
         self.act, self.logits = self._act(M, w.F), f(M, w.V)
         self.part = f(M, w.n) if self.tp is not None and self.tp.size > 1 else None
         # RMSNorms folded into the projections around them (bf16 weights,
-        # unsharded layers): per-16-column partial sums of squares of h
-        self.fold = (w.bf16 and self.part is None
-                     and os.environ.get("TLLM_NORM_FOLD", "1") != "0")
-        self.ss = f(-(-w.n // 16), M) if self.fold else None
+        # unsharded layers, every projection on the tensor-core kernel, whose
+        # idle warps sum the producer's partials during the weight stream; the
+        # skinny kernel would wait for those loads on its critical path):
+        # partial sums of squares of h per column part
+        self._fold_ok = (w.bf16 and self.part is None
+                         and os.environ.get("TLLM_NORM_FOLD", "1") != "0")
+        self.ss = (f(-(-w.n // 16), M) if self._fold_ok and self._all_tensor_core(M)
+                   else None)
         self.peer = None
         if self.part is not None and self._p2p:
             self.peer = self.tp.peer_group(M, w.n)
@@ -263,6 +267,12 @@ class LlamaSession:
                 and all(w.layers[0][k].tiled for k in ("o", "gu", "down"))):
             self.mlp_ws = _mlp.MlpWorkspace(M, w.H * w.D, w.n, w.F)
 
+    def _all_tensor_core(self, M):
+        """Whether every projection of a layer (and the lm_head) runs on the
+        tcgen05 kernel for M rows."""
+        return all(kernel_name(m, n, k) == "linear_tc_kernel"
+                   for (m, n, k) in self.w.linear_shapes(M))
+
     def _prefill_buffers(self, M, attn_budget):
         w = self.w
         f = lambda *s: gpu.allocate(s, np.float32)  # noqa: E731
@@ -270,7 +280,8 @@ class LlamaSession:
         self.p_q, self.p_attn = f(M, w.H, w.D), self._act(M, w.H * w.D)
         self.p_act = self._act(M, w.F)
         self.p_part = f(M, w.n) if self.part is not None else None
-        self.p_ss = f(-(-w.n // 16), M) if self.fold else None
+        self.p_ss = (f(-(-w.n // 16), M) if self._fold_ok and self._all_tensor_core(M)
+                     else None)
         self.p_ids = gpu.allocate((M,), np.int32)
         self.p_seq = gpu.allocate((M,), np.int32)
         self.p_pos = gpu.allocate((M,), np.int32)
