@@ -269,8 +269,8 @@ int tllm_gqa_rows(const float *q, long q_row_stride, long q_head_stride,
  *     fx[m, n] = out[m, n] * next_norm_w[n] in operand format (fx_dtype
  *     TLLM_SPLIT or TLLM_BF16, planes fx_plane_rows rows apart, rows of N)
  *     and ss_out[p * ss_ld + m] = sum of out[m, n]^2 over column part p
- *     (tllm_linear_fold_parts gives the number of parts per row: the
- *     128-column tiles or the 16-column blocks of the kernel that runs);
+ *     (the 128-column weight tiles: tllm_linear_fold_parts gives their
+ *     number); a folded call always runs on the tensor-core kernel;
  *   consumer (op STORE, SWIGLU or QKV, the projection that reads fx):
  *     divides row m of the product by
  *     sqrt(sum_{p < ss_parts} ss_in[p * ss_ld + m] / ss_cols + eps)

@@ -747,9 +747,9 @@ def test_folded_norm_producer(gpu, M, N, K, planes):
     else:
         hi = ops.bf16_round(want_fx)
         np.testing.assert_array_equal(got_fx, hi + ops.bf16_round(want_fx - hi))
-    from triton_llm.kernels.linear import fold_parts, kernel_name
+    from triton_llm.kernels.linear import fold_parts
     parts = fold_parts(M, N, K)
-    width = 16 if kernel_name(M, N, K) == "linear_mma_kernel" else 128
+    width = 128      # folded calls run on the tensor-core kernel: one part per tile
     assert parts == -(-N // width)
     pad = np.zeros((M, parts * width), np.float64)
     pad[:, :N] = h.astype(np.float64) ** 2
@@ -811,8 +811,8 @@ def test_folded_norm_consumer(gpu, op, M, planes):
     xa = gpu.act_empty(M, n, planes)
     rms_norm_rows(hd, wd, xa, M, 1e-5)
     want = run(xa, None)
-    # folded: the operand h * w and the partial sums a skinny producer
-    # (M rows, K = 576: 16-column parts) would write
+    # folded: the operand h * w and partial sums over 16-column parts (the
+    # consumer adds whatever parts it is given)
     fx = gpu.to_device_split((h * wn).astype(F32), planes=planes)
     parts = n // 16
     ssh = (h.astype(F32) ** 2).reshape(M, parts, 16).sum(axis=2, dtype=F32).T.copy()

@@ -84,10 +84,10 @@ struct Epilogue {
   int *err;
   // EPI_SCATTER
   const P2PDev *p2p;
-  // RMSNorm folded into the neighbouring projections. Producer (EPI_RESID):
-  // besides out, fx[m, n] = out[m, n] * fx_w[n] in operand format and
-  // ss_out[part * ss_ld + m] = sum of out[m, n]^2 over each column part (the
-  // 128 columns of a tcgen05 tile, the 16 of a skinny weight block).
+  // RMSNorm folded into the neighbouring projections (tcgen05 kernel only).
+  // Producer (EPI_RESID): besides out, fx[m, n] = out[m, n] * fx_w[n] in
+  // operand format and ss_out[tile * ss_ld + m] = sum of out[m, n]^2 over
+  // each 128-column weight tile.
   // Consumer (EPI_STORE / EPI_SWIGLU / EPI_QKV): row m of the product divided
   // by sqrt(sum_{p < ss_parts} ss_in[p * ss_ld + m] / ss_cols + eps).
   const float *fx_w;
@@ -1051,8 +1051,7 @@ __device__ __forceinline__ const uint16_t *sk_w(const uint16_t *w, bool tiled, i
 // memory round trip per row.
 template <int NB>
 __device__ __forceinline__ void sk_epilogue(const Epilogue &e, int N, int M, int r, int q,
-                                            float (&v)[NB][4], unsigned bmask,
-                                            const float (&rrow)[NB][2]) {
+                                            const float (&v)[NB][4], unsigned bmask) {
   const int r1 = r + 8;
   const bool ok0 = r < N, ok1 = r1 < N;
   bool okm[NB][2];
@@ -1065,17 +1064,6 @@ __device__ __forceinline__ void sk_epilogue(const Epilogue &e, int N, int M, int
       okm[b][t] = ((bmask >> b) & 1) && mm[b][t] < M;
     }
   const int op = e.op;
-  if (e.ss_in && op != EPI_RESID) {
-    // folded RMSNorm consumer: row m of the product divided by its rms
-#pragma unroll
-    for (int b = 0; b < NB; ++b)
-#pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        const float rms = okm[b][t] ? rrow[b][t] : 1.f;
-        v[b][t] = v[b][t] / rms;
-        v[b][2 + t] = v[b][2 + t] / rms;
-      }
-  }
   if (op == EPI_STORE || op == EPI_RESID || op == EPI_GELU) {
     const float b0 = e.bias && ok0 ? e.bias[r] : 0.f;
     const float b1 = e.bias && ok1 ? e.bias[r1] : 0.f;
@@ -1106,36 +1094,6 @@ __device__ __forceinline__ void sk_epilogue(const Epilogue &e, int N, int M, int
         if (ok0) store_out(e, o + r, a0);
         if (ok1) store_out(e, o + r1, a1);
       }
-    if (op == EPI_RESID && e.ss_out) {
-      // the next RMSNorm, folded: h * w as its projection's operand and the
-      // sums of squares of h over this 16-row weight block (the 8 lanes of
-      // one q hold its rows r, r + 8 for the same activation rows)
-      const float w0 = ok0 ? e.fx_w[r] : 0.f, w1 = ok1 ? e.fx_w[r1] : 0.f;
-#pragma unroll
-      for (int b = 0; b < NB; ++b)
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          const size_t o = (size_t)mm[b][t] * e.ld_out;
-          const float a0 = v[b][t] + b0 + rv[b][t][0];
-          const float a1 = v[b][2 + t] + b1 + rv[b][t][1];
-          float sq = 0.f;
-          if (okm[b][t]) {
-            if (ok0) {
-              store_act(e.fx, e.fx_plane, o + r, a0 * w0, e.fx_planes);
-              sq = fmaf(a0, a0, sq);
-            }
-            if (ok1) {
-              store_act(e.fx, e.fx_plane, o + r1, a1 * w1, e.fx_planes);
-              sq = fmaf(a1, a1, sq);
-            }
-          }
-          sq += __shfl_xor_sync(0xffffffffu, sq, 4);
-          sq += __shfl_xor_sync(0xffffffffu, sq, 8);
-          sq += __shfl_xor_sync(0xffffffffu, sq, 16);
-          if (okm[b][t] && (threadIdx.x & 31) < 4)
-            e.ss_out[(size_t)(r >> 4) * e.ss_ld + mm[b][t]] = sq;
-        }
-    }
   } else if (op == EPI_SWIGLU) {
     if (!ok1) return;
     const int j = (r >> 4) * 8 + (r & 7);
@@ -1217,35 +1175,6 @@ __global__ void __launch_bounds__(kSkWarps * 32)
     wb[u] = in ? ld_stream(sk_w(w, tiled, kc, K, nb8, k)) : z;
   }
   griddep_wait();   // the activations and the epilogue's inputs
-  // folded RMSNorm consumer: the rms of this lane's activation rows
-  // b * 8 + 2q + t; the 8 lanes of one q split the partials (lane g adds
-  // parts g, g + 8, ...) and meet in a fixed butterfly. No block barrier:
-  // these loads overlap the activation loads below.
-  float rrow[NB][2];
-#pragma unroll
-  for (int b = 0; b < NB; ++b) rrow[b][0] = rrow[b][1] = 1.f;
-  if (e.ss_in) {
-    float acc_r[NB][2];
-#pragma unroll
-    for (int b = 0; b < NB; ++b)
-#pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        const int m = min(b * 8 + 2 * q + t, M - 1);
-        float a = 0.f;
-        for (int p = g; p < e.ss_parts; p += 8) a += e.ss_in[(size_t)p * e.ss_ld + m];
-        acc_r[b][t] = a;
-      }
-#pragma unroll
-    for (int b = 0; b < NB; ++b)
-#pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        float a = acc_r[b][t];
-        a += __shfl_xor_sync(0xffffffffu, a, 4);
-        a += __shfl_xor_sync(0xffffffffu, a, 8);
-        a += __shfl_xor_sync(0xffffffffu, a, 16);
-        rrow[b][t] = sqrtf(a / (float)e.ss_cols + e.ss_eps);
-      }
-  }
   float acc[NB][4];
 #pragma unroll
   for (int b = 0; b < NB; ++b)
@@ -1324,7 +1253,7 @@ __global__ void __launch_bounds__(kSkWarps * 32)
   } else {
     if (!live) return;
   }
-  sk_epilogue<NB>(e, N, M, ra, q, acc, bmask, rrow);
+  sk_epilogue<NB>(e, N, M, ra, q, acc, bmask);
 }
 
 template <int MT, int PL>
@@ -1657,10 +1586,11 @@ int tllm_linear_workspace(int M, int N, int K, size_t *partial_bytes,
 }
 
 int tllm_linear_fold_parts(int M, int N, int K, int *parts) {
+  // a folded call always runs on the tensor-core kernel: one part per
+  // 128-column weight tile
   TLLM_CHECK_ARG(parts, "NULL output");
   TLLM_CHECK_ARG(M > 0 && N > 0 && K > 0, "M, N, K must be > 0");
-  const bool skinny = M <= sk_max_m() && (size_t)N * K * 2 <= sk_max_bytes();
-  *parts = skinny ? (N + 15) / 16 : (N + kTcBN - 1) / kTcBN;
+  *parts = (N + kTcBN - 1) / kTcBN;
   return TLLM_OK;
 }
 
@@ -1833,7 +1763,11 @@ int tllm_linear_folded(const void *x, int x_dtype, int x_plane_rows, const void 
   (void)partial;
   (void)partial_bytes;
   (void)counters;
-  if (op != EPI_SCATTER && M <= sk_max_m() && (size_t)N * K * 2 <= sk_max_bytes()) {
+  // the skinny kernel has no folded-norm epilogues: folded calls take the
+  // tensor-core kernel, whose idle warps sum the partials during the stream
+  const bool folded = e.ss_in || e.ss_out;
+  if (op != EPI_SCATTER && !folded && M <= sk_max_m() &&
+      (size_t)N * K * 2 <= sk_max_bytes()) {
     // K slices per 16-row block: enough warps for two CTAs of 8 on every
     // SM, at least one 32-k step each
     const int blocks16 = (N + 15) / 16;
