@@ -719,11 +719,13 @@ def test_mlp_block_rejects_bad_shapes(gpu):
 # ---------------------------------------------------------- folded RMSNorm --
 @pytest.mark.parametrize("planes", [1, 2])
 @pytest.mark.parametrize("M,N,K", [(64, 3072, 3072), (8, 576, 576), (33, 1000, 1536)])
-def test_folded_norm_producer(gpu, M, N, K, planes):
-    """op RESID with a folded norm: h is what the plain RESID call writes
-    (bit for bit), fx = the operand format of h * w, and the partial sums
-    are the sums of squares of h over each 16-column block."""
+def test_folded_norm_producer(gpu, monkeypatch, M, N, K, planes):
+    """op RESID with a folded norm: h is what the plain RESID call on the
+    same (tensor-core) kernel writes, bit for bit; fx = the operand format of
+    h * w; the partial sums are the sums of squares of h over each 128-column
+    weight tile."""
     from triton_llm import _lib
+    monkeypatch.setenv("TLLM_SKINNY_MAX_M", "0")   # the plain call on tcgen05 too
     from triton_llm.kernels.linear import FoldedNorm, Linear, LinearWorkspace, linear
     rng = np.random.default_rng(M + N)
     lin = Linear((rng.standard_normal((N, K), dtype=F32) * 0.05).astype(F32), "bfloat16")
