@@ -954,9 +954,12 @@ int dispatch_d(int D, int G, const DecodeParams &p, const CUtensorMap &mk,
   return TLLM_ERR_UNSUPPORTED;
 }
 
+// The mma kernel instance for G query heads, its dynamic shared memory, and
+// its CTAs per SM (the attribute is set once per device and instance).
 template <int D>
-int launch_mma(const DecodeParams &p, int G, const CUtensorMap &mk,
-               const CUtensorMap &mv, dim3 grid, cudaStream_t st) {
+int mma_kernel_setup(int G, void (**kern_out)(const DecodeParams, const int,
+                                              const CUtensorMap, const CUtensorMap),
+                     size_t *smem_out, int *per_sm) {
   using S = MmaShape<D>;
   const size_t merge = (size_t)kConsumerWarps * G * (D + 2) * sizeof(float);
   const size_t sweights = (size_t)G * kMaxSplits * sizeof(float);
@@ -966,16 +969,50 @@ int launch_mma(const DecodeParams &p, int G, const CUtensorMap &mk,
   // query heads per CTA as n8 blocks of the swapped MMA
   auto kern = G <= 8 ? gqa_decode_mma_kernel<D, 1> : gqa_decode_mma_kernel<D, 2>;
   static bool configured[64][2] = {};
+  static int occ[64][2] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   const int qi = G <= 8 ? 0 : 1;
   if (dev < 0 || dev >= 64 || !configured[dev][qi]) {
     TLLM_CUDA(cudaFuncSetAttribute(
         kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    if (dev >= 0 && dev < 64) configured[dev][qi] = true;
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kThreads, smem) !=
+        cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
+    }
+    if (dev >= 0 && dev < 64) {
+      configured[dev][qi] = true;
+      occ[dev][qi] = n;
+    }
   }
+  *kern_out = kern;
+  *smem_out = smem;
+  if (per_sm) *per_sm = (dev >= 0 && dev < 64) ? occ[dev][qi] : 0;
+  return TLLM_OK;
+}
+
+template <int D>
+int launch_mma(const DecodeParams &p, int G, const CUtensorMap &mk,
+               const CUtensorMap &mv, dim3 grid, cudaStream_t st) {
+  void (*kern)(const DecodeParams, const int, const CUtensorMap, const CUtensorMap);
+  size_t smem = 0;
+  int rc = mma_kernel_setup<D>(G, &kern, &smem, nullptr);
+  if (rc) return rc;
   TLLM_CUDA(launch_pdl(kern, grid, dim3(kThreads), smem, st, p, G, mk, mv));
   return TLLM_OK;
+}
+
+// CTAs of the mma kernel that are resident at once on this device (0 if
+// unknown).
+int mma_slots(int head_dim, int G) {
+  void (*kern)(const DecodeParams, const int, const CUtensorMap, const CUtensorMap);
+  size_t smem = 0;
+  int per_sm = 0;
+  int rc = head_dim == 64 ? mma_kernel_setup<64>(G, &kern, &smem, &per_sm)
+                          : mma_kernel_setup<128>(G, &kern, &smem, &per_sm);
+  return rc ? 0 : per_sm * sm_count();
 }
 
 bool use_mma(int kv_dtype, int D) {
@@ -998,10 +1035,13 @@ int pick_group_tile_mma(int group) {
 // long chunks amortise, while too few CTAs leave SMs idle; on B200 the best
 // chunk measured was ~3/8 of the longest sequence's tiles, between 3 and 32
 // tiles (config 2: 12 of 32, config 3: 3-4 of 12, config 4: 16-32 of 128).
-// Never more than kMaxSplits splits.
-int pick_chunk(int rows, int batch, int ygrid, int max_len) {
-  (void)batch;
-  (void)ygrid;
+// With few long sequences (batch x KV-head groups small against the GPU:
+// config 5 at TP = 8 has 8 sequences x 1 KV head of 32768 keys) that chunk
+// leaves SMs idle, so the chunk is also capped at the size that fills ~85 %
+// of one wave of resident CTAs (`slots`; 0 = unknown): 16-17 tiles there
+// measured 0.66 of HBM against 0.51 with 32, while a grid just over one
+// wave (12 tiles) fell to 0.48. Never more than kMaxSplits splits.
+int pick_chunk(int rows, int batch, int ygrid, int max_len, int slots) {
   const long tiles = (max_len + rows - 1) / rows;
   if (tiles <= 1) return rows;
   static int env_tiles = -1;
@@ -1016,6 +1056,12 @@ int pick_chunk(int rows, int batch, int ygrid, int max_len) {
     chunk_tiles = (3 * tiles + 7) / 8;
     if (chunk_tiles < 3) chunk_tiles = 3;
     if (chunk_tiles > 32) chunk_tiles = 32;
+    if (slots > 0) {
+      const long work = (long)batch * ygrid * tiles;
+      long fill = (work * 100 + 85L * slots - 1) / (85L * slots);
+      if (fill < 3) fill = 3;
+      if (fill < chunk_tiles) chunk_tiles = fill;
+    }
   }
   long min_tiles = (tiles + kMaxSplits - 1) / kMaxSplits;
   if (chunk_tiles < min_tiles) chunk_tiles = min_tiles;
@@ -1069,7 +1115,8 @@ static int rows_impl(const float *q, long q_sb, long q_sh, const void *k_cache,
   const int ygrid = n_kv_head * n_gsub;
   TLLM_CHECK_ARG(ygrid <= 65535 && batch <= 65535, "grid too large");
 
-  int chunk = pick_chunk(rows, batch, ygrid, max_len);
+  int chunk = pick_chunk(rows, batch, ygrid, max_len,
+                         mma ? mma_slots(head_dim, G) : 0);
   int max_splits = (max_len + chunk - 1) / chunk;
   if (max_splits < 1) max_splits = 1;
   if (max_splits > 1) {
