@@ -506,69 +506,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 
   // ---- epilogue ----
-  // 0. while the MMAs finish: the inputs of this warp's first pass of rows
-  //    (residual rows; positions, sequences and RoPE table entries) into
-  //    registers, so the row epilogue does not wait on global memory
-  const int S = p.S;
-  const int rank = S > 1 ? (int)cluster_ctarank() : 0;
-  const int row0 = nt * kTcBN;
-  const int mlb0 = rank + warp * S;
-  griddep_wait();   // the epilogue reads / writes buffers of earlier kernels
-  float pre_rv[kTcRB][4];
-  int pre_pos[kTcRB], pre_seq[kTcRB];
-  float pre_cs[kTcRB][2], pre_sn[kTcRB][2];
-#pragma unroll
-  for (int i = 0; i < kTcRB; ++i) {
-    const int ml = mlb0 + i * kTcWarps * S;
-    const int m = mt * MT + ml;
-    const bool okr = ml < MT && m < p.M;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) pre_rv[i][k] = 0.f;
-    pre_pos[i] = pre_seq[i] = -1;
-    pre_cs[i][0] = pre_cs[i][1] = 1.f;
-    pre_sn[i][0] = pre_sn[i][1] = 0.f;
-    if constexpr (OP == EPI_RESID) {
-      const int n = row0 + lane * 4;
-      if (okr) {
-        const size_t o = (size_t)m * p.e.ld_out + n;
-        if (n + 3 < p.N && (o & 3) == 0) {
-          const float4 t = *reinterpret_cast<const float4 *>(&p.e.resid[o]);
-          pre_rv[i][0] = t.x;
-          pre_rv[i][1] = t.y;
-          pre_rv[i][2] = t.z;
-          pre_rv[i][3] = t.w;
-        } else {
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            if (n + k < p.N) pre_rv[i][k] = p.e.resid[o + k];
-        }
-      }
-    }
-    if constexpr (OP == EPI_QKV) {
-      if (okr) {
-        pre_pos[i] = p.e.row_pos[m];
-        pre_seq[i] = p.e.row_seq[m];
-        const int ps = pre_pos[i];
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int pr = lane * 2 + h;
-          const int r = row0 + (pr >> 3) * 16 + (pr & 7);
-          if (p.e.cos && r + 8 < p.N && ps >= 0 && ps < p.e.max_seq) {
-            const QkvGeom g = qkv_geom(p.e, r);
-            if (!g.is_v) {
-              const size_t t = (size_t)ps * (p.e.D / 2) + g.d0;
-              pre_cs[i][h] = p.e.cos[t];
-              pre_sn[i][h] = p.e.sin[t];
-            }
-          }
-        }
-      }
-    }
-  }
   // 1. the four warps copy the accumulator (TMEM lanes 32*warp..+31) into
   //    shared memory, column-major: tile[m * 128 + r] (the rings are free)
   const bool acc_ok = mbar_wait_bounded(accb, 0);
   tc_fence_after();
+  griddep_wait();   // the epilogue reads / writes buffers of earlier kernels
   if constexpr (OP == EPI_SCATTER) {
     // calls completed so far (this rank's reader of the previous call has
     // finished): this call's number
@@ -591,26 +533,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (int j = 0; j < CW; ++j) v[j] = 0.f;
     if (valid) {
       const int nacc = NACC / NI;
-      // two accumulators per TMEM round trip, added in accumulator order
-      // (fixed: deterministic); an issuer that got no chunk adds nothing
 #pragma unroll 1
-      for (int acc = 0; acc < NACC; acc += 2) {
-        float u[CW], w2[CW];
-        const bool e0 = s_empty_acc[acc / nacc] != 0;
-        const bool e1 = acc + 1 >= NACC || s_empty_acc[(acc + 1) / nacc] != 0;
-        tmem_ld_pair<CW>(t_lane + acc * MT + c0,
-                         t_lane + (acc + 1 < NACC ? acc + 1 : acc) * MT + c0, u, w2);
+      for (int acc = 0; acc < NACC; ++acc) {   // fixed order: deterministic
+        if (s_empty_acc[acc / nacc]) continue;
+        float u[CW];
+        if constexpr (CW == 32)
+          tmem_ld32(t_lane + acc * MT + c0, u);
+        else
+          tmem_ld16(t_lane + acc * MT + c0, u);
 #pragma unroll
-        for (int j = 0; j < CW; ++j) {
-          if (!e0) v[j] += u[j];
-          if (!e1) v[j] += w2[j];
-        }
+        for (int j = 0; j < CW; ++j) v[j] += u[j];
       }
     }
 #pragma unroll
     for (int j = 0; j < CW; ++j) tile[(c0 + j) * kTcBN + r_own] = v[j];
   }
   // 2. every split of this tile has staged its partial
+  const int S = p.S;
   if (S > 1)
     cluster_sync();
   else
@@ -619,10 +558,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   //    tile, one warp per row: the splits are summed in rank order and the
   //    epilogue stores whole output rows (lane l covers weight rows
   //    4l .. 4l + 3 of the tile)
+  const int rank = S > 1 ? (int)cluster_ctarank() : 0;
   const uint32_t tile_s = smem_u32(tile);
+  const int row0 = nt * kTcBN;
 #pragma unroll 1
-  for (int mlb = mlb0; mlb < MT; mlb += kTcWarps * S * kTcRB) {
-    const bool first_pass = mlb == mlb0;
+  for (int mlb = rank + warp * S; mlb < MT; mlb += kTcWarps * S * kTcRB) {
     int mrow[kTcRB];
     bool in_tile[kTcRB], ok[kTcRB];
 #pragma unroll
@@ -700,10 +640,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
         for (int i = 0; i < kTcRB; ++i) {
 #pragma unroll
-          for (int k = 0; k < 4; ++k) rv[i][k] = first_pass ? pre_rv[i][k] : 0.f;
+          for (int k = 0; k < 4; ++k) rv[i][k] = 0.f;
           if constexpr (OP == EPI_RESID) {
             const size_t o = (size_t)mrow[i] * e.ld_out + n;
-            if (!ok[i] || first_pass) continue;
+            if (!ok[i]) continue;
             if (full && (o & 3) == 0) {
               const float4 t = *reinterpret_cast<const float4 *>(&e.resid[o]);
               rv[i][0] = t.x;
@@ -860,36 +800,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           b1[h] = (e.bias && live[h]) ? e.bias[r + 8] : 0.f;
         }
         int pos[kTcRB], seq[kTcRB];
+#pragma unroll
+        for (int i = 0; i < kTcRB; ++i) {
+          pos[i] = ok[i] ? e.row_pos[mrow[i]] : -1;
+          seq[i] = ok[i] ? e.row_seq[mrow[i]] : -1;
+        }
         float cs[kTcRB][2], sn[kTcRB][2];
-        if (first_pass) {
 #pragma unroll
-          for (int i = 0; i < kTcRB; ++i) {
-            pos[i] = pre_pos[i];
-            seq[i] = pre_seq[i];
+        for (int i = 0; i < kTcRB; ++i) {
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              cs[i][h] = pre_cs[i][h];
-              sn[i][h] = pre_sn[i][h];
-            }
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < kTcRB; ++i) {
-            pos[i] = ok[i] ? e.row_pos[mrow[i]] : -1;
-            seq[i] = ok[i] ? e.row_seq[mrow[i]] : -1;
-          }
-#pragma unroll
-          for (int i = 0; i < kTcRB; ++i) {
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              cs[i][h] = 1.f;
-              sn[i][h] = 0.f;
-              if (ok[i] && live[h] && e.cos && !g[h].is_v && pos[i] >= 0 &&
-                  pos[i] < e.max_seq) {
-                const size_t t = (size_t)pos[i] * (e.D / 2) + g[h].d0;
-                cs[i][h] = e.cos[t];
-                sn[i][h] = e.sin[t];
-              }
+          for (int h = 0; h < 2; ++h) {
+            cs[i][h] = 1.f;
+            sn[i][h] = 0.f;
+            if (ok[i] && live[h] && e.cos && !g[h].is_v && pos[i] >= 0 &&
+                pos[i] < e.max_seq) {
+              const size_t t = (size_t)pos[i] * (e.D / 2) + g[h].d0;
+              cs[i][h] = e.cos[t];
+              sn[i][h] = e.sin[t];
             }
           }
         }
