@@ -447,6 +447,19 @@ int tllm_embedding(const int32_t *ids, const void *wte, int wte_dtype,
  * pos_inc[m] += 1 when pos_inc != NULL. ld = row stride (0: V). */
 int tllm_argmax(const float *logits, int M, int V, int ld, int32_t *ids,
                 int32_t *pos_inc, tllm_stream_t stream);
+/* Temperature / top-k sample of each row (smollm2_triton/model.py:566-582):
+ * ids[m] = the first index i (index order) whose cumulative weight
+ * exp(logits[m,i]/T - max) / sum exceeds u[m], over the top_k largest
+ * entries when 0 < top_k < V (ties at the threshold keep the lowest indices),
+ * else over all V. u[m] in [0, 1) is the uniform the reference's
+ * np.random.choice draws (random_sample()); the caller draws it from the same
+ * generator so the random stream is consumed as the reference consumes it.
+ * temperature must be > 1e-6 (the reference takes argmax below that: call
+ * tllm_argmax). pos_inc[m] += 1 when pos_inc != NULL; ld = row stride (0: V).
+ * u is device memory, 8-byte aligned. */
+int tllm_sample(const float *logits, int M, int V, int ld, float temperature,
+                int top_k, const double *u, int32_t *ids, int32_t *pos_inc,
+                tllm_stream_t stream);
 /* triton_llm/kernels/rope.py:153-222: in-place rotate-half RoPE of x
  * (n_rows, d), row r at position (r % seq_len) + position_offset, tables
  * (max_seq, d/2) f32. */

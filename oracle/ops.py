@@ -228,3 +228,37 @@ def softmax(x):
 def argmax(logits):
     """Greedy sampling: first maximal index (smollm2_triton/model.py:583)."""
     return np.argmax(np.asarray(logits), axis=-1)
+
+
+def sample(logits, temperature, top_k, u):
+    """Temperature / top-k sampling (smollm2_triton/model.py:566-582) with
+    the uniform ``u`` that np.random.choice would draw.
+
+    Restates the reference's arithmetic: scaled = logits / T in float32,
+    probs = exp(scaled - max) in float32 widened to float64 and normalised;
+    with 0 < top_k the top_k largest probabilities are kept and renormalised
+    (np.argpartition). Here they are the top_k largest logits, which are top_k
+    largest probabilities because exp(x / T - max) does not decrease in x;
+    among equal logits the lowest indices are kept (the reference leaves the
+    choice among equal probabilities open). Then NumPy's
+    choice(V, p=probs): cdf = cumsum(p); cdf /= cdf[-1]; the sample is
+    cdf.searchsorted(u, side='right'), the first index whose cdf exceeds u.
+    ``temperature`` must be > 1e-6 (the reference takes argmax below that).
+    """
+    return int(sample_cdf(logits, temperature, top_k).searchsorted(float(u), side="right"))
+
+
+def sample_cdf(logits, temperature, top_k):
+    """The normalised cdf ``sample`` searches (for boundary-distance checks)."""
+    x = np.asarray(logits, F32).reshape(-1)
+    scaled = (x / F32(temperature)).astype(F32)
+    probs = np.exp(scaled - np.max(scaled)).astype(np.float64)
+    probs = probs / np.sum(probs)
+    if top_k > 0:
+        k = min(int(top_k), len(probs))
+        order = np.argsort(-x, kind="stable")[:k]
+        filtered = np.zeros_like(probs)
+        filtered[order] = probs[order]
+        probs = filtered / filtered.sum()
+    cdf = np.cumsum(probs)
+    return cdf / cdf[-1]

@@ -21,6 +21,10 @@ Fixtures written next to this script (small .npz files, committed):
                      rounded to bf16, 4-token prompt + 2 greedy steps
   gpt2_small_slice.npz (--slow) GPT-2 small N(0,0.02) seed 0, 8-token
                      prompt + 2 greedy steps
+  sample.npz         the reference's _sample (temperature / top-k) on
+                     inputs.SAMPLE_CASES after np.random.seed(case.rng),
+                     and a tiny SmolLM2 run sampled at T=0.8, top_k=20
+                     (np.random.seed(7)): tokens and per-step logits
   gpt2_cfg1.npz      (--slow) BASELINE config 1: GPT-2 small N(0,0.02) seed
                      0, 32-token prompt + 32 greedy steps; tokens and a
                      digest of the per-step logits (inputs.logits_digest)
@@ -191,6 +195,39 @@ def smol_run(shape, weights, prompt, n_new):
     return np.array(toks, np.int32), np.stack(steps)
 
 
+def smol_sampled_run(shape, weights, prompt, n_new, temperature, top_k, seed):
+    """The reference's generate loop (model.py:455-469) with sampling, after
+    np.random.seed(seed); keeps the per-step logits."""
+    from smollm2_triton.config import SmolLM2Config
+    from smollm2_triton.model import SmolLM2ForCausalLM
+    cfg = SmolLM2Config(**shape.config_kwargs())
+    model = SmolLM2ForCausalLM(cfg, weights)
+    model._init_cache_gpu(max_seq=len(prompt) + n_new)
+    np.random.seed(seed)
+    logits = model._forward_cached(np.array([prompt], np.int32))
+    toks = list(prompt)
+    steps = []
+    for step in range(n_new):
+        last = logits[0, -1]
+        steps.append(last.copy())
+        t = model._sample(last, temperature, top_k)
+        toks.append(t)
+        if step < n_new - 1:
+            logits = model._forward_cached(np.array([[t]], np.int32))
+    return np.array(toks, np.int32), np.stack(steps)
+
+
+def sample_cases():
+    """The reference's _sample on each of inputs.SAMPLE_CASES."""
+    from smollm2_triton.model import SmolLM2ForCausalLM
+    toks = []
+    for c in inputs.SAMPLE_CASES:
+        np.random.seed(c.rng)
+        toks.append(SmolLM2ForCausalLM._sample(None, inputs.sample_logits(c),
+                                               c.temperature, c.top_k))
+    return np.array(toks, np.int64)
+
+
 def gpt2_run(shape, weights, prompt, n_new):
     from gpt2_triton.config import GPT2Config
     from gpt2_triton.model import GPT2Model
@@ -227,6 +264,17 @@ def main():
         toks, logits = smol_run(inputs.SMOL_TINY, w, [5, 12, 7], 5)
         _log(f"  tokens {toks.tolist()}")
         np.savez_compressed(HERE / "smol_tiny.npz", tokens=toks, logits=logits)
+    if want("sample"):
+        _log("sample")
+        case_tokens = sample_cases()
+        w = inputs.llama_weights_legacy(inputs.SMOL_TINY, seed=42)
+        toks, logits = smol_sampled_run(inputs.SMOL_TINY, w, [5, 12, 7], 16,
+                                        0.8, 20, 7)
+        _log(f"  cases {case_tokens.tolist()}")
+        _log(f"  tiny sampled tokens {toks.tolist()}")
+        np.savez_compressed(HERE / "sample.npz", case_tokens=case_tokens,
+                            tiny_tokens=toks, tiny_logits=logits,
+                            tiny_meta=np.array([0.8, 20, 7], np.float64))
     if want("gpt2_tiny"):
         _log("gpt2_tiny")
         w = inputs.gpt2_weights_legacy(inputs.GPT2_TINY, seed=42)

@@ -318,3 +318,47 @@ def pack_cache(seqs, max_seq):
     for b, s in enumerate(seqs):
         out[b, :, : s.shape[1]] = s
     return out
+
+
+# ------------------------------------------------ temperature / top-k ----
+@dataclass(frozen=True)
+class SampleCase:
+    """One call of the reference's ``_sample(logits, temperature, top_k)``
+    after ``np.random.seed(rng)``: logits = N(0,1) * scale (default_rng(seed),
+    float32) of length V."""
+    seed: int
+    V: int
+    scale: float
+    temperature: float
+    top_k: int
+    rng: int
+
+
+def _sample_cases():
+    vocabs = (100, 49152, 50257, 128256)
+    temps = (0.3, 0.7, 1.0, 1.5)
+    ks = (0, 1, 5, 50, 1000, -1, -2)   # -1: top_k = V, -2: top_k = V + 7
+    scales = (1.0, 3.0, 8.0)
+    out = []
+    for i in range(48):
+        V = vocabs[i % 4]
+        k = ks[(i // 4) % 7]
+        k = V if k == -1 else V + 7 if k == -2 else min(k, V)
+        out.append(SampleCase(seed=100 + i, V=V, scale=scales[i % 3],
+                              temperature=temps[(i // 2) % 4], top_k=k,
+                              rng=1000 + i))
+    return tuple(out)
+
+
+SAMPLE_CASES = _sample_cases()
+
+
+def sample_logits(case: SampleCase) -> np.ndarray:
+    rng = np.random.default_rng(case.seed)
+    return (rng.standard_normal(case.V, dtype=F32) * F32(case.scale)).astype(F32)
+
+
+def sample_uniform(rng_seed: int, n: int = 1) -> np.ndarray:
+    """The uniforms np.random.choice draws after np.random.seed(rng_seed):
+    one random_sample() per call, from the legacy global generator."""
+    return np.random.RandomState(rng_seed).random_sample(n)

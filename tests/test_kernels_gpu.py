@@ -8,7 +8,9 @@ projection (tllm_linear) is checked against an fp64 product of the weights
 the device holds; bf16 weights are exact, the activations are split into a
 bf16 head and residual, so the bound is 3e-5 of the row's sum |x| |w|.
 KV append through the QKV epilogue is checked bit-exact against the oracle's
-rotation of the same projection output.
+rotation of the same projection output. Temperature / top-k draws equal the
+oracle's (itself pinned to the reference's _sample) unless the uniform lies
+within 1e-6 of every cdf boundary between the two draws.
 """
 
 from __future__ import annotations
@@ -16,6 +18,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
+import inputs
 from oracle import ops
 
 pytestmark = pytest.mark.gpu
@@ -120,6 +123,132 @@ def test_softmax_and_argmax(gpu):
     _lib.call("tllm_argmax", xd.ptr, 5, 49152, 49152, ids.ptr, pos.ptr, None)
     np.testing.assert_array_equal(ids.to_numpy(), np.argmax(x, axis=-1))
     np.testing.assert_array_equal(pos.to_numpy(), np.arange(5) + 1)
+
+
+def _sample_dev(gpu, x, temperature, top_k, us, ld=None, pos=None):
+    """tllm_sample over the rows of x (M, V) (row stride ld), uniforms us."""
+    from triton_llm import _lib
+    M, V = x.shape
+    ld = ld or V
+    xs = np.zeros((M, ld), F32)
+    xs[:, :V] = x
+    xd = gpu.to_device(xs)
+    ud = gpu.to_device(np.asarray(us, np.float64).reshape(M))
+    ids = gpu.zeros((M,), np.int32)
+    _lib.call("tllm_sample", xd.ptr, M, V, ld, float(temperature), int(top_k),
+              ud.ptr, ids.ptr, pos.ptr if pos is not None else None, None)
+    return ids.to_numpy()
+
+
+SAMPLE_BOUNDARY = 1e-6   # |cdf - u| inside which fp32 exp ulps may flip a draw
+
+
+def _check_draw(got, x, T, k, u, label):
+    """got must be the oracle's draw, unless u lies within SAMPLE_BOUNDARY of
+    every cdf boundary between the two (the device's expf and summation
+    order differ from NumPy's by ulps). Returns 1 for such a flip."""
+    want = ops.sample(x, T, k, u)
+    if got == want:
+        return 0
+    cdf = ops.sample_cdf(x, T, k)
+    lo, hi = min(got, want), max(got, want)
+    gap = float(np.max(np.abs(cdf[lo:hi] - u)))
+    w = cdf[got] - (cdf[got - 1] if got else 0.0)
+    assert gap < SAMPLE_BOUNDARY and w > 0, (
+        f"{label}: drew {got}, oracle {want} (u={u!r}, cdf gap {gap:.3g}, "
+        f"weight of {got} {w:.3g})")
+    return 1
+
+
+def test_sample_matches_reference_cases(gpu, golden):
+    """Every reference _sample case (V 100..128256, T 0.3..1.5, top_k 0, 1,
+    5, 50, 1000, V, V + 7): the device draws the reference's token with the
+    uniform np.random.choice draws."""
+    g = golden("sample")
+    flips = 0
+    for c, want in zip(inputs.SAMPLE_CASES, g["case_tokens"]):
+        x = inputs.sample_logits(c)
+        u = inputs.sample_uniform(c.rng)[0]
+        got = int(_sample_dev(gpu, x[None], c.temperature, c.top_k, [u])[0])
+        flip = _check_draw(got, x, c.temperature, c.top_k, u, str(c))
+        assert got == int(want) or flip, (c, got, int(want))
+        flips += flip
+    print(f"sample cases: {len(inputs.SAMPLE_CASES) - flips}/"
+          f"{len(inputs.SAMPLE_CASES)} identical to the reference")
+
+
+@pytest.mark.parametrize("V,T,k,pad", [(49152, 1.0, 0, 0), (49152, 0.7, 50, 0),
+                                       (128256, 0.7, 0, 64), (128256, 1.3, 1000, 64),
+                                       (50257, 0.5, 7, 3)])
+def test_sample_uniform_sweep_vs_oracle(gpu, V, T, k, pad):
+    """256 rows of one logits vector with uniforms spread over [0, 1): each
+    draw equals the oracle's (rows strided by V + pad)."""
+    rng = np.random.default_rng(V + k)
+    x = (rng.standard_normal(V) * 4).astype(F32)
+    us = (np.arange(256) + rng.random(256)) / 256.0
+    got = _sample_dev(gpu, np.repeat(x[None], 256, 0), T, k, us, ld=V + pad)
+    flips = sum(_check_draw(int(gv), x, T, k, float(u), f"V={V} T={T} k={k}")
+                for gv, u in zip(got, us))
+    assert flips <= 1
+    assert len(set(got.tolist())) > (1 if k == 1 else 10)
+
+
+def test_sample_edges(gpu):
+    from triton_llm import _lib
+    rng = np.random.default_rng(9)
+    x = (rng.standard_normal((4, 3000)) * 2).astype(F32)
+    # top_k = 1 is the first argmax, whatever u is
+    x[2, [17, 2500]] = 50.0
+    got = _sample_dev(gpu, x, 0.9, 1, [0.0, 0.5, 0.99, 0.999999])
+    np.testing.assert_array_equal(got, np.argmax(x, axis=-1))
+    # equal logits at the threshold keep the lowest indices
+    y = np.zeros((64, 4096), F32)
+    y[:, [2, 5, 7, 4000]] = 1.0
+    us = np.linspace(0.0, 0.999, 64)
+    got = _sample_dev(gpu, y, 1.0, 2, us)
+    assert set(got.tolist()) == {2, 5}
+    for gv, u in zip(got, us):
+        _check_draw(int(gv), y[0], 1.0, 2, float(u), "ties")
+    # top_k >= V is top_k = 0; pos advances by one
+    pos = gpu.to_device(np.array([3, 9], np.int32))
+    a = _sample_dev(gpu, x[:2], 1.1, 3000, [0.25, 0.75], pos=pos)
+    b = _sample_dev(gpu, x[:2], 1.1, 0, [0.25, 0.75])
+    np.testing.assert_array_equal(a, b)
+    np.testing.assert_array_equal(pos.to_numpy(), [4, 10])
+    # u = 0 draws the first index, u just below 1 the last
+    got = _sample_dev(gpu, x[:2], 1.0, 0, [0.0, np.nextafter(1.0, 0.0)])
+    np.testing.assert_array_equal(got, [0, 2999])
+    # M = 0 is a no-op; a greedy temperature and a negative top_k are refused
+    _lib.call("tllm_sample", None, 0, 10, 10, 1.0, 0, None, None, None, None)
+    xd, ud, ids = gpu.to_device(x), gpu.zeros((4,), np.float64), gpu.zeros((4,), np.int32)
+    with pytest.raises(ValueError):
+        _lib.call("tllm_sample", xd.ptr, 4, 3000, 3000, 1e-7, 0, ud.ptr, ids.ptr, None, None)
+    with pytest.raises(ValueError):
+        _lib.call("tllm_sample", xd.ptr, 4, 3000, 3000, 1.0, -1, ud.ptr, ids.ptr, None, None)
+
+
+def test_sample_time_at_config4_rows(gpu):
+    """64 rows of the Llama vocabulary (config 4's batch) in one launch: the
+    draw costs a small fraction of a decode step (printed)."""
+    from triton_llm import _lib
+    rng = np.random.default_rng(4)
+    xd = gpu.to_device((rng.standard_normal((64, 128256)) * 3).astype(F32))
+    ud = gpu.to_device(rng.random(64))
+    ids = gpu.zeros((64,), np.int32)
+    for k in (0, 50):
+        for _ in range(3):
+            _lib.call("tllm_sample", xd.ptr, 64, 128256, 128256, 0.8, k, ud.ptr,
+                      ids.ptr, None, None)
+        e0, e1 = gpu.Event(), gpu.Event()
+        e0.record()
+        for _ in range(20):
+            _lib.call("tllm_sample", xd.ptr, 64, 128256, 128256, 0.8, k, ud.ptr,
+                      ids.ptr, None, None)
+        e1.record()
+        gpu.synchronize()
+        us = e0.elapsed_ms(e1) * 1e3 / 20
+        print(f"tllm_sample 64 x 128256 top_k={k}: {us:.1f} us")
+        assert us < 1000.0
 
 
 def test_fill_random_matches_host_formula(gpu):

@@ -25,6 +25,7 @@ import pytest
 
 import inputs
 from oracle import models as omodels
+from oracle import ops
 
 pytestmark = pytest.mark.gpu
 
@@ -110,6 +111,94 @@ def test_smol_tiny_generate_matches_reference(gpu, golden):
     streamed = [t for t, _ in m.generate_stream_gpu(np.array([[5, 12, 7]], np.int32),
                                                     max_new_tokens=5, temperature=0.0)]
     np.testing.assert_array_equal(streamed, g["tokens"][3:])
+
+
+SAMPLE_NEAR = 1e-4   # |cdf - u| at which logits within 1e-4 may flip a draw
+
+
+def _assert_draws(got, want, ref_logits, us, T, k, label):
+    """Sampled tokens must be identical at every step. A draw may differ only
+    where the step's uniform lies within SAMPLE_NEAR of every boundary of the
+    reference's cdf between the two tokens; the comparison stops there (the
+    runs then continue from different tokens)."""
+    got, want = np.asarray(got).reshape(-1), np.asarray(want).reshape(-1)
+    assert len(got) == len(want), f"{label}: {len(got)} vs {len(want)} tokens"
+    n0 = len(want) - len(ref_logits)
+    np.testing.assert_array_equal(got[:n0], want[:n0])
+    for step in range(len(ref_logits)):
+        a, b = int(got[n0 + step]), int(want[n0 + step])
+        if a == b:
+            continue
+        cdf = ops.sample_cdf(ref_logits[step], T, k)
+        lo, hi = min(a, b), max(a, b)
+        gap = float(np.max(np.abs(cdf[lo:hi] - us[step])))
+        assert gap < SAMPLE_NEAR, (f"{label}: draw {step} differs: {a} vs {b} "
+                                   f"(u {us[step]:.6f}, cdf gap {gap:.3g}); "
+                                   f"{step}/{len(ref_logits)} draws matched")
+        print(f"{label}: draws identical for {step}/{len(ref_logits)} steps, then "
+              f"u within {gap:.3g} of a cdf boundary")
+        return
+    print(f"{label}: draws identical for {len(ref_logits)}/{len(ref_logits)} steps")
+
+
+def test_smol_tiny_sampled_generate_matches_reference(gpu, golden):
+    """generate_gpu / generate_stream_gpu at temperature 0.8, top_k 20 after
+    np.random.seed(7) give the reference's sampled tokens: the first draw on
+    the host from the prompt's logits, the rest on the device with the
+    uniforms the reference's np.random.choice draws."""
+    g = golden("sample")
+    T, k, seed = float(g["tiny_meta"][0]), int(g["tiny_meta"][1]), int(g["tiny_meta"][2])
+    want, steps = g["tiny_tokens"], g["tiny_logits"]
+    n = len(steps)
+    us = inputs.sample_uniform(seed, n)
+    m = _smol(inputs.SMOL_TINY, inputs.llama_weights_legacy(inputs.SMOL_TINY, 42))
+    prompt = np.array([[5, 12, 7]], np.int32)
+    np.random.seed(seed)
+    out = m.generate_gpu(prompt, max_new_tokens=n, temperature=T, top_k=k)
+    _assert_draws(out[0], want, steps, us, T, k, "generate_gpu")
+    np.random.seed(seed)
+    streamed = [t for t, _ in m.generate_stream_gpu(prompt, max_new_tokens=n,
+                                                    temperature=T, top_k=k)]
+    _assert_draws(np.concatenate([prompt[0], streamed]), want, steps, us, T, k,
+                  "generate_stream_gpu")
+
+
+def test_device_sampling_equals_host_sampling(gpu):
+    """SmolLM2-135M geometry: a batch of decode steps sampled on the device
+    (tllm_sample inside decode_step) equals the reference's host _sample on
+    the same device logits with the same uniforms, step by step."""
+    from smollm2_triton import SmolLM2Config
+    from smollm2_triton.engine import LlamaSession
+    w = inputs.round_linear_weights_bf16(inputs.llama_weights(inputs.SMOL_135M, 0))
+    m = _smol(inputs.SMOL_135M, w, dtype="bfloat16", kv_dtype="bfloat16",
+              act_dtype="split")
+    m._init_gpu_weights()
+    rng = np.random.default_rng(11)
+    prompts = [rng.integers(0, 49152, int(n)).astype(np.int32) for n in (5, 9, 3, 17)]
+    B = len(prompts)
+    T, k = 0.9, 40
+    s = LlamaSession(m.dev, B, 64, kv_dtype="bfloat16", act_dtype="split")
+    s.prefill(prompts)
+    ur = np.random.RandomState(3)
+    flips = 0
+    for step in range(8):
+        pos0, ids0 = s.pos.to_numpy(), s.ids.to_numpy()
+        s.decode_step(sample=False)
+        host_logits = s.logits.to_numpy()[:B]
+        u = ur.random_sample(B)
+        s.set_state(pos0, ids0)
+        s.u.from_numpy(u)
+        s.decode_step(sample=True, temperature=T, top_k=k)
+        dev = s.ids.to_numpy()
+        np.testing.assert_array_equal(s.pos.to_numpy(), pos0 + 1)
+        for b in range(B):
+            want = ops.sample(host_logits[b], T, k, u[b])
+            if int(dev[b]) != want:
+                cdf = ops.sample_cdf(host_logits[b], T, k)
+                lo, hi = sorted((int(dev[b]), want))
+                assert np.max(np.abs(cdf[lo:hi] - u[b])) < 1e-6, (step, b, dev[b], want)
+                flips += 1
+    assert flips <= 1
 
 
 def _oracle_act(act):

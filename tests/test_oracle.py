@@ -217,3 +217,48 @@ def test_gpt2_cfg1_32_steps(golden):
     np.testing.assert_allclose(logits[:, g["cols"]], g["at_cols"], atol=1e-4)
     np.testing.assert_allclose(np.take_along_axis(logits, g["top_idx"], axis=1),
                                g["top_val"], atol=1e-4)
+
+
+# ------------------------------------------------ temperature / top-k ----
+def test_sample_matches_reference_cases(golden):
+    """The oracle's sampler picks the reference _sample's token on every
+    case (vocabularies 100 to 128256; T 0.3 to 1.5; top_k 0, 1, 5, 50, 1000,
+    V and V + 7), with the uniform np.random.choice draws after the case's
+    np.random.seed."""
+    g = golden("sample")
+    for c, want in zip(inputs.SAMPLE_CASES, g["case_tokens"]):
+        u = inputs.sample_uniform(c.rng)[0]
+        got = ops.sample(inputs.sample_logits(c), c.temperature, c.top_k, u)
+        assert got == int(want), (c, got, int(want))
+
+
+def test_sample_replays_reference_sampled_run(golden):
+    """The reference's tiny SmolLM2 generate at T=0.8, top_k=20 after
+    np.random.seed(7): the oracle sampler on the reference's own per-step
+    logits with the generator's successive uniforms gives its tokens."""
+    g = golden("sample")
+    T, k, seed = g["tiny_meta"]
+    steps = g["tiny_logits"]
+    us = inputs.sample_uniform(int(seed), len(steps))
+    got = [ops.sample(lg, float(T), int(k), u) for lg, u in zip(steps, us)]
+    np.testing.assert_array_equal(got, g["tiny_tokens"][3:])
+
+
+def test_sample_properties():
+    rng = np.random.default_rng(5)
+    x = (rng.standard_normal(1000) * 3).astype(F32)
+    # top_k = 1 is the argmax whatever u is
+    for u in (0.0, 0.3, 0.999999):
+        assert ops.sample(x, 0.7, 1, u) == int(np.argmax(x))
+    # u = 0 picks the first index with positive weight; u -> 1 the last one
+    assert ops.sample(x, 1.0, 0, 0.0) == 0
+    assert ops.sample(x, 1.0, 0, np.nextafter(1.0, 0.0)) == 999
+    # equal logits at the top_k threshold: the lowest indices are kept
+    y = np.zeros(10, F32)
+    y[[2, 5, 7]] = 1.0
+    picks = {ops.sample(y, 1.0, 2, u) for u in np.linspace(0, 0.999, 50)}
+    assert picks == {2, 5}
+    # the cdf is monotone, ends at 1 and its steps are the kept weights
+    cdf = ops.sample_cdf(x, 0.7, 50)
+    assert np.all(np.diff(cdf) >= 0) and cdf[-1] == 1.0
+    assert np.count_nonzero(np.diff(np.concatenate([[0.0], cdf]))) == 50

@@ -217,6 +217,7 @@ class LlamaSession:
         self.pos = gpu.zeros((B,), np.int32)     # next position of each sequence
         self.lens = gpu.zeros((B,), np.int32)    # keys attended in the current step
         self.ids = gpu.zeros((B,), np.int32)     # tokens fed to the next step
+        self.u = gpu.zeros((B,), np.float64)     # uniforms of a sampled step
         self.row_seq = gpu.to_device(np.arange(B, dtype=np.int32))
         self._p2p = bool(p2p)
         self._buffers(B)
@@ -493,11 +494,14 @@ class LlamaSession:
         self.lens.from_numpy(np.asarray(pos, np.int32))
         self.ids.from_numpy(np.asarray(ids, np.int32))
 
-    def decode_step(self, sample=True):
-        """One greedy decode step for all B sequences, device only.
+    def decode_step(self, sample=True, temperature=0.0, top_k=0):
+        """One decode step for all B sequences, device only.
 
         Reads ``ids`` / ``pos``; leaves the step's logits in ``self.logits``
-        and (sample=True) the argmax in ``ids`` with ``pos`` advanced.
+        and (sample=True) the next tokens in ``ids`` with ``pos`` advanced:
+        the argmax when temperature <= 1e-6, else a temperature / top-k draw
+        with the uniforms in ``self.u`` (one per sequence, set by the caller
+        from the generator the reference's np.random.choice uses).
         Returns the number of kernel launches.
         """
         w = self.w
@@ -517,7 +521,11 @@ class LlamaSession:
             self._final_norm(self.h, self.x, B, self._decode_part())
             linear(self.x, w.lm_head, out_dev=self.logits, ws=self.lin_ws, M=B)
             n = 1 + (4 if self.mlp_ws is not None else 7) * w.L + 2
-        if sample:
+        if sample and temperature > 1e-6:
+            _lib.call("tllm_sample", self.logits.ptr, B, w.V, w.V, float(temperature),
+                      int(top_k), self.u.ptr, self.ids.ptr, self.pos.ptr, None)
+            n += 1
+        elif sample:
             _lib.call("tllm_argmax", self.logits.ptr, B, w.V, w.V, self.ids.ptr,
                       self.pos.ptr, None)
             n += 1

@@ -8,7 +8,7 @@
 ``_cache_len``. Underneath, the batched engine (engine.py) runs every step on
 the GPU: the KV cache is written and read in place (the reference copies the
 whole prefix between host and device in every layer, model.py:301-308), and
-greedy decoding samples on the device.
+decode steps sample on the device, greedy or temperature / top-k.
 
 ``generate_batch`` adds ragged-batch greedy generation over many prompts.
 """
@@ -202,9 +202,11 @@ class SmolLM2ForCausalLM:
                      eos_token_id: int | None = None) -> np.ndarray:
         """Autoregressive generation (smollm2_triton/model.py:408-469).
 
-        Returns (1, seq + generated) int32. Greedy decoding
-        (temperature <= 1e-6) samples on the device; otherwise logits come to
-        the host and ``_sample`` draws like the reference.
+        Returns (1, seq + generated) int32. Every decode step samples on the
+        device (argmax when temperature <= 1e-6, else temperature / top-k with
+        the uniform drawn from NumPy's global generator, as the reference's
+        np.random.choice draws it); the first token, from the prompt's
+        logits, is drawn by ``_sample`` on the host like the reference.
         """
         token_ids = np.asarray(token_ids)
         self._validate(token_ids, max_new_tokens, temperature, top_k)
@@ -239,22 +241,22 @@ class SmolLM2ForCausalLM:
         logits = self._forward_cached(token_ids)
         t_step = t0
         for step in range(max_new_tokens):
-            if greedy:
-                tok = int(np.argmax(logits[0, -1, :])) if step == 0 else int(s.ids.to_numpy()[0])
-            else:
+            if step == 0:
                 tok = self._sample(logits[0, -1, :], temperature, top_k)
+            else:
+                tok = int(s.ids.to_numpy()[0])
             yield tok, time.perf_counter() - t_step
             if eos_token_id is not None and tok == eos_token_id:
                 return
             if step < max_new_tokens - 1:
                 t_step = time.perf_counter()
-                if greedy:
-                    s.set_state(np.array([self._cache_len], np.int32),
-                                np.array([tok], np.int32))
-                    s.decode_step(sample=True)
-                    self._cache_len += 1
-                else:
-                    logits = self._forward_cached(np.array([[tok]], dtype=np.int32))
+                s.set_state(np.array([self._cache_len], np.int32),
+                            np.array([tok], np.int32))
+                if not greedy:
+                    # the one uniform np.random.choice would draw this step
+                    s.u.from_numpy(np.array([np.random.random_sample()], np.float64))
+                s.decode_step(sample=True, temperature=temperature, top_k=top_k)
+                self._cache_len += 1
 
     def generate_batch(self, prompts, max_new_tokens: int = 20,
                        eos_token_id: int | None = None, use_graph: bool = True):

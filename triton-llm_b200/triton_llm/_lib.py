@@ -129,6 +129,7 @@ SIGNATURES: dict[str, list] = {
     "tllm_split_bf16": [_vp, _vp, _i, _i, _i, _i, _vp],
     "tllm_embedding": [_vp, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i, _vp],
     "tllm_argmax": [_vp, _i, _i, _i, _vp, _vp, _vp],
+    "tllm_sample": [_vp, _i, _i, _i, _f, _i, _vp, _vp, _vp, _vp],
     "tllm_rope": [_vp, _vp, _vp, _i, _i, _i, _i, _vp],
     "tllm_elementwise": [_i, _vp, _vp, _vp, _l, _vp],
     "tllm_softmax": [_vp, _vp, _i, _i, _vp],
