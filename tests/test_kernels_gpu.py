@@ -190,7 +190,7 @@ def test_sample_uniform_sweep_vs_oracle(gpu, V, T, k, pad):
     flips = sum(_check_draw(int(gv), x, T, k, float(u), f"V={V} T={T} k={k}")
                 for gv, u in zip(got, us))
     assert flips <= 1
-    assert len(set(got.tolist())) > (1 if k == 1 else 10)
+    assert len(set(got.tolist())) >= min(k or 10, 5)   # the draws spread
 
 
 def test_sample_edges(gpu):
@@ -209,6 +209,15 @@ def test_sample_edges(gpu):
     assert set(got.tolist()) == {2, 5}
     for gv, u in zip(got, us):
         _check_draw(int(gv), y[0], 1.0, 2, float(u), "ties")
+    # more equal logits at the threshold than the shared buffer holds: the
+    # remaining digits and the index cut are selected over the whole row
+    z = np.zeros((64, 49152), F32)
+    z[:, ::7] = 1.0
+    us = np.linspace(0.0, 0.999, 64)
+    got = _sample_dev(gpu, z, 1.0, 10000, us)
+    for gv, u in zip(got, us):
+        _check_draw(int(gv), z[0], 1.0, 10000, float(u), "wide tie")
+    assert np.any(got % 7 != 0)   # kept zeros (the lowest indices) are drawn
     # top_k >= V is top_k = 0; pos advances by one
     pos = gpu.to_device(np.array([3, 9], np.int32))
     a = _sample_dev(gpu, x[:2], 1.1, 3000, [0.25, 0.75], pos=pos)
@@ -235,19 +244,20 @@ def test_sample_time_at_config4_rows(gpu):
     xd = gpu.to_device((rng.standard_normal((64, 128256)) * 3).astype(F32))
     ud = gpu.to_device(rng.random(64))
     ids = gpu.zeros((64,), np.int32)
-    for k in (0, 50):
+    for rows, k in ((64, 0), (64, 50), (64, 1000), (1, 0), (1, 50)):
         for _ in range(3):
-            _lib.call("tllm_sample", xd.ptr, 64, 128256, 128256, 0.8, k, ud.ptr,
+            _lib.call("tllm_sample", xd.ptr, rows, 128256, 128256, 0.8, k, ud.ptr,
                       ids.ptr, None, None)
         e0, e1 = gpu.Event(), gpu.Event()
         e0.record()
         for _ in range(20):
-            _lib.call("tllm_sample", xd.ptr, 64, 128256, 128256, 0.8, k, ud.ptr,
+            _lib.call("tllm_sample", xd.ptr, rows, 128256, 128256, 0.8, k, ud.ptr,
                       ids.ptr, None, None)
         e1.record()
         gpu.synchronize()
         us = e0.elapsed_ms(e1) * 1e3 / 20
-        print(f"tllm_sample 64 x 128256 top_k={k}: {us:.1f} us")
+        print(f"tllm_sample {rows} x 128256 top_k={k}: {us:.1f} us "
+              f"({rows * 128256 * 4 / us / 1e3:.0f} GB/s of logits)")
         assert us < 1000.0
 
 
