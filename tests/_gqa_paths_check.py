@@ -47,6 +47,11 @@ def main():
     lens = [0, 1, 63, 64, 65, 127, 300, 1023, 1100, 2048]
     for (H, Hkv, D) in ((9, 3, 64), (24, 8, 128), (12, 12, 64), (32, 2, 128)):
         worst = max(worst, run(H, Hkv, D, lens, 2048, H * 7 + D))
+    # a small ragged batch at config-4 geometry (splits far shorter than
+    # max_len for most rows)
+    rng = np.random.default_rng(11)
+    lens8 = sorted(rng.integers(512, 4096, 8).tolist())
+    worst = max(worst, run(24, 8, 128, lens8, 4096, 5))
     lens_c2, q, ks, vs = inputs.cfg2_inputs(batch=32)
     kc = inputs.pack_cache(ks, 2048)
     vc = inputs.pack_cache(vs, 2048)

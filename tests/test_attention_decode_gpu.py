@@ -141,9 +141,12 @@ def test_uniform_length_without_lens_array(gpu):
     np.testing.assert_allclose(od.to_numpy(), ref, atol=ATOL)
 
 
-@pytest.mark.parametrize("env", [{"TLLM_GQA_NO_MMA": "1"}, {}])
+@pytest.mark.parametrize("env", [{"TLLM_GQA_NO_MMA": "1"}, {}, {"TLLM_GQA_GROUPS": "1"},
+                                 {"TLLM_GQA_GROUPS": "2"}])
 def test_every_kernel_path(env):
-    """Tensor-core and CUDA-core kernels each match the oracle on bf16."""
+    """Tensor-core and CUDA-core kernels each match the oracle on bf16; the
+    tensor-core kernel with one and with two consumer groups at every head
+    geometry (the default picks two at head_dim 64 with <= 8 heads per CTA)."""
     import os
     import subprocess
     import sys

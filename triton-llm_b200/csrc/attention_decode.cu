@@ -447,7 +447,8 @@ __global__ void __launch_bounds__(kThreads)
 // the keys as the M rows and the CTA's query heads as the N columns:
 //   S^T (16 keys x 8 heads)  = K_w (16 x D) . Q^T      per consumer warp
 //   O^T (D x 8 heads)       += V_w^T (D x 16 keys) . P^T
-// where warp w owns keys [16w, 16w + 16) of every 64-key tile; a decode
+// where warp w of a consumer group owns keys [16 (w % 4), + 16) of every
+// 64-key tile the group takes (tiles t = group mod NG); a decode
 // group of G <= 8 heads (16 with two n8 blocks) fills the narrow side, so
 // half the MMAs of the heads-as-rows form are spent. q and p are each split
 // into a bf16 head and a bf16 residual (x = hi + lo) and both halves are
@@ -465,26 +466,37 @@ __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
 }
 
 
-template <int D>
+// NG consumer groups of four warps: group i takes the tiles t = i (mod NG)
+// with its own online-softmax state, so NG tiles are in the consumers' hands
+// at once (one group's dependent MMA / shuffle / exp chain per tile bounds a
+// CTA otherwise). The ring depth is a multiple of NG, so every ring slot
+// belongs to one group, which waits for that slot's fills strictly in order
+// (a slot shared by two groups would let one group pass a parity wait on a
+// fill two phases old while the other group's fill is still in flight).
+template <int D, int NG>
 struct MmaShape {
   static constexpr int KT = 64;                    // keys per tile
   static constexpr int SUB = D / 64;               // 128-byte sub-tiles per row
   static constexpr int SUB_BYTES = KT * 128;       // 8 KB
   static constexpr int TILE_BYTES = SUB * SUB_BYTES;
-  static constexpr int STAGES = D <= 64 ? 4 : 3;
+  static constexpr int STAGES = (D <= 64 || NG == 2) ? 4 : 3;
   static constexpr int KSTEPS = D / 16;
+  static constexpr int CONSUMERS = 4 * NG;         // consumer warps
+  static constexpr int THREADS = (CONSUMERS + 1) * 32;
   static constexpr size_t RING =
       2 * (size_t)STAGES * TILE_BYTES + 2 * STAGES * sizeof(uint64_t);
+  static_assert(STAGES % NG == 0, "every ring slot must belong to one group");
 };
 
-template <int D, int QB>
-__global__ void __launch_bounds__(kThreads)
+template <int D, int QB, int NG>
+__global__ void __launch_bounds__(MmaShape<D, NG>::THREADS)
     gqa_decode_mma_kernel(const DecodeParams p, const int G,
                           const __grid_constant__ CUtensorMap tmk,
                           const __grid_constant__ CUtensorMap tmv) {
   griddep_launch();
   griddep_wait();   // q, lengths and the cache come from earlier kernels
-  using S = MmaShape<D>;
+  using S = MmaShape<D, NG>;
+  constexpr int NCW = S::CONSUMERS;
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t *k_st = smem;
   uint8_t *v_st = smem + S::STAGES * S::TILE_BYTES;
@@ -506,19 +518,22 @@ __global__ void __launch_bounds__(kThreads)
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
+  const int grp = warp >> 2;   // consumer group (tiles t = grp mod NG)
+  const int wq = warp & 3;     // key quarter of every tile of the group
 
   int len = p.seq_lens ? p.seq_lens[b] : p.max_len;
   len = len < 0 ? 0 : (len > p.max_seq ? p.max_seq : len);
-  int n_splits = (len + p.chunk - 1) / p.chunk;
+  const int chunk = p.chunk;
+  int n_splits = (len + chunk - 1) / chunk;
   if (n_splits < 1) n_splits = 1;
   if (n_splits > p.max_splits) {
     if (tid == 0 && j == 0) atomicOr(p.err, DEV_ERR_LEN_CLAMPED);
     n_splits = p.max_splits;
-    len = n_splits * p.chunk;
+    len = n_splits * chunk;
   }
   if (j >= n_splits) return;
-  const int start = j * p.chunk;
-  const int end = min(start + p.chunk, len);
+  const int start = j * chunk;
+  const int end = min(start + chunk, len);
   const int nrows = end > start ? end - start : 0;
   const int ntiles = (nrows + S::KT - 1) / S::KT;
   const int head0 = kvh * p.group + gsub * G;
@@ -526,7 +541,7 @@ __global__ void __launch_bounds__(kThreads)
   if (tid == 0) {
     for (int s = 0; s < S::STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumerWarps);
+      mbar_init(&empty[s], 4);   // the four warps of the slot's group
     }
     fence_mbar_init();
     s_flag = 0;
@@ -534,7 +549,7 @@ __global__ void __launch_bounds__(kThreads)
   __syncthreads();
 
   bool failed = false;
-  if (warp == kConsumerWarps) {
+  if (warp == NCW) {
     if (lane == 0) {
       const int plane = (p.row_seq ? p.row_seq[b] : b) * p.n_kv + kvh;
       for (int t = 0; t < ntiles; ++t) {
@@ -574,7 +589,7 @@ __global__ void __launch_bounds__(kThreads)
     m_r[qb][0] = m_r[qb][1] = -INFINITY;
     l_r[qb][0] = l_r[qb][1] = 0.f;
   }
-  if (warp < kConsumerWarps) {
+  if (warp < NCW) {
     // ---- Q^T fragments (B operand: k = dims, n = heads), scaled, hi / lo
     uint32_t qh[QB][S::KSTEPS][2], ql[QB][S::KSTEPS][2];
 #pragma unroll
@@ -603,12 +618,12 @@ __global__ void __launch_bounds__(kThreads)
 
     // ldmatrix lane addressing: K as the A operand (rows = keys), V^T as
     // the A operand via .trans (source rows = keys)
-    const int a_key = warp * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
+    const int a_key = wq * 16 + ((lane >> 3) & 1) * 8 + (lane & 7);
     const int a_dof = ((lane >> 4) & 1) * 8;
-    const int t_key = warp * 16 + ((lane >> 4) & 1) * 8 + (lane & 7);
+    const int t_key = wq * 16 + ((lane >> 4) & 1) * 8 + (lane & 7);
     const int t_dof = ((lane >> 3) & 1) * 8;
 
-    for (int t = 0; t < ntiles; ++t) {
+    for (int t = grp; t < ntiles; t += NG) {
       const int s = t % S::STAGES;
       const bool ok = __all_sync(
           0xffffffffu, mbar_wait_bounded(&full[s], (t / S::STAGES) & 1));
@@ -647,7 +662,7 @@ __global__ void __launch_bounds__(kThreads)
         for (int qb = 0; qb < QB; ++qb)
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const int key = warp * 16 + r0 + 8 * (e >> 1);
+            const int key = wq * 16 + r0 + 8 * (e >> 1);
             if (key >= valid) sc[qb][e] = -INFINITY;
           }
       }
@@ -688,11 +703,11 @@ __global__ void __launch_bounds__(kThreads)
         pb[qb][3] = movmatrix_t(l23);
       }
 
-      if (partial && warp * 16 + 16 > valid) {
+      if (partial && wq * 16 + 16 > valid) {
         // rows past the end may hold anything (even NaN): zero this warp's
         // share of them so that 0 * row stays 0 in P . V
         for (int idx = lane; idx < 16 * S::SUB * 8; idx += 32) {
-          const int key = warp * 16 + idx / (S::SUB * 8);
+          const int key = wq * 16 + idx / (S::SUB * 8);
           const int rem = idx % (S::SUB * 8);
           if (key >= valid)
             *reinterpret_cast<uint4 *>(vt + (rem >> 3) * S::SUB_BYTES +
@@ -744,11 +759,11 @@ __global__ void __launch_bounds__(kThreads)
     return;
   }
 
-  // ---- merge the 4 consumer warps (heads < G)
-  float *w_acc = reinterpret_cast<float *>(smem);   // [4][G][D]
-  float *w_m = w_acc + kConsumerWarps * G * D;      // [4][G]
-  float *w_l = w_m + kConsumerWarps * G;            // [4][G]
-  if (warp < kConsumerWarps) {
+  // ---- merge the consumer warps (heads < G), in warp order
+  float *w_acc = reinterpret_cast<float *>(smem);   // [NCW][G][D]
+  float *w_m = w_acc + NCW * G * D;      // [NCW][G]
+  float *w_l = w_m + NCW * G;            // [NCW][G]
+  if (warp < NCW) {
 #pragma unroll
     for (int qb = 0; qb < QB; ++qb) {
 #pragma unroll
@@ -771,16 +786,16 @@ __global__ void __launch_bounds__(kThreads)
   __syncthreads();
 
   const bool single = (n_splits == 1);
-  for (int idx = tid; idx < G * D; idx += kThreads) {
+  for (int idx = tid; idx < G * D; idx += S::THREADS) {
     const int g = idx / D;
     const int d = idx - g * D;
     float mx = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) mx = fmaxf(mx, w_m[w * G + g]);
+    for (int w = 0; w < NCW; ++w) mx = fmaxf(mx, w_m[w * G + g]);
     float num = 0.f, den = 0.f;
     if (mx != -INFINITY) {
 #pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) {
+      for (int w = 0; w < NCW; ++w) {
         const float wm = w_m[w * G + g];
         if (wm != -INFINITY) {
           const float sc = fast_exp2(wm - mx);
@@ -816,7 +831,7 @@ __global__ void __launch_bounds__(kThreads)
   __threadfence();
 
   float *sw = reinterpret_cast<float *>(smem);  // [G][kMaxSplits]
-  for (int g = warp; g < G; g += kConsumerWarps + 1) {
+  for (int g = warp; g < G; g += NCW + 1) {
     const size_t base = ((size_t)b * p.n_head + head0 + g) * p.max_splits;
     float mx = -INFINITY;
     for (int s = lane; s < n_splits; s += 32)
@@ -838,7 +853,7 @@ __global__ void __launch_bounds__(kThreads)
     for (int s = lane; s < n_splits; s += 32) sw[g * kMaxSplits + s] *= inv;
   }
   __syncthreads();
-  for (int idx = tid; idx < G * D; idx += kThreads) {
+  for (int idx = tid; idx < G * D; idx += S::THREADS) {
     const int g = idx / D;
     const int d = idx - g * D;
     const size_t row = (size_t)b * p.n_head + head0 + g;
@@ -954,20 +969,40 @@ int dispatch_d(int D, int G, const DecodeParams &p, const CUtensorMap &mk,
   return TLLM_ERR_UNSUPPORTED;
 }
 
-// The mma kernel instance for G query heads, its dynamic shared memory, and
-// its CTAs per SM (the attribute is set once per device and instance).
-template <int D>
-int mma_kernel_setup(int G, void (**kern_out)(const DecodeParams, const int,
-                                              const CUtensorMap, const CUtensorMap),
-                     size_t *smem_out, int *per_sm) {
-  using S = MmaShape<D>;
-  const size_t merge = (size_t)kConsumerWarps * G * (D + 2) * sizeof(float);
+// Consumer groups of the mma kernel for head_dim D and G query heads per
+// CTA: two at D = 64 with G <= 8 (four ring stages either way, 71 registers,
+// three CTAs per SM), one otherwise: at D = 128 two groups need four 32 KB
+// stages (one CTA per SM instead of two), and two column blocks (G > 8) at
+// D = 64 take 124 registers (one CTA per SM instead of three).
+// TLLM_GQA_GROUPS=1 or 2 overrides the choice.
+int mma_groups(int D, int G) {
+  static int env = -1;
+  if (env < 0) {
+    const char *e = getenv("TLLM_GQA_GROUPS");
+    env = e ? atoi(e) : 0;
+  }
+  if (env == 1 || env == 2) return env;
+  return (D <= 64 && G <= 8) ? 2 : 1;
+}
+
+using MmaKern = void (*)(const DecodeParams, const int, const CUtensorMap,
+                         const CUtensorMap);
+
+// The mma kernel instance for G query heads and NG consumer groups, its
+// dynamic shared memory, threads and CTAs per SM (the attribute is set once
+// per device and instance).
+template <int D, int NG>
+int mma_kernel_setup_ng(int G, MmaKern *kern_out, size_t *smem_out,
+                        int *threads_out, int *per_sm) {
+  using S = MmaShape<D, NG>;
+  const size_t merge = (size_t)S::CONSUMERS * G * (D + 2) * sizeof(float);
   const size_t sweights = (size_t)G * kMaxSplits * sizeof(float);
   size_t smem = S::RING;
   if (merge > smem) smem = merge;
   if (sweights > smem) smem = sweights;
   // query heads per CTA as n8 blocks of the swapped MMA
-  auto kern = G <= 8 ? gqa_decode_mma_kernel<D, 1> : gqa_decode_mma_kernel<D, 2>;
+  MmaKern kern = G <= 8 ? gqa_decode_mma_kernel<D, 1, NG>
+                        : gqa_decode_mma_kernel<D, 2, NG>;
   static bool configured[64][2] = {};
   static int occ[64][2] = {};
   int dev = 0;
@@ -977,7 +1012,7 @@ int mma_kernel_setup(int G, void (**kern_out)(const DecodeParams, const int,
     TLLM_CUDA(cudaFuncSetAttribute(
         kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kThreads, smem) !=
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, S::THREADS, smem) !=
         cudaSuccess) {
       cudaGetLastError();
       n = 0;
@@ -989,29 +1024,39 @@ int mma_kernel_setup(int G, void (**kern_out)(const DecodeParams, const int,
   }
   *kern_out = kern;
   *smem_out = smem;
+  *threads_out = S::THREADS;
   if (per_sm) *per_sm = (dev >= 0 && dev < 64) ? occ[dev][qi] : 0;
   return TLLM_OK;
 }
 
 template <int D>
+int mma_kernel_setup(int G, MmaKern *kern_out, size_t *smem_out,
+                     int *threads_out, int *per_sm) {
+  return mma_groups(D, G) == 2
+             ? mma_kernel_setup_ng<D, 2>(G, kern_out, smem_out, threads_out, per_sm)
+             : mma_kernel_setup_ng<D, 1>(G, kern_out, smem_out, threads_out, per_sm);
+}
+
+template <int D>
 int launch_mma(const DecodeParams &p, int G, const CUtensorMap &mk,
                const CUtensorMap &mv, dim3 grid, cudaStream_t st) {
-  void (*kern)(const DecodeParams, const int, const CUtensorMap, const CUtensorMap);
+  MmaKern kern;
   size_t smem = 0;
-  int rc = mma_kernel_setup<D>(G, &kern, &smem, nullptr);
+  int threads = 0;
+  int rc = mma_kernel_setup<D>(G, &kern, &smem, &threads, nullptr);
   if (rc) return rc;
-  TLLM_CUDA(launch_pdl(kern, grid, dim3(kThreads), smem, st, p, G, mk, mv));
+  TLLM_CUDA(launch_pdl(kern, grid, dim3(threads), smem, st, p, G, mk, mv));
   return TLLM_OK;
 }
 
 // CTAs of the mma kernel that are resident at once on this device (0 if
 // unknown).
 int mma_slots(int head_dim, int G) {
-  void (*kern)(const DecodeParams, const int, const CUtensorMap, const CUtensorMap);
+  MmaKern kern;
   size_t smem = 0;
-  int per_sm = 0;
-  int rc = head_dim == 64 ? mma_kernel_setup<64>(G, &kern, &smem, &per_sm)
-                          : mma_kernel_setup<128>(G, &kern, &smem, &per_sm);
+  int threads = 0, per_sm = 0;
+  int rc = head_dim == 64 ? mma_kernel_setup<64>(G, &kern, &smem, &threads, &per_sm)
+                          : mma_kernel_setup<128>(G, &kern, &smem, &threads, &per_sm);
   return rc ? 0 : per_sm * sm_count();
 }
 
@@ -1110,13 +1155,13 @@ static int rows_impl(const float *q, long q_sb, long q_sh, const void *k_cache,
   const bool mma = use_mma(kv_dtype, head_dim);
   const int G = mma ? pick_group_tile_mma(group) : pick_group_tile(group);
   const int n_gsub = group / G;
-  const int rows = mma ? MmaShape<64>::KT : tile_rows(kv_dtype, head_dim);
+  const int rows = mma ? MmaShape<64, 1>::KT : tile_rows(kv_dtype, head_dim);
   TLLM_CHECK_ARG(rows >= 1, "head_dim %d too large", head_dim);
   const int ygrid = n_kv_head * n_gsub;
   TLLM_CHECK_ARG(ygrid <= 65535 && batch <= 65535, "grid too large");
 
-  int chunk = pick_chunk(rows, batch, ygrid, max_len,
-                         mma ? mma_slots(head_dim, G) : 0);
+  const int slots = mma ? mma_slots(head_dim, G) : 0;
+  int chunk = pick_chunk(rows, batch, ygrid, max_len, slots);
   int max_splits = (max_len + chunk - 1) / chunk;
   if (max_splits < 1) max_splits = 1;
   if (max_splits > 1) {
