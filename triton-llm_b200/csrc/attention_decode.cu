@@ -488,8 +488,14 @@ struct MmaShape {
   static_assert(STAGES % NG == 0, "every ring slot must belong to one group");
 };
 
+// CTAs per SM the shared memory allows each instance, given to the register
+// allocator as its minimum (one column block only: two need more registers).
+__host__ __device__ constexpr int mma_min_blocks(int D, int QB, int NG) {
+  return QB > 1 ? 1 : D <= 64 ? 3 : NG == 2 ? 1 : 2;
+}
+
 template <int D, int QB, int NG>
-__global__ void __launch_bounds__(MmaShape<D, NG>::THREADS)
+__global__ void __launch_bounds__(MmaShape<D, NG>::THREADS, mma_min_blocks(D, QB, NG))
     gqa_decode_mma_kernel(const DecodeParams p, const int G,
                           const __grid_constant__ CUtensorMap tmk,
                           const __grid_constant__ CUtensorMap tmv) {
