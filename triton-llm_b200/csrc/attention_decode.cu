@@ -500,7 +500,6 @@ __global__ void __launch_bounds__(MmaShape<D, NG>::THREADS, mma_min_blocks(D, QB
                           const __grid_constant__ CUtensorMap tmk,
                           const __grid_constant__ CUtensorMap tmv) {
   griddep_launch();
-  griddep_wait();   // q, lengths and the cache come from earlier kernels
   using S = MmaShape<D, NG>;
   constexpr int NCW = S::CONSUMERS;
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -527,6 +526,20 @@ __global__ void __launch_bounds__(MmaShape<D, NG>::THREADS, mma_min_blocks(D, QB
   const int grp = warp >> 2;   // consumer group (tiles t = grp mod NG)
   const int wq = warp & 3;     // key quarter of every tile of the group
 
+  // the barriers need nothing from earlier kernels: set them up before the
+  // dependency wait
+  if (tid == 0) {
+    for (int s = 0; s < S::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 4);   // the four warps of the slot's group
+    }
+    fence_mbar_init();
+    s_flag = 0;
+  }
+  __syncthreads();
+  griddep_wait();   // q, lengths and the cache come from earlier kernels
+  // both index loads in flight together
+  const int cache_seq = p.row_seq ? p.row_seq[b] : b;
   int len = p.seq_lens ? p.seq_lens[b] : p.max_len;
   len = len < 0 ? 0 : (len > p.max_seq ? p.max_seq : len);
   const int chunk = p.chunk;
@@ -544,20 +557,10 @@ __global__ void __launch_bounds__(MmaShape<D, NG>::THREADS, mma_min_blocks(D, QB
   const int ntiles = (nrows + S::KT - 1) / S::KT;
   const int head0 = kvh * p.group + gsub * G;
 
-  if (tid == 0) {
-    for (int s = 0; s < S::STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 4);   // the four warps of the slot's group
-    }
-    fence_mbar_init();
-    s_flag = 0;
-  }
-  __syncthreads();
-
   bool failed = false;
   if (warp == NCW) {
     if (lane == 0) {
-      const int plane = (p.row_seq ? p.row_seq[b] : b) * p.n_kv + kvh;
+      const int plane = cache_seq * p.n_kv + kvh;
       for (int t = 0; t < ntiles; ++t) {
         const int s = t % S::STAGES;
         if (t >= S::STAGES &&
