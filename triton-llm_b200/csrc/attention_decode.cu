@@ -839,17 +839,39 @@ __global__ void __launch_bounds__(MmaShape<D, NG>::THREADS, mma_min_blocks(D, QB
   if (s_flag != 2) return;
   __threadfence();
 
+  // Merge the splits of this (sequence, KV group) in split order: the
+  // weights (split maxima and sums, one lane per split) and the first kPf
+  // values of each thread's first output element are loaded together, so
+  // a merge of up to kPf splits waits for one L2 round trip.
+  constexpr int kPf = 4;
+  float pre[kPf];
+  if (tid < G * D) {
+    const int g = tid / D;
+    const int d = tid - g * D;
+    const float *acc = p.part_acc + ((size_t)b * p.n_head + head0 + g) * p.max_splits * D + d;
+#pragma unroll
+    for (int q = 0; q < kPf; ++q) pre[q] = q < n_splits ? __ldcg(&acc[(size_t)q * D]) : 0.f;
+  }
+  const float2 *ml2 = reinterpret_cast<const float2 *>(p.part_ml);
   float *sw = reinterpret_cast<float *>(smem);  // [G][kMaxSplits]
   for (int g = warp; g < G; g += NCW + 1) {
     const size_t base = ((size_t)b * p.n_head + head0 + g) * p.max_splits;
-    float mx = -INFINITY;
-    for (int s = lane; s < n_splits; s += 32)
+    // lane l: splits l, l + 32, ...; the first one's (max, sum) is kept
+    const float2 v0 = lane < n_splits ? __ldcg(&ml2[base + lane])
+                                      : make_float2(-INFINITY, 0.f);
+    float mx = v0.x;
+    for (int s = lane + 32; s < n_splits; s += 32)
       mx = fmaxf(mx, __ldcg(&p.part_ml[(base + s) * 2]));
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1)
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
     float den = 0.f;
-    for (int s = lane; s < n_splits; s += 32) {
+    if (lane < n_splits) {
+      const float w = (v0.x == -INFINITY) ? 0.f : fast_exp2(v0.x - mx);
+      sw[g * kMaxSplits + lane] = w;
+      den = fmaf(v0.y, w, den);
+    }
+    for (int s = lane + 32; s < n_splits; s += 32) {
       const float ms = __ldcg(&p.part_ml[(base + s) * 2]);
       const float w = (ms == -INFINITY) ? 0.f : fast_exp2(ms - mx);
       sw[g * kMaxSplits + s] = w;
@@ -868,7 +890,14 @@ __global__ void __launch_bounds__(MmaShape<D, NG>::THREADS, mma_min_blocks(D, QB
     const size_t row = (size_t)b * p.n_head + head0 + g;
     const size_t base = row * p.max_splits;
     float o2 = 0.f;
-    for (int s = 0; s < n_splits; ++s)
+    int s0 = 0;
+    if (idx == tid) {   // the prefetched first splits
+#pragma unroll
+      for (int q = 0; q < kPf; ++q)
+        if (q < n_splits) o2 = fmaf(sw[g * kMaxSplits + q], pre[q], o2);
+      s0 = n_splits < kPf ? n_splits : kPf;
+    }
+    for (int s = s0; s < n_splits; ++s)
       o2 = fmaf(sw[g * kMaxSplits + s], __ldcg(&p.part_acc[(base + s) * D + d]),
                 o2);
     store_o(p, b * p.o_sb + (long)(head0 + g) * p.o_sh + d, o2);
