@@ -325,13 +325,14 @@ class LlamaDecodeWorkload:
             for i in range(w.L):
                 k, v = s.kv[i]
                 gqa_rows(s.q, k, v, s.row_seq, s.lens, s.attn, s.B, w.H, w.H * w.D,
-                         w.D, w.H * w.D, w.D, s.S, workspace=s.attn_ws)
+                         w.D, w.H * w.D, w.D, s.S, workspace=s.attn_ws,
+                         keys_hint=s._keys_hint)   # the step's own split plan
         ms = _time_graph(gpu, g, 5) / w.L
         lens = s.lens.to_numpy().astype(np.int64)
         alg = (2 * w.Hkv * w.D * 2 * int(lens.sum())            # K and V, bf16
                + 2 * s.B * w.H * w.D * 4 + s.B * 4)             # q, out, lens
         achieved = alg / (ms / 1e3) / 1e9
-        return {"kernel": "gqa_decode_mma_kernel<128> (+ split merge)",
+        return {"kernel": "gqa_decode_mma_kernel<128, 1, 1> (+ split merge)",
                 "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "bound": "hbm",
                 "algorithmic_bytes_per_launch": alg,
@@ -560,7 +561,7 @@ class SmolDecodeWorkload(LlamaDecodeWorkload):
 
     def kernel_roofline(self, gpu, peak):
         r = super().kernel_roofline(gpu, peak)
-        r["kernel"] = "gqa_decode_mma_kernel<64> (+ split merge)"
+        r["kernel"] = "gqa_decode_mma_kernel<64, 1, 2> (+ split merge)"
         r["traffic"] = None
         r.pop("traffic_source", None)
         return r
@@ -894,7 +895,7 @@ class GQAWorkload:
         gpu.device_synchronize()
         ms = e0.elapsed_ms(e1) / reps
         achieved = self.bytes_per_step / (ms / 1e3) / 1e9
-        return {"kernel": "gqa_decode_mma_kernel<64> (+ split merge)",
+        return {"kernel": "gqa_decode_mma_kernel<64, 1, 2> (+ split merge)",
                 "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "bound": "hbm",
                 "algorithmic_bytes_per_launch": self.bytes_per_step,
@@ -986,7 +987,7 @@ class GQALlamaLayerWorkload(_IsolatedWorkload):
     head_dim 128, bf16 cache filled N(0, 1)."""
 
     name = "gqa_llama3b"
-    kernel = "gqa_decode_mma_kernel<128> (+ split merge)"
+    kernel = "gqa_decode_mma_kernel<128, 1, 1> (+ split merge)"
     copies = 1      # one launch reads ~1.2 GB, far above L2
 
     def setup(self):

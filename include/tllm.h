@@ -212,6 +212,24 @@ int tllm_gqa_rows(const float *q, long q_row_stride, long q_head_stride,
                   int head_dim, int cache_batch, int max_seq, int max_len,
                   float sm_scale, void *partial, size_t partial_bytes,
                   int32_t *counters, tllm_stream_t stream);
+/* tllm_gqa_rows with the caller's estimate of the keys the rows read in
+ * all (keys_hint: the sum of row_len at launch; 0 = unknown). The split of
+ * each row's keys over CTAs is then planned from that total instead of
+ * from max_len alone, which for a small ragged batch (fewer row x KV-group
+ * pairs than ~85 % of the resident CTAs) gives longer or shorter splits
+ * that fill one wave of the GPU. Results are correct for any hint; only the
+ * split boundaries (and so the fp32 rounding of the merge) follow it. Used
+ * by the decode step of smollm2_triton/engine.py, whose lengths are known
+ * on the host when the step's graph is captured. Replaces the same
+ * reference interface as tllm_gqa_rows (triton_llm/kernels/attention_gqa.py:149-269). */
+int tllm_gqa_rows_hint(const float *q, long q_row_stride, long q_head_stride,
+                       const void *k_cache, const void *v_cache, int kv_dtype,
+                       const int32_t *row_seq, const int32_t *row_len, void *out,
+                       int out_dtype, long out_plane_rows, long out_row_stride,
+                       long out_head_stride, int rows, int n_head, int n_kv_head,
+                       int head_dim, int cache_batch, int max_seq, int max_len,
+                       float sm_scale, void *partial, size_t partial_bytes,
+                       int32_t *counters, long keys_hint, tllm_stream_t stream);
 
 /* ------------------------------------------------------------------------ */
 /* Projections (GEMM with fused epilogues)                                   */

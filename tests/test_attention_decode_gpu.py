@@ -127,6 +127,37 @@ def test_repeat_calls_are_deterministic(gpu):
     assert np.all(ws.counters.to_numpy() == 0)
 
 
+def test_rows_keys_hint_any_value(gpu):
+    """tllm_gqa_rows_hint: the split sizes follow the caller's estimate of the
+    keys read (a tiny hint: the shortest splits; the true sum: one wave; a
+    huge hint: one split per row), and every plan matches the oracle and the
+    call without a hint (16 ragged rows at Llama-3B head geometry, few
+    enough row x KV-head pairs for the hint to apply)."""
+    from triton_llm.kernels import DecodeWorkspace, gqa_rows
+    rng = np.random.default_rng(21)
+    B, H, Hkv, D, S = 16, 24, 8, 128, 4160
+    lens = rng.integers(1024, 4096, B).astype(np.int32)
+    q = inputs.bf16_round(rng.standard_normal((B, H, D), dtype=F32))
+    kc = inputs.bf16_round(rng.standard_normal((B, Hkv, S, D), dtype=F32))
+    vc = inputs.bf16_round(rng.standard_normal((B, Hkv, S, D), dtype=F32))
+    for b, L in enumerate(lens):
+        kc[b, :, L:] = np.nan
+        vc[b, :, L:] = np.inf
+    qd, kd, vd = gpu.to_device(q), gpu.to_device_bf16(kc), gpu.to_device_bf16(vc)
+    ld = gpu.to_device(lens)
+    ws = DecodeWorkspace(B, H, Hkv, D, S)
+    ref = ops.gqa_decode(q, kc, vc, lens)
+    outs = []
+    for hint in (0, 1, int(lens.sum()), 10 ** 9):
+        od = gpu.allocate((B, H, D), np.float32)
+        gqa_rows(qd, kd, vd, None, ld, od, B, H, H * D, D, H * D, D, S,
+                 workspace=ws, keys_hint=hint)
+        outs.append(od.to_numpy())
+        np.testing.assert_allclose(outs[-1], ref, atol=ATOL, err_msg=f"hint {hint}")
+        np.testing.assert_allclose(outs[-1], outs[0], atol=ATOL, err_msg=f"hint {hint}")
+    assert np.all(ws.counters.to_numpy() == 0)
+
+
 def test_uniform_length_without_lens_array(gpu):
     rng = np.random.default_rng(3)
     B, H, Hkv, D, S = 3, 6, 2, 64, 500

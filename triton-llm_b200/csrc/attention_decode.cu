@@ -1124,6 +1124,16 @@ int pick_group_tile_mma(int group) {
 // of one wave of resident CTAs (`slots`; 0 = unknown): 16-17 tiles there
 // measured 0.66 of HBM against 0.51 with 32, while a grid just over one
 // wave (12 tiles) fell to 0.48. Never more than kMaxSplits splits.
+// TLLM_GQA_CHUNK_TILES (tuning) fixes the chunk for every launch.
+bool chunk_env_fixed() {
+  static int env = -1;
+  if (env < 0) {
+    const char *e = getenv("TLLM_GQA_CHUNK_TILES");
+    env = (e && atoi(e) > 0) ? 1 : 0;
+  }
+  return env == 1;
+}
+
 int pick_chunk(int rows, int batch, int ygrid, int max_len, int slots) {
   const long tiles = (max_len + rows - 1) / rows;
   if (tiles <= 1) return rows;
@@ -1151,6 +1161,32 @@ int pick_chunk(int rows, int batch, int ygrid, int max_len, int slots) {
   return (int)(chunk_tiles * rows);
 }
 
+// Keys per CTA from the caller's estimate of the keys all rows read
+// (`keys`: the sum of the row lengths; the host sees only max_len, which
+// overstates a ragged batch): the smallest whole number of 64-key tiles c,
+// at least 3 and at most the longest row, whose working CTAs, estimated as
+//   ygrid * (keys / (64 c) + batch / 2)   (a row's last split is partial),
+// fill at most 85 % of one wave of resident CTAs. Measured on B200 at the
+// optimum chunk of each case: 8 ragged rows x 8 KV heads, 24 tiles (one
+// wave: 0.78 of HBM against 0.74 with the max_len plan of 32); 16 rows,
+// 48-56 tiles (0.89-0.91 against 0.76 at 32: 1.3 waves); 8 rows of 32k
+// keys x 1 KV head, 17; config 2, 12. Only for batches with fewer (row, KV
+// group) pairs than that target; larger ones fill the GPU at any split.
+int chunk_from_keys(int rows, int batch, int ygrid, long keys, int max_len,
+                    int slots, int fallback) {
+  const long target = (long)slots * 85 / 100;
+  if (keys <= 0 || slots <= 0 || (long)batch * ygrid >= target) return fallback;
+  const long max_tiles = ((long)max_len + rows - 1) / rows;
+  long lo = (max_tiles + kMaxSplits - 1) / kMaxSplits;
+  if (lo < 3) lo = 3;
+  if (lo >= max_tiles) return fallback;
+  const double tiles = (double)keys / rows;
+  for (long c = lo; c <= max_tiles; ++c)
+    if ((double)ygrid * (tiles / (double)c + 0.5 * batch) <= (double)target)
+      return (int)(c * rows);
+  return (int)(max_tiles * rows);
+}
+
 // Validation, split selection, tensor maps and launch shared by the decode
 // entry points; `err_word` is the device int that receives error codes.
 //   rows = query rows (B for decode); row r reads cache sequence
@@ -1163,7 +1199,7 @@ static int rows_impl(const float *q, long q_sb, long q_sh, const void *k_cache,
                      long out_plane_rows, long o_sb, long o_sh, int batch, int n_head, int n_kv_head, int head_dim,
                      int cache_batch, int max_seq, int max_len, float sm_scale,
                      void *partial, size_t partial_bytes, int32_t *counters,
-                     int *err_word, tllm_stream_t stream) {
+                     int *err_word, tllm_stream_t stream, long keys_hint = 0) {
   TLLM_CHECK_ARG(batch >= 0 && n_head > 0 && n_kv_head > 0,
                  "invalid head counts n_head=%d n_kv_head=%d", n_head,
                  n_kv_head);
@@ -1200,6 +1236,8 @@ static int rows_impl(const float *q, long q_sb, long q_sh, const void *k_cache,
 
   const int slots = mma ? mma_slots(head_dim, G) : 0;
   int chunk = pick_chunk(rows, batch, ygrid, max_len, slots);
+  if (mma && keys_hint > 0 && !chunk_env_fixed())
+    chunk = chunk_from_keys(rows, batch, ygrid, keys_hint, max_len, slots, chunk);
   int max_splits = (max_len + chunk - 1) / chunk;
   if (max_splits < 1) max_splits = 1;
   if (max_splits > 1) {
@@ -1319,6 +1357,23 @@ int tllm_gqa_rows(const float *q, long q_row_stride, long q_head_stride,
                    out_row_stride, out_head_stride, rows, n_head, n_kv_head, head_dim, cache_batch, max_seq,
                    max_len, sm_scale, partial, partial_bytes, counters,
                    device_error_ptr(), stream);
+}
+
+int tllm_gqa_rows_hint(const float *q, long q_row_stride, long q_head_stride,
+                       const void *k_cache, const void *v_cache, int kv_dtype,
+                       const int32_t *row_seq, const int32_t *row_len, void *out,
+                       int out_dtype, long out_plane_rows, long out_row_stride,
+                       long out_head_stride, int rows, int n_head, int n_kv_head,
+                       int head_dim, int cache_batch, int max_seq, int max_len,
+                       float sm_scale, void *partial, size_t partial_bytes,
+                       int32_t *counters, long keys_hint, tllm_stream_t stream) {
+  TLLM_INJECT("launch");
+  TLLM_CHECK_ARG(keys_hint >= 0, "keys_hint (%ld) must be >= 0", keys_hint);
+  return rows_impl(q, q_row_stride, q_head_stride, k_cache, v_cache, kv_dtype,
+                   row_len, row_seq, out, out_dtype, out_plane_rows,
+                   out_row_stride, out_head_stride, rows, n_head, n_kv_head, head_dim, cache_batch, max_seq,
+                   max_len, sm_scale, partial, partial_bytes, counters,
+                   device_error_ptr(), stream, keys_hint);
 }
 
 }  // extern "C"

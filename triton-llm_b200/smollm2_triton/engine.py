@@ -229,6 +229,10 @@ class LlamaSession:
         if max_prefill_rows:
             self._prefill_buffers(max_prefill_rows, attn_budget_bytes)
         self.graph = None
+        # keys a decode step's attention reads in all (sum of pos + 1), as
+        # last known on the host: plans the split-KV sizes of small batches
+        # (tllm_gqa_rows_hint); 0 = unknown
+        self._keys_hint = 0
 
     def _act(self, rows, cols):
         """A projection-input buffer: bf16 operand format for bf16 weights,
@@ -329,7 +333,8 @@ class LlamaSession:
         else:
             gqa_rows(q, k, v, row_seq, lens if decode else row_len, attn, M, w.H,
                      w.H * w.D, w.D, w.H * w.D, w.D,
-                     self.S if decode else (max_len or self.S), workspace=attn_ws)
+                     self.S if decode else (max_len or self.S), workspace=attn_ws,
+                     keys_hint=self._keys_hint if decode else 0)
         if part is None and decode and self.mlp_ws is not None:
             _mlp.mlp_block(attn, L["o"], h, L["ln2"], x, L["gu"], act, L["down"], M,
                            w.eps, self.mlp_ws)
@@ -486,6 +491,7 @@ class LlamaSession:
         self.ids.from_numpy(ids_full)
         self.pos.from_numpy(pos_full)
         self.lens.from_numpy(pos_full)
+        self._keys_hint = int(np.sum(pos_full, dtype=np.int64)) + self.B
         return host
 
     def set_state(self, pos: np.ndarray, ids: np.ndarray):
@@ -493,6 +499,7 @@ class LlamaSession:
         self.pos.from_numpy(np.asarray(pos, np.int32))
         self.lens.from_numpy(np.asarray(pos, np.int32))
         self.ids.from_numpy(np.asarray(ids, np.int32))
+        self._keys_hint = int(np.sum(np.asarray(pos), dtype=np.int64)) + self.B
 
     def decode_step(self, sample=True, temperature=0.0, top_k=0):
         """One decode step for all B sequences, device only.

@@ -93,6 +93,8 @@ SIGNATURES: dict[str, list] = {
                          _i, _i, _i, _i, _i, _f, _vp],
     "tllm_gqa_rows": [_vp, _l, _l, _vp, _vp, _i, _vp, _vp, _vp, _i, _l, _l, _l,
                       _i, _i, _i, _i, _i, _i, _i, _f, _vp, _sz, _vp, _vp],
+    "tllm_gqa_rows_hint": [_vp, _l, _l, _vp, _vp, _i, _vp, _vp, _vp, _i, _l, _l, _l,
+                           _i, _i, _i, _i, _i, _i, _i, _f, _vp, _sz, _vp, _l, _vp],
     # projections
     "tllm_linear_workspace": [_i, _i, _i, _psz, _psz],
     "tllm_linear_plan": [_i, _i, _i, _i, _pi],

@@ -25,20 +25,26 @@ from .attention_gqa import DecodeWorkspace, _kv_dtype
 
 def gqa_rows(q_dev, k_cache, v_cache, row_seq_dev, row_len_dev, out_dev, rows,
              n_head, q_row_stride, q_head_stride, out_row_stride, out_head_stride,
-             max_len, workspace=None, sm_scale=None, stream=None):
+             max_len, workspace=None, sm_scale=None, stream=None, keys_hint=0):
     """Low-level wrapper of tllm_gqa_rows (strides in elements). ``out_dev``
-    is fp32 or a TLLM_SPLIT buffer (``gpu.split_empty``)."""
+    is fp32 or a TLLM_SPLIT buffer (``gpu.split_empty``). ``keys_hint`` > 0
+    (the sum of the row lengths, as far as the caller knows it) plans the
+    split of each row's keys from that total (tllm_gqa_rows_hint)."""
     Bc, Hkv, S, D = k_cache.shape
     kvd = _kv_dtype(k_cache)
     if workspace is None:
         workspace = DecodeWorkspace(rows, n_head, Hkv, D, S, kvd)
     optr, odt, oplane = gpu.act_args(out_dev)
-    _lib.call("tllm_gqa_rows", q_dev.ptr, int(q_row_stride), int(q_head_stride),
-              k_cache.ptr, v_cache.ptr, kvd, _lib.ptr(row_seq_dev),
-              _lib.ptr(row_len_dev), optr, odt, oplane, int(out_row_stride),
-              int(out_head_stride), int(rows), int(n_head), Hkv, D, Bc, S,
-              int(max_len), float(sm_scale or 0.0), workspace.partial.ptr,
-              workspace.partial_bytes, workspace.counters.ptr, stream)
+    args = (q_dev.ptr, int(q_row_stride), int(q_head_stride),
+            k_cache.ptr, v_cache.ptr, kvd, _lib.ptr(row_seq_dev),
+            _lib.ptr(row_len_dev), optr, odt, oplane, int(out_row_stride),
+            int(out_head_stride), int(rows), int(n_head), Hkv, D, Bc, S,
+            int(max_len), float(sm_scale or 0.0), workspace.partial.ptr,
+            workspace.partial_bytes, workspace.counters.ptr)
+    if keys_hint and int(keys_hint) > 0:
+        _lib.call("tllm_gqa_rows_hint", *args, int(keys_hint), stream)
+    else:
+        _lib.call("tllm_gqa_rows", *args, stream)
     return out_dev
 
 
